@@ -1,0 +1,118 @@
+"""Seeded synthetic inputs for the KDA parity fixtures and GPU parity tests.
+
+Every tensor is drawn from a CPU ``torch.Generator`` in a fixed order, so the
+same case name always yields the same inputs on any machine.  Distributions
+follow the benchmark configurations of the KDA layer:
+
+* q/k/v (pre-conv) and decay/beta logits ~ N(0, 1);
+* ShortConv weights ~ N(0, 0.5) (``[H*D, 4]`` each for q, k, v);
+* ``A_log`` and ``dt_bias`` either zero (so ``g = -5 * sigmoid(N(0, 1))``) or
+  drawn like the reference module's initialisation;
+* optional initial state ~ N(0, 0.1) (fp32, ``[N, H, D, D]``);
+* upstream gradients dO ~ N(0, 1), dS ~ N(0, 0.1).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass
+class Case:
+    name: str
+    B: int
+    T: int
+    H: int
+    D: int = 128
+    conv: bool = True
+    h0: bool = False
+    final_state_grad: bool = False
+    cu_seqlens: list[int] | None = None
+    random_gate_params: bool = False
+    seed: int = 42
+    lower_bound: float = -5.0
+    extras: dict = field(default_factory=dict)
+
+
+CASES = {
+    # one full chunk plus a partial one, two heads, initial state and dS
+    "small": Case("small", B=1, T=80, H=2, h0=True, final_state_grad=True,
+                  random_gate_params=True, seed=7),
+    # the chunk_kda seam alone (inputs are post-conv)
+    "noconv": Case("noconv", B=2, T=70, H=1, conv=False, h0=True,
+                   final_state_grad=True, seed=11),
+    # packed documents with boundaries inside and on chunk edges
+    "varlen": Case("varlen", B=1, T=150, H=1, cu_seqlens=[0, 37, 101, 150],
+                   h0=True, final_state_grad=True, random_gate_params=True,
+                   seed=13),
+    # two full chunks, default gate parameters
+    "two_chunks": Case("two_chunks", B=1, T=128, H=1, seed=42),
+}
+
+
+def _normal(g, shape, std=1.0):
+    return torch.randn(*shape, generator=g, dtype=torch.float32) * std
+
+
+def make_inputs(case: Case) -> dict[str, torch.Tensor]:
+    """Returns float32 CPU tensors for ``case`` (always drawn in this order)."""
+    g = torch.Generator().manual_seed(case.seed)
+    B, T, H, D = case.B, case.T, case.H, case.D
+    out: dict[str, torch.Tensor] = {}
+    out["q"] = _normal(g, (B, T, H, D))
+    out["k"] = _normal(g, (B, T, H, D))
+    out["v"] = _normal(g, (B, T, H, D))
+    out["g"] = _normal(g, (B, T, H, D))
+    out["beta"] = _normal(g, (B, T, H))
+    out["conv_q"] = _normal(g, (H * D, 4), 0.5)
+    out["conv_k"] = _normal(g, (H * D, 4), 0.5)
+    out["conv_v"] = _normal(g, (H * D, 4), 0.5)
+    if case.random_gate_params:
+        out["A_log"] = _normal(g, (H,), 0.5)
+        dt = torch.exp(torch.rand(H * D, generator=g) * (math.log(1e-1) - math.log(1e-3))
+                       + math.log(1e-3)).clamp_min(1e-4)
+        out["dt_bias"] = dt + torch.log(-torch.expm1(-dt))
+    else:
+        out["A_log"] = torch.zeros(H)
+        out["dt_bias"] = torch.zeros(H * D)
+    N = B if case.cu_seqlens is None else len(case.cu_seqlens) - 1
+    out["h0"] = _normal(g, (N, H, D, D), 0.1)
+    out["do"] = _normal(g, (B, T, H, D))
+    out["dht"] = _normal(g, (N, H, D, D), 0.1)
+    return out
+
+
+# Configuration 0 of the benchmark: the full SophiaKDA projections on CPU.
+CFG0 = dict(B=1, T=512, dim=1536, H=16, D=128, rank=128, seed=42)
+
+
+def make_cfg0_inputs() -> dict[str, torch.Tensor]:
+    """x ~ N(0,1) ``[1,512,1536]``; q/k/v and decay projections ~ N(0, 0.02);
+    beta projection ~ N(0, 0.02); conv ~ N(0, 0.5); ``A_log = dt_bias = 0``.
+    Projections are evaluated in float64 and rounded to float32 so the KDA
+    inputs are bit-identical across machines."""
+    c = CFG0
+    g = torch.Generator().manual_seed(c["seed"])
+    inner = c["H"] * c["D"]
+    x = _normal(g, (c["B"], c["T"], c["dim"]))
+    wq = _normal(g, (inner, c["dim"]), 0.02)
+    wk = _normal(g, (inner, c["dim"]), 0.02)
+    wv = _normal(g, (inner, c["dim"]), 0.02)
+    wd = _normal(g, (c["rank"], c["dim"]), 0.02)
+    wu = _normal(g, (inner, c["rank"]), 0.02)
+    wb = _normal(g, (c["H"], c["dim"]), 0.02)
+    conv = [_normal(g, (inner, 4), 0.5) for _ in range(3)]
+    xd = x.double()
+    shp = (c["B"], c["T"], c["H"], c["D"])
+    return {
+        "q": (xd @ wq.double().T).float().view(shp),
+        "k": (xd @ wk.double().T).float().view(shp),
+        "v": (xd @ wv.double().T).float().view(shp),
+        "g": ((xd @ wd.double().T) @ wu.double().T).float().view(shp),
+        "beta": (xd @ wb.double().T).float(),
+        "conv_q": conv[0], "conv_k": conv[1], "conv_v": conv[2],
+        "A_log": torch.zeros(c["H"]), "dt_bias": torch.zeros(inner),
+    }

@@ -1,0 +1,147 @@
+"""Generates the KDA golden fixtures from Sophia's own reference modules.
+
+Usage::
+
+    python tests/golden/make_golden.py --reference <path to the Sophia checkout>
+
+The script imports ``ml.runtime.model.attention`` from the given checkout and
+runs, for every case of ``cases.py``:
+
+* ``CausalDepthwiseConv1d.forward`` (``attention.py:32-60``) on q/k/v unless
+  the case is post-conv,
+* ``SophiaKDA._reference_kda`` (``attention.py:260-294``) -- the reference's
+  own per-token recurrence, float32 inside,
+* torch autograd of ``sum(o * dO) + sum(S * dS)`` for every gradient,
+
+one document at a time for packed cases (state and conv history reset at each
+boundary).  Results go to ``tests/golden/<case>.npz``; configuration 0 of the
+benchmark (the full projections, T=512) goes to ``tests/golden/cfg0.npz`` as
+strided slices plus whole-tensor sums.  The fixtures are small enough to
+commit; the reference checkout is only needed to regenerate them.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+from cases import CASES, CFG0, make_cfg0_inputs, make_inputs  # noqa: E402
+
+
+def _module(reference_root: str, H: int, D: int, lower_bound: float):
+    sys.path.insert(0, reference_root)
+    from ml.runtime.model.attention import CausalDepthwiseConv1d, SophiaKDA
+    from ml.runtime.model.config import ModelArgs
+
+    args = ModelArgs(dim=64, num_heads=H, head_dim=D, kda_decay_rank=16,
+                     kda_output_gate_rank=16, mla_q_rank=16, mla_kv_rank=16,
+                     kda_backend="reference", use_cache=False,
+                     kda_decay_lower_bound=lower_bound, vocab_size=128,
+                     ffn_hidden=128, n_layers=4, max_batch_size=2)
+    return SophiaKDA(args), CausalDepthwiseConv1d
+
+
+def _input_sums(inputs: dict[str, torch.Tensor]) -> dict[str, float]:
+    return {k: float(v.double().sum()) for k, v in inputs.items()}
+
+
+def run_case(reference_root: str, case) -> dict[str, np.ndarray]:
+    inp = make_inputs(case)
+    mod, Conv = _module(reference_root, case.H, case.D, case.lower_bound)
+    HD = case.H * case.D
+    leaves = {k: v.clone().requires_grad_(True) for k, v in inp.items()
+              if k not in ("do", "dht")}
+    # the module's own parameters are the differentiable leaves
+    mod.A_log = torch.nn.Parameter(inp["A_log"].clone())
+    mod.dt_bias = torch.nn.Parameter(inp["dt_bias"].clone())
+    leaves["A_log"], leaves["dt_bias"] = mod.A_log, mod.dt_bias
+    convs = []
+    for name in ("conv_q", "conv_k", "conv_v"):
+        c = Conv(HD, 4)
+        c.weight = torch.nn.Parameter(inp[name].clone())
+        leaves[name] = c.weight
+        convs.append(c)
+
+    B = case.B
+    if case.cu_seqlens is None:
+        docs = [(b, 0, case.T) for b in range(B)]
+    else:
+        cu = case.cu_seqlens
+        docs = [(0, cu[n], cu[n + 1]) for n in range(len(cu) - 1)]
+    o_full = torch.zeros(B, case.T, case.H, case.D)
+    states = []
+    loss = torch.zeros((), dtype=torch.float32)
+    for n, (b, bos, eos) in enumerate(docs):
+        sl = slice(bos, eos)
+        xs = [leaves[k][b:b + 1, sl] for k in ("q", "k", "v")]
+        if case.conv:
+            post = []
+            for x, c in zip(xs, convs):
+                y, _ = c(x.reshape(1, eos - bos, HD))
+                post.append(y.reshape(1, eos - bos, case.H, case.D))
+            xs = post
+        h0 = leaves["h0"][n:n + 1] if case.h0 else None
+        o, S = mod._reference_kda(xs[0], xs[1], xs[2], leaves["g"][b:b + 1, sl],
+                                  leaves["beta"][b:b + 1, sl], h0)
+        loss = loss + (o * inp["do"][b:b + 1, sl]).sum()
+        if case.final_state_grad:
+            loss = loss + (S * inp["dht"][n:n + 1]).sum()
+        o_full[b:b + 1, sl] = o.detach()
+        states.append(S.detach())
+    loss.backward()
+    out = {"o": o_full.numpy(), "final_state": torch.cat(states).numpy()}
+    for k, v in leaves.items():
+        grad = v.grad if v.grad is not None else torch.zeros_like(v)
+        out["d_" + k] = grad.detach().numpy()
+    out["input_sums"] = np.array(json.dumps(_input_sums(inp)))
+    return out
+
+
+def run_cfg0(reference_root: str) -> dict[str, np.ndarray]:
+    inp = make_cfg0_inputs()
+    c = CFG0
+    mod, Conv = _module(reference_root, c["H"], c["D"], -5.0)
+    with torch.no_grad():
+        mod.A_log.zero_()
+        mod.dt_bias.zero_()
+        HD = c["H"] * c["D"]
+        post = []
+        for name, key in (("conv_q", "q"), ("conv_k", "k"), ("conv_v", "v")):
+            conv = Conv(HD, 4)
+            conv.weight.copy_(inp[name])
+            y, _ = conv(inp[key].reshape(c["B"], c["T"], HD))
+            post.append(y.reshape(c["B"], c["T"], c["H"], c["D"]))
+        o, S = mod._reference_kda(post[0], post[1], post[2], inp["g"], inp["beta"], None)
+    o64, S64 = o.double(), S.double()
+    return {
+        "o_slice": o[:, ::16].numpy(),
+        "state_slice": S[:, :, ::4].numpy(),
+        "o_stats": np.array([o64.sum(), o64.abs().sum(), (o64 ** 2).sum()]),
+        "state_stats": np.array([S64.sum(), S64.abs().sum(), (S64 ** 2).sum()]),
+        "input_sums": np.array(json.dumps(_input_sums(inp))),
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True,
+                    help="root of the Sophia checkout (contains ml/)")
+    ap.add_argument("--out", default=str(HERE))
+    a = ap.parse_args()
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    for name, case in CASES.items():
+        np.savez_compressed(Path(a.out) / f"{name}.npz", **run_case(a.reference, case))
+        print("wrote", name)
+    np.savez_compressed(Path(a.out) / "cfg0.npz", **run_cfg0(a.reference))
+    print("wrote cfg0")
+
+
+if __name__ == "__main__":
+    main()
