@@ -1,0 +1,353 @@
+"""Benchmark of the B200 KDA layer (forward + backward), one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg1|cfg3]
+
+Step = one forward + backward of the KDA layer (ShortConv+SiLU, L2 norms,
+gate, beta, chunked gated delta rule) over one batch of synthetic inputs of
+configuration 1 (8 sequences x 4096 tokens x 16 heads x 128, bf16, fp32 state)
+per GPU, then one NCCL all-reduce of the layer's weight gradients when N > 1
+(weak scaling: every rank processes its own 8 sequences).  ``--workload cfg3``
+shards configuration 3's 320 sequences over the ranks instead (strong scaling).
+
+Timing: W untimed warm-up steps, then K steps between a barrier +
+synchronize on both sides, CUDA events on the launch stream, max over ranks.
+Inputs (q, k, v, g, dO: 128 MiB each) exceed the 126 MB L2, so no flush is
+needed between steps.  The ``e2e`` figure repeats the step through the public
+API with the step's inputs copied from pinned host memory and the weight
+gradients read back each step.  ``--impl reference`` times the reference's CPU
+implementation (the oracle restatement of ``SophiaKDA._reference_kda`` +
+``CausalDepthwiseConv1d`` with autograd) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "KDA layer fwd+bwd tokens/s at H=16,D=128,T=4096 (1/2/4/8 B200) + % roofline"
+H, D, T = 16, 128, 4096
+
+# Algorithmic HBM bytes per token-head of each kernel (reads + writes of its
+# interface tensors, each once; bf16 activations, fp32 per-chunk vectors).
+KERNEL_BYTES_PER_TOKEN_HEAD = {
+    "fwd_intra": 1026 + 1160,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C out
+    "fwd_state": 1160 + 1024,   # W,U,Qt,Kbar,M,2^Gam_C in; o, chunk states, v_new out
+    "bwd_state": 1928 + 1160,   # W,Qt,Kbar,M,2^Gam_C,v_new,dO,chunk states in; dE,dQt,dW,dKbar,dM,dGam_C out
+    "bwd_intra": 2186 + 1042,   # inputs + dE,dW,dQt,dKbar,dM,dGam_C in; dq_hat,dk_hat,dv,dg,dbeta,partials out
+    "bwd_post": 1536 + 768,     # q,k,v and dq_hat,dk_hat,dv in; dq,dk,dv out
+}
+# Tensor-core FLOPs per token-head of each kernel (algorithmic, no recompute).
+KERNEL_FLOPS_PER_TOKEN_HEAD = {
+    "fwd_intra": 2 * (2 * 64 * 128 + 2 * 64 * 128) + 2731,  # L', M, W, U and the inverse
+    "fwd_state": 2 * 3 * 128 * 128 + 2 * 64 * 128,          # E, O (state part + M E), S update
+    "bwd_state": 2 * 2 * (2 * 3 * 128 * 128 + 2 * 64 * 128),
+    "bwd_intra": 2 * 2 * (2 * (2 * 64 * 128 + 2 * 64 * 128) + 2731),
+    "bwd_post": 0,
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg1", "cfg3"], default="cfg1")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        load = [x for x in sm if x > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(B, device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *s, std=1.0: torch.randn(*s, device=device, generator=g) * std  # noqa: E731
+    x = {k: rn(B, T, H, D).to(torch.bfloat16) for k in ("q", "k", "v", "g")}
+    x["beta"] = rn(B, T, H).to(torch.bfloat16)
+    x["do"] = rn(B, T, H, D).to(torch.bfloat16)
+    w = {"A_log": torch.zeros(H, device=device), "dt_bias": torch.zeros(H * D, device=device)}
+    for k in ("conv_q", "conv_k", "conv_v"):
+        w[k] = rn(H * D, 4, std=0.5)
+    return x, w
+
+
+def bench_ours(a, rank, world, local_rank):
+    import torch.distributed as dist
+    from sophia_b200 import _lib, kda_layer
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    B = 8 if a.workload == "cfg1" else 320 // world
+    x, w = make_inputs(B, device, 42 + rank)
+    acts = {k: x[k].clone().requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
+    params = {k: v.clone().requires_grad_(True) for k, v in w.items()}
+    bucket = torch.empty(H + H * D + 3 * H * D * 4, device=device, dtype=torch.float32)
+
+    def step(inputs=None):
+        src = acts if inputs is None else inputs
+        for t in list(src.values()) + list(params.values()):
+            t.grad = None
+        o, _ = kda_layer(src["q"], src["k"], src["v"], src["g"], src["beta"], params["A_log"], params["dt_bias"],
+                         params["conv_q"], params["conv_k"], params["conv_v"])
+        o.backward(x["do"] if inputs is None else inputs["_do"])
+        torch.cat([params[k].grad.reshape(-1) for k in ("A_log", "dt_bias", "conv_q", "conv_k", "conv_v")],
+                  out=bucket)
+        if world > 1:
+            dist.all_reduce(bucket)
+        return bucket
+
+    def timed(fn, steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms
+
+    for _ in range(a.warmup):
+        step()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    ms = timed(step, a.steps)
+    clocks = sampler.stop()
+    tokens = world * B * T * a.steps
+    value = tokens / (ms / 1e3)
+
+    # per-kernel device times (second pass, CUDA events around every launch)
+    _lib.timing_reset()
+    _lib.timing_enable(True)
+    ms_prof = timed(step, a.steps)
+    _lib.timing_enable(False)
+    kern = _lib.timing_read()
+    _lib.timing_reset()
+    launches = sum(n for n, _ in kern.values())
+
+    # end to end through the public API: pinned host inputs copied in, weight
+    # gradients read back, every step
+    host = {k: x[k].cpu().pin_memory() for k in ("q", "k", "v", "g", "beta", "do")}
+    dev_in = {k: torch.empty_like(x[k]) for k in host}
+    out_host = torch.empty(bucket.numel(), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        for k in host:
+            dev_in[k].copy_(host[k], non_blocking=True)
+        inp = {k: dev_in[k].requires_grad_(True) if k != "do" else dev_in[k] for k in ("q", "k", "v", "g", "beta")}
+        inp["_do"] = dev_in["do"]
+        step(inp)
+        out_host.copy_(bucket, non_blocking=True)
+        for k in ("q", "k", "v", "g", "beta"):
+            dev_in[k].requires_grad_(False)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(a.steps, 10))
+    ms_e2e = timed(e2e_step, e2e_steps)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    hbm, tc, tc_sus, src = peaks()
+    # dominant kernel and its roofline
+    th = B * T * H  # token-heads per launch
+    dom = max((k for k in kern if k in KERNEL_BYTES_PER_TOKEN_HEAD), key=lambda k: kern[k][1])
+    n_l, tot = kern[dom]
+    per_launch_ms = tot / max(1, n_l)
+    alg_bytes = KERNEL_BYTES_PER_TOKEN_HEAD[dom] * th
+    achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tr = json.load(f)
+            if dom in tr:
+                traffic = tr[dom]["bytes_per_token_head"] * th
+        except Exception:
+            traffic = None
+    # per-kernel roofline of the whole step: sum_k max(F_k/P, B_k/BW)
+    roof_ms = 0.0
+    for k, bpt in KERNEL_BYTES_PER_TOKEN_HEAD.items():
+        f = KERNEL_FLOPS_PER_TOKEN_HEAD[k] * th
+        roof_ms += max(f / (tc_sus * 1e12), bpt * th / (hbm * 1e9)) * 1e3
+    kernel_ms_per_step = {k: round(v[1] / a.steps, 4) for k, v in kern.items() if v[0]}
+    return {
+        "value": value, "ms": ms / a.steps, "B": B, "clocks": clocks,
+        "e2e": {"value": world * B * T * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "peak_source": src,
+                     "per_kernel_roofline_ms": round(roof_ms, 4),
+                     "per_kernel_roofline_frac": round(roof_ms / (ms_prof / a.steps), 4),
+                     "kernel_ms_per_step": kernel_ms_per_step},
+    }
+
+
+def cpu_sample(tokens: int, threads: int | None = None):
+    """The reference's CPU path (oracle restatement) fwd+bwd on one sequence
+    of `tokens` tokens x 16 heads, fp32, torch autograd.  Returns tokens/s."""
+    sys.path.insert(0, ROOT)
+    from oracle.kda_oracle import kda_layer as oracle_layer
+    if threads:
+        torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    mk = lambda *s, std=1.0: (torch.randn(*s, generator=g) * std).requires_grad_(True)  # noqa: E731
+    q, k, v, gg = (mk(1, tokens, H, D) for _ in range(4))
+    beta = mk(1, tokens, H)
+    A, dtb = torch.zeros(H, requires_grad=True), torch.zeros(H * D, requires_grad=True)
+    convs = [mk(H * D, 4, std=0.5) for _ in range(3)]
+    do = torch.randn(1, tokens, H, D, generator=g)
+    t0 = time.perf_counter()
+    out = oracle_layer(q, k, v, gg, beta, A, dtb, conv_weights=convs, compute_dtype=torch.float32)
+    (out.o * do).sum().backward()
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt
+
+
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": a.workload, "global_batch": (8 * world if a.workload == "cfg1" else 320),
+              "seq_len": T, "heads": H, "head_dim": D, "chunk": 64,
+              "parallelism": f"dp{world}", "l2": "inputs larger than L2 (128 MiB per tensor), no flush"}
+    if a.impl == "reference":
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        sample_tokens = 512
+        for _ in range(a.warmup):
+            cpu_sample(64)
+        rates, secs = [], 0.0
+        for _ in range(a.steps):
+            r, dt = cpu_sample(sample_tokens)
+            rates.append(r)
+            secs += dt
+        value = sample_tokens * a.steps / secs
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": secs / a.steps * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "impl": "reference",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": f"1 x {sample_tokens} tokens x 16 heads fwd+bwd per step (oracle "
+                                           "restatement of the reference CPU path, torch fp32 autograd)"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    res = bench_ours(a, rank, world, local_rank)
+    cpu = None
+    if rank == 0 and world == 1:
+        threads = os.cpu_count() or 1
+        rate, dt = cpu_sample(2048, threads)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"1 x 2048 tokens x 16 heads fwd+bwd ({dt:.1f} s; oracle restatement of the reference "
+                         "CPU path, torch fp32 autograd)"}
+    if rank == 0:
+        line = {"metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": res["ms"], "higher_is_better": True,
+                "scaling": "weak" if a.workload == "cfg1" else "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config, "roofline": res["roofline"], "cpu_baseline": cpu,
+                "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

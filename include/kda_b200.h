@@ -1,0 +1,125 @@
+/*
+ * kda_b200 -- C ABI of the B200 (sm_100a) Kimi Delta Attention layer.
+ *
+ * The reference (Sophia) reaches this path through two Python seams, and this
+ * ABI is what those seams bind to (see INTEGRATION.md for the ctypes stub):
+ *
+ *   SophiaKDA._fla_chunk_kda() -> chunk_kda(q, k, v, g, beta, ...)
+ *       ml/runtime/model/attention.py:305-312 (seam), called at :349-365 with
+ *       use_qk_l2norm_in_kernel / use_gate_in_kernel / use_beta_sigmoid_in_kernel
+ *       / safe_gate all true and lower_bound = kda_decay_lower_bound; the
+ *       callee's contract is flash-linear-attention's chunk_kda
+ *       (fla/ops/kda/chunk.py:167-411).  -> kda_b200_fwd / kda_b200_bwd with
+ *       the conv taps set to NULL.
+ *   CausalDepthwiseConv1d.forward (attention.py:32-60) followed by the
+ *       recurrence (attention.py:373-410) -> kda_b200_fwd / kda_b200_bwd with
+ *       the three conv tap tensors: the ShortConv+SiLU is fused into the chunk
+ *       prologue.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer; `stream` is a cudaStream_t.  Nothing
+ *     allocates: the caller passes the `saved` (forward -> backward) and
+ *     `workspace` buffers whose sizes the *_bytes functions return.  Nothing
+ *     synchronises with the host, so calls can be captured in CUDA graphs.
+ *   - q, k, v, g, o and all their gradients are bf16 [B, T, H, 128]; beta and
+ *     dbeta are bf16 [B, T, H]; A_log [H], dt_bias [H*128], conv taps
+ *     [H*128, 4], states [N, H, 128, 128] are fp32.
+ *   - cu_seqlens (int32 [N+1], device) packs N sequences along T (then B == 1);
+ *     the recurrent state and the conv history restart at every boundary.
+ *   - Return value: KDA_OK or an error code; kda_b200_last_error() describes
+ *     the last failure of the calling thread.
+ */
+#ifndef KDA_B200_H_
+#define KDA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDA_OK 0
+#define KDA_ERR_INVALID 1     /* bad shape, pointer, alignment or parameter   */
+#define KDA_ERR_UNSUPPORTED 2 /* valid in the reference but not implemented  */
+#define KDA_ERR_CUDA 3        /* a CUDA launch failed                          */
+
+/* Library version string. */
+const char* kda_b200_version(void);
+
+/* Description of the last error returned to the calling thread. */
+const char* kda_b200_last_error(void);
+
+/* Bytes of the forward -> backward buffer (chunk intermediates, chunk-start
+ * states, v_new).  total_tokens = B*T; N = number of sequences. */
+size_t kda_b200_saved_bytes(int64_t total_tokens, int H, int N, int packed);
+
+/* Bytes of scratch for kda_b200_fwd.  training = 0 means `saved` is NULL and
+ * the intermediates live in the workspace instead. */
+size_t kda_b200_fwd_workspace_bytes(int64_t total_tokens, int H, int N, int packed, int training);
+
+/* Bytes of scratch for kda_b200_bwd. */
+size_t kda_b200_bwd_workspace_bytes(int64_t total_tokens, int H, int N, int packed);
+
+/*
+ * Forward.  Replaces chunk_kda's forward (fla/ops/kda/chunk.py:22-115) in the
+ * configuration of attention.py:349-365, optionally preceded by the ShortConv
+ * of attention.py:32-60 when conv_q/conv_k/conv_v are non-NULL.
+ *   h0: initial state or NULL (zeros).  ht: final state or NULL.
+ *   saved: NULL for inference, else kda_b200_saved_bytes() bytes to hand to
+ *   kda_b200_bwd.
+ */
+int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                 const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                 const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H, int D,
+                 int N, float scale, float lower_bound, void* o, float* ht, void* saved, size_t saved_bytes,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward.  Replaces ChunkKDAFunction.backward (fla/ops/kda/chunk.py:117-162)
+ * plus, with conv taps, the autograd of attention.py:32-60.  Inputs as in the
+ * forward plus `saved`, the output gradient do_ and the final-state gradient
+ * dht (NULL = zero).  Writes dq, dk, dv (w.r.t. the inputs as given, i.e.
+ * pre-conv when conv taps are set), dg (gate logits), dbeta (beta logits),
+ * dA_log [H], ddt_bias [H*128], dconv_* [H*128, 4] (when conv) and dh0 (when
+ * non-NULL).
+ */
+int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                 const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                 const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H, int D,
+                 int N, float scale, float lower_bound, const void* saved, size_t saved_bytes, const void* do_,
+                 const float* dht, void* dq, void* dk, void* dv, void* dg, void* dbeta, float* dA_log,
+                 float* ddt_bias, float* dconv_q, float* dconv_k, float* dconv_v, float* dh0, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/*
+ * Packed-sequence chunk table (integer bookkeeping of prepare_chunk_indices /
+ * prepare_chunk_offsets, fla/ops/utils/index.py:138-158), built on the device
+ * without a host sync.  offsets: int32 [N+1]; chunk_seq: int32 [max_chunks]
+ * with max_chunks >= total_tokens/64 + N; error_flag: int32, written 1 when
+ * cu_seqlens does not start at 0, decreases, or does not end at total_tokens
+ * (then every offset is 0 and the layer calls that use the table do nothing).
+ * kda_b200_fwd / kda_b200_bwd build this table in their workspace.
+ */
+int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens, int32_t* offsets,
+                         int32_t* chunk_seq, int32_t* error_flag, void* stream);
+
+/*
+ * Per-kernel device timing, for benchmarks and profiling summaries.  While
+ * enabled, every kernel launch of kda_b200_fwd / kda_b200_bwd is bracketed by
+ * two cudaEventRecord calls on its stream.  kda_b200_timing_read synchronises
+ * those events and returns, per kernel, its static name, the number of
+ * launches and the summed milliseconds since the last reset.  It returns the
+ * number of kernels (> 0), or minus an error code on failure.  The
+ * reference has no counterpart (its tracing is version/hash records only,
+ * ml/training/pretrain/engine/sm120_concurrent_ffn.py:468-477).
+ */
+int kda_b200_timing_enable(int on);
+int kda_b200_timing_reset(void);
+int kda_b200_timing_read(int max_kernels, const char** names, int* launches, float* total_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDA_B200_H_ */

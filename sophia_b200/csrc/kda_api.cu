@@ -1,0 +1,484 @@
+// C ABI of the KDA layer (declared in include/kda_b200.h): argument checks,
+// buffer carving and kernel launches.  No allocation, no host sync.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kda_b200.h"
+#include "kda_bwd_intra.cuh"
+#include "kda_post.cuh"
+
+using namespace kda;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int64_t max_chunks(int64_t tokens, int N) { return tokens / C + N; }
+
+// Sub-buffer carving of a caller buffer.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+  template <typename T>
+  T* take(size_t bytes) {
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += align256(bytes);
+    return p;
+  }
+};
+
+struct SavedView {
+  bf16 *W, *U, *Qt, *Kb, *E, *M, *hs;
+  float* dC;
+};
+
+SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) {
+  SavedView s;
+  const size_t row = (size_t)TT * H * D * 2;
+  s.W = cv.take<bf16>(row);
+  s.U = cv.take<bf16>(row);
+  s.Qt = cv.take<bf16>(row);
+  s.Kb = cv.take<bf16>(row);
+  s.M = cv.take<bf16>((size_t)TT * H * 64 * 2);
+  s.dC = cv.take<float>((size_t)mc * H * D * 4);
+  if (with_bwd) {
+    s.E = cv.take<bf16>(row);
+    s.hs = cv.take<bf16>((size_t)mc * H * D * D * 2);
+  } else {
+    s.E = nullptr;
+    s.hs = nullptr;
+  }
+  return s;
+}
+
+struct Table {
+  int* offsets;
+  int* chunk_seq;
+  int* err;
+};
+
+Table carve_table(Carver& cv, int N, int64_t mc) {
+  Table t;
+  t.offsets = cv.take<int>((size_t)(N + 1) * 4);
+  t.chunk_seq = cv.take<int>((size_t)mc * 4);
+  t.err = cv.take<int>(4);
+  return t;
+}
+
+struct BwdView {
+  bf16 *dE, *dQt, *dW, *dKb, *dM, *dq_hat, *dk_hat, *dv_hat;
+  float *dGC, *partA, *partB, *partW;
+};
+
+BwdView carve_bwd(Carver& cv, int64_t TT, int H, int64_t mc) {
+  BwdView b;
+  const size_t row = (size_t)TT * H * D * 2;
+  b.dE = cv.take<bf16>(row);
+  b.dQt = cv.take<bf16>(row);
+  b.dW = cv.take<bf16>(row);
+  b.dKb = cv.take<bf16>(row);
+  b.dq_hat = cv.take<bf16>(row);
+  b.dk_hat = cv.take<bf16>(row);
+  b.dv_hat = cv.take<bf16>(row);
+  b.dM = cv.take<bf16>((size_t)TT * H * 64 * 2);
+  b.dGC = cv.take<float>((size_t)mc * H * D * 4);
+  b.partA = cv.take<float>((size_t)mc * H * D * 4);
+  b.partB = cv.take<float>((size_t)mc * H * D * 4);
+  b.partW = cv.take<float>((size_t)mc * 3 * H * D * 4 * 4);
+  return b;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+struct Problem {
+  int B, T, H, N;
+  bool packed, conv;
+  int64_t TT, mc;
+  int grid_chunks;
+  SeqInfo seq;
+};
+
+int check_common(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* A_log,
+                 const float* dt_bias, const float* cq, const float* ck, const float* cvv, const int32_t* cu, int B,
+                 int T, int H, int D_, int N, float lower_bound, Problem& pr) {
+  if (D_ != D) return fail(KDA_ERR_UNSUPPORTED, "head dim must be 128, got " + std::to_string(D_));
+  if (B < 1 || T < 0 || H < 1) return fail(KDA_ERR_INVALID, "B >= 1, T >= 0 and H >= 1 are required");
+  if (!(lower_bound >= -5.f && lower_bound < 0.f))
+    return fail(KDA_ERR_INVALID, "`lower_bound` must be in the safe range [-5, 0), got " + std::to_string(lower_bound));
+  if (!q || !k || !v || !g || !beta || !A_log || !dt_bias) return fail(KDA_ERR_INVALID, "null input pointer");
+  const bool anyconv = cq || ck || cvv, allconv = cq && ck && cvv;
+  if (anyconv && !allconv) return fail(KDA_ERR_INVALID, "conv taps must be given for all of q, k, v or none");
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(g, 16))
+    return fail(KDA_ERR_INVALID, "q, k, v and g must be 16-byte aligned");
+  if (!aligned(dt_bias, 16)) return fail(KDA_ERR_INVALID, "dt_bias must be 16-byte aligned");
+  if (allconv && (!aligned(cq, 16) || !aligned(ck, 16) || !aligned(cvv, 16)))
+    return fail(KDA_ERR_INVALID, "conv taps must be 16-byte aligned");
+  if (cu) {
+    if (B != 1)
+      return fail(KDA_ERR_INVALID, "The batch size is expected to be 1 rather than " + std::to_string(B) +
+                                       " when using `cu_seqlens`.");
+    if (N < 1) return fail(KDA_ERR_INVALID, "N >= 1 sequences are required with cu_seqlens");
+  } else if (N != B) {
+    return fail(KDA_ERR_INVALID, "N must equal B without cu_seqlens");
+  }
+  pr.B = B; pr.T = T; pr.H = H; pr.N = N;
+  pr.packed = cu != nullptr;
+  pr.conv = allconv;
+  pr.TT = (int64_t)B * T;
+  pr.mc = max_chunks(pr.TT, N);
+  pr.seq.cu_seqlens = cu;
+  pr.seq.chunk_offsets = nullptr;
+  pr.seq.chunk_seq = nullptr;
+  pr.seq.N = N;
+  pr.seq.T = T;
+  pr.seq.nt = (T + C - 1) / C;
+  pr.grid_chunks = pr.packed ? (int)pr.mc : B * pr.seq.nt;
+  if (pr.mc > (int64_t)INT32_MAX / 2) return fail(KDA_ERR_INVALID, "too many tokens");
+  return KDA_OK;
+}
+
+// ---- optional per-launch device timing (CUDA events on the launch stream)
+enum KernelId { K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_COUNT };
+const char* const kKernelNames[K_COUNT] = {"chunk_table", "fwd_intra", "fwd_state", "bwd_state",
+                                           "bwd_intra",   "bwd_post",  "reduce"};
+
+struct Timing {
+  std::mutex mu;
+  bool on = false;
+  std::vector<cudaEvent_t> pool;  // pairs (start, stop)
+  std::vector<int> ids;           // kernel id of each recorded pair
+  size_t used = 0;
+};
+Timing g_timing;
+
+struct TimedLaunch {
+  cudaEvent_t stop = nullptr;
+  cudaStream_t st;
+  TimedLaunch(int id, cudaStream_t s) : st(s) {
+    if (!g_timing.on) return;
+    std::lock_guard<std::mutex> lk(g_timing.mu);
+    if (g_timing.used + 2 > g_timing.pool.size()) {
+      for (int i = 0; i < 64; ++i) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return;
+        g_timing.pool.push_back(e);
+      }
+    }
+    cudaEvent_t start = g_timing.pool[g_timing.used];
+    stop = g_timing.pool[g_timing.used + 1];
+    g_timing.used += 2;
+    g_timing.ids.push_back(id);
+    cudaEventRecord(start, st);
+  }
+  ~TimedLaunch() {
+    if (stop) cudaEventRecord(stop, st);
+  }
+};
+
+int launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(KDA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return KDA_OK;
+}
+
+template <typename K>
+int set_smem(K kernel, int bytes, const char* name) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(KDA_ERR_CUDA, std::string(name) + " smem attribute: " + cudaGetErrorString(e));
+  return KDA_OK;
+}
+
+int build_table(Problem& pr, Table& t, cudaStream_t st) {
+  if (!pr.packed) return KDA_OK;
+  {
+    TimedLaunch tl(K_TABLE, st);
+    kda_chunk_table_kernel<<<1, 1024, 0, st>>>(pr.seq.cu_seqlens, pr.N, (long long)pr.TT, t.offsets, t.chunk_seq,
+                                               t.err);
+  }
+  pr.seq.chunk_offsets = t.offsets;
+  pr.seq.chunk_seq = t.chunk_seq;
+  return launch_check("chunk table");
+}
+
+PrologueIn prologue_in(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* A_log,
+                       const float* dt_bias, const float* cq, const float* ck, const float* cvv, int H, float scale,
+                       float lb) {
+  PrologueIn in;
+  in.q = static_cast<const bf16*>(q);
+  in.k = static_cast<const bf16*>(k);
+  in.v = static_cast<const bf16*>(v);
+  in.g = static_cast<const bf16*>(g);
+  in.beta = static_cast<const bf16*>(beta);
+  in.A_log = A_log;
+  in.dt_bias = dt_bias;
+  in.conv_q = cq;
+  in.conv_k = ck;
+  in.conv_v = cvv;
+  in.H = H;
+  in.scale = scale;
+  in.lower_bound = lb;
+  return in;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* kda_b200_version(void) { return "kda_b200 0.1.0 (sm_100a)"; }
+
+const char* kda_b200_last_error(void) { return g_last_error.c_str(); }
+
+size_t kda_b200_saved_bytes(int64_t total_tokens, int H, int N, int packed) {
+  (void)packed;
+  Carver cv(nullptr);
+  carve_saved(cv, total_tokens, H, max_chunks(total_tokens, N), true);
+  return cv.off;
+}
+
+size_t kda_b200_fwd_workspace_bytes(int64_t total_tokens, int H, int N, int packed, int training) {
+  (void)packed;
+  Carver cv(nullptr);
+  int64_t mc = max_chunks(total_tokens, N);
+  carve_table(cv, N, mc);
+  if (!training) carve_saved(cv, total_tokens, H, mc, false);
+  return cv.off;
+}
+
+size_t kda_b200_bwd_workspace_bytes(int64_t total_tokens, int H, int N, int packed) {
+  (void)packed;
+  Carver cv(nullptr);
+  int64_t mc = max_chunks(total_tokens, N);
+  carve_table(cv, N, mc);
+  carve_bwd(cv, total_tokens, H, mc);
+  return cv.off;
+}
+
+int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens, int32_t* offsets,
+                         int32_t* chunk_seq, int32_t* error_flag, void* stream) {
+  if (!cu_seqlens || !offsets || !chunk_seq || !error_flag || N < 1)
+    return fail(KDA_ERR_INVALID, "chunk table needs cu_seqlens, offsets, chunk_seq, error_flag and N >= 1");
+  kda_chunk_table_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(cu_seqlens, N, (long long)total_tokens,
+                                                                            offsets, chunk_seq, error_flag);
+  return launch_check("chunk table");
+}
+
+int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* A_log,
+                 const float* dt_bias, const float* conv_q, const float* conv_k, const float* conv_v, const float* h0,
+                 const int32_t* cu_seqlens, int B, int T, int H, int D_, int N, float scale, float lower_bound,
+                 void* o, float* ht, void* saved, size_t saved_bytes, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  Problem pr;
+  int rc = check_common(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, cu_seqlens, B, T, H, D_, N,
+                        lower_bound, pr);
+  if (rc) return rc;
+  if (!o) return fail(KDA_ERR_INVALID, "null output pointer");
+  if (!aligned(o, 16)) return fail(KDA_ERR_INVALID, "o must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool training = saved != nullptr;
+  size_t need_ws = kda_b200_fwd_workspace_bytes(pr.TT, H, N, pr.packed, training);
+  if (!workspace || workspace_bytes < need_ws)
+    return fail(KDA_ERR_INVALID, "workspace too small: need " + std::to_string(need_ws) + " bytes");
+  if (training && saved_bytes < kda_b200_saved_bytes(pr.TT, H, N, pr.packed))
+    return fail(KDA_ERR_INVALID, "saved buffer too small");
+  if (pr.TT == 0) {
+    if (ht) {
+      size_t bytes = (size_t)N * H * D * D * 4;
+      cudaError_t e = h0 ? cudaMemcpyAsync(ht, h0, bytes, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(ht, 0, bytes, st);
+      if (e != cudaSuccess) return fail(KDA_ERR_CUDA, cudaGetErrorString(e));
+    }
+    return KDA_OK;
+  }
+  Carver wcv(workspace);
+  Table tab = carve_table(wcv, N, pr.mc);
+  Carver scv(training ? saved : nullptr);
+  SavedView sv = training ? carve_saved(scv, pr.TT, H, pr.mc, true) : carve_saved(wcv, pr.TT, H, pr.mc, false);
+  if ((rc = build_table(pr, tab, st))) return rc;
+
+  FwdIntraParams ip;
+  ip.in = prologue_in(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, H, scale, lower_bound);
+  ip.seq = pr.seq;
+  ip.conv = pr.conv;
+  ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC;
+  if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
+  {
+    TimedLaunch tl(K_FWD_INTRA, st);
+    kda_fwd_intra_kernel<<<dim3(pr.grid_chunks, H), 256, IntraSmem::END, st>>>(ip);
+  }
+  if ((rc = launch_check("fwd intra"))) return rc;
+
+  FwdStateParams sp;
+  sp.seq = pr.seq;
+  sp.H = H;
+  sp.W = sv.W; sp.U = sv.U; sp.Qt = sv.Qt; sp.Kb = sv.Kb; sp.M = sv.M; sp.dC = sv.dC;
+  sp.h0 = h0;
+  sp.o = static_cast<bf16*>(o);
+  sp.hs = sv.hs;
+  sp.E = sv.E;
+  sp.ht = ht;
+  if ((rc = set_smem(kda_fwd_state_kernel, StateSmem::END, "fwd state"))) return rc;
+  {
+    TimedLaunch tl(K_FWD_STATE, st);
+    kda_fwd_state_kernel<<<dim3(N, H), 256, StateSmem::END, st>>>(sp);
+  }
+  return launch_check("fwd state");
+}
+
+int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* A_log,
+                 const float* dt_bias, const float* conv_q, const float* conv_k, const float* conv_v, const float* h0,
+                 const int32_t* cu_seqlens, int B, int T, int H, int D_, int N, float scale, float lower_bound,
+                 const void* saved, size_t saved_bytes, const void* do_, const float* dht, void* dq, void* dk,
+                 void* dv, void* dg, void* dbeta, float* dA_log, float* ddt_bias, float* dconv_q, float* dconv_k,
+                 float* dconv_v, float* dh0, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)h0;
+  Problem pr;
+  int rc = check_common(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, cu_seqlens, B, T, H, D_, N,
+                        lower_bound, pr);
+  if (rc) return rc;
+  if (!saved || saved_bytes < kda_b200_saved_bytes(pr.TT, H, N, pr.packed))
+    return fail(KDA_ERR_INVALID, "saved buffer missing or too small");
+  if (!do_ || !dq || !dk || !dv || !dg || !dbeta || !dA_log || !ddt_bias)
+    return fail(KDA_ERR_INVALID, "null gradient pointer");
+  if (pr.conv && (!dconv_q || !dconv_k || !dconv_v)) return fail(KDA_ERR_INVALID, "null conv gradient pointer");
+  if (!aligned(do_, 16) || !aligned(dq, 16) || !aligned(dk, 16) || !aligned(dv, 16) || !aligned(dg, 4))
+    return fail(KDA_ERR_INVALID, "gradient tensors must be 16-byte aligned");
+  size_t need_ws = kda_b200_bwd_workspace_bytes(pr.TT, H, N, pr.packed);
+  if (!workspace || workspace_bytes < need_ws)
+    return fail(KDA_ERR_INVALID, "workspace too small: need " + std::to_string(need_ws) + " bytes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pr.TT == 0) {
+    cudaMemsetAsync(dA_log, 0, (size_t)H * 4, st);
+    cudaMemsetAsync(ddt_bias, 0, (size_t)H * D * 4, st);
+    if (pr.conv) {
+      cudaMemsetAsync(dconv_q, 0, (size_t)H * D * 16, st);
+      cudaMemsetAsync(dconv_k, 0, (size_t)H * D * 16, st);
+      cudaMemsetAsync(dconv_v, 0, (size_t)H * D * 16, st);
+    }
+    if (dh0) {
+      size_t bytes = (size_t)N * H * D * D * 4;
+      if (dht) cudaMemcpyAsync(dh0, dht, bytes, cudaMemcpyDeviceToDevice, st);
+      else cudaMemsetAsync(dh0, 0, bytes, st);
+    }
+    return launch_check("empty backward");
+  }
+  Carver wcv(workspace);
+  Table tab = carve_table(wcv, N, pr.mc);
+  BwdView bv = carve_bwd(wcv, pr.TT, H, pr.mc);
+  Carver scv(const_cast<void*>(saved));
+  SavedView sv = carve_saved(scv, pr.TT, H, pr.mc, true);
+  if ((rc = build_table(pr, tab, st))) return rc;
+
+  BwdStateParams bs;
+  bs.seq = pr.seq;
+  bs.H = H;
+  bs.W = sv.W; bs.Qt = sv.Qt; bs.Kb = sv.Kb; bs.M = sv.M; bs.E = sv.E; bs.hs = sv.hs;
+  bs.dO = static_cast<const bf16*>(do_);
+  bs.dC = sv.dC;
+  bs.dht = dht;
+  bs.dE = bv.dE; bs.dQt = bv.dQt; bs.dW = bv.dW; bs.dKb = bv.dKb; bs.dM = bv.dM; bs.dGC = bv.dGC;
+  bs.dh0 = dh0;
+  if ((rc = set_smem(kda_bwd_state_kernel, BwdStateSmem::END, "bwd state"))) return rc;
+  {
+    TimedLaunch tl(K_BWD_STATE, st);
+    kda_bwd_state_kernel<<<dim3(N, H), 256, BwdStateSmem::END, st>>>(bs);
+  }
+  if ((rc = launch_check("bwd state"))) return rc;
+
+  BwdIntraParams bi;
+  bi.in = prologue_in(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, H, scale, lower_bound);
+  bi.seq = pr.seq;
+  bi.conv = pr.conv;
+  bi.dE = bv.dE; bi.dW = bv.dW; bi.dQt = bv.dQt; bi.dKb = bv.dKb; bi.dM = bv.dM; bi.dGC = bv.dGC;
+  bi.dq_hat = bv.dq_hat;
+  bi.dk_hat = bv.dk_hat;
+  bi.dv = pr.conv ? bv.dv_hat : static_cast<bf16*>(dv);
+  bi.dg = static_cast<bf16*>(dg);
+  bi.dbeta = static_cast<bf16*>(dbeta);
+  bi.partA = bv.partA;
+  bi.partB = bv.partB;
+  if ((rc = set_smem(kda_bwd_intra_kernel, BwdIntraSmem::END, "bwd intra"))) return rc;
+  {
+    TimedLaunch tl(K_BWD_INTRA, st);
+    kda_bwd_intra_kernel<<<dim3(pr.grid_chunks, H), 256, BwdIntraSmem::END, st>>>(bi);
+  }
+  if ((rc = launch_check("bwd intra"))) return rc;
+
+  PostParams pp;
+  pp.seq = pr.seq;
+  pp.H = H;
+  pp.conv = pr.conv;
+  pp.scale = scale;
+  pp.q = static_cast<const bf16*>(q);
+  pp.k = static_cast<const bf16*>(k);
+  pp.v = static_cast<const bf16*>(v);
+  pp.conv_q = conv_q; pp.conv_k = conv_k; pp.conv_v = conv_v;
+  pp.dq_hat = bv.dq_hat; pp.dk_hat = bv.dk_hat; pp.dv_hat = bv.dv_hat;
+  pp.dq = static_cast<bf16*>(dq);
+  pp.dk = static_cast<bf16*>(dk);
+  pp.dv = static_cast<bf16*>(dv);
+  pp.partW = bv.partW;
+  if ((rc = set_smem(kda_bwd_post_kernel, PostSmem::END, "bwd post"))) return rc;
+  {
+    TimedLaunch tl(K_BWD_POST, st);
+    kda_bwd_post_kernel<<<dim3(pr.grid_chunks, H), 256, PostSmem::END, st>>>(pp);
+  }
+  if ((rc = launch_check("bwd post"))) return rc;
+
+  ReduceParams rp;
+  rp.seq = pr.seq;
+  rp.H = H;
+  rp.conv = pr.conv;
+  rp.partA = bv.partA; rp.partB = bv.partB; rp.partW = bv.partW;
+  rp.dA_log = dA_log; rp.ddt_bias = ddt_bias;
+  rp.dconv_q = dconv_q; rp.dconv_k = dconv_k; rp.dconv_v = dconv_v;
+  {
+    TimedLaunch tl(K_REDUCE, st);
+    kda_reduce_kernel<<<dim3(H, pr.conv ? 2 : 1), 128, 0, st>>>(rp);
+  }
+  return launch_check("reduce");
+}
+
+int kda_b200_timing_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_timing.mu);
+  g_timing.on = on != 0;
+  return KDA_OK;
+}
+
+int kda_b200_timing_reset(void) {
+  std::lock_guard<std::mutex> lk(g_timing.mu);
+  g_timing.used = 0;
+  g_timing.ids.clear();
+  return KDA_OK;
+}
+
+int kda_b200_timing_read(int max_kernels, const char** names, int* launches, float* total_ms) {
+  std::lock_guard<std::mutex> lk(g_timing.mu);
+  if (max_kernels < K_COUNT || !names || !launches || !total_ms)
+    return -fail(KDA_ERR_INVALID, "timing_read needs room for " + std::to_string((int)K_COUNT) + " kernels");
+  for (int k = 0; k < K_COUNT; ++k) {
+    names[k] = kKernelNames[k];
+    launches[k] = 0;
+    total_ms[k] = 0.f;
+  }
+  for (size_t i = 0; i < g_timing.ids.size(); ++i) {
+    cudaEvent_t a = g_timing.pool[2 * i], b = g_timing.pool[2 * i + 1];
+    if (cudaEventSynchronize(b) != cudaSuccess) return -fail(KDA_ERR_CUDA, "timing event");
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, a, b) != cudaSuccess) return -fail(KDA_ERR_CUDA, "timing elapsed");
+    launches[g_timing.ids[i]] += 1;
+    total_ms[g_timing.ids[i]] += ms;
+  }
+  return K_COUNT;
+}
+
+}  // extern "C"

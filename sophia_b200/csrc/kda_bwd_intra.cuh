@@ -1,0 +1,496 @@
+// Chunk-parallel backward of the chunked KDA layer.
+//
+// One CTA per (chunk, head).  Recomputes the prologue and the intra-chunk
+// quantities (operand tiles, L', A = (I + diag(beta) L')^-1, T = A diag(beta)),
+// then, from the state-pass gradient pieces (dE, dW, dQt, dKbar, dM, dGC):
+//   dv  = T^T dE                      (written out as the value gradient)
+//   dKe = T^T dW,  dT = dE v^T + dW Ke^T,  dbeta += colsum(dT o A)
+//   dA  = dT diag(beta),  dL = -A^T dA A^T (strictly lower)
+//   dbeta += rowsum(dL o L'),  dL' = diag(beta) dL
+//   block products of dM and dL' against the decayed q/k operands give the
+//   gradients through M (Aqk) and L'
+//   dGam collects q o dq + k o dk terms; dg = reverse cumsum of dGam inside
+//   the chunk; the gate and beta sigmoids are differentiated last.
+// Outputs: dq_hat, dk_hat (gradients of the normalised, scaled q and of the
+// normalised k; the L2-norm and conv backward run in the post kernel), dv,
+// dg_logits, dbeta_logits and per-chunk partial sums for dA_log and dt_bias.
+//
+// Accumulator layout "F": warp w owns rows 16*(w&3) .. +15 and columns
+// 64*(w>>2) .. +63 of every 64x128 per-chunk gradient.
+#pragma once
+
+#include "kda_bwd_state.cuh"
+
+namespace kda {
+
+struct BwdIntraParams {
+  PrologueIn in;
+  SeqInfo seq;
+  bool conv;
+  const bf16 *dE, *dW, *dQt, *dKb, *dM;
+  const float* dGC;
+  bf16 *dq_hat, *dk_hat, *dv;  // [T_total][H][128]
+  bf16 *dg, *dbeta;            // [T_total][H][128], [T_total][H]
+  float *partA, *partB;        // [chunks][H][128]
+};
+
+struct BwdIntraSmem {
+  static constexpr int OPSZ = 64 * LD128 * 2;                // 17408
+  static constexpr int OPS = 0;                              // 6 operand tiles
+  static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x 128 fp32
+  static constexpr int DEW = GAM + 64 * D * 4;               // dE, dW tiles (graw during prologue)
+  static constexpr int RAW = DEW + 2 * OPSZ;                 // raw q/k/v, later small tiles
+  static constexpr int RAWSZ = 52224;
+  static constexpr int CVEC = RAW + RAWSZ;                   // 6 x 128 fp32
+  static constexpr int ER = CVEC + 6 * D * 4;                // 4 x 128 fp32
+  static constexpr int EC = ER + 4 * D * 4;                  // 4 x 128 fp32
+  static constexpr int BETA = EC + 4 * D * 4;                // 64 fp32
+  static constexpr int BRAW = BETA + 64 * 4;                 // 64 bf16
+  static constexpr int END = BRAW + 64 * 2;
+  // RAW aliases after the operands are built
+  static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
+  static constexpr int AINV = RAW + 16640;                   // fp32 64 x LDF64
+  static constexpr int XTMP = RAW + 33280;                   // fp32 3 x 256
+  static constexpr int LPB = RAW + 33280;                    // bf16 64 x LD64 (after inverse)
+  static constexpr int ABF = RAW;                            // bf16 64 x LD64 (after Lp fp32 is dead)
+  static constexpr int TBF = RAW + 42496;                    // bf16 64 x LD64
+  static constexpr int DMS = RAW + 9216;                     // bf16 64 x LD64
+  static constexpr int DLS = RAW + 18432;                    // bf16 64 x LD64
+  static constexpr int DBT = RAW + 27648;                    // fp32 4 x 64   (dbeta from T)
+  static constexpr int DBL = DBT + 1024;                     // fp32 2 x 64   (dbeta from L)
+  static constexpr int COLS = DBL + 512;                     // fp32 4 x 128  (sum Kbar o dKbar)
+  static_assert(COLS + 2048 <= LPB, "small tiles overlap Lp bf16");
+  static_assert(TBF + 64 * LD64 * 2 <= RAWSZ + RAW, "T tile overflows");
+  // DEW aliases after the WY backward
+  static constexpr int DAS = DEW;                            // bf16 64 x LD64
+  static constexpr int XS = DEW + 9216;                      // bf16 64 x LD64
+};
+
+__global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int c = blockIdx.x, h = blockIdx.y;
+  ChunkPos pos = chunk_pos(P.seq, c);
+  if (!pos.valid) return;
+  const int H = P.in.H;
+  const int nv = pos.t1 - pos.t0;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const size_t cidx = (size_t)c * H + h;
+
+  PrologueSmem ps;
+  ps.xq = reinterpret_cast<bf16*>(smem + BwdIntraSmem::RAW);
+  ps.xk = ps.xq + 67 * D;
+  ps.xv = ps.xk + 67 * D;
+  ps.graw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
+  ps.braw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::BRAW);
+  ps.gam = reinterpret_cast<float*>(smem + BwdIntraSmem::GAM);
+  ps.beta = reinterpret_cast<float*>(smem + BwdIntraSmem::BETA);
+  ps.tot = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS);
+
+  prologue_issue_loads(P.in, ps, pos, h, P.conv);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  Strip s;
+  prologue_compute(P.in, ps, pos, h, P.conv, s);
+
+  Operands op;
+  op.Qa = reinterpret_cast<bf16*>(smem + BwdIntraSmem::OPS);
+  op.Ka = op.Qa + 64 * LD128;
+  op.Kd = op.Ka + 64 * LD128;
+  op.Kb = op.Kd + 64 * LD128;
+  op.V = op.Kb + 64 * LD128;
+  op.Ke = op.V + 64 * LD128;
+  op.cvec = reinterpret_cast<float*>(smem + BwdIntraSmem::CVEC);
+  op.er = reinterpret_cast<float*>(smem + BwdIntraSmem::ER);
+  op.ec = reinterpret_cast<float*>(smem + BwdIntraSmem::EC);
+  build_operands<false>(s, ps.gam, op, nullptr, nullptr);
+  __syncthreads();
+
+  bf16* dEs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
+  bf16* dWs = dEs + 64 * LD128;
+  load_tile128(dEs, P.dE, pos.t0, nv, H, h);
+  load_tile128(dWs, P.dW, pos.t0, nv, H, h);
+  cp_async_commit();
+
+  float* Lp = reinterpret_cast<float*>(smem + BwdIntraSmem::LP);
+  float* Ainv = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
+  float* xtmp = reinterpret_cast<float*>(smem + BwdIntraSmem::XTMP);
+  lm_blocks(op, Lp, nullptr);
+  __syncthreads();
+  tri_inverse(Lp, ps.beta, Ainv, xtmp);
+  bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
+  for (int i = tid; i < 64 * 64; i += blockDim.x) {
+    int r = i >> 6, cc = i & 63;
+    Lpb[r * LD64 + cc] = __float2bfloat16(Lp[r * LDF64 + cc]);
+  }
+  __syncthreads();
+  bf16* Abf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::ABF);
+  bf16* Tbf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::TBF);
+  {
+    // Ainv (fp32, [16640, 33280)) -> Abf ([0, 9216)) and Tbf: Abf only overlaps the dead Lp
+    float av[16];
+    int r = tid >> 2, c0 = (tid & 3) * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) av[i] = (c0 + i <= r) ? Ainv[r * LDF64 + c0 + i] : 0.f;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      Abf[r * LD64 + c0 + i] = __float2bfloat16(av[i]);
+      Tbf[r * LD64 + c0 + i] = __float2bfloat16(av[i] * ps.beta[c0 + i]);
+    }
+  }
+  bf16* dMs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DMS);
+  __syncthreads();
+  load_tile64(dMs, P.dM, pos.t0, nv, H, h);
+  cp_async_commit();
+  cp_async_wait<1>();  // dE, dW
+  __syncthreads();
+
+  const int I = warp & 3;             // row block of this warp
+  const int m0 = 16 * I, n0 = 64 * (warp >> 2);
+  float dq[8][4], dk[8][4], dG[8][4];
+  // ---- WY backward and the state-side pieces --------------------------------
+  {
+    float acc[8][4];
+    zero_acc<8>(acc);
+    warp_mma<8, true, true>(acc, Tbf, LD64, m0, dEs, LD128, n0, 0, 64);  // dv = T^T dE
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+        if (r < nv)
+          *reinterpret_cast<uint32_t*>(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + cc) =
+              pack_bf16(acc[j][e], acc[j][e + 1]);
+      }
+    zero_acc<8>(acc);
+    warp_mma<8, true, true>(acc, Tbf, LD64, m0, dWs, LD128, n0, 0, 64);  // dKe = T^T dW
+    const float* gam = ps.gam;
+    float colsum[8][2];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+        size_t goff = ((size_t)(pos.t0 + r) * H + h) * D + cc;
+        float2 gq = make_float2(0.f, 0.f), gk = make_float2(0.f, 0.f);
+        if (r < nv) {
+          gq = unpack_bf16(__ldg(reinterpret_cast<const unsigned int*>(P.dQt + goff)));
+          gk = unpack_bf16(__ldg(reinterpret_cast<const unsigned int*>(P.dKb + goff)));
+        }
+        float2 qa = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Qa + r * LD128 + cc));
+        float2 kb = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kb + r * LD128 + cc));
+        float2 ke = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Ke + r * LD128 + cc));
+        float qav[2] = {qa.x, qa.y}, kbv[2] = {kb.x, kb.y}, kev[2] = {ke.x, ke.y};
+        float gqv[2] = {gq.x, gq.y}, gkv[2] = {gk.x, gk.y};
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          int col = cc + u;
+          float G = gam[r * D + col];
+          float a = ex2(G - gam[m0 * D + col]);
+          float b = ex2(gam[(m0 + 15) * D + col] - G);
+          float eg = a * op.er[I * D + col];
+          float egc = b * op.ec[I * D + col];
+          float dke = acc[j][e + u];
+          dq[j][e + u] = gqv[u] * eg;
+          dk[j][e + u] = dke * eg + gkv[u] * egc;
+          float kbar = kbv[u] * op.ec[I * D + col];
+          float qt = qav[u] * op.er[I * D + col];
+          dG[j][e + u] = kev[u] * dke + qt * gqv[u] - kbar * gkv[u];
+          if (e == 0) colsum[j][u] = kbar * gkv[u]; else colsum[j][u] += kbar * gkv[u];
+        }
+      }
+    }
+    // column sums of Kbar o dKbar (lanes sharing a column differ in bits 2..4)
+    float* cols = reinterpret_cast<float*>(smem + BwdIntraSmem::COLS);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float x = colsum[j][u];
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
+        x += __shfl_xor_sync(0xffffffffu, x, 16);
+        colsum[j][u] = x;
+      }
+    if ((tid & 31) < 4) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) cols[I * D + n0 + acc_col(j, u)] = colsum[j][u];
+    }
+  }
+  // dT = dE V^T + dW Ke^T (64x64), warp tile rows m0, cols n1
+  {
+    const int n1 = 32 * (warp >> 2);
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4, false, false>(acc, dEs, LD128, m0, op.V, LD128, n1, 0, 128);
+    warp_mma<4, false, false>(acc, dWs, LD128, m0, op.Ke, LD128, n1, 0, 128);
+    // dbeta_T[j] = sum_i dT_ij A_ij ; dA = dT diag(beta)
+    float cs[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float sum = 0.f;
+#pragma unroll
+        for (int e = u; e < 4; e += 2) {
+          int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
+          sum += acc[j][e] * __bfloat162float(Abf[r * LD64 + cc]);
+        }
+        cs[j][u] = sum;
+      }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        cs[j][u] += __shfl_xor_sync(0xffffffffu, cs[j][u], 4);
+        cs[j][u] += __shfl_xor_sync(0xffffffffu, cs[j][u], 8);
+        cs[j][u] += __shfl_xor_sync(0xffffffffu, cs[j][u], 16);
+      }
+    float* dbt = reinterpret_cast<float*>(smem + BwdIntraSmem::DBT);
+    if ((tid & 31) < 4) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) dbt[I * 64 + n1 + acc_col(j, u)] = cs[j][u];
+    }
+    __syncthreads();  // all reads of dE / dW are done
+    bf16* dAs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DAS);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
+        *reinterpret_cast<uint32_t*>(dAs + r * LD64 + cc) =
+            pack_bf16(acc[j][e] * ps.beta[cc], acc[j][e + 1] * ps.beta[cc + 1]);
+      }
+  }
+  __syncthreads();
+  // X = dA A^T ; dL = -A^T X (strictly lower)
+  {
+    const int n1 = 32 * (warp >> 2);
+    bf16* dAs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DAS);
+    bf16* Xs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::XS);
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4, false, false>(acc, dAs, LD64, m0, Abf, LD64, n1, 0, 64);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
+        *reinterpret_cast<uint32_t*>(Xs + r * LD64 + cc) = pack_bf16(acc[j][e], acc[j][e + 1]);
+      }
+    __syncthreads();
+    zero_acc<4>(acc);
+    warp_mma_neg<4, true, true>(acc, Abf, LD64, m0, Xs, LD64, n1, 0, 64);
+    bf16* dLs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DLS);
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
+        float x0 = cc < r ? acc[j][e] : 0.f;
+        float x1 = cc + 1 < r ? acc[j][e + 1] : 0.f;
+        rs[e >> 1] += x0 * __bfloat162float(Lpb[r * LD64 + cc]) + x1 * __bfloat162float(Lpb[r * LD64 + cc + 1]);
+        float br = ps.beta[r];
+        *reinterpret_cast<uint32_t*>(dLs + r * LD64 + cc) = pack_bf16(x0 * br, x1 * br);
+      }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 1);
+      rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 2);
+    }
+    float* dbl = reinterpret_cast<float*>(smem + BwdIntraSmem::DBL);
+    if ((tid & 3) == 0) {
+      dbl[(warp >> 2) * 64 + m0 + acc_row(0)] = rs[0];
+      dbl[(warp >> 2) * 64 + m0 + acc_row(2)] = rs[1];
+    }
+  }
+  cp_async_wait<0>();  // dM
+  __syncthreads();
+
+  const bf16* dLs = reinterpret_cast<const bf16*>(smem + BwdIntraSmem::DLS);
+  const float* gam = ps.gam;
+  // ---- gradients through M (Aqk) and L' -------------------------------------
+  // row side: rows of block I, reduction over j <= i
+#pragma unroll 1
+  for (int which = 0; which < 2; ++which) {
+    const bf16* dX = which == 0 ? dMs : dLs;
+    const bf16* rowop = which == 0 ? op.Qa : op.Ka;
+    float acc[8][4];
+    zero_acc<8>(acc);
+    {
+      uint32_t a[4];
+      load_A(a, dX, LD64, m0, 16 * I);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t b[4];
+        load_B_kn(b, op.Kd, LD128, n0 + 8 * j, 16 * I);
+        mma16816(acc[j], a, b[0], b[1]);
+        mma16816(acc[j + 1], a, b[2], b[3]);
+      }
+    }
+    for (int J = 0; J < I; ++J) {
+      float tmp[8][4];
+      zero_acc<8>(tmp);
+      uint32_t a[4];
+      load_A(a, dX, LD64, m0, 16 * J);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t b[4];
+        load_B_kn(b, op.Kb, LD128, n0 + 8 * j, 16 * J);
+        mma16816(tmp[j], a, b[0], b[1]);
+        mma16816(tmp[j + 1], a, b[2], b[3]);
+      }
+      const float* cv = op.cvec + pair_index(I, J) * D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][e] += cv[n0 + acc_col(j, e)] * tmp[j][e];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+        float2 ro = unpack_bf16(*reinterpret_cast<const uint32_t*>(rowop + r * LD128 + cc));
+        float rov[2] = {ro.x, ro.y};
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float a = ex2(gam[r * D + cc + u] - gam[m0 * D + cc + u]);
+          float gval = acc[j][e + u];
+          if (which == 0) dq[j][e + u] += a * gval; else dk[j][e + u] += a * gval;
+          dG[j][e + u] += rov[u] * gval;
+        }
+      }
+  }
+  // column side: rows j of block I (as the column block), reduction over i >= j
+#pragma unroll 1
+  for (int which = 0; which < 2; ++which) {
+    const bf16* dX = which == 0 ? dMs : dLs;
+    const bf16* rowop = which == 0 ? op.Qa : op.Ka;
+    float acc[8][4];
+    zero_acc<8>(acc);
+    {
+      uint32_t a[4];
+      load_AT(a, dX, LD64, m0, 16 * I);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t b[4];
+        load_B_kn(b, rowop, LD128, n0 + 8 * j, 16 * I);
+        mma16816(acc[j], a, b[0], b[1]);
+        mma16816(acc[j + 1], a, b[2], b[3]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+        float2 kd = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kd + r * LD128 + cc));
+        float kdv[2] = {kd.x, kd.y};
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          float ia = ex2(gam[m0 * D + cc + u] - gam[r * D + cc + u]);
+          dk[j][e + u] += ia * acc[j][e + u];
+          dG[j][e + u] -= kdv[u] * acc[j][e + u];
+        }
+      }
+    if (I < 3) {
+      zero_acc<8>(acc);
+      for (int Ib = I + 1; Ib < 4; ++Ib) {
+        float tmp[8][4];
+        zero_acc<8>(tmp);
+        uint32_t a[4];
+        load_AT(a, dX, LD64, m0, 16 * Ib);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          uint32_t b[4];
+          load_B_kn(b, rowop, LD128, n0 + 8 * j, 16 * Ib);
+          mma16816(tmp[j], a, b[0], b[1]);
+          mma16816(tmp[j + 1], a, b[2], b[3]);
+        }
+        const float* cv = op.cvec + pair_index(Ib, I) * D;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[j][e] += cv[n0 + acc_col(j, e)] * tmp[j][e];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+          float2 kb = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kb + r * LD128 + cc));
+          float kbv[2] = {kb.x, kb.y};
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            float b = ex2(gam[(m0 + 15) * D + cc + u] - gam[r * D + cc + u]);
+            dk[j][e + u] += b * acc[j][e + u];
+            dG[j][e + u] -= kbv[u] * acc[j][e + u];
+          }
+        }
+    }
+  }
+  // ---- outputs ---------------------------------------------------------------
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+      if (r < nv) {
+        size_t off = ((size_t)(pos.t0 + r) * H + h) * D + cc;
+        *reinterpret_cast<uint32_t*>(P.dq_hat + off) = pack_bf16(dq[j][e], dq[j][e + 1]);
+        *reinterpret_cast<uint32_t*>(P.dk_hat + off) = pack_bf16(dk[j][e], dk[j][e + 1]);
+      }
+    }
+  const float* cols = reinterpret_cast<const float*>(smem + BwdIntraSmem::COLS);
+  __syncthreads();  // every read of gam is done
+  float* dGs = ps.gam;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+      *reinterpret_cast<float2*>(dGs + r * D + cc) = make_float2(dG[j][e], dG[j][e + 1]);
+    }
+  __syncthreads();
+  if (tid < D) {
+    const int col = tid;
+    float run = P.dGC[cidx * D + col] + cols[col] + cols[D + col] + cols[2 * D + col] + cols[3 * D + col];
+    const float eA = __expf(__ldg(P.in.A_log + h));
+    const float bias = __ldg(P.in.dt_bias + (size_t)h * D + col);
+    float sA = 0.f, sB = 0.f;
+    for (int r = 63; r >= 0; --r) {
+      run += dGs[r * D + col];
+      if (r < nv) {
+        size_t off = ((size_t)(pos.t0 + r) * H + h) * D + col;
+        float x = __bfloat162float(P.in.g[off]) + bias;
+        float z = eA * x;
+        float sg = sigmoidf_(z);
+        float dz = run * P.in.lower_bound * sg * (1.f - sg);
+        float dx = dz * eA;
+        P.dg[off] = __float2bfloat16(dx);
+        sA += dz * z;
+        sB += dx;
+      }
+    }
+    P.partA[cidx * D + col] = sA;
+    P.partB[cidx * D + col] = sB;
+  } else if (tid < D + 64) {
+    int r = tid - D;
+    if (r < nv) {
+      const float* dbt = reinterpret_cast<const float*>(smem + BwdIntraSmem::DBT);
+      const float* dbl = reinterpret_cast<const float*>(smem + BwdIntraSmem::DBL);
+      float db = dbt[r] + dbt[64 + r] + dbt[128 + r] + dbt[192 + r] + dbl[r] + dbl[64 + r];
+      float bt = ps.beta[r];
+      P.dbeta[(size_t)(pos.t0 + r) * H + h] = __float2bfloat16(db * bt * (1.f - bt));
+    }
+  }
+}
+
+}  // namespace kda

@@ -1,0 +1,168 @@
+"""GPU parity of the CUDA KDA layer against the CPU oracle and the golden
+fixtures made by the reference.  Tolerance (bf16 path): every element within
+rtol 2e-2 / atol 2e-3 of the float64 oracle run on the same bf16-rounded inputs
+(atol in units of max(1, rms) of each tensor), and a relative Frobenius error
+below 1e-2, for outputs, final states and all gradients."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from cases import CASES, Case, make_inputs
+from kda_cuda_runner import ATOL, RTOL, compare, failures, round_inputs_bf16, run_cuda
+from oracle_runner import run_oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+RANDOM_CASES = {
+    # exact chunk multiple, several heads, batch > 1
+    "b2_t128_h2": Case("b2_t128_h2", B=2, T=128, H=2, h0=True, final_state_grad=True, seed=3),
+    # lengths around the chunk and sub-chunk edges
+    "t1": Case("t1", B=1, T=1, H=1, h0=True, final_state_grad=True, seed=4),
+    "t15": Case("t15", B=1, T=15, H=1, seed=5),
+    "t17": Case("t17", B=1, T=17, H=1, random_gate_params=True, seed=6),
+    "t63": Case("t63", B=1, T=63, H=1, h0=True, seed=7),
+    "t65": Case("t65", B=1, T=65, H=1, final_state_grad=True, seed=8),
+    "t200_noconv": Case("t200_noconv", B=1, T=200, H=2, conv=False, h0=True, final_state_grad=True, seed=9),
+    # packed documents including one-token and chunk-aligned documents
+    "varlen_edges": Case("varlen_edges", B=1, T=260, H=2, cu_seqlens=[0, 1, 65, 129, 130, 200, 260],
+                         h0=True, final_state_grad=True, random_gate_params=True, seed=10),
+    # strongest allowed decay everywhere (gate logits pushed to saturation)
+    "strong_decay": Case("strong_decay", B=1, T=192, H=1, seed=12, extras={"g_shift": 8.0}),
+    # no decay at all (g -> 0)
+    "no_decay": Case("no_decay", B=1, T=128, H=1, seed=14, extras={"g_shift": -30.0}),
+}
+
+
+def _inputs(case):
+    inp = make_inputs(case)
+    shift = case.extras.get("g_shift")
+    if shift is not None:
+        inp["g"] = inp["g"] + shift
+    return inp
+
+
+def _check(case, inp=None, strict=True):
+    inp = round_inputs_bf16(_inputs(case) if inp is None else inp)
+    ref = run_oracle(case, inputs=inp)
+    got = run_cuda(case, inputs=inp)
+    rep = compare(got, ref)
+    return rep, failures(rep)
+
+
+@pytest.mark.parametrize("name", sorted(CASES) + sorted(RANDOM_CASES))
+def test_cuda_matches_oracle(name):
+    case = CASES.get(name) or RANDOM_CASES[name]
+    rep, bad = _check(case)
+    msg = "\n".join(f"{k}: viol={v[0]:.3f} rel={v[1]:.2e}" for k, v in sorted(rep.items()))
+    assert not bad, msg
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_cuda_matches_reference_golden(name):
+    """Against the reference's own float32 outputs (unrounded inputs)."""
+    gold = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    got = run_cuda(CASES[name])
+    ref = {k: torch.from_numpy(gold[k]) for k in gold.files if k != "input_sums"}
+    rep = compare(got, ref)
+    bad = failures(rep)
+    assert not bad, "\n".join(f"{k}: viol={v[0]:.3f} rel={v[1]:.2e}" for k, v in sorted(rep.items()))
+
+
+def test_packed_equals_unpacked_bit_exact():
+    """cu_seqlens resets: each packed document gives exactly the bits of the
+    same document run alone (chunks start at document starts)."""
+    case = RANDOM_CASES["varlen_edges"]
+    inp = round_inputs_bf16(_inputs(case))
+    packed = run_cuda(case, inputs=inp)
+    cu = case.cu_seqlens
+    for n in range(len(cu) - 1):
+        L = cu[n + 1] - cu[n]
+        one = Case("one", B=1, T=L, H=case.H, h0=True, final_state_grad=True,
+                   random_gate_params=True)
+        sub = dict(inp)
+        for k in ("q", "k", "v", "g", "beta", "do"):
+            sub[k] = inp[k][:, cu[n]:cu[n + 1]]
+        sub["h0"] = inp["h0"][n:n + 1]
+        sub["dht"] = inp["dht"][n:n + 1]
+        alone = run_cuda(one, inputs=sub)
+        sl = slice(cu[n], cu[n + 1])
+        assert torch.equal(packed["o"][:, sl], alone["o"])
+        assert torch.equal(packed["final_state"][n:n + 1], alone["final_state"])
+        for k in ("d_q", "d_k", "d_v", "d_g", "d_beta"):
+            assert torch.equal(packed[k][:, sl], alone[k]), k
+        assert torch.equal(packed["d_h0"][n:n + 1], alone["d_h0"])
+
+
+def test_state_carry_equals_one_shot():
+    """Two calls chained through initial_state / final_state equal one call
+    when the split falls on a chunk edge (seam-level state carry)."""
+    from sophia_b200 import chunk_kda
+    case = Case("carry", B=2, T=256, H=2, conv=False, seed=21)
+    inp = round_inputs_bf16(_inputs(case))
+    dev = "cuda"
+    t = {k: inp[k].to(dev, torch.bfloat16 if k in ("q", "k", "v", "g", "beta") else torch.float32)
+         for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias")}
+    kw = dict(use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, use_beta_sigmoid_in_kernel=True,
+              safe_gate=True, lower_bound=-5.0, A_log=t["A_log"], dt_bias=t["dt_bias"])
+    with torch.no_grad():
+        o, ht = chunk_kda(t["q"], t["k"], t["v"], t["g"], t["beta"], output_final_state=True, **kw)
+        sl1, sl2 = slice(0, 128), slice(128, 256)
+        o1, h1 = chunk_kda(*(t[k][:, sl1] for k in ("q", "k", "v", "g", "beta")), output_final_state=True, **kw)
+        o2, h2 = chunk_kda(*(t[k][:, sl2] for k in ("q", "k", "v", "g", "beta")), initial_state=h1,
+                           output_final_state=True, **kw)
+    assert torch.equal(o[:, sl1], o1)
+    assert torch.equal(o[:, sl2], o2)
+    assert torch.equal(ht, h2)
+
+
+def test_full_size_forward_is_causal_and_matches_prefix_oracle():
+    """Config-1 shape (B=8, T=4096, H=16): outputs are finite, and the first
+    128 tokens of a row equal the oracle on that prefix alone."""
+    from sophia_b200 import kda_layer
+    B, T, H = 8, 4096, 16
+    gen = torch.Generator().manual_seed(42)
+    x = {k: torch.randn(B, T, H, 128, generator=gen) for k in ("q", "k", "v", "g")}
+    beta = torch.randn(B, T, H, generator=gen)
+    convs = [torch.randn(H * 128, 4, generator=gen) * 0.5 for _ in range(3)]
+    dev = "cuda"
+    with torch.no_grad():
+        o, ht = kda_layer(*(x[k].to(dev, torch.bfloat16) for k in ("q", "k", "v", "g")),
+                          beta.to(dev, torch.bfloat16), torch.zeros(H, device=dev),
+                          torch.zeros(H * 128, device=dev), *(c.to(dev) for c in convs),
+                          output_final_state=True)
+    assert torch.isfinite(o.float()).all() and torch.isfinite(ht).all()
+    from oracle.kda_oracle import kda_layer as oracle_layer
+    P = 128
+    sel = lambda t: t[5:6, :P, 3:5].to(torch.bfloat16).double()  # noqa: E731
+    convs_h = [c.view(H, 128, 4)[3:5].reshape(-1, 4).double() for c in convs]
+    ref = oracle_layer(sel(x["q"]), sel(x["k"]), sel(x["v"]), sel(x["g"]),
+                       beta[5:6, :P, 3:5].to(torch.bfloat16).double(), torch.zeros(2, dtype=torch.float64),
+                       torch.zeros(256, dtype=torch.float64), conv_weights=convs_h)
+    rep = compare({"o": o[5:6, :P, 3:5].double().cpu()}, {"o": ref.o})
+    assert not failures(rep), rep
+
+
+def test_errors_are_raised_on_host():
+    from sophia_b200 import chunk_kda
+    q = torch.zeros(2, 64, 1, 128, device="cuda", dtype=torch.bfloat16)
+    g = torch.zeros_like(q)
+    b = torch.zeros(2, 64, 1, device="cuda", dtype=torch.bfloat16)
+    A = torch.zeros(1, device="cuda")
+    kw = dict(use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True, use_beta_sigmoid_in_kernel=True,
+              safe_gate=True, A_log=A)
+    with pytest.raises(ValueError, match="lower_bound"):
+        chunk_kda(q, q, q, g, b, lower_bound=-6.0, **kw)
+    with pytest.raises(ValueError, match="batch size is expected to be 1"):
+        chunk_kda(q, q, q, g, b, lower_bound=-5.0, cu_seqlens=torch.tensor([0, 64], device="cuda"), **kw)
+    with pytest.raises(AssertionError, match="float32"):
+        chunk_kda(q, q, q, g, b, lower_bound=-5.0, initial_state=torch.zeros(2, 1, 128, 128, device="cuda",
+                                                                             dtype=torch.bfloat16), **kw)
+    with pytest.raises(ValueError, match="chunk_size"):
+        chunk_kda(q, q, q, g, b, lower_bound=-5.0, chunk_size=16, **kw)
