@@ -313,7 +313,7 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
   {
     TimedLaunch tl(K_FWD_INTRA, st);
-    kda_fwd_intra_kernel<<<dim3(pr.grid_chunks, H), 256, IntraSmem::END, st>>>(ip);
+    kda_fwd_intra_kernel<<<dim3(pr.grid_chunks, H), INTRA_THREADS, IntraSmem::END, st>>>(ip);
   }
   if ((rc = launch_check("fwd intra"))) return rc;
 
@@ -409,7 +409,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   if ((rc = set_smem(kda_bwd_intra_kernel, BwdIntraSmem::END, "bwd intra"))) return rc;
   {
     TimedLaunch tl(K_BWD_INTRA, st);
-    kda_bwd_intra_kernel<<<dim3(pr.grid_chunks, H), 256, BwdIntraSmem::END, st>>>(bi);
+    kda_bwd_intra_kernel<<<dim3(pr.grid_chunks, H), INTRA_THREADS, BwdIntraSmem::END, st>>>(bi);
   }
   if ((rc = launch_check("bwd intra"))) return rc;
 
@@ -443,7 +443,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   rp.dconv_q = dconv_q; rp.dconv_k = dconv_k; rp.dconv_v = dconv_v;
   {
     TimedLaunch tl(K_REDUCE, st);
-    kda_reduce_kernel<<<dim3(H, pr.conv ? 2 : 1), 128, 0, st>>>(rp);
+    kda_reduce_kernel<<<dim3(2 * H + (pr.conv ? 12 * H : 0)), 256, 0, st>>>(rp);
   }
   return launch_check("reduce");
 }

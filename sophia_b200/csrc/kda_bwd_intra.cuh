@@ -15,8 +15,9 @@
 // normalised k; the L2-norm and conv backward run in the post kernel), dv,
 // dg_logits, dbeta_logits and per-chunk partial sums for dA_log and dt_bias.
 //
-// Accumulator layout "F": warp w owns rows 16*(w&3) .. +15 and columns
-// 64*(w>>2) .. +63 of every 64x128 per-chunk gradient.
+// 512 threads.  Accumulator layout "F": warp w owns rows 16*(w&3) .. +15 and
+// columns 32*(w>>2) .. +31 of every 64x128 per-chunk gradient; the per-element
+// decay factors of that tile stay in registers for the whole kernel.
 #pragma once
 
 #include "kda_bwd_state.cuh"
@@ -37,10 +38,10 @@ struct BwdIntraParams {
 struct BwdIntraSmem {
   static constexpr int OPSZ = 64 * LD128 * 2;                // 17408
   static constexpr int OPS = 0;                              // 6 operand tiles
-  static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x 128 fp32
-  static constexpr int DEW = GAM + 64 * D * 4;               // dE, dW tiles (graw during prologue)
+  static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x LDG fp32
+  static constexpr int DEW = GAM + 64 * LDG * 4;             // dE, dW tiles (graw during prologue)
   static constexpr int RAW = DEW + 2 * OPSZ;                 // raw q/k/v, later small tiles
-  static constexpr int RAWSZ = 52224;
+  static constexpr int RAWSZ = 51712;
   static constexpr int CVEC = RAW + RAWSZ;                   // 6 x 128 fp32
   static constexpr int ER = CVEC + 6 * D * 4;                // 4 x 128 fp32
   static constexpr int EC = ER + 4 * D * 4;                  // 4 x 128 fp32
@@ -50,23 +51,26 @@ struct BwdIntraSmem {
   // RAW aliases after the operands are built
   static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
   static constexpr int AINV = RAW + 16640;                   // fp32 64 x LDF64
-  static constexpr int XTMP = RAW + 33280;                   // fp32 3 x 256
+  static constexpr int XTMP = RAW + 33280;                   // fp32 3 warps x 16 x 17
   static constexpr int LPB = RAW + 33280;                    // bf16 64 x LD64 (after inverse)
   static constexpr int ABF = RAW;                            // bf16 64 x LD64 (after Lp fp32 is dead)
   static constexpr int TBF = RAW + 42496;                    // bf16 64 x LD64
   static constexpr int DMS = RAW + 9216;                     // bf16 64 x LD64
   static constexpr int DLS = RAW + 18432;                    // bf16 64 x LD64
   static constexpr int DBT = RAW + 27648;                    // fp32 4 x 64   (dbeta from T)
-  static constexpr int DBL = DBT + 1024;                     // fp32 2 x 64   (dbeta from L)
-  static constexpr int COLS = DBL + 512;                     // fp32 4 x 128  (sum Kbar o dKbar)
+  static constexpr int DBL = DBT + 1024;                     // fp32 4 x 64   (dbeta from L)
+  static constexpr int COLS = DBL + 1024;                    // fp32 4 x 128  (sum Kbar o dKbar)
   static_assert(COLS + 2048 <= LPB, "small tiles overlap Lp bf16");
   static_assert(TBF + 64 * LD64 * 2 <= RAWSZ + RAW, "T tile overflows");
+  static_assert(XTMP + 3 * 16 * 17 * 4 <= TBF, "inverse scratch overlaps T");
   // DEW aliases after the WY backward
   static constexpr int DAS = DEW;                            // bf16 64 x LD64
   static constexpr int XS = DEW + 9216;                      // bf16 64 x LD64
+  static constexpr int GRE = DEW + 18432;                    // bf16 64 x 128 gate logits (reloaded)
+  static_assert(GRE + 64 * D * 2 <= RAW, "gate reload overflows");
 };
 
-__global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P) {
+__global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntraParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int c = blockIdx.x, h = blockIdx.y;
   ChunkPos pos = chunk_pos(P.seq, c);
@@ -85,6 +89,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   ps.gam = reinterpret_cast<float*>(smem + BwdIntraSmem::GAM);
   ps.beta = reinterpret_cast<float*>(smem + BwdIntraSmem::BETA);
   ps.tot = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS);
+  ps.taps = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS + 8192);
 
   prologue_issue_loads(P.in, ps, pos, h, P.conv);
   cp_async_commit();
@@ -104,6 +109,20 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   op.er = reinterpret_cast<float*>(smem + BwdIntraSmem::ER);
   op.ec = reinterpret_cast<float*>(smem + BwdIntraSmem::EC);
   build_operands<false>(s, ps.gam, op, nullptr, nullptr);
+
+  // F layout of this warp and its per-element decay factors
+  const int I = warp & 3;             // row block
+  const int m0 = 16 * I, n0 = 32 * (warp >> 2);
+  float af[4][4], bfv[4][4];          // a = 2^(Gam - Gam_r(I)), b = 2^(Gam_e(I) - Gam)
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int r = m0 + acc_row(e), col = n0 + acc_col(j, e);
+      float G = ps.gam[r * LDG + col];
+      af[j][e] = ex2(G - ps.gam[m0 * LDG + col]);
+      bfv[j][e] = ex2(ps.gam[(m0 + 15) * LDG + col] - G);
+    }
   __syncthreads();
 
   bf16* dEs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
@@ -119,24 +138,27 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   __syncthreads();
   tri_inverse(Lp, ps.beta, Ainv, xtmp);
   bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
-  for (int i = tid; i < 64 * 64; i += blockDim.x) {
-    int r = i >> 6, cc = i & 63;
-    Lpb[r * LD64 + cc] = __float2bfloat16(Lp[r * LDF64 + cc]);
+  for (int i = tid; i < 64 * 32; i += blockDim.x) {
+    int r = i >> 5, cc = 2 * (i & 31);
+    float x0 = cc < r ? Lp[r * LDF64 + cc] : 0.f;
+    float x1 = cc + 1 < r ? Lp[r * LDF64 + cc + 1] : 0.f;
+    *reinterpret_cast<uint32_t*>(Lpb + r * LD64 + cc) = pack_bf16(x0, x1);
   }
   __syncthreads();
   bf16* Abf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::ABF);
   bf16* Tbf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::TBF);
   {
-    // Ainv (fp32, [16640, 33280)) -> Abf ([0, 9216)) and Tbf: Abf only overlaps the dead Lp
-    float av[16];
-    int r = tid >> 2, c0 = (tid & 3) * 16;
+    // Ainv (fp32 at [16640, 33280)) -> Abf ([0, 9216)) and Tbf: Abf only overlaps the dead Lp
+    float av[8];
+    const int r = tid >> 3, c0 = (tid & 7) * 8;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) av[i] = (c0 + i <= r) ? Ainv[r * LDF64 + c0 + i] : 0.f;
+    for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Ainv[r * LDF64 + c0 + i] : 0.f;
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      Abf[r * LD64 + c0 + i] = __float2bfloat16(av[i]);
-      Tbf[r * LD64 + c0 + i] = __float2bfloat16(av[i] * ps.beta[c0 + i]);
+    for (int i = 0; i < 8; i += 2) {
+      *reinterpret_cast<uint32_t*>(Abf + r * LD64 + c0 + i) = pack_bf16(av[i], av[i + 1]);
+      *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + c0 + i) =
+          pack_bf16(av[i] * ps.beta[c0 + i], av[i + 1] * ps.beta[c0 + i + 1]);
     }
   }
   bf16* dMs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DMS);
@@ -146,16 +168,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   cp_async_wait<1>();  // dE, dW
   __syncthreads();
 
-  const int I = warp & 3;             // row block of this warp
-  const int m0 = 16 * I, n0 = 64 * (warp >> 2);
-  float dq[8][4], dk[8][4], dG[8][4];
+  float dq[4][4], dk[4][4], dG[4][4];
   // ---- WY backward and the state-side pieces --------------------------------
   {
-    float acc[8][4];
-    zero_acc<8>(acc);
-    warp_mma<8, true, true>(acc, Tbf, LD64, m0, dEs, LD128, n0, 0, 64);  // dv = T^T dE
+    float acc[4][4];
+    zero_acc<4>(acc);
+    warp_mma<4, true, true>(acc, Tbf, LD64, m0, dEs, LD128, n0, 0, 64);  // dv = T^T dE
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
@@ -163,12 +183,11 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
           *reinterpret_cast<uint32_t*>(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + cc) =
               pack_bf16(acc[j][e], acc[j][e + 1]);
       }
-    zero_acc<8>(acc);
-    warp_mma<8, true, true>(acc, Tbf, LD64, m0, dWs, LD128, n0, 0, 64);  // dKe = T^T dW
-    const float* gam = ps.gam;
-    float colsum[8][2];
+    zero_acc<4>(acc);
+    warp_mma<4, true, true>(acc, Tbf, LD64, m0, dWs, LD128, n0, 0, 64);  // dKe = T^T dW
+    float colsum[4][2];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
@@ -181,30 +200,28 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
         float2 qa = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Qa + r * LD128 + cc));
         float2 kb = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kb + r * LD128 + cc));
         float2 ke = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Ke + r * LD128 + cc));
+        float2 er = *reinterpret_cast<const float2*>(op.er + I * D + cc);
+        float2 ec = *reinterpret_cast<const float2*>(op.ec + I * D + cc);
         float qav[2] = {qa.x, qa.y}, kbv[2] = {kb.x, kb.y}, kev[2] = {ke.x, ke.y};
-        float gqv[2] = {gq.x, gq.y}, gkv[2] = {gk.x, gk.y};
+        float gqv[2] = {gq.x, gq.y}, gkv[2] = {gk.x, gk.y}, erv[2] = {er.x, er.y}, ecv[2] = {ec.x, ec.y};
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          int col = cc + u;
-          float G = gam[r * D + col];
-          float a = ex2(G - gam[m0 * D + col]);
-          float b = ex2(gam[(m0 + 15) * D + col] - G);
-          float eg = a * op.er[I * D + col];
-          float egc = b * op.ec[I * D + col];
+          float eg = af[j][e + u] * erv[u];
+          float egc = bfv[j][e + u] * ecv[u];
           float dke = acc[j][e + u];
           dq[j][e + u] = gqv[u] * eg;
           dk[j][e + u] = dke * eg + gkv[u] * egc;
-          float kbar = kbv[u] * op.ec[I * D + col];
-          float qt = qav[u] * op.er[I * D + col];
+          float kbar = kbv[u] * ecv[u];
+          float qt = qav[u] * erv[u];
           dG[j][e + u] = kev[u] * dke + qt * gqv[u] - kbar * gkv[u];
           if (e == 0) colsum[j][u] = kbar * gkv[u]; else colsum[j][u] += kbar * gkv[u];
         }
       }
     }
-    // column sums of Kbar o dKbar (lanes sharing a column differ in bits 2..4)
+    // column sums of Kbar o dKbar over the chunk (lanes sharing a column differ in bits 2..4)
     float* cols = reinterpret_cast<float*>(smem + BwdIntraSmem::COLS);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         float x = colsum[j][u];
@@ -215,22 +232,22 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
       }
     if ((tid & 31) < 4) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int u = 0; u < 2; ++u) cols[I * D + n0 + acc_col(j, u)] = colsum[j][u];
     }
   }
-  // dT = dE V^T + dW Ke^T (64x64), warp tile rows m0, cols n1
+  // dT = dE V^T + dW Ke^T (64x64), warp tile rows m0, cols n1 (two n8 tiles)
+  const int n1 = 16 * (warp >> 2);
   {
-    const int n1 = 32 * (warp >> 2);
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4, false, false>(acc, dEs, LD128, m0, op.V, LD128, n1, 0, 128);
-    warp_mma<4, false, false>(acc, dWs, LD128, m0, op.Ke, LD128, n1, 0, 128);
+    float acc[2][4];
+    zero_acc<2>(acc);
+    warp_mma<2, false, false>(acc, dEs, LD128, m0, op.V, LD128, n1, 0, 128);
+    warp_mma<2, false, false>(acc, dWs, LD128, m0, op.Ke, LD128, n1, 0, 128);
     // dbeta_T[j] = sum_i dT_ij A_ij ; dA = dT diag(beta)
-    float cs[4][2];
+    float cs[2][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         float sum = 0.f;
@@ -239,27 +256,22 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
           int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
           sum += acc[j][e] * __bfloat162float(Abf[r * LD64 + cc]);
         }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
         cs[j][u] = sum;
-      }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        cs[j][u] += __shfl_xor_sync(0xffffffffu, cs[j][u], 4);
-        cs[j][u] += __shfl_xor_sync(0xffffffffu, cs[j][u], 8);
-        cs[j][u] += __shfl_xor_sync(0xffffffffu, cs[j][u], 16);
       }
     float* dbt = reinterpret_cast<float*>(smem + BwdIntraSmem::DBT);
     if ((tid & 31) < 4) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int u = 0; u < 2; ++u) dbt[I * 64 + n1 + acc_col(j, u)] = cs[j][u];
     }
     __syncthreads();  // all reads of dE / dW are done
     bf16* dAs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DAS);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
@@ -270,32 +282,32 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   __syncthreads();
   // X = dA A^T ; dL = -A^T X (strictly lower)
   {
-    const int n1 = 32 * (warp >> 2);
     bf16* dAs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DAS);
     bf16* Xs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::XS);
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma<4, false, false>(acc, dAs, LD64, m0, Abf, LD64, n1, 0, 64);
+    float acc[2][4];
+    zero_acc<2>(acc);
+    warp_mma<2, false, false>(acc, dAs, LD64, m0, Abf, LD64, n1, 0, 64);
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
         *reinterpret_cast<uint32_t*>(Xs + r * LD64 + cc) = pack_bf16(acc[j][e], acc[j][e + 1]);
       }
     __syncthreads();
-    zero_acc<4>(acc);
-    warp_mma_neg<4, true, true>(acc, Abf, LD64, m0, Xs, LD64, n1, 0, 64);
+    zero_acc<2>(acc);
+    warp_mma_neg<2, true, true>(acc, Abf, LD64, m0, Xs, LD64, n1, 0, 64);
     bf16* dLs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DLS);
     float rs[2] = {0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
         float x0 = cc < r ? acc[j][e] : 0.f;
         float x1 = cc + 1 < r ? acc[j][e + 1] : 0.f;
-        rs[e >> 1] += x0 * __bfloat162float(Lpb[r * LD64 + cc]) + x1 * __bfloat162float(Lpb[r * LD64 + cc + 1]);
+        float2 lp = unpack_bf16(*reinterpret_cast<const uint32_t*>(Lpb + r * LD64 + cc));
+        rs[e >> 1] += x0 * lp.x + x1 * lp.y;
         float br = ps.beta[r];
         *reinterpret_cast<uint32_t*>(dLs + r * LD64 + cc) = pack_bf16(x0 * br, x1 * br);
       }
@@ -310,24 +322,32 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
       dbl[(warp >> 2) * 64 + m0 + acc_row(2)] = rs[1];
     }
   }
-  cp_async_wait<0>();  // dM
+  // the gate logits are needed again at the end: fetch them now (region free)
+  bf16* gre = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GRE);
+  for (int i = tid; i < 64 * 16; i += blockDim.x) {
+    int r = i >> 4, cc = i & 15;
+    bool ok = r < nv;
+    cp_async16(gre + r * D + cc * 8,
+               P.in.g + (ok ? ((size_t)(pos.t0 + r) * H + h) * D + cc * 8 : 0), ok);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();  // dM and the gate logits
   __syncthreads();
 
   const bf16* dLs = reinterpret_cast<const bf16*>(smem + BwdIntraSmem::DLS);
-  const float* gam = ps.gam;
   // ---- gradients through M (Aqk) and L' -------------------------------------
   // row side: rows of block I, reduction over j <= i
 #pragma unroll 1
   for (int which = 0; which < 2; ++which) {
     const bf16* dX = which == 0 ? dMs : dLs;
     const bf16* rowop = which == 0 ? op.Qa : op.Ka;
-    float acc[8][4];
-    zero_acc<8>(acc);
+    float acc[4][4];
+    zero_acc<4>(acc);
     {
       uint32_t a[4];
       load_A(a, dX, LD64, m0, 16 * I);
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
+      for (int j = 0; j < 4; j += 2) {
         uint32_t b[4];
         load_B_kn(b, op.Kd, LD128, n0 + 8 * j, 16 * I);
         mma16816(acc[j], a, b[0], b[1]);
@@ -335,12 +355,12 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
       }
     }
     for (int J = 0; J < I; ++J) {
-      float tmp[8][4];
-      zero_acc<8>(tmp);
+      float tmp[4][4];
+      zero_acc<4>(tmp);
       uint32_t a[4];
       load_A(a, dX, LD64, m0, 16 * J);
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
+      for (int j = 0; j < 4; j += 2) {
         uint32_t b[4];
         load_B_kn(b, op.Kb, LD128, n0 + 8 * j, 16 * J);
         mma16816(tmp[j], a, b[0], b[1]);
@@ -348,12 +368,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
       }
       const float* cv = op.cvec + pair_index(I, J) * D;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 4; ++j) {
+        float2 c2 = *reinterpret_cast<const float2*>(cv + n0 + acc_col(j, 0));
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] += cv[n0 + acc_col(j, e)] * tmp[j][e];
+        for (int e = 0; e < 4; ++e) acc[j][e] += ((e & 1) ? c2.y : c2.x) * tmp[j][e];
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
@@ -361,9 +383,8 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
         float rov[2] = {ro.x, ro.y};
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          float a = ex2(gam[r * D + cc + u] - gam[m0 * D + cc + u]);
           float gval = acc[j][e + u];
-          if (which == 0) dq[j][e + u] += a * gval; else dk[j][e + u] += a * gval;
+          if (which == 0) dq[j][e + u] += af[j][e + u] * gval; else dk[j][e + u] += af[j][e + u] * gval;
           dG[j][e + u] += rov[u] * gval;
         }
       }
@@ -373,13 +394,13 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   for (int which = 0; which < 2; ++which) {
     const bf16* dX = which == 0 ? dMs : dLs;
     const bf16* rowop = which == 0 ? op.Qa : op.Ka;
-    float acc[8][4];
-    zero_acc<8>(acc);
+    float acc[4][4];
+    zero_acc<4>(acc);
     {
       uint32_t a[4];
       load_AT(a, dX, LD64, m0, 16 * I);
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
+      for (int j = 0; j < 4; j += 2) {
         uint32_t b[4];
         load_B_kn(b, rowop, LD128, n0 + 8 * j, 16 * I);
         mma16816(acc[j], a, b[0], b[1]);
@@ -387,7 +408,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
       }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
@@ -395,20 +416,20 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
         float kdv[2] = {kd.x, kd.y};
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          float ia = ex2(gam[m0 * D + cc + u] - gam[r * D + cc + u]);
+          float ia = rcp(af[j][e + u]);
           dk[j][e + u] += ia * acc[j][e + u];
           dG[j][e + u] -= kdv[u] * acc[j][e + u];
         }
       }
     if (I < 3) {
-      zero_acc<8>(acc);
+      zero_acc<4>(acc);
       for (int Ib = I + 1; Ib < 4; ++Ib) {
-        float tmp[8][4];
-        zero_acc<8>(tmp);
+        float tmp[4][4];
+        zero_acc<4>(tmp);
         uint32_t a[4];
         load_AT(a, dX, LD64, m0, 16 * Ib);
 #pragma unroll
-        for (int j = 0; j < 8; j += 2) {
+        for (int j = 0; j < 4; j += 2) {
           uint32_t b[4];
           load_B_kn(b, rowop, LD128, n0 + 8 * j, 16 * Ib);
           mma16816(tmp[j], a, b[0], b[1]);
@@ -416,12 +437,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
         }
         const float* cv = op.cvec + pair_index(Ib, I) * D;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 4; ++j) {
+          float2 c2 = *reinterpret_cast<const float2*>(cv + n0 + acc_col(j, 0));
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[j][e] += cv[n0 + acc_col(j, e)] * tmp[j][e];
+          for (int e = 0; e < 4; ++e) acc[j][e] += ((e & 1) ? c2.y : c2.x) * tmp[j][e];
+        }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
         for (int e = 0; e < 4; e += 2) {
           int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
@@ -429,8 +452,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
           float kbv[2] = {kb.x, kb.y};
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            float b = ex2(gam[(m0 + 15) * D + cc + u] - gam[r * D + cc + u]);
-            dk[j][e + u] += b * acc[j][e + u];
+            dk[j][e + u] += bfv[j][e + u] * acc[j][e + u];
             dG[j][e + u] -= kbv[u] * acc[j][e + u];
           }
         }
@@ -438,7 +460,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
   }
   // ---- outputs ---------------------------------------------------------------
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
@@ -449,27 +471,35 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
       }
     }
   const float* cols = reinterpret_cast<const float*>(smem + BwdIntraSmem::COLS);
-  __syncthreads();  // every read of gam is done
-  float* dGs = ps.gam;
+  float* dGs = ps.gam;  // Gam is dead: every decay factor is in registers
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-      *reinterpret_cast<float2*>(dGs + r * D + cc) = make_float2(dG[j][e], dG[j][e + 1]);
+      *reinterpret_cast<float2*>(dGs + r * LDG + cc) = make_float2(dG[j][e], dG[j][e + 1]);
     }
   __syncthreads();
-  if (tid < D) {
-    const int col = tid;
+  // reverse cumsum over the chunk and the gate backward: thread (part, col)
+  // with col = tid % 128 owns rows 16*part .. 16*part+15 of one channel
+  {
+    const int col = tid & 127, part = tid >> 7;
+    float own = 0.f;
+#pragma unroll 4
+    for (int r = 16 * part; r < 16 * part + 16; ++r) own += dGs[r * LDG + col];
+    float* partsum = reinterpret_cast<float*>(smem + BwdIntraSmem::DAS);  // 4 x 128 fp32 (dA is dead)
+    partsum[part * D + col] = own;
+    __syncthreads();
     float run = P.dGC[cidx * D + col] + cols[col] + cols[D + col] + cols[2 * D + col] + cols[3 * D + col];
+    for (int p2 = part + 1; p2 < 4; ++p2) run += partsum[p2 * D + col];
     const float eA = __expf(__ldg(P.in.A_log + h));
     const float bias = __ldg(P.in.dt_bias + (size_t)h * D + col);
     float sA = 0.f, sB = 0.f;
-    for (int r = 63; r >= 0; --r) {
-      run += dGs[r * D + col];
+    for (int r = 16 * part + 15; r >= 16 * part; --r) {
+      run += dGs[r * LDG + col];
       if (r < nv) {
         size_t off = ((size_t)(pos.t0 + r) * H + h) * D + col;
-        float x = __bfloat162float(P.in.g[off]) + bias;
+        float x = __bfloat162float(gre[r * D + col]) + bias;
         float z = eA * x;
         float sg = sigmoidf_(z);
         float dz = run * P.in.lower_bound * sg * (1.f - sg);
@@ -479,14 +509,23 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_intra_kernel(BwdIntraParams P)
         sB += dx;
       }
     }
-    P.partA[cidx * D + col] = sA;
-    P.partB[cidx * D + col] = sB;
-  } else if (tid < D + 64) {
-    int r = tid - D;
+    __syncthreads();
+    partsum[part * D + col] = sA;
+    partsum[4 * D + part * D + col] = sB;
+    __syncthreads();
+    if (part == 0) {
+      P.partA[cidx * D + col] = partsum[col] + partsum[D + col] + partsum[2 * D + col] + partsum[3 * D + col];
+      P.partB[cidx * D + col] = partsum[4 * D + col] + partsum[5 * D + col] + partsum[6 * D + col] +
+                                partsum[7 * D + col];
+    }
+  }
+  if (tid < 64) {
+    int r = tid;
     if (r < nv) {
       const float* dbt = reinterpret_cast<const float*>(smem + BwdIntraSmem::DBT);
       const float* dbl = reinterpret_cast<const float*>(smem + BwdIntraSmem::DBL);
-      float db = dbt[r] + dbt[64 + r] + dbt[128 + r] + dbt[192 + r] + dbl[r] + dbl[64 + r];
+      float db = dbt[r] + dbt[64 + r] + dbt[128 + r] + dbt[192 + r] + dbl[r] + dbl[64 + r] + dbl[128 + r] +
+                 dbl[192 + r];
       float bt = ps.beta[r];
       P.dbeta[(size_t)(pos.t0 + r) * H + h] = __float2bfloat16(db * bt * (1.f - bt));
     }

@@ -24,6 +24,7 @@ constexpr int SUB = 16;      // sub-chunk length
 constexpr int LD128 = 136;   // padded row stride (elements) of 128-wide bf16 tiles
 constexpr int LD64 = 72;     // padded row stride (elements) of 64-wide bf16 tiles
 constexpr int LDF64 = 65;    // padded row stride (floats) of 64x64 fp32 tiles
+constexpr int LDG = 132;     // padded row stride (floats) of the 64x128 fp32 decay tile
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
@@ -115,6 +116,20 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D = A(16x8 tf32, row) * B(8x8 tf32, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma1688_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
@@ -127,6 +142,21 @@ __device__ __forceinline__ float rcp(float x) {
 }
 // logistic sigmoid from ex2 and rcp (relative error ~1e-7)
 __device__ __forceinline__ float sigmoidf_(float x) { return rcp(1.f + ex2(-x * LOG2E)); }
+
+// Sigmoid and SiLU through one tanh.approx: sigmoid(x) = (1 + tanh(x/2)) / 2,
+// x * sigmoid(x) = h + h tanh(h) with h = x/2.  tanh.approx.f32 has a relative
+// error below 2^-10.9, under the bf16 rounding the results go through; used for
+// the ShortConv activation, where the forward and backward kernels must agree.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;\n" : "=f"(t) : "f"(x));
+  return t;
+}
+__device__ __forceinline__ float sigmoid_fast(float x) { return fmaf(0.5f, tanh_fast(0.5f * x), 0.5f); }
+__device__ __forceinline__ float silu_fast(float x) {
+  float h = 0.5f * x;
+  return fmaf(h, tanh_fast(h), h);
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -27,8 +27,8 @@ struct FwdIntraParams {
 struct IntraSmem {
   static constexpr int RAW = 0;                         // 3 x 67 x 128 bf16
   static constexpr int GRAW = RAW + 3 * 67 * D * 2;     // 64 x 128 bf16
-  static constexpr int GAM = GRAW + 64 * D * 2;         // 64 x 128 fp32
-  static constexpr int OPS = GAM + 64 * D * 4;          // 6 x 64 x LD128 bf16
+  static constexpr int GAM = GRAW + 64 * D * 2;         // 64 x LDG fp32
+  static constexpr int OPS = GAM + 64 * LDG * 4;        // 6 x 64 x LD128 bf16
   static constexpr int OPSZ = 64 * LD128 * 2;
   static constexpr int CVEC = OPS + 6 * OPSZ;           // 6 x 128 fp32
   static constexpr int BETA = CVEC + 6 * D * 4;         // 64 fp32
@@ -37,8 +37,8 @@ struct IntraSmem {
   // aliases valid after the operands are built (raw inputs are dead)
   static constexpr int LP = RAW;                        // 64 x LDF64 fp32
   static constexpr int AINV = LP + 64 * LDF64 * 4;      // 64 x LDF64 fp32
-  static constexpr int XTMP = AINV + 64 * LDF64 * 4;    // 3 x 256 fp32
-  static constexpr int TBF = XTMP + 3 * 256 * 4;        // 64 x LD64 bf16
+  static constexpr int XTMP = AINV + 64 * LDF64 * 4;    // 3 warps x 16 x 17 fp32
+  static constexpr int TBF = XTMP + 3 * 16 * 17 * 4;    // 64 x LD64 bf16
   static constexpr int MSM = GRAW;                      // 64 x LD64 bf16
   static_assert(TBF + 64 * LD64 * 2 <= GRAW, "aliases overflow the raw region");
   static_assert(64 * LD64 * 2 <= GAM - GRAW, "M staging overflows");
@@ -60,7 +60,7 @@ __device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, 
   }
 }
 
-__global__ void __launch_bounds__(256, 1) kda_fwd_intra_kernel(FwdIntraParams P) {
+__global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntraParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int c = blockIdx.x, h = blockIdx.y;
   ChunkPos pos = chunk_pos(P.seq, c);
@@ -77,6 +77,7 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_intra_kernel(FwdIntraParams P)
   ps.gam = reinterpret_cast<float*>(smem + IntraSmem::GAM);
   ps.beta = reinterpret_cast<float*>(smem + IntraSmem::BETA);
   ps.tot = reinterpret_cast<float*>(smem + IntraSmem::OPS);  // scratch, before operands
+  ps.taps = reinterpret_cast<float*>(smem + IntraSmem::OPS + 8192);
 
   prologue_issue_loads(P.in, ps, pos, h, P.conv);
   cp_async_commit();
@@ -97,12 +98,12 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_intra_kernel(FwdIntraParams P)
   op.er = nullptr;
   op.ec = nullptr;
   {
-    float qt[4][8], kbar[4][8];
+    float qt[STRIP][8], kbar[STRIP][8];
     build_operands<true>(s, ps.gam, op, qt, kbar);
     const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      int t = 4 * tg + r;
+    for (int r = 0; r < STRIP; ++r) {
+      int t = STRIP * tg + r;
       if (t < nvalid) {
         size_t off = ((size_t)(pos.t0 + t) * H + h) * D + 8 * cg;
         *reinterpret_cast<bf16x8*>(P.Qt + off) = pack8(qt[r]);
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_intra_kernel(FwdIntraParams P)
       }
     }
     if (threadIdx.x < D)
-      P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * D + threadIdx.x]);
+      P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
   }
   __syncthreads();
 
@@ -122,29 +123,30 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_intra_kernel(FwdIntraParams P)
   lm_blocks(op, Lp, Msm);
   __syncthreads();
   tri_inverse(Lp, ps.beta, Ainv, xtmp);
-  // T = A diag(beta) as bf16
-  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
-    int r = i >> 6, cc = i & 63;
-    float x = (cc <= r) ? Ainv[r * LDF64 + cc] * ps.beta[cc] : 0.f;
-    Tbf[r * LD64 + cc] = __float2bfloat16(x);
+  // T = A diag(beta) as bf16 (A's strictly-upper part is not stored: zeros)
+  for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
+    int r = i >> 5, cc = 2 * (i & 31);
+    float x0 = (cc <= r) ? Ainv[r * LDF64 + cc] * ps.beta[cc] : 0.f;
+    float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
+    *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
   }
   store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
   __syncthreads();
 
-  // W = T Ke, U = T V ; warp w -> rows 16(w&3), cols 64(w>>2)
+  // W = T Ke, U = T V ; warp w -> rows 16(w&3), cols 32(w>>2)
   {
     const int warp = threadIdx.x >> 5;
-    const int m0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
-    float accW[8][4], accU[8][4];
-    zero_acc<8>(accW);
-    zero_acc<8>(accU);
-    warp_mma<8, false, true>(accW, Tbf, LD64, m0, op.Ke, LD128, n0, 0, 64);
-    warp_mma<8, false, true>(accU, Tbf, LD64, m0, op.V, LD128, n0, 0, 64);
+    const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
+    float accW[4][4], accU[4][4];
+    zero_acc<4>(accW);
+    zero_acc<4>(accU);
+    warp_mma<4, false, true>(accW, Tbf, LD64, m0, op.Ke, LD128, n0, 0, 64);
+    warp_mma<4, false, true>(accU, Tbf, LD64, m0, op.V, LD128, n0, 0, 64);
     __syncthreads();  // Qa/Ka are dead: reuse them as staging
     bf16* Wst = op.Qa;
     bf16* Ust = op.Ka;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);

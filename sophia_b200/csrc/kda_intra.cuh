@@ -1,9 +1,9 @@
 // Intra-chunk stages shared by the forward and backward chunk kernels.
 //
-// One CTA of 256 threads owns one (chunk, head).  Elementwise work uses the
-// "strip" mapping: thread tid owns tokens 4*tg .. 4*tg+3 (tg = tid / 16) and
-// channels 8*cg .. 8*cg+7 (cg = tid % 16); the 16 threads of a half-warp share
-// a token group, so a row reduction over 128 channels is a 16-lane shuffle.
+// One CTA of 512 threads (16 warps) owns one (chunk, head).  Elementwise work
+// uses the "strip" mapping: thread tid owns tokens 2*tg, 2*tg+1 (tg = tid / 16)
+// and channels 8*cg .. 8*cg+7 (cg = tid % 16); the 16 threads of a half-warp
+// share a token pair, so a row reduction over 128 channels is a 16-lane shuffle.
 //
 // Overflow-safe factorisation of exp(Gam_i - Gam_j) (per channel, i >= j):
 //   diagonal 16x16 block (I == J):   a_i * ia_j,   a = 2^(Gam - Gam_r(I)) <= 1,
@@ -20,8 +20,9 @@
 
 namespace kda {
 
-// Per-channel ShortConv taps (fp32 [H*128][4]) of one tensor.
-struct ConvTaps { const float* w; };
+constexpr int INTRA_THREADS = 512;
+constexpr int INTRA_WARPS = INTRA_THREADS / 32;
+constexpr int STRIP = 2;  // tokens per thread in the strip mapping
 
 struct PrologueIn {
   const bf16* q; const bf16* k; const bf16* v;  // [T_total][H][128] (pre-conv if conv)
@@ -37,9 +38,10 @@ struct PrologueSmem {
   bf16* xq; bf16* xk; bf16* xv;  // [67][128] raw rows t0-3 .. t0+63 (row stride 128)
   bf16* graw;                    // [64][128]
   bf16* braw;                    // [64]
-  float* gam;                    // [64][128] log2 cumulative decay
+  float* gam;                    // [64][LDG] log2 cumulative decay
   float* beta;                   // [64]
-  float* tot;                    // [16][128] scratch for the cumsum
+  float* tot;                    // [16][128] scratch for the cumsum (one row per warp)
+  float* taps;                   // [3][4][128] conv taps, tap-major (conflict-free reads)
 };
 
 // Issue cp.async loads of the raw chunk inputs (zero fill outside [bos, t1)).
@@ -76,36 +78,41 @@ __device__ __forceinline__ void prologue_issue_loads(const PrologueIn& in, const
 // and sm.beta are complete and the calling thread holds its strip of the
 // normalised (q scaled) q, k, post-conv v and log2 decays.
 struct Strip {
-  float q[4][8], k[4][8], v[4][8], gam[4][8];
+  float q[STRIP][8], k[STRIP][8], v[STRIP][8], gam[STRIP][8];
 };
 
+// w: tap-major [4][128] taps of this head in shared memory.
 __device__ __forceinline__ void conv_strip(const bf16* x, const float* w, int tg, int cg, bool conv,
-                                           float (&out)[4][8]) {
+                                           float (&out)[STRIP][8]) {
   if (conv) {
-    float xs[7][8];
+    float xs[STRIP + 3][8];
 #pragma unroll
-    for (int r = 0; r < 7; ++r) {
-      bf16x8 v = *reinterpret_cast<const bf16x8*>(x + (4 * tg + r) * D + 8 * cg);
+    for (int r = 0; r < STRIP + 3; ++r) {
+      bf16x8 v = *reinterpret_cast<const bf16x8*>(x + (STRIP * tg + r) * D + 8 * cg);
       unpack8(v, xs[r]);
     }
-    float wt[8][4];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float4 t4 = __ldg(reinterpret_cast<const float4*>(w) + (8 * cg + c));
-      wt[c][0] = t4.x; wt[c][1] = t4.y; wt[c][2] = t4.z; wt[c][3] = t4.w;
+    for (int r = 0; r < STRIP; ++r)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) out[r][c] = 0.f;
+#pragma unroll
+    for (int tap = 0; tap < 4; ++tap) {
+      float4 w0 = *reinterpret_cast<const float4*>(w + tap * D + 8 * cg);
+      float4 w1 = *reinterpret_cast<const float4*>(w + tap * D + 8 * cg + 4);
+      float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int r = 0; r < STRIP; ++r)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) out[r][c] = fmaf(wv[c], xs[r + tap][c], out[r][c]);
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < STRIP; ++r)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float a = wt[c][0] * xs[r][c] + wt[c][1] * xs[r + 1][c] + wt[c][2] * xs[r + 2][c] +
-                  wt[c][3] * xs[r + 3][c];
-        out[r][c] = a * sigmoidf_(a);
-      }
+      for (int c = 0; c < 8; ++c) out[r][c] = silu_fast(out[r][c]);
   } else {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      bf16x8 v = *reinterpret_cast<const bf16x8*>(x + (3 + 4 * tg + r) * D + 8 * cg);
+    for (int r = 0; r < STRIP; ++r) {
+      bf16x8 v = *reinterpret_cast<const bf16x8*>(x + (3 + STRIP * tg + r) * D + 8 * cg);
       unpack8(v, out[r]);
     }
   }
@@ -113,19 +120,30 @@ __device__ __forceinline__ void conv_strip(const bf16* x, const float* w, int tg
 
 __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const PrologueSmem& sm,
                                                  const ChunkPos& p, int h, bool conv, Strip& s) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tg = tid >> 4, cg = tid & 15;
   const int nvalid = p.t1 - p.t0;
-  const float* wq = conv ? in.conv_q + (size_t)h * D * 4 : nullptr;
-  const float* wk = conv ? in.conv_k + (size_t)h * D * 4 : nullptr;
-  const float* wv = conv ? in.conv_v + (size_t)h * D * 4 : nullptr;
+  if (conv) {
+    // [H*128][4] taps -> tap-major [4][128] per tensor
+    for (int i = tid; i < 3 * D; i += blockDim.x) {
+      int X = i >> 7, ch = i & 127;
+      const float* src = (X == 0 ? in.conv_q : (X == 1 ? in.conv_k : in.conv_v)) + ((size_t)h * D + ch) * 4;
+      float4 t4 = __ldg(reinterpret_cast<const float4*>(src));
+      float* dst = sm.taps + X * 4 * D + ch;
+      dst[0] = t4.x; dst[D] = t4.y; dst[2 * D] = t4.z; dst[3 * D] = t4.w;
+    }
+    __syncthreads();
+  }
+  const float* wq = sm.taps;
+  const float* wk = sm.taps + 4 * D;
+  const float* wv = sm.taps + 8 * D;
   conv_strip(sm.xq, wq, tg, cg, conv, s.q);
   conv_strip(sm.xk, wk, tg, cg, conv, s.k);
   conv_strip(sm.xv, wv, tg, cg, conv, s.v);
   // mask padded tokens, L2 normalise q and k per token (reduction over 16 lanes)
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    bool ok = 4 * tg + r < nvalid;
+  for (int r = 0; r < STRIP; ++r) {
+    bool ok = STRIP * tg + r < nvalid;
     float sq = 0.f, sk = 0.f;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -156,10 +174,10 @@ __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const Pro
 #pragma unroll
   for (int c = 0; c < 8; ++c) run[c] = 0.f;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < STRIP; ++r) {
     float gx[8];
-    unpack8(*reinterpret_cast<const bf16x8*>(sm.graw + (4 * tg + r) * D + 8 * cg), gx);
-    bool ok = 4 * tg + r < nvalid;
+    unpack8(*reinterpret_cast<const bf16x8*>(sm.graw + (STRIP * tg + r) * D + 8 * cg), gx);
+    bool ok = STRIP * tg + r < nvalid;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       float z = eA * (gx[c] + bias[c]);
@@ -168,27 +186,48 @@ __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const Pro
       s.gam[r][c] = run[c];
     }
   }
-  *reinterpret_cast<float4*>(sm.tot + tg * D + 8 * cg) = make_float4(run[0], run[1], run[2], run[3]);
-  *reinterpret_cast<float4*>(sm.tot + tg * D + 8 * cg + 4) = make_float4(run[4], run[5], run[6], run[7]);
+  // token-pair totals: the odd half-warp adds the even half-warp's, the warp
+  // total (4 tokens) goes to tot[warp]
+  float inw[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float up = __shfl_up_sync(0xffffffffu, run[c], 16);
+    inw[c] = lane >= 16 ? up : 0.f;
+  }
+  if (lane >= 16) {
+    float* tp = sm.tot + warp * D + 8 * cg;
+    *reinterpret_cast<float4*>(tp) = make_float4(inw[0] + run[0], inw[1] + run[1], inw[2] + run[2], inw[3] + run[3]);
+    *reinterpret_cast<float4*>(tp + 4) = make_float4(inw[4] + run[4], inw[5] + run[5], inw[6] + run[6], inw[7] + run[7]);
+  }
   if (tid < 64) {
     float b = __bfloat162float(sm.braw[tid]);
     sm.beta[tid] = (tid < nvalid) ? sigmoidf_(b) : 0.f;
   }
   __syncthreads();
-  float off[8];
+  // exclusive prefix of the 16 warp totals, per channel, in place (one thread
+  // per channel walks the 16 rows)
+  if (tid < D) {
+    float acc = 0.f;
 #pragma unroll
-  for (int c = 0; c < 8; ++c) off[c] = 0.f;
-  for (int u = 0; u < tg; ++u) {
-    float4 a = *reinterpret_cast<const float4*>(sm.tot + u * D + 8 * cg);
-    float4 b = *reinterpret_cast<const float4*>(sm.tot + u * D + 8 * cg + 4);
-    off[0] += a.x; off[1] += a.y; off[2] += a.z; off[3] += a.w;
-    off[4] += b.x; off[5] += b.y; off[6] += b.z; off[7] += b.w;
+    for (int u = 0; u < INTRA_WARPS; ++u) {
+      float t = sm.tot[u * D + tid];
+      sm.tot[u * D + tid] = acc;
+      acc += t;
+    }
+  }
+  __syncthreads();
+  float off[8];
+  {
+    float4 a = *reinterpret_cast<const float4*>(sm.tot + warp * D + 8 * cg);
+    float4 b = *reinterpret_cast<const float4*>(sm.tot + warp * D + 8 * cg + 4);
+    off[0] = inw[0] + a.x; off[1] = inw[1] + a.y; off[2] = inw[2] + a.z; off[3] = inw[3] + a.w;
+    off[4] = inw[4] + b.x; off[5] = inw[5] + b.y; off[6] = inw[6] + b.z; off[7] = inw[7] + b.w;
   }
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < STRIP; ++r) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) s.gam[r][c] += off[c];
-    float* gp = sm.gam + (4 * tg + r) * D + 8 * cg;
+    float* gp = sm.gam + (STRIP * tg + r) * LDG + 8 * cg;
     *reinterpret_cast<float4*>(gp) = make_float4(s.gam[r][0], s.gam[r][1], s.gam[r][2], s.gam[r][3]);
     *reinterpret_cast<float4*>(gp + 4) = make_float4(s.gam[r][4], s.gam[r][5], s.gam[r][6], s.gam[r][7]);
   }
@@ -212,43 +251,48 @@ __device__ __forceinline__ int pair_index(int I, int J) { return I * (I - 1) / 2
 
 // Builds the operand tiles; optionally also returns the strip of q*2^Gam and
 // k*2^(Gam_C - Gam) (the forward's Qt and Kbar) through qt/kbar.
+//   a = 2^(Gam - Gam_r(J)) <= 1, ia = 1/a (exact exponent, second ex2),
+//   b = 2^(Gam_e(J) - Gam) = ia * 2^(Gam_e(J) - Gam_r(J)): a product of a
+//   factor in [1, 2^116] and one in [2^-116, 1], so neither overflows and the
+//   product is at least 2^-116.
 template <bool WANT_QK_DECAYED>
 __device__ __forceinline__ void build_operands(const Strip& s, const float* gam, const Operands& op,
                                                float (*qt)[8], float (*kbar)[8]) {
   const int tid = threadIdx.x;
   const int tg = tid >> 4, cg = tid & 15;
-  const int J = tg >> 2;
-  const float* grow = gam + (16 * J) * D + 8 * cg;       // row r(J)
-  const float* gend = gam + (16 * J + 15) * D + 8 * cg;  // row e(J)
-  const float* gC = gam + 63 * D + 8 * cg;               // row C-1
-  float Gr[8], Ge[8], erv[8], ecv[8];
+  const int J = (STRIP * tg) >> 4;
+  const float* grow = gam + (16 * J) * LDG + 8 * cg;       // row r(J)
+  const float* gend = gam + (16 * J + 15) * LDG + 8 * cg;  // row e(J)
+  const float* gC = gam + 63 * LDG + 8 * cg;               // row C-1
+  float Gr[8], erv[8], ecv[8], rev[8];
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     Gr[c] = grow[c];
-    Ge[c] = gend[c];
+    float Ge = gend[c];
     erv[c] = ex2(Gr[c]);
-    ecv[c] = ex2(gC[c] - Ge[c]);
+    ecv[c] = ex2(gC[c] - Ge);
+    rev[c] = ex2(Ge - Gr[c]);
   }
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < STRIP; ++r) {
     float qa[8], ka[8], kd[8], kb[8], ke[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       float G = s.gam[r][c];
       float a = ex2(G - Gr[c]);
       float ia = ex2(Gr[c] - G);
-      float b = ex2(Ge[c] - G);
+      float b = ia * rev[c];
       qa[c] = s.q[r][c] * a;
       ka[c] = s.k[r][c] * a;
       kd[c] = s.k[r][c] * ia;
       kb[c] = s.k[r][c] * b;
-      ke[c] = s.k[r][c] * (a * erv[c]);
+      ke[c] = ka[c] * erv[c];
       if (WANT_QK_DECAYED) {
-        qt[r][c] = s.q[r][c] * (a * erv[c]);
-        kbar[r][c] = s.k[r][c] * (b * ecv[c]);
+        qt[r][c] = qa[c] * erv[c];
+        kbar[r][c] = kb[c] * ecv[c];
       }
     }
-    int row = (4 * tg + r) * LD128 + 8 * cg;
+    int row = (STRIP * tg + r) * LD128 + 8 * cg;
     *reinterpret_cast<bf16x8*>(op.Qa + row) = pack8(qa);
     *reinterpret_cast<bf16x8*>(op.Ka + row) = pack8(ka);
     *reinterpret_cast<bf16x8*>(op.Kd + row) = pack8(kd);
@@ -261,13 +305,13 @@ __device__ __forceinline__ void build_operands(const Strip& s, const float* gam,
     int pidx = i / D, d = i - pidx * D;
     int I = pidx >= 3 ? 3 : (pidx >= 1 ? 2 : 1);
     int Jp = pidx - pair_index(I, 0);
-    op.cvec[i] = ex2(gam[(16 * I) * D + d] - gam[(16 * Jp + 15) * D + d]);
+    op.cvec[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
   }
   if (op.er) {
     for (int i = tid; i < 4 * D; i += blockDim.x) {
       int Jp = i / D, d = i - Jp * D;
-      op.er[i] = ex2(gam[(16 * Jp) * D + d]);
-      op.ec[i] = ex2(gam[63 * D + d] - gam[(16 * Jp + 15) * D + d]);
+      op.er[i] = ex2(gam[(16 * Jp) * LDG + d]);
+      op.ec[i] = ex2(gam[63 * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
     }
   }
 }
@@ -293,7 +337,7 @@ __device__ __forceinline__ void block_product(float (&acc)[2][4], const bf16* Ar
   const bool diag = I == J;
   const bf16* Bt = diag ? op.Kd : op.Kb;
   const float* sv = diag ? nullptr : op.cvec + pair_index(I, J) * D;
-#pragma unroll 2
+#pragma unroll
   for (int kk = 0; kk < D; kk += 16) {
     uint32_t a[4], b[4];
     load_A(a, Arow, LD128, 16 * I, kk);
@@ -305,20 +349,22 @@ __device__ __forceinline__ void block_product(float (&acc)[2][4], const bf16* Ar
 }
 
 // Computes the strictly-lower L' blocks (and the lower-inclusive M blocks when
-// Msm != nullptr) into Lp (fp32 [64][LDF64], upper part zeroed) and Msm (bf16
-// [64][LD64], upper part zeroed).  Caller syncs afterwards.
+// Msm != nullptr) into Lp (fp32 [64][LDF64]) and Msm (bf16 [64][LD64], whose
+// strictly-upper 16x16 blocks are zeroed).  Only the lower blocks of Lp are
+// written: every reader masks the rest.  Caller syncs afterwards.
 __device__ __forceinline__ void lm_blocks(const Operands& op, float* Lp, bf16* Msm) {
   const int warp = threadIdx.x >> 5;
   const int ntask = Msm ? 20 : 10;
-  // zero the strictly-upper blocks
-  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
-    int r = i >> 6, c = i & 63;
-    if ((c >> 4) > (r >> 4)) {
-      Lp[r * LDF64 + c] = 0.f;
-      if (Msm) Msm[r * LD64 + c] = __float2bfloat16(0.f);
+  if (Msm) {
+    // six strictly-upper blocks: (0,1),(0,2),(0,3),(1,2),(1,3),(2,3)
+    for (int i = threadIdx.x; i < 6 * 256; i += blockDim.x) {
+      int blk = i >> 8, e = i & 255;
+      int I = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+      int J = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+      Msm[(16 * I + (e >> 4)) * LD64 + 16 * J + (e & 15)] = __float2bfloat16(0.f);
     }
   }
-  for (int task = warp; task < ntask; task += 8) {
+  for (int task = warp; task < ntask; task += INTRA_WARPS) {
     bool isM = task >= 10;
     int bi = isM ? task - 10 : task;
     // block list in order (0,0),(1,0),(1,1),(2,0),(2,1),(2,2),(3,0),...
@@ -344,30 +390,55 @@ __device__ __forceinline__ void lm_blocks(const Operands& op, float* Lp, bf16* M
   }
 }
 
-// A = (I + diag(beta) Lp)^-1 (unit lower triangular, fp32).  Uses xtmp
-// ([3][16][16] fp32).  Ends with __syncthreads().
-__device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, float* A, float* xtmp) {
-  const int tid = threadIdx.x;
-  // zero the strictly-upper blocks of A
-  for (int i = tid; i < 64 * 64; i += blockDim.x) {
-    int r = i >> 6, c = i & 63;
-    if ((c >> 4) > (r >> 4)) A[r * LDF64 + c] = 0.f;
+// A = (I + diag(beta) Lp)^-1 (unit lower triangular, fp32; only the lower
+// 16x16 blocks are written).  Ends with __syncthreads().
+//   diagonal blocks: forward substitution in fp32, one column per thread;
+//   off-diagonal blocks, by distance d = I - J:
+//       X = sum_{K=J}^{I-1} L_IK A_KJ,   A_IJ = -A_II X
+//   as 16x16x16 tensor-core products (tf32 in, fp32 accumulate), one warp per
+//   block, X staged through the warp's slice of xtmp ([16 warps][16][17]).
+__device__ __forceinline__ void warp_tf32_16x16(float (&acc)[2][4], const float* Am, int lda, const float* rowscale,
+                                                const float* Bm, int ldb) {
+  // acc[16 x 16] += diag(rowscale) Am[16 x 16] * Bm[16 x 16] (row-major fp32 tiles)
+  const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
+  const float s0 = rowscale ? rowscale[g] : 1.f, s1 = rowscale ? rowscale[g + 8] : 1.f;
+#pragma unroll
+  for (int k0 = 0; k0 < 16; k0 += 8) {
+    uint32_t a[4];
+    a[0] = to_tf32(s0 * Am[g * lda + k0 + t]);
+    a[1] = to_tf32(s1 * Am[(g + 8) * lda + k0 + t]);
+    a[2] = to_tf32(s0 * Am[g * lda + k0 + t + 4]);
+    a[3] = to_tf32(s1 * Am[(g + 8) * lda + k0 + t + 4]);
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      uint32_t b0 = to_tf32(Bm[(k0 + t) * ldb + 8 * n + g]);
+      uint32_t b1 = to_tf32(Bm[(k0 + t + 4) * ldb + 8 * n + g]);
+      mma1688_tf32(acc[n], a, b0, b1);
+    }
   }
-  // diagonal blocks by forward substitution, one column per thread
+}
+
+__device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, float* A, float* xtmp) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // (strictly-upper blocks of A are never written; readers mask them)
   if (tid < 64) {
-    int blk = tid >> 4, col = tid & 15;
-    int o = 16 * blk;
+    const int blk = tid >> 4, col = tid & 15;
+    const int o = 16 * blk;
     float x[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       float acc = (r == col) ? 1.f : 0.f;
       if (r > col) {
-        float bi = beta[o + r];
-        float sum = 0.f;
+        const float* lrow = Lp + (o + r) * LDF64 + o;
+        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-        for (int m = 0; m < 15; ++m)
-          if (m < r && m >= col) sum += Lp[(o + r) * LDF64 + o + m] * x[m];
-        acc = -bi * sum;
+        for (int m = 0; m < 15; m += 4) {
+          if (m < r && m >= col) p0 = fmaf(lrow[m], x[m], p0);
+          if (m + 1 < r && m + 1 >= col) p1 = fmaf(lrow[m + 1], x[m + 1], p1);
+          if (m + 2 < r && m + 2 >= col) p2 = fmaf(lrow[m + 2], x[m + 2], p2);
+          if (m + 3 < 15 && m + 3 < r && m + 3 >= col) p3 = fmaf(lrow[m + 3], x[m + 3], p3);
+        }
+        acc = -beta[o + r] * ((p0 + p1) + (p2 + p3));
       }
       x[r] = acc;
     }
@@ -375,29 +446,33 @@ __device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, 
     for (int r = 0; r < 16; ++r) A[(o + r) * LDF64 + o + col] = x[r];
   }
   __syncthreads();
-  // off-diagonal blocks, by distance I - J
+  float* xs = xtmp + warp * 16 * 17;
+  const int g = lane >> 2, t = lane & 3;
   for (int dist = 1; dist <= 3; ++dist) {
-    int npairs = 4 - dist;
-    // xtmp_p = sum_{K=J}^{I-1} L_IK A_KJ
-    for (int e = tid; e < npairs * 256; e += blockDim.x) {
-      int pp = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      int J = pp, I = pp + dist;
-      float bi = beta[16 * I + r];
-      float sum = 0.f;
+    if (warp < 4 - dist) {
+      const int J = warp, I = warp + dist;
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       for (int K = J; K < I; ++K)
+        warp_tf32_16x16(acc, Lp + (16 * I) * LDF64 + 16 * K, LDF64, beta + 16 * I,
+                        A + (16 * K) * LDF64 + 16 * J, LDF64);
 #pragma unroll
-        for (int m = 0; m < 16; ++m)
-          sum += Lp[(16 * I + r) * LDF64 + 16 * K + m] * A[(16 * K + m) * LDF64 + 16 * J + c];
-      xtmp[e] = bi * sum;
-    }
-    __syncthreads();
-    for (int e = tid; e < npairs * 256; e += blockDim.x) {
-      int pp = e >> 8, r = (e >> 4) & 15, c = e & 15;
-      int J = pp, I = pp + dist;
-      float sum = 0.f;
+      for (int n = 0; n < 2; ++n) {
+        xs[g * 17 + 8 * n + 2 * t] = acc[n][0];
+        xs[g * 17 + 8 * n + 2 * t + 1] = acc[n][1];
+        xs[(g + 8) * 17 + 8 * n + 2 * t] = acc[n][2];
+        xs[(g + 8) * 17 + 8 * n + 2 * t + 1] = acc[n][3];
+      }
+      __syncwarp();
+      float out[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      warp_tf32_16x16(out, A + (16 * I) * LDF64 + 16 * I, LDF64, nullptr, xs, 17);
 #pragma unroll
-      for (int m = 0; m < 16; ++m) sum += A[(16 * I + r) * LDF64 + 16 * I + m] * xtmp[(pp << 8) + m * 16 + c];
-      A[(16 * I + r) * LDF64 + 16 * J + c] = -sum;
+      for (int n = 0; n < 2; ++n) {
+        float* dst = A + (16 * I + g) * LDF64 + 16 * J + 8 * n + 2 * t;
+        dst[0] = -out[n][0];
+        dst[1] = -out[n][1];
+        dst[8 * LDF64] = -out[n][2];
+        dst[8 * LDF64 + 1] = -out[n][3];
+      }
     }
     __syncthreads();
   }

@@ -33,8 +33,9 @@ struct PostSmem {
   static constexpr int XS = 0;                      // 70 x 128 bf16
   static constexpr int DS = XS + 70 * D * 2;        // 67 x 128 bf16
   static constexpr int DC = DS + 67 * D * 2;        // 67 x 128 fp32
-  static constexpr int PW = DC + 67 * D * 4;        // 16 x 128 x 4 fp32
-  static constexpr int END = PW + 16 * D * 4 * 4;
+  static constexpr int PW = DC + 67 * D * 4;        // 16 x 4 x 128 fp32 (row group, tap, channel)
+  static constexpr int TAPS = PW + 16 * 4 * D * 4;  // 4 x 128 fp32, tap-major
+  static constexpr int END = TAPS + 4 * D * 4;
 };
 
 __global__ void __launch_bounds__(256) kda_bwd_post_kernel(PostParams P) {
@@ -77,10 +78,18 @@ __global__ void __launch_bounds__(256) kda_bwd_post_kernel(PostParams P) {
     __syncthreads();
     float wt[8][4];
     if (P.conv) {
+      float* taps = reinterpret_cast<float*>(smem + PostSmem::TAPS);
+      for (int i = tid; i < D; i += blockDim.x) {
+        float4 t4 = __ldg(reinterpret_cast<const float4*>(w) + i);
+        taps[i] = t4.x; taps[D + i] = t4.y; taps[2 * D + i] = t4.z; taps[3 * D + i] = t4.w;
+      }
+      __syncthreads();
 #pragma unroll
-      for (int cch = 0; cch < 8; ++cch) {
-        float4 t4 = __ldg(reinterpret_cast<const float4*>(w) + (8 * cg + cch));
-        wt[cch][0] = t4.x; wt[cch][1] = t4.y; wt[cch][2] = t4.z; wt[cch][3] = t4.w;
+      for (int tap = 0; tap < 4; ++tap) {
+        float4 a = *reinterpret_cast<const float4*>(taps + tap * D + 8 * cg);
+        float4 b = *reinterpret_cast<const float4*>(taps + tap * D + 8 * cg + 4);
+        wt[0][tap] = a.x; wt[1][tap] = a.y; wt[2][tap] = a.z; wt[3][tap] = a.w;
+        wt[4][tap] = b.x; wt[5][tap] = b.y; wt[6][tap] = b.z; wt[7][tap] = b.w;
       }
     }
     // dc (or the norm backward alone) for rows tg, tg+16, ...; every lane runs
@@ -99,7 +108,7 @@ __global__ void __launch_bounds__(256) kda_bwd_post_kernel(PostParams P) {
         for (int cch = 0; cch < 8; ++cch) {
           float a = wt[cch][0] * xr[0][cch] + wt[cch][1] * xr[1][cch] + wt[cch][2] * xr[2][cch] + wt[cch][3] * xr[3][cch];
           cv[cch] = a;
-          y[cch] = a * sigmoidf_(a);
+          y[cch] = silu_fast(a);
         }
       } else {
         unpack8(*reinterpret_cast<const bf16x8*>(xs + rr * D + 8 * cg), y);
@@ -137,7 +146,7 @@ __global__ void __launch_bounds__(256) kda_bwd_post_kernel(PostParams P) {
         float dcv[8];
 #pragma unroll
         for (int cch = 0; cch < 8; ++cch) {
-          float sg = sigmoidf_(cv[cch]);
+          float sg = sigmoid_fast(cv[cch]);
           dcv[cch] = rowok ? dyv[cch] * sg * (1.f + cv[cch] * (1.f - sg)) : 0.f;
         }
         float* dp = dcs + r * D + 8 * cg;
@@ -178,14 +187,18 @@ __global__ void __launch_bounds__(256) kda_bwd_post_kernel(PostParams P) {
         *reinterpret_cast<bf16x8*>(dx + (size_t)(pos.t0 + r) * rowH + (size_t)h * D + 8 * cg) = pack8(dxv);
       }
 #pragma unroll
-      for (int cch = 0; cch < 8; ++cch)
-        *reinterpret_cast<float4*>(pw + (tg * D + 8 * cg + cch) * 4) =
-            make_float4(acc[cch][0], acc[cch][1], acc[cch][2], acc[cch][3]);
+      for (int tap = 0; tap < 4; ++tap) {
+        float* dst = pw + (tg * 4 + tap) * D + 8 * cg;
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[0][tap], acc[1][tap], acc[2][tap], acc[3][tap]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4][tap], acc[5][tap], acc[6][tap], acc[7][tap]);
+      }
       __syncthreads();
       for (int i = tid; i < D * 4; i += blockDim.x) {
+        // output layout [channel][tap]: i = channel * 4 + tap
+        const int ch = i >> 2, tap = i & 3;
         float sum = 0.f;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) sum += pw[u * D * 4 + i];
+        for (int u = 0; u < 16; ++u) sum += pw[(u * 4 + tap) * D + ch];
         P.partW[(((size_t)c * 3 + X) * H + h) * D * 4 + i] = sum;
       }
     }
@@ -201,34 +214,49 @@ struct ReduceParams {
   float *dA_log, *ddt_bias, *dconv_q, *dconv_k, *dconv_v;
 };
 
-// grid (H, 1+conv), 128 threads: block (h, 0) reduces dA_log[h] and
-// ddt_bias[h, :]; block (h, 1) reduces the 3 x 128 x 4 conv taps of head h.
-__global__ void __launch_bounds__(128) kda_reduce_kernel(ReduceParams P) {
-  const int h = blockIdx.x, H = P.H, tid = threadIdx.x;
+// Deterministic sums over chunks of the per-chunk partials, 256 threads per
+// block and 128 columns per block: warp w adds chunks w, w+8, ... (lane l owns
+// four consecutive columns, float4 loads), then the eight warp partials are
+// added in a fixed order.
+//   blocks [0, H):        ddt_bias[h, :]   = sum_c partB[c, h, :]
+//   blocks [H, 2H):       dA_log[h]        = sum_c sum_d partA[c, h, d]
+//   blocks [2H, 2H+12H):  dconv (3 x H x 128 x 4 columns of partW)
+__global__ void __launch_bounds__(256) kda_reduce_kernel(ReduceParams P) {
+  __shared__ float4 red[8][32];
+  const int H = P.H, b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nchunks = P.seq.cu_seqlens ? P.seq.chunk_offsets[P.seq.N] : P.seq.N * P.seq.nt;
-  if (blockIdx.y == 0) {
-    float sa = 0.f, sb = 0.f;
-    for (int c = 0; c < nchunks; ++c) {
-      sa += P.partA[((size_t)c * H + h) * D + tid];
-      sb += P.partB[((size_t)c * H + h) * D + tid];
+  const float* src;
+  size_t stride, col0;
+  int kind;
+  if (b < H) { kind = 0; src = P.partB; stride = (size_t)H * D; col0 = (size_t)b * D; }
+  else if (b < 2 * H) { kind = 1; src = P.partA; stride = (size_t)H * D; col0 = (size_t)(b - H) * D; }
+  else { kind = 2; src = P.partW; stride = (size_t)3 * H * D * 4; col0 = (size_t)(b - 2 * H) * 128; }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = warp; c < nchunks; c += 8) {
+    float4 v = __ldg(reinterpret_cast<const float4*>(src + (size_t)c * stride + col0) + lane);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float4 t = red[0][lane];
+    for (int w = 1; w < 8; ++w) {
+      float4 v = red[w][lane];
+      t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
     }
-    P.ddt_bias[(size_t)h * D + tid] = sb;
-    __shared__ float red[128];
-    red[tid] = sa;
-    __syncthreads();
-    for (int s = 64; s > 0; s >>= 1) {
-      if (tid < s) red[tid] += red[tid + s];
-      __syncthreads();
-    }
-    if (tid == 0) P.dA_log[h] = red[0];
-  } else {
-    for (int X = 0; X < 3; ++X) {
+    if (kind == 0) {
+      reinterpret_cast<float4*>(P.ddt_bias + col0)[lane] = t;
+    } else if (kind == 1) {
+      float sum = t.x + t.y + t.z + t.w;
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) P.dA_log[b - H] = sum;
+    } else {
+      // column index col0 + 4*lane within the [3][H][128][4] layout
+      size_t col = col0 + 4 * (size_t)lane;
+      size_t per = (size_t)H * D * 4;
+      int X = (int)(col / per);
       float* out = X == 0 ? P.dconv_q : (X == 1 ? P.dconv_k : P.dconv_v);
-      for (int i = tid; i < D * 4; i += 128) {
-        float s = 0.f;
-        for (int c = 0; c < nchunks; ++c) s += P.partW[(((size_t)c * 3 + X) * H + h) * D * 4 + i];
-        out[(size_t)h * D * 4 + i] = s;
-      }
+      reinterpret_cast<float4*>(out + (col - (size_t)X * per))[0] = t;
     }
   }
 }

@@ -52,6 +52,38 @@ CASES = {
     "two_chunks": Case("two_chunks", B=1, T=128, H=1, seed=42),
 }
 
+# Further seeded cases checked on the GPU (no reference fixture; the oracle is
+# pinned by CASES above).
+RANDOM_CASES = {
+    # exact chunk multiple, several heads, batch > 1
+    "b2_t128_h2": Case("b2_t128_h2", B=2, T=128, H=2, h0=True, final_state_grad=True, seed=3),
+    # lengths around the chunk and sub-chunk edges
+    "t1": Case("t1", B=1, T=1, H=1, h0=True, final_state_grad=True, seed=4),
+    "t15": Case("t15", B=1, T=15, H=1, seed=5),
+    "t17": Case("t17", B=1, T=17, H=1, random_gate_params=True, seed=6),
+    "t63": Case("t63", B=1, T=63, H=1, h0=True, seed=7),
+    "t65": Case("t65", B=1, T=65, H=1, final_state_grad=True, seed=8),
+    "t200_noconv": Case("t200_noconv", B=1, T=200, H=2, conv=False, h0=True, final_state_grad=True, seed=9),
+    # packed documents including one-token and chunk-aligned documents
+    "varlen_edges": Case("varlen_edges", B=1, T=260, H=2, cu_seqlens=[0, 1, 65, 129, 130, 200, 260],
+                         h0=True, final_state_grad=True, random_gate_params=True, seed=10),
+    # strongest allowed decay everywhere (gate logits pushed to saturation)
+    "strong_decay": Case("strong_decay", B=1, T=192, H=1, seed=12, extras={"g_shift": 8.0}),
+    # no decay at all (g -> 0)
+    "no_decay": Case("no_decay", B=1, T=128, H=1, seed=14, extras={"g_shift": -30.0}),
+}
+
+ALL_CASES = {**CASES, **RANDOM_CASES}
+
+
+def make_case_inputs(case: Case) -> dict[str, torch.Tensor]:
+    """make_inputs plus the case's gate-logit shift (saturation cases)."""
+    inp = make_inputs(case)
+    shift = case.extras.get("g_shift")
+    if shift is not None:
+        inp["g"] = inp["g"] + shift
+    return inp
+
 
 def _normal(g, shape, std=1.0):
     return torch.randn(*shape, generator=g, dtype=torch.float32) * std

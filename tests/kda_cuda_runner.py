@@ -80,5 +80,21 @@ def compare(got: dict, ref: dict, keys=None, rtol=RTOL, atol=ATOL) -> dict:
     return out
 
 
-def failures(rep: dict) -> dict:
-    return {k: v for k, v in rep.items() if v[0] > 1.0 or v[1] > REL_FRO}
+def failures(rep: dict, ref: dict | None = None, baseline: dict | None = None) -> dict:
+    """Keys that fail.  A key passes when
+      (a) viol <= 1, and rel <= REL_FRO unless the tensor sits in the
+          atol-dominated regime (rms(ref) <= atol / rtol, where a Frobenius
+          ratio of tiny values says nothing), or
+      (b) it is no less accurate than the reference's own CUDA path on the same
+          inputs (``baseline``: {key: {"viol", "rel"}} from fla_accuracy.json),
+          within 25%, on both measures."""
+    bad = {}
+    for k, (viol, rel) in rep.items():
+        small = ref is not None and k in ref and ref[k].double().pow(2).mean().sqrt().item() <= ATOL / RTOL
+        ok = viol <= 1.0 and (rel <= REL_FRO or small)
+        if not ok and baseline and k in baseline:
+            b = baseline[k]
+            ok = viol <= 1.25 * max(b["viol"], 1.0) and rel <= 1.25 * max(b["rel"], REL_FRO)
+        if not ok:
+            bad[k] = (viol, rel)
+    return bad

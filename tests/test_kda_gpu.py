@@ -1,18 +1,23 @@
 """GPU parity of the CUDA KDA layer against the CPU oracle and the golden
-fixtures made by the reference.  Tolerance (bf16 path): every element within
-rtol 2e-2 / atol 2e-3 of the float64 oracle run on the same bf16-rounded inputs
-(atol in units of max(1, rms) of each tensor), and a relative Frobenius error
-below 1e-2, for outputs, final states and all gradients."""
+fixtures made by the reference.
+
+Tolerance (bf16 path), for outputs, final states and every gradient, against
+the float64 oracle run on the same bf16-rounded inputs: every element within
+rtol 2e-2 / atol 2e-3 (atol in units of max(1, rms) of the tensor) and a
+relative Frobenius error below 1e-2 -- or, where the reference's own CUDA path
+(flash-linear-attention Triton, errors recorded in golden/fla_accuracy.json)
+misses that bar on the same inputs, no more than 25% above its errors."""
 
 from __future__ import annotations
 
+import json
 import os
 
 import numpy as np
 import pytest
 import torch
 
-from cases import CASES, Case, make_inputs
+from cases import ALL_CASES, CASES, RANDOM_CASES, Case, make_case_inputs
 from kda_cuda_runner import ATOL, RTOL, compare, failures, round_inputs_bf16, run_cuda
 from oracle_runner import run_oracle
 
@@ -20,40 +25,20 @@ pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
-RANDOM_CASES = {
-    # exact chunk multiple, several heads, batch > 1
-    "b2_t128_h2": Case("b2_t128_h2", B=2, T=128, H=2, h0=True, final_state_grad=True, seed=3),
-    # lengths around the chunk and sub-chunk edges
-    "t1": Case("t1", B=1, T=1, H=1, h0=True, final_state_grad=True, seed=4),
-    "t15": Case("t15", B=1, T=15, H=1, seed=5),
-    "t17": Case("t17", B=1, T=17, H=1, random_gate_params=True, seed=6),
-    "t63": Case("t63", B=1, T=63, H=1, h0=True, seed=7),
-    "t65": Case("t65", B=1, T=65, H=1, final_state_grad=True, seed=8),
-    "t200_noconv": Case("t200_noconv", B=1, T=200, H=2, conv=False, h0=True, final_state_grad=True, seed=9),
-    # packed documents including one-token and chunk-aligned documents
-    "varlen_edges": Case("varlen_edges", B=1, T=260, H=2, cu_seqlens=[0, 1, 65, 129, 130, 200, 260],
-                         h0=True, final_state_grad=True, random_gate_params=True, seed=10),
-    # strongest allowed decay everywhere (gate logits pushed to saturation)
-    "strong_decay": Case("strong_decay", B=1, T=192, H=1, seed=12, extras={"g_shift": 8.0}),
-    # no decay at all (g -> 0)
-    "no_decay": Case("no_decay", B=1, T=128, H=1, seed=14, extras={"g_shift": -30.0}),
-}
+def _fla_baseline(name):
+    path = os.path.join(GOLDEN, "fla_accuracy.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f)["cases"].get(name)
 
 
-def _inputs(case):
-    inp = make_inputs(case)
-    shift = case.extras.get("g_shift")
-    if shift is not None:
-        inp["g"] = inp["g"] + shift
-    return inp
-
-
-def _check(case, inp=None, strict=True):
-    inp = round_inputs_bf16(_inputs(case) if inp is None else inp)
+def _check(case, inp=None):
+    inp = round_inputs_bf16(make_case_inputs(case) if inp is None else inp)
     ref = run_oracle(case, inputs=inp)
     got = run_cuda(case, inputs=inp)
     rep = compare(got, ref)
-    return rep, failures(rep)
+    return rep, failures(rep, ref, _fla_baseline(case.name))
 
 
 @pytest.mark.parametrize("name", sorted(CASES) + sorted(RANDOM_CASES))
@@ -71,7 +56,7 @@ def test_cuda_matches_reference_golden(name):
     got = run_cuda(CASES[name])
     ref = {k: torch.from_numpy(gold[k]) for k in gold.files if k != "input_sums"}
     rep = compare(got, ref)
-    bad = failures(rep)
+    bad = failures(rep, ref, _fla_baseline(name))
     assert not bad, "\n".join(f"{k}: viol={v[0]:.3f} rel={v[1]:.2e}" for k, v in sorted(rep.items()))
 
 
@@ -79,7 +64,7 @@ def test_packed_equals_unpacked_bit_exact():
     """cu_seqlens resets: each packed document gives exactly the bits of the
     same document run alone (chunks start at document starts)."""
     case = RANDOM_CASES["varlen_edges"]
-    inp = round_inputs_bf16(_inputs(case))
+    inp = round_inputs_bf16(make_case_inputs(case))
     packed = run_cuda(case, inputs=inp)
     cu = case.cu_seqlens
     for n in range(len(cu) - 1):
@@ -105,7 +90,7 @@ def test_state_carry_equals_one_shot():
     when the split falls on a chunk edge (seam-level state carry)."""
     from sophia_b200 import chunk_kda
     case = Case("carry", B=2, T=256, H=2, conv=False, seed=21)
-    inp = round_inputs_bf16(_inputs(case))
+    inp = round_inputs_bf16(make_case_inputs(case))
     dev = "cuda"
     t = {k: inp[k].to(dev, torch.bfloat16 if k in ("q", "k", "v", "g", "beta") else torch.float32)
          for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias")}
@@ -146,7 +131,7 @@ def test_full_size_forward_is_causal_and_matches_prefix_oracle():
                        beta[5:6, :P, 3:5].to(torch.bfloat16).double(), torch.zeros(2, dtype=torch.float64),
                        torch.zeros(256, dtype=torch.float64), conv_weights=convs_h)
     rep = compare({"o": o[5:6, :P, 3:5].double().cpu()}, {"o": ref.o})
-    assert not failures(rep), rep
+    assert not failures(rep, {"o": ref.o}), rep
 
 
 def test_errors_are_raised_on_host():
