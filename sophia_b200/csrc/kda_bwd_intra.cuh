@@ -38,7 +38,7 @@ struct BwdIntraParams {
 struct BwdIntraSmem {
   static constexpr int OPSZ = 64 * LD128 * 2;                // 17408
   static constexpr int OPS = 0;                              // 6 operand tiles
-  static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x LDG fp32
+  static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x LDG fp32 (later dQt, dKbar, dGam)
   static constexpr int DEW = GAM + 64 * LDG * 4;             // dE, dW tiles (graw during prologue)
   static constexpr int RAW = DEW + 2 * OPSZ;                 // raw q/k/v, later small tiles
   static constexpr int RAWSZ = 51712;
@@ -129,12 +129,24 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   bf16* dWs = dEs + 64 * LD128;
   load_tile128(dEs, P.dE, pos.t0, nv, H, h);
   load_tile128(dWs, P.dW, pos.t0, nv, H, h);
+  // dQt and dKbar are only read elementwise: unpadded [64][128] tiles in the
+  // (now dead) decay region, 16-byte chunks XOR-swizzled by row so that the
+  // fragment-position reads below are bank-conflict free
+  bf16* dQs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GAM);
+  bf16* dKs = dQs + 64 * D;
+  for (int i = tid; i < 2 * 64 * 16; i += blockDim.x) {
+    int which = i >> 10, r = (i >> 4) & 63, cc = i & 15;
+    bool ok = r < nv;
+    const bf16* src = which ? P.dKb : P.dQt;
+    bf16* dst = which ? dKs : dQs;
+    cp_async16(dst + r * D + ((cc ^ (r & 7)) << 3), src + (ok ? ((size_t)(pos.t0 + r) * H + h) * D + cc * 8 : 0), ok);
+  }
   cp_async_commit();
 
   float* Lp = reinterpret_cast<float*>(smem + BwdIntraSmem::LP);
   float* Ainv = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
   float* xtmp = reinterpret_cast<float*>(smem + BwdIntraSmem::XTMP);
-  lm_blocks(op, Lp, nullptr);
+  l_blocks(op, Lp);
   __syncthreads();
   tri_inverse(Lp, ps.beta, Ainv, xtmp);
   bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
@@ -165,7 +177,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   __syncthreads();
   load_tile64(dMs, P.dM, pos.t0, nv, H, h);
   cp_async_commit();
-  cp_async_wait<1>();  // dE, dW
+  cp_async_wait<1>();  // dE, dW, dQt, dKbar
   __syncthreads();
 
   float dq[4][4], dk[4][4], dG[4][4];
@@ -191,12 +203,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        size_t goff = ((size_t)(pos.t0 + r) * H + h) * D + cc;
-        float2 gq = make_float2(0.f, 0.f), gk = make_float2(0.f, 0.f);
-        if (r < nv) {
-          gq = unpack_bf16(__ldg(reinterpret_cast<const unsigned int*>(P.dQt + goff)));
-          gk = unpack_bf16(__ldg(reinterpret_cast<const unsigned int*>(P.dKb + goff)));
-        }
+        const int sw = r * D + ((((cc >> 3) ^ (r & 7))) << 3) + (cc & 7);
+        float2 gq = unpack_bf16(*reinterpret_cast<const uint32_t*>(dQs + sw));
+        float2 gk = unpack_bf16(*reinterpret_cast<const uint32_t*>(dKs + sw));
         float2 qa = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Qa + r * LD128 + cc));
         float2 kb = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kb + r * LD128 + cc));
         float2 ke = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Ke + r * LD128 + cc));

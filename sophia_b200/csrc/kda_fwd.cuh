@@ -120,9 +120,20 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
   float* xtmp = reinterpret_cast<float*>(smem + IntraSmem::XTMP);
   bf16* Tbf = reinterpret_cast<bf16*>(smem + IntraSmem::TBF);
   bf16* Msm = reinterpret_cast<bf16*>(smem + IntraSmem::MSM);
-  lm_blocks(op, Lp, Msm);
+  l_blocks(op, Lp);
   __syncthreads();
-  tri_inverse(Lp, ps.beta, Ainv, xtmp);
+  // the diagonal inverse (warps 0-1) overlaps the M blocks (warps 4-15)
+  {
+    const int warp = threadIdx.x >> 5;
+    if (warp < 2) {
+      tri_inverse_diag(Lp, ps.beta, Ainv);
+    } else if (warp >= 4) {
+      if (warp < 14) lm_block_task(op, 1, warp - 4, Lp, Msm);
+      zero_m_upper(Msm, 128, INTRA_THREADS - 128);
+    }
+  }
+  __syncthreads();
+  tri_inverse_offdiag(Lp, ps.beta, Ainv, xtmp);
   // T = A diag(beta) as bf16 (A's strictly-upper part is not stored: zeros)
   for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
     int r = i >> 5, cc = 2 * (i & 31);

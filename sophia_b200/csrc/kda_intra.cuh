@@ -348,46 +348,46 @@ __device__ __forceinline__ void block_product(float (&acc)[2][4], const bf16* Ar
   }
 }
 
-// Computes the strictly-lower L' blocks (and the lower-inclusive M blocks when
-// Msm != nullptr) into Lp (fp32 [64][LDF64]) and Msm (bf16 [64][LD64], whose
-// strictly-upper 16x16 blocks are zeroed).  Only the lower blocks of Lp are
-// written: every reader masks the rest.  Caller syncs afterwards.
-__device__ __forceinline__ void lm_blocks(const Operands& op, float* Lp, bf16* Msm) {
-  const int warp = threadIdx.x >> 5;
-  const int ntask = Msm ? 20 : 10;
-  if (Msm) {
-    // six strictly-upper blocks: (0,1),(0,2),(0,3),(1,2),(1,3),(2,3)
-    for (int i = threadIdx.x; i < 6 * 256; i += blockDim.x) {
-      int blk = i >> 8, e = i & 255;
-      int I = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-      int J = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-      Msm[(16 * I + (e >> 4)) * LD64 + 16 * J + (e & 15)] = __float2bfloat16(0.f);
-    }
-  }
-  for (int task = warp; task < ntask; task += INTRA_WARPS) {
-    bool isM = task >= 10;
-    int bi = isM ? task - 10 : task;
-    // block list in order (0,0),(1,0),(1,1),(2,0),(2,1),(2,2),(3,0),...
-    int I = bi >= 6 ? 3 : (bi >= 3 ? 2 : (bi >= 1 ? 1 : 0));
-    int J = bi - I * (I + 1) / 2;
-    float acc[2][4];
-    block_product(acc, isM ? op.Qa : op.Ka, op, I, J);
+// One 16x16 block of L' (which == 0, strictly lower on the diagonal, fp32 into
+// Lp) or of M (which == 1, lower-inclusive on the diagonal, bf16 into Msm).
+// Blocks are numbered (0,0),(1,0),(1,1),(2,0),(2,1),(2,2),(3,0),...
+__device__ __forceinline__ void lm_block_task(const Operands& op, int which, int bi, float* Lp, bf16* Msm) {
+  int I = bi >= 6 ? 3 : (bi >= 3 ? 2 : (bi >= 1 ? 1 : 0));
+  int J = bi - I * (I + 1) / 2;
+  float acc[2][4];
+  block_product(acc, which ? op.Qa : op.Ka, op, I, J);
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+  for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int r = acc_row(e), c = acc_col(j, e);
-        int gi = 16 * I + r, gj = 16 * J + c;
-        float x = acc[j][e];
-        if (isM) {
-          if (I == J && c > r) x = 0.f;
-          Msm[gi * LD64 + gj] = __float2bfloat16(x);
-        } else {
-          if (I == J && c >= r) x = 0.f;
-          Lp[gi * LDF64 + gj] = x;
-        }
+    for (int e = 0; e < 4; ++e) {
+      int r = acc_row(e), c = acc_col(j, e);
+      int gi = 16 * I + r, gj = 16 * J + c;
+      float x = acc[j][e];
+      if (which) {
+        if (I == J && c > r) x = 0.f;
+        Msm[gi * LD64 + gj] = __float2bfloat16(x);
+      } else {
+        if (I == J && c >= r) x = 0.f;
+        Lp[gi * LDF64 + gj] = x;
       }
+    }
+}
+
+// Zeroes the six strictly-upper 16x16 blocks of M, using threads [t0, t0+nt).
+__device__ __forceinline__ void zero_m_upper(bf16* Msm, int t0, int nt) {
+  for (int i = threadIdx.x - t0; i < 6 * 256; i += nt) {
+    int blk = i >> 8, e = i & 255;
+    int I = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
+    int J = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
+    Msm[(16 * I + (e >> 4)) * LD64 + 16 * J + (e & 15)] = __float2bfloat16(0.f);
   }
+}
+
+// L' blocks only (10 tasks over the 16 warps).  Only the lower blocks of Lp
+// are written: every reader masks the rest.  Caller syncs afterwards.
+__device__ __forceinline__ void l_blocks(const Operands& op, float* Lp) {
+  const int warp = threadIdx.x >> 5;
+  if (warp < 10) lm_block_task(op, 0, warp, Lp, nullptr);
 }
 
 // A = (I + diag(beta) Lp)^-1 (unit lower triangular, fp32; only the lower
@@ -418,8 +418,9 @@ __device__ __forceinline__ void warp_tf32_16x16(float (&acc)[2][4], const float*
   }
 }
 
-__device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, float* A, float* xtmp) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Diagonal 16x16 blocks of A, threads 0..63 (one column each); no sync.
+__device__ __forceinline__ void tri_inverse_diag(const float* Lp, const float* beta, float* A) {
+  const int tid = threadIdx.x;
   // (strictly-upper blocks of A are never written; readers mask them)
   if (tid < 64) {
     const int blk = tid >> 4, col = tid & 15;
@@ -445,7 +446,13 @@ __device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, 
 #pragma unroll
     for (int r = 0; r < 16; ++r) A[(o + r) * LDF64 + o + col] = x[r];
   }
-  __syncthreads();
+}
+
+// Off-diagonal blocks of A by distance (the diagonal blocks must be complete
+// and visible).  Ends with __syncthreads().
+__device__ __forceinline__ void tri_inverse_offdiag(const float* Lp, const float* beta, float* A, float* xtmp) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  (void)tid;
   float* xs = xtmp + warp * 16 * 17;
   const int g = lane >> 2, t = lane & 3;
   for (int dist = 1; dist <= 3; ++dist) {
@@ -476,6 +483,13 @@ __device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, 
     }
     __syncthreads();
   }
+}
+
+// Whole inverse: diagonal blocks, sync, off-diagonal blocks.
+__device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, float* A, float* xtmp) {
+  tri_inverse_diag(Lp, beta, A);
+  __syncthreads();
+  tri_inverse_offdiag(Lp, beta, A, xtmp);
 }
 
 }  // namespace kda
