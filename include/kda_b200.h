@@ -105,6 +105,16 @@ int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens,
                          int32_t* chunk_seq, int32_t* error_flag, void* stream);
 
 /*
+ * Device-side failure flag of the tensor-core kernels.  Their waits on
+ * asynchronous MMA completion are bounded; a wait that runs out makes the
+ * kernel record a nonzero code here and return early (its outputs are then
+ * invalid) instead of hanging the GPU.  Synchronises with the device; reset = 1
+ * clears the flag.  Returns the flag, or minus an error code.  The reference
+ * has no counterpart (its kernels run in Triton without such waits).
+ */
+int kda_b200_device_error(int reset);
+
+/*
  * Per-kernel device timing, for benchmarks and profiling summaries.  While
  * enabled, every kernel launch of kda_b200_fwd / kda_b200_bwd is bracketed by
  * two cudaEventRecord calls on its stream.  kda_b200_timing_read synchronises

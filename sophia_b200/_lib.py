@@ -29,6 +29,7 @@ SIGNATURES = {
     "kda_b200_bwd": ([c_void_p] * 12 + [c_int] * 5 + [c_float, c_float]
                      + [c_void_p, c_size_t] + [c_void_p] * 13 + [c_void_p, c_size_t, c_void_p], c_int),
     "kda_b200_chunk_table": ([c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p], c_int),
+    "kda_b200_device_error": ([c_int], c_int),
     "kda_b200_timing_enable": ([c_int], c_int),
     "kda_b200_timing_reset": ([], c_int),
     "kda_b200_timing_read": ([c_int, c_void_p, c_void_p, c_void_p], c_int),
@@ -87,3 +88,8 @@ def timing_read() -> dict[str, tuple[int, float]]:
     if rc <= 0:
         raise KdaError(load().kda_b200_last_error().decode())
     return {names[i].decode(): (launches[i], ms[i]) for i in range(rc)}
+
+
+def device_error(reset: bool = True) -> int:
+    """Nonzero when a tensor-core kernel hit a bounded-wait timeout (synchronises)."""
+    return int(load().kda_b200_device_error(int(reset)))

@@ -8,6 +8,7 @@
 
 #include "../../include/kda_b200.h"
 #include "kda_bwd_intra.cuh"
+#include "kda_fwd_state_tc.cuh"
 #include "kda_post.cuh"
 
 using namespace kda;
@@ -326,10 +327,10 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   sp.hs = sv.hs;
   sp.E = sv.E;
   sp.ht = ht;
-  if ((rc = set_smem(kda_fwd_state_kernel, StateSmem::END, "fwd state"))) return rc;
+  if ((rc = set_smem(kda_fwd_state_tc_kernel, StateTcSmem::END, "fwd state"))) return rc;
   {
     TimedLaunch tl(K_FWD_STATE, st);
-    kda_fwd_state_kernel<<<dim3(N, H), 256, StateSmem::END, st>>>(sp);
+    kda_fwd_state_tc_kernel<<<dim3(N, H), 256, StateTcSmem::END, st>>>(sp);
   }
   return launch_check("fwd state");
 }
@@ -446,6 +447,17 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
     kda_reduce_kernel<<<dim3(2 * H + (pr.conv ? 12 * H : 0)), 256, 0, st>>>(rp);
   }
   return launch_check("reduce");
+}
+
+int kda_b200_device_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kda_device_error, sizeof(int)) != cudaSuccess)
+    return -fail(KDA_ERR_CUDA, "reading the device error flag failed");
+  if (reset) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_kda_device_error, &z, sizeof(int));
+  }
+  return v;
 }
 
 int kda_b200_timing_enable(int on) {

@@ -38,13 +38,23 @@ from oracle_runner import run_oracle  # noqa: E402
 
 def main() -> None:
     import fla
-    out = {"fla_version": getattr(fla, "__version__", "unknown"), "cases": {}}
+    import numpy as np
+    import torch
+    from cases import CASES
+    out = {"fla_version": getattr(fla, "__version__", "unknown"), "cases": {}, "golden": {}}
     for name, case in ALL_CASES.items():
         inp = round_inputs_bf16(make_case_inputs(case))
         ref = run_oracle(case, inputs=inp)
         rep = compare(run_fla(case, inputs=inp), ref)
         out["cases"][name] = {k: {"viol": v[0], "rel": v[1]} for k, v in rep.items()}
         print(name, flush=True)
+    # against the reference's own float32 outputs on the unrounded inputs
+    for name, case in CASES.items():
+        gold = np.load(HERE / f"{name}.npz")
+        ref = {k: torch.from_numpy(gold[k]) for k in gold.files if k != "input_sums"}
+        rep = compare(run_fla(case), ref)
+        out["golden"][name] = {k: {"viol": v[0], "rel": v[1]} for k, v in rep.items()}
+        print("golden", name, flush=True)
     with open(HERE / "fla_accuracy.json", "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
 

@@ -51,6 +51,8 @@ def run_cuda(case: Case, inputs: dict | None = None, grads: bool = True) -> dict
             g = t[k].grad
             res["d_" + k] = (torch.zeros_like(t[k]) if g is None else g).detach().float().cpu()
     torch.cuda.synchronize()
+    from sophia_b200 import _lib
+    assert _lib.device_error(reset=True) == 0, "a tensor-core kernel timed out"
     return res
 
 

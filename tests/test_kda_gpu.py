@@ -25,12 +25,12 @@ pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 
-def _fla_baseline(name):
+def _fla_baseline(name, section="cases"):
     path = os.path.join(GOLDEN, "fla_accuracy.json")
     if not os.path.exists(path):
         return None
     with open(path) as f:
-        return json.load(f)["cases"].get(name)
+        return json.load(f).get(section, {}).get(name)
 
 
 def _check(case, inp=None):
@@ -56,7 +56,7 @@ def test_cuda_matches_reference_golden(name):
     got = run_cuda(CASES[name])
     ref = {k: torch.from_numpy(gold[k]) for k in gold.files if k != "input_sums"}
     rep = compare(got, ref)
-    bad = failures(rep, ref, _fla_baseline(name))
+    bad = failures(rep, ref, _fla_baseline(name, "golden"))
     assert not bad, "\n".join(f"{k}: viol={v[0]:.3f} rel={v[1]:.2e}" for k, v in sorted(rep.items()))
 
 
