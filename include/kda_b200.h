@@ -128,6 +128,33 @@ int kda_b200_timing_enable(int on);
 int kda_b200_timing_reset(void);
 int kda_b200_timing_read(int max_kernels, const char** names, int* launches, float* total_ms);
 
+/*
+ * Forward (inference) that allocates nothing -- no counterpart in the
+ * reference.  For callers that cannot allocate device memory themselves: a
+ * host binding (cgo, JNI, a C serving loop) that has no device allocator of
+ * its own, or a process that reserves all device memory up front and forbids
+ * later allocations.  Same arguments and results as kda_b200_fwd with
+ * saved = NULL, minus the workspace: the scratch is a static device array of
+ * KDA_NOALLOC_SCRATCH_BYTES (64 MiB) that every GPU loading this library holds
+ * until the process exits.
+ *   - A call whose kda_b200_fwd_workspace_bytes(B*T, H, N, packed, 0) exceeds
+ *     that size returns KDA_ERR_INVALID (no kernel runs).
+ *   - The first call on a device does a one-time set-up: it resolves the
+ *     array's device address on the current device (cudaGetSymbolAddress);
+ *     later calls reuse it.  Make that first call before any stream capture
+ *     begins.
+ *   - All calls share the one array and it keeps the last call's contents;
+ *     nothing in it has to start at zero (every call writes what it reads).
+ *     Calls that overlap on the GPU (other streams, other host threads) race on
+ *     it: serialise them.
+ *   - No cudaMalloc, cudaFree or allocating library routine is called.
+ */
+#define KDA_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+int kda_b200_fwd_noalloc(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                         const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                         const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H,
+                         int D, int N, float scale, float lower_bound, void* o, float* ht, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

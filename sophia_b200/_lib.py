@@ -30,6 +30,8 @@ SIGNATURES = {
                      + [c_void_p, c_size_t] + [c_void_p] * 13 + [c_void_p, c_size_t, c_void_p], c_int),
     "kda_b200_chunk_table": ([c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p], c_int),
     "kda_b200_device_error": ([c_int], c_int),
+    "kda_b200_fwd_noalloc": ([c_void_p] * 12 + [c_int] * 5 + [c_float, c_float] + [c_void_p, c_void_p, c_void_p],
+                             c_int),
     "kda_b200_timing_enable": ([c_int], c_int),
     "kda_b200_timing_reset": ([], c_int),
     "kda_b200_timing_read": ([c_int, c_void_p, c_void_p, c_void_p], c_int),
