@@ -26,7 +26,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -55,14 +54,26 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
     "bwd_post": 0,
 }
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per token-head of
+# each kernel from one ncu capture of `python bench.py --batch 2 --steps 1
+# --warmup 3 --profile` (B=2: the per-launch traffic scales with the token-heads
+# processed); summary in profiles/kda_kernels_dram_b2.md.
+NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
+    "fwd_intra": 1826.0, "fwd_state": 1824.5, "bwd_state": 2803.2, "bwd_intra": 2997.7, "bwd_post": 2141.1,
+}
+
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["cfg1", "cfg3"], default="cfg1")
+    ap.add_argument("--profile", action="store_true",
+                    help="run the warm-up and K layer steps only, print nothing (command for ncu captures)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences per rank (default 8 for cfg1); smaller for ncu captures")
     return ap.parse_args()
 
 
@@ -77,59 +88,72 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region."""
+    """SM clock and clock-event reasons sampled every 10 ms through NVML in a
+    background thread; only samples taken inside the timed window (host time
+    from the opening synchronize to the closing one) are kept."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, device: torch.device):
+        self.samples: list[tuple[float, float, int]] = []
+        self.window = (0.0, 0.0)
+        self.error = None
+        self.stop_evt = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(device).uuid)
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report it instead of clocks
+            self.nvml, self.error = None, f"nvml unavailable: {e}"
+
+    def _poll(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_evt.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                self.samples.append((time.perf_counter(), float(mhz), int(get_reasons(self.handle))))
+            except Exception as e:
+                self.error = str(e)
+                return
+            time.sleep(0.01)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
-        except Exception:
-            self.proc = None
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def mark(self, t0: float, t1: float):
+        self.window = (t0, t1)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error], "samples": 0}
+        self.stop_evt.set()
         self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
-        load = [x for x in sm if x > 0.5 * max(sm)] or sm
-        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        t0, t1 = self.window
+        inside = [(m, r) for t, m, r in self.samples if t0 <= t <= t1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [self.error or "no samples"],
+                    "samples": 0}
+        reasons = set()
+        for name, const in self.REASONS:
+            bit = getattr(self.nvml, const, 0)
+            if any(r & bit for _, r in inside):
+                reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(inside)}
 
 
 def make_inputs(B, device, seed):
@@ -150,7 +174,7 @@ def bench_ours(a, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    B = 8 if a.workload == "cfg1" else 320 // world
+    B = a.batch or (8 if a.workload == "cfg1" else 320 // world)
     x, w = make_inputs(B, device, 42 + rank)
     acts = {k: x[k].clone().requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
     params = {k: v.clone().requires_grad_(True) for k, v in w.items()}
@@ -169,10 +193,11 @@ def bench_ours(a, rank, world, local_rank):
             dist.all_reduce(bucket)
         return bucket
 
-    def timed(fn, steps):
+    def timed(fn, steps, sampler=None):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        h0 = time.perf_counter()
         st = torch.cuda.current_stream()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
@@ -180,6 +205,8 @@ def bench_ours(a, rank, world, local_rank):
             fn()
         e1.record(st)
         torch.cuda.synchronize()
+        if sampler is not None:
+            sampler.mark(h0, time.perf_counter())
         if world > 1:
             dist.barrier()
         ms = e0.elapsed_time(e1)
@@ -191,9 +218,12 @@ def bench_ours(a, rank, world, local_rank):
 
     for _ in range(a.warmup):
         step()
-    sampler = ClockSampler(local_rank)
+    if a.profile:
+        timed(step, a.steps)
+        return None
+    sampler = ClockSampler(device)
     sampler.start()
-    ms = timed(step, a.steps)
+    ms = timed(step, a.steps, sampler)
     clocks = sampler.stop()
     tokens = world * B * T * a.steps
     value = tokens / (ms / 1e3)
@@ -239,15 +269,8 @@ def bench_ours(a, rank, world, local_rank):
     alg_bytes = KERNEL_BYTES_PER_TOKEN_HEAD[dom] * th
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
-        try:
-            with open(tpath) as f:
-                tr = json.load(f)
-            if dom in tr:
-                traffic = tr[dom]["bytes_per_token_head"] * th
-        except Exception:
-            traffic = None
+    if dom in NCU_DRAM_BYTES_PER_TOKEN_HEAD:
+        traffic = round(NCU_DRAM_BYTES_PER_TOKEN_HEAD[dom] * th)
     # per-kernel roofline of the whole step: sum_k max(F_k/P, B_k/BW)
     roof_ms = 0.0
     for k, bpt in KERNEL_BYTES_PER_TOKEN_HEAD.items():
@@ -294,7 +317,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    config = {"workload": a.workload, "global_batch": (8 * world if a.workload == "cfg1" else 320),
+    per_rank = a.batch or (8 if a.workload == "cfg1" else 320 // world)
+    config = {"workload": a.workload, "global_batch": per_rank * world,
               "seq_len": T, "heads": H, "head_dim": D, "chunk": 64,
               "parallelism": f"dp{world}", "l2": "inputs larger than L2 (128 MiB per tensor), no flush"}
     if a.impl == "reference":
@@ -329,6 +353,12 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     res = bench_ours(a, rank, world, local_rank)
+    if res is None:  # --profile
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     cpu = None
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
