@@ -428,10 +428,12 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   pp.dk = static_cast<bf16*>(dk);
   pp.dv = static_cast<bf16*>(dv);
   pp.partW = bv.partW;
-  if ((rc = set_smem(kda_bwd_post_kernel, PostSmem::END, "bwd post"))) return rc;
   {
     TimedLaunch tl(K_BWD_POST, st);
-    kda_bwd_post_kernel<<<dim3(pr.grid_chunks, H), 256, PostSmem::END, st>>>(pp);
+    if (pr.conv)
+      kda_bwd_post_kernel<true><<<dim3(pr.grid_chunks, H, 3), POST_THREADS, POST_DC_BYTES, st>>>(pp);
+    else
+      kda_bwd_post_kernel<false><<<dim3(pr.grid_chunks, H, 2), POST_THREADS, 0, st>>>(pp);
   }
   if ((rc = launch_check("bwd post"))) return rc;
 

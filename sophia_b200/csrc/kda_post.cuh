@@ -1,7 +1,7 @@
 // Backward epilogue: L2-norm and ShortConv(+SiLU) backward, and the final
 // deterministic reductions of the per-chunk partial sums.
 //
-//   kda_bwd_post_kernel  (one CTA per (chunk, head))
+//   kda_bwd_post_kernel  (one CTA per (chunk, head, tensor))
 //     given dq_hat / dk_hat (gradients of the normalised inputs) and dv from
 //     the chunk kernel, recomputes the conv output c = conv(x), y = silu(c)
 //     and the norms, then
@@ -29,180 +29,215 @@ struct PostParams {
   float* partW;                                 // [chunks][3][H][128][4]
 };
 
-struct PostSmem {
-  static constexpr int XS = 0;                      // 70 x 128 bf16
-  static constexpr int DS = XS + 70 * D * 2;        // 67 x 128 bf16
-  static constexpr int DC = DS + 67 * D * 2;        // 67 x 128 fp32
-  static constexpr int PW = DC + 67 * D * 4;        // 16 x 4 x 128 fp32 (row group, tap, channel)
-  static constexpr int TAPS = PW + 16 * 4 * D * 4;  // 4 x 128 fp32, tap-major
-  static constexpr int END = TAPS + 4 * D * 4;
-};
+// One CTA per (chunk, head, tensor), 256 threads: warp w owns dc rows
+// 8w .. 8w+7 and lane l channels 4l .. 4l+3, so a warp covers whole rows (the
+// L2 norm of a row is a warp shuffle reduction) and each 8-byte load of a row
+// is part of one 256-byte coalesced access.  A thread's conv input rows (x rows
+// 8w-3 .. 8w+7) and gradient rows are loaded straight from global memory into
+// registers, all in flight together.  The fp32 dc tile goes through shared
+// memory because the conv backward of row t needs dc rows t .. t+3; rows
+// 64 .. 66 are the next chunk's first rows and are computed by warp 7.
+constexpr int POST_THREADS = 256;
+constexpr int POST_DC_BYTES = 67 * D * 4;
 
-__global__ void __launch_bounds__(256) kda_bwd_post_kernel(PostParams P) {
+struct alignas(8) bf16x4 { uint32_t u[2]; };
+
+__device__ __forceinline__ void unpack4(const bf16x4& v, float (&f)[4]) {
+  const float2 a = unpack_bf16(v.u[0]), b = unpack_bf16(v.u[1]);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+}
+__device__ __forceinline__ bf16x4 pack4(const float (&f)[4]) {
+  bf16x4 v;
+  v.u[0] = pack_bf16(f[0], f[1]);
+  v.u[1] = pack_bf16(f[2], f[3]);
+  return v;
+}
+
+__device__ __forceinline__ bf16x4 post_ld(const bf16* base, int t, bool ok, size_t rowH, int h, int lane) {
+  uint2 u = make_uint2(0u, 0u);
+  if (ok) u = __ldg(reinterpret_cast<const uint2*>(base + (size_t)t * rowH + (size_t)h * D + 4 * lane));
+  bf16x4 v;
+  v.u[0] = u.x; v.u[1] = u.y;
+  return v;
+}
+
+// L2-norm backward of one row (full-warp shuffles): dn = dscale g,
+// n = y / |y|, result (dn - n (n . dn)) / |y|.
+__device__ __forceinline__ void post_norm_bwd(const float (&y)[4], const float (&g)[4], float dscale,
+                                              float (&dyv)[4]) {
+  float ss = 0.f, dot = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) { ss += y[ch] * y[ch]; dot += y[ch] * g[ch]; }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    dot += __shfl_xor_sync(0xffffffffu, dot, m);
+  }
+  const float nrm = sqrtf(ss);
+  if (nrm > 1e-12f) {
+    const float inv = 1.f / nrm, nd = dot * inv * dscale;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) dyv[ch] = (dscale * g[ch] - y[ch] * inv * nd) * inv;
+  } else {
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) dyv[ch] = dscale * g[ch] * 1e12f;
+  }
+}
+
+// dc of one row: conv c from x rows row-3 .. row, SiLU y = c sigmoid(c) and
+// sigmoid(c) from one tanh.approx (the forward prologue's silu_fast on the
+// same c), the L2-norm backward (q, k), dc = dy sigmoid(c) (1 + c (1 - sigmoid(c)));
+// zero for rows past the sequence end.
+__device__ __forceinline__ float4 post_dc_row(const bf16x4& x0, const bf16x4& x1, const bf16x4& x2,
+                                              const bf16x4& x3, const float (&wt)[4][4], const bf16x4& gr,
+                                              bool rowok, bool norm, float dscale) {
+  float xa[4][4];
+  unpack4(x0, xa[0]); unpack4(x1, xa[1]); unpack4(x2, xa[2]); unpack4(x3, xa[3]);
+  float cv[4], y[4], sg[4], g[4], dyv[4];
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    const float a = wt[ch][0] * xa[0][ch] + wt[ch][1] * xa[1][ch] + wt[ch][2] * xa[2][ch] + wt[ch][3] * xa[3][ch];
+    const float hh = 0.5f * a, t = tanh_fast(hh);
+    cv[ch] = a;
+    y[ch] = fmaf(hh, t, hh);
+    sg[ch] = fmaf(0.5f, t, 0.5f);
+  }
+  unpack4(gr, g);
+  if (norm) {
+    post_norm_bwd(y, g, dscale, dyv);
+  } else {
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) dyv[ch] = g[ch];
+  }
+  float dc[4];
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) dc[ch] = rowok ? dyv[ch] * sg[ch] * (1.f + cv[ch] * (1.f - sg[ch])) : 0.f;
+  return make_float4(dc[0], dc[1], dc[2], dc[3]);
+}
+
+template <bool CONV>
+__global__ void __launch_bounds__(POST_THREADS, 2) kda_bwd_post_kernel(PostParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int c = blockIdx.x, h = blockIdx.y, H = P.H;
-  ChunkPos pos = chunk_pos(P.seq, c);
+  const int c = blockIdx.x, h = blockIdx.y, X = blockIdx.z, H = P.H;
+  const ChunkPos pos = chunk_pos(P.seq, c);
   if (!pos.valid) return;
   const int eos = seq_eos(P.seq, pos.seq);
-  const int nv = pos.t1 - pos.t0;
-  const int tid = threadIdx.x, tg = tid >> 4, cg = tid & 15;
-  bf16* xs = reinterpret_cast<bf16*>(smem + PostSmem::XS);
-  bf16* ds = reinterpret_cast<bf16*>(smem + PostSmem::DS);
-  float* dcs = reinterpret_cast<float*>(smem + PostSmem::DC);
-  float* pw = reinterpret_cast<float*>(smem + PostSmem::PW);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t rowH = (size_t)H * D;
+  const bf16* x = X == 0 ? P.q : (X == 1 ? P.k : P.v);
+  const bf16* gy = X == 0 ? P.dq_hat : (X == 1 ? P.dk_hat : P.dv_hat);
+  bf16* dx = X == 0 ? P.dq : (X == 1 ? P.dk : P.dv);
+  const float dscale = X == 0 ? P.scale : 1.f;
+  const int r0 = 8 * warp;  // first row of this warp
 
-  for (int X = 0; X < 3; ++X) {
-    if (!P.conv && X == 2) break;  // dv passes through unchanged
-    const bf16* x = X == 0 ? P.q : (X == 1 ? P.k : P.v);
-    const bf16* dy = X == 0 ? P.dq_hat : (X == 1 ? P.dk_hat : P.dv_hat);
-    bf16* dx = X == 0 ? P.dq : (X == 1 ? P.dk : P.dv);
-    const float* w = P.conv ? (X == 0 ? P.conv_q : (X == 1 ? P.conv_k : P.conv_v)) + (size_t)h * D * 4 : nullptr;
-    const float dscale = X == 0 ? P.scale : 1.f;
-    const int nrow = P.conv ? 67 : nv;  // rows of dc needed
-    // loads: x rows t0-3 .. t0+66 (conv) or t0 .. t1-1, gradient rows t0 .. t0+nrow-1
-    for (int i = tid; i < 70 * 16; i += blockDim.x) {
-      int r = i >> 4, cc = i & 15;
-      int t = P.conv ? pos.t0 - 3 + r : pos.t0 + r;
-      bool ok = (t >= pos.bos) && (t < eos) && (P.conv ? r < 70 : r < nv);
-      cp_async16(xs + r * D + cc * 8, x + (ok ? (size_t)t * rowH + (size_t)h * D + cc * 8 : 0), ok);
+  if (!CONV) {  // L2-norm backward only (q and k)
+    bf16x4 xr[8], gr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = pos.t0 + r0 + j;
+      xr[j] = post_ld(x, t, t < pos.t1, rowH, h, lane);
+      gr[j] = post_ld(gy, t, t < pos.t1, rowH, h, lane);
     }
-    for (int i = tid; i < 67 * 16; i += blockDim.x) {
-      int r = i >> 4, cc = i & 15;
-      int t = pos.t0 + r;
-      bool ok = (t < eos) && (r < nrow);
-      cp_async16(ds + r * D + cc * 8, dy + (ok ? (size_t)t * rowH + (size_t)h * D + cc * 8 : 0), ok);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float y[4], g[4], dyv[4];
+      unpack4(xr[j], y);
+      unpack4(gr[j], g);
+      post_norm_bwd(y, g, dscale, dyv);
+      const int t = pos.t0 + r0 + j;
+      if (t < pos.t1) *reinterpret_cast<bf16x4*>(dx + (size_t)t * rowH + (size_t)h * D + 4 * lane) = pack4(dyv);
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncthreads();
-    float wt[8][4];
-    if (P.conv) {
-      float* taps = reinterpret_cast<float*>(smem + PostSmem::TAPS);
-      for (int i = tid; i < D; i += blockDim.x) {
-        float4 t4 = __ldg(reinterpret_cast<const float4*>(w) + i);
-        taps[i] = t4.x; taps[D + i] = t4.y; taps[2 * D + i] = t4.z; taps[3 * D + i] = t4.w;
-      }
-      __syncthreads();
+    return;
+  }
+
+  float wt[4][4];
+  {
+    const float4* w = reinterpret_cast<const float4*>((X == 0 ? P.conv_q : (X == 1 ? P.conv_k : P.conv_v)) +
+                                                      ((size_t)h * D + 4 * lane) * 4);
 #pragma unroll
-      for (int tap = 0; tap < 4; ++tap) {
-        float4 a = *reinterpret_cast<const float4*>(taps + tap * D + 8 * cg);
-        float4 b = *reinterpret_cast<const float4*>(taps + tap * D + 8 * cg + 4);
-        wt[0][tap] = a.x; wt[1][tap] = a.y; wt[2][tap] = a.z; wt[3][tap] = a.w;
-        wt[4][tap] = b.x; wt[5][tap] = b.y; wt[6][tap] = b.z; wt[7][tap] = b.w;
-      }
+    for (int ch = 0; ch < 4; ++ch) {
+      const float4 t4 = __ldg(w + ch);
+      wt[ch][0] = t4.x; wt[ch][1] = t4.y; wt[ch][2] = t4.z; wt[ch][3] = t4.w;
     }
-    // dc (or the norm backward alone) for rows tg, tg+16, ...; every lane runs
-    // all five iterations so the full-warp shuffles stay uniform
-    for (int it = 0; it < 5; ++it) {
-      const int r = tg + 16 * it;
-      const bool live = r < 67;
-      const int rr = live ? r : 66;
-      float cv[8], y[8], g[8];
-      unpack8(*reinterpret_cast<const bf16x8*>(ds + rr * D + 8 * cg), g);
-      if (P.conv) {
-        float xr[4][8];
+  }
+  const bool norm = X < 2;
+  float4* dcs = reinterpret_cast<float4*>(smem);  // [67 rows][32 lanes]
+  // x rows r0-3 .. r0+7 (zero before the sequence start and past its end)
+  bf16x4 xr[11], gr[8];
 #pragma unroll
-        for (int sidx = 0; sidx < 4; ++sidx) unpack8(*reinterpret_cast<const bf16x8*>(xs + (rr + sidx) * D + 8 * cg), xr[sidx]);
+  for (int j = 0; j < 11; ++j) {
+    const int t = pos.t0 + r0 - 3 + j;
+    xr[j] = post_ld(x, t, t >= pos.bos && t < eos, rowH, h, lane);
+  }
 #pragma unroll
-        for (int cch = 0; cch < 8; ++cch) {
-          float a = wt[cch][0] * xr[0][cch] + wt[cch][1] * xr[1][cch] + wt[cch][2] * xr[2][cch] + wt[cch][3] * xr[3][cch];
-          cv[cch] = a;
-          y[cch] = silu_fast(a);
-        }
-      } else {
-        unpack8(*reinterpret_cast<const bf16x8*>(xs + rr * D + 8 * cg), y);
+  for (int j = 0; j < 8; ++j) {
+    const int t = pos.t0 + r0 + j;
+    gr[j] = post_ld(gy, t, t < eos, rowH, h, lane);
+  }
 #pragma unroll
-        for (int cch = 0; cch < 8; ++cch) cv[cch] = 0.f;
-      }
-      float dyv[8];
-      if (X < 2) {
-        float ss = 0.f, dot = 0.f;
+  for (int j = 0; j < 8; ++j)
+    dcs[(r0 + j) * 32 + lane] =
+        post_dc_row(xr[j], xr[j + 1], xr[j + 2], xr[j + 3], wt, gr[j], pos.t0 + r0 + j < eos, norm, dscale);
+  if (warp == 7) {  // dc rows 64 .. 66: the next chunk's first rows (x rows 61 .. 66)
+    bf16x4 xe[6], ge[3];
 #pragma unroll
-        for (int cch = 0; cch < 8; ++cch) { ss += y[cch] * y[cch]; dot += y[cch] * g[cch]; }
-#pragma unroll
-        for (int m = 8; m >= 1; m >>= 1) {
-          ss += __shfl_xor_sync(0xffffffffu, ss, m);
-          dot += __shfl_xor_sync(0xffffffffu, dot, m);
-        }
-        float nrm = sqrtf(ss);
-        if (nrm > 1e-12f) {
-          float inv = 1.f / nrm;
-          // n = y/nrm, dn = dscale*g: dy = (dn - n (n.dn)) / nrm
-          float nd = dot * inv * dscale;
-#pragma unroll
-          for (int cch = 0; cch < 8; ++cch) dyv[cch] = (dscale * g[cch] - y[cch] * inv * nd) * inv;
-        } else {
-#pragma unroll
-          for (int cch = 0; cch < 8; ++cch) dyv[cch] = dscale * g[cch] * 1e12f;
-        }
-      } else {
-#pragma unroll
-        for (int cch = 0; cch < 8; ++cch) dyv[cch] = g[cch];
-      }
-      bool rowok = live && pos.t0 + r < eos;
-      if (!live) continue;
-      if (P.conv) {
-        float dcv[8];
-#pragma unroll
-        for (int cch = 0; cch < 8; ++cch) {
-          float sg = sigmoid_fast(cv[cch]);
-          dcv[cch] = rowok ? dyv[cch] * sg * (1.f + cv[cch] * (1.f - sg)) : 0.f;
-        }
-        float* dp = dcs + r * D + 8 * cg;
-        *reinterpret_cast<float4*>(dp) = make_float4(dcv[0], dcv[1], dcv[2], dcv[3]);
-        *reinterpret_cast<float4*>(dp + 4) = make_float4(dcv[4], dcv[5], dcv[6], dcv[7]);
-      } else if (r < nv) {
-        *reinterpret_cast<bf16x8*>(dx + (size_t)(pos.t0 + r) * rowH + (size_t)h * D + 8 * cg) = pack8(dyv);
-      }
+    for (int j = 0; j < 6; ++j) {
+      const int t = pos.t0 + 61 + j;
+      xe[j] = post_ld(x, t, t < eos, rowH, h, lane);
     }
-    if (P.conv) {
-      __syncthreads();
-      float acc[8][4];
 #pragma unroll
-      for (int cch = 0; cch < 8; ++cch) acc[cch][0] = acc[cch][1] = acc[cch][2] = acc[cch][3] = 0.f;
-      for (int r = tg; r < nv; r += 16) {
-        float dcr[4][8];
-#pragma unroll
-        for (int sidx = 0; sidx < 4; ++sidx) {
-          const float* dp = dcs + (r + sidx) * D + 8 * cg;
-          float4 a = *reinterpret_cast<const float4*>(dp);
-          float4 b = *reinterpret_cast<const float4*>(dp + 4);
-          dcr[sidx][0] = a.x; dcr[sidx][1] = a.y; dcr[sidx][2] = a.z; dcr[sidx][3] = a.w;
-          dcr[sidx][4] = b.x; dcr[sidx][5] = b.y; dcr[sidx][6] = b.z; dcr[sidx][7] = b.w;
-        }
-        float xr[4][8];
-#pragma unroll
-        for (int sidx = 0; sidx < 4; ++sidx) unpack8(*reinterpret_cast<const bf16x8*>(xs + (r + sidx) * D + 8 * cg), xr[sidx]);
-        float dxv[8];
-#pragma unroll
-        for (int cch = 0; cch < 8; ++cch) {
-          // dx_t = sum_s w_s dc_(t+3-s): dc row r+3-s
-          dxv[cch] = wt[cch][0] * dcr[3][cch] + wt[cch][1] * dcr[2][cch] + wt[cch][2] * dcr[1][cch] +
-                     wt[cch][3] * dcr[0][cch];
-          // dw_s += dc_t x_(t-3+s): x row r+s
-#pragma unroll
-          for (int sidx = 0; sidx < 4; ++sidx) acc[cch][sidx] += dcr[0][cch] * xr[sidx][cch];
-        }
-        *reinterpret_cast<bf16x8*>(dx + (size_t)(pos.t0 + r) * rowH + (size_t)h * D + 8 * cg) = pack8(dxv);
-      }
-#pragma unroll
-      for (int tap = 0; tap < 4; ++tap) {
-        float* dst = pw + (tg * 4 + tap) * D + 8 * cg;
-        *reinterpret_cast<float4*>(dst) = make_float4(acc[0][tap], acc[1][tap], acc[2][tap], acc[3][tap]);
-        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4][tap], acc[5][tap], acc[6][tap], acc[7][tap]);
-      }
-      __syncthreads();
-      for (int i = tid; i < D * 4; i += blockDim.x) {
-        // output layout [channel][tap]: i = channel * 4 + tap
-        const int ch = i >> 2, tap = i & 3;
-        float sum = 0.f;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) sum += pw[(u * 4 + tap) * D + ch];
-        P.partW[(((size_t)c * 3 + X) * H + h) * D * 4 + i] = sum;
-      }
+    for (int j = 0; j < 3; ++j) {
+      const int t = pos.t0 + 64 + j;
+      ge[j] = post_ld(gy, t, t < eos, rowH, h, lane);
     }
-    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      dcs[(64 + j) * 32 + lane] =
+          post_dc_row(xe[j], xe[j + 1], xe[j + 2], xe[j + 3], wt, ge[j], pos.t0 + 64 + j < eos, norm, dscale);
+  }
+  __syncthreads();
+
+  // conv backward: dx_t = sum_s w_s dc_(t+3-s), dw_s += dc_t x_(t-3+s)
+  float acc[4][4];
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) acc[ch][0] = acc[ch][1] = acc[ch][2] = acc[ch][3] = 0.f;
+  float4 win[4];  // dc rows t .. t+3 (ring)
+#pragma unroll
+  for (int i = 0; i < 3; ++i) win[i] = dcs[(r0 + i) * 32 + lane];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    win[(j + 3) & 3] = dcs[(r0 + j + 3) * 32 + lane];
+    const float4 d0 = win[j & 3], d1 = win[(j + 1) & 3], d2 = win[(j + 2) & 3], d3 = win[(j + 3) & 3];
+    const float e0[4] = {d0.x, d0.y, d0.z, d0.w}, e1[4] = {d1.x, d1.y, d1.z, d1.w};
+    const float e2[4] = {d2.x, d2.y, d2.z, d2.w}, e3[4] = {d3.x, d3.y, d3.z, d3.w};
+    float xs[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) unpack4(xr[j + i], xs[i]);
+    float dxv[4];
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      dxv[ch] = wt[ch][0] * e3[ch] + wt[ch][1] * e2[ch] + wt[ch][2] * e1[ch] + wt[ch][3] * e0[ch];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[ch][i] += e0[ch] * xs[i][ch];
+    }
+    const int t = pos.t0 + r0 + j;
+    if (t < pos.t1) *reinterpret_cast<bf16x4*>(dx + (size_t)t * rowH + (size_t)h * D + 4 * lane) = pack4(dxv);
+  }
+  // tap-gradient partial of this chunk: the eight warps through shared memory
+  // (reusing the dc tile), added in a fixed order
+  __syncthreads();
+  float4* red = dcs;  // [8 warps][128 channels] of 4 taps
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) red[warp * D + 4 * lane + ch] = make_float4(acc[ch][0], acc[ch][1], acc[ch][2], acc[ch][3]);
+  __syncthreads();
+  if (tid < D) {
+    float4 s4 = red[tid];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      const float4 a = red[w * D + tid];
+      s4.x += a.x; s4.y += a.y; s4.z += a.z; s4.w += a.w;
+    }
+    reinterpret_cast<float4*>(P.partW + (((size_t)c * 3 + X) * H + h) * D * 4)[tid] = s4;
   }
 }
 
