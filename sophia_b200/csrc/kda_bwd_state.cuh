@@ -45,16 +45,21 @@ struct BwdStateParams {
   float* dh0;        // [N][H][128][128] or null
 };
 
+// Loads come in two cp.async groups per chunk:
+//   A = M, Kbar, dO, 2^Gam_C  -- everything dE needs; double-buffered and
+//       prefetched one chunk ahead, so dE starts as soon as a chunk begins;
+//   B = W, Qt, E, S0          -- issued at the chunk start, first used after dE.
 struct BwdStateSmem {
   static constexpr int TILE = 64 * LD128 * 2;
-  static constexpr int W = 0, QT = TILE, KB = 2 * TILE, DO = 3 * TILE, E = 4 * TILE;
-  static constexpr int M = 5 * TILE;                       // 64 x LD64
-  static constexpr int S0 = M + 64 * LD64 * 2;              // 128 x LD128
-  static constexpr int DC = S0 + 128 * LD128 * 2;           // 128 fp32
-  static constexpr int DS = DC + D * 4;                     // 128 x LD128
+  static constexpr int A_M = 0, A_KB = 64 * LD64 * 2, A_DO = A_KB + TILE, A_DC = A_DO + TILE;
+  static constexpr int A_STAGE = A_DC + D * 4;              // 44544
+  static constexpr int W = 2 * A_STAGE, QT = W + TILE, E = QT + TILE;
+  static constexpr int S0 = E + TILE;                       // 128 x LD128
+  static constexpr int DS = S0 + 128 * LD128 * 2;           // 128 x LD128
   static constexpr int DE = DS + 128 * LD128 * 2;           // 64 x LD128
   static constexpr int END = DE + 64 * LD128 * 2;
 };
+static_assert(BwdStateSmem::END <= 232448, "bwd state shared memory");
 
 __device__ __forceinline__ void store_frag_rows(bf16* g, const float (&acc)[8][4], int m0, int n0, int nv, int t0,
                                                 int H, int h, bool neg) {
@@ -80,14 +85,22 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_kernel(BwdStateParams P)
   const int cbase = seq_chunk_base(P.seq, n);
   bf16* Wt = reinterpret_cast<bf16*>(smem + BwdStateSmem::W);
   bf16* Qt = reinterpret_cast<bf16*>(smem + BwdStateSmem::QT);
-  bf16* Kb = reinterpret_cast<bf16*>(smem + BwdStateSmem::KB);
-  bf16* dO = reinterpret_cast<bf16*>(smem + BwdStateSmem::DO);
   bf16* Et = reinterpret_cast<bf16*>(smem + BwdStateSmem::E);
-  bf16* Mt = reinterpret_cast<bf16*>(smem + BwdStateSmem::M);
   bf16* S0 = reinterpret_cast<bf16*>(smem + BwdStateSmem::S0);
-  float* dC = reinterpret_cast<float*>(smem + BwdStateSmem::DC);
   bf16* dSs = reinterpret_cast<bf16*>(smem + BwdStateSmem::DS);
   bf16* dEs = reinterpret_cast<bf16*>(smem + BwdStateSmem::DE);
+  auto stage = [&](int b) { return smem + b * BwdStateSmem::A_STAGE; };
+  auto issue_A = [&](int ci, int b) {
+    const int t0 = bos + ci * C, nv = min(C, eos - t0);
+    unsigned char* st = stage(b);
+    load_tile64(reinterpret_cast<bf16*>(st + BwdStateSmem::A_M), P.M, t0, nv, H, h);
+    load_tile128(reinterpret_cast<bf16*>(st + BwdStateSmem::A_KB), P.Kb, t0, nv, H, h);
+    load_tile128(reinterpret_cast<bf16*>(st + BwdStateSmem::A_DO), P.dO, t0, nv, H, h);
+    load_vec128(reinterpret_cast<float*>(st + BwdStateSmem::A_DC), P.dC + ((size_t)(cbase + ci) * H + h) * D);
+  };
+
+  if (nchunks > 0) issue_A(nchunks - 1, (nchunks - 1) & 1);
+  cp_async_commit();
 
   float dS[16][4];
   const float* dht = P.dht ? P.dht + ((size_t)n * H + h) * D * D : nullptr;
@@ -104,12 +117,16 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_kernel(BwdStateParams P)
     const int t0 = bos + ci * C;
     const int nv = min(C, eos - t0);
     const size_t cidx = (size_t)(cbase + ci) * H + h;
+    unsigned char* st = stage(ci & 1);
+    const bf16* Mt = reinterpret_cast<const bf16*>(st + BwdStateSmem::A_M);
+    const bf16* Kb = reinterpret_cast<const bf16*>(st + BwdStateSmem::A_KB);
+    const bf16* dO = reinterpret_cast<const bf16*>(st + BwdStateSmem::A_DO);
+    const float* dC = reinterpret_cast<const float*>(st + BwdStateSmem::A_DC);
+    // group B of this chunk, then group A of the next one (an empty group at
+    // the last step keeps the group count uniform)
     load_tile128(Wt, P.W, t0, nv, H, h);
     load_tile128(Qt, P.Qt, t0, nv, H, h);
-    load_tile128(Kb, P.Kb, t0, nv, H, h);
-    load_tile128(dO, P.dO, t0, nv, H, h);
     load_tile128(Et, P.E, t0, nv, H, h);
-    load_tile64(Mt, P.M, t0, nv, H, h);
     {
       const bf16* src = P.hs + cidx * D * D;
       for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {
@@ -117,9 +134,10 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_kernel(BwdStateParams P)
         cp_async16(S0 + r * LD128 + cc * 8, src + r * D + cc * 8, true);
       }
     }
-    load_vec128(dC, P.dC + cidx * D);
     cp_async_commit();
-    // dS -> bf16 tile (overlaps the loads)
+    if (ci > 0) issue_A(ci - 1, (ci - 1) & 1);
+    cp_async_commit();
+    // dS -> bf16 tile
 #pragma unroll
     for (int j = 0; j < 16; ++j)
 #pragma unroll
@@ -127,7 +145,25 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_kernel(BwdStateParams P)
         int r = 16 * warp + acc_row(e), cc = acc_col(j, e);
         *reinterpret_cast<uint32_t*>(dSs + r * LD128 + cc) = pack_bf16(dS[j][e], dS[j][e + 1]);
       }
-    cp_async_wait<0>();
+    cp_async_wait<2>();  // group A of this chunk
+    __syncthreads();
+    // dE = M^T dO + Kbar dS
+    {
+      float acc[8][4];
+      zero_acc<8>(acc);
+      warp_mma<8, true, true>(acc, Mt, LD64, m0, dO, LD128, n0, 0, 64);
+      warp_mma<8, false, true>(acc, Kb, LD128, m0, dSs, LD128, n0, 0, 128);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+          uint32_t pk = pack_bf16(acc[j][e], acc[j][e + 1]);
+          *reinterpret_cast<uint32_t*>(dEs + r * LD128 + cc) = pk;
+          if (r < nv) *reinterpret_cast<uint32_t*>(P.dE + ((size_t)(t0 + r) * H + h) * D + cc) = pk;
+        }
+    }
+    cp_async_wait<1>();  // group B
     __syncthreads();
     // dGC = 2^Gam_C * rowsum(dS o S0)
     {
@@ -151,23 +187,6 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_kernel(BwdStateParams P)
         P.dGC[cidx * D + r0 + 8] = dC[r0 + 8] * part[1];
       }
     }
-    // dE = M^T dO + Kbar dS
-    {
-      float acc[8][4];
-      zero_acc<8>(acc);
-      warp_mma<8, true, true>(acc, Mt, LD64, m0, dO, LD128, n0, 0, 64);
-      warp_mma<8, false, true>(acc, Kb, LD128, m0, dSs, LD128, n0, 0, 128);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-          uint32_t pk = pack_bf16(acc[j][e], acc[j][e + 1]);
-          *reinterpret_cast<uint32_t*>(dEs + r * LD128 + cc) = pk;
-          if (r < nv) *reinterpret_cast<uint32_t*>(P.dE + ((size_t)(t0 + r) * H + h) * D + cc) = pk;
-        }
-    }
-    __syncthreads();
     // dS <- diag(dC) dS + Qt^T dO - W^T dE
 #pragma unroll
     for (int j = 0; j < 16; ++j)
@@ -207,6 +226,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_kernel(BwdStateParams P)
     }
     __syncthreads();
   }
+  cp_async_wait<0>();
   if (P.dh0) {
     float* dst = P.dh0 + ((size_t)n * H + h) * D * D;
 #pragma unroll
