@@ -9,6 +9,7 @@
 #include "../../include/kda_b200.h"
 #include "kda_bwd_intra.cuh"
 #include "kda_fwd_state_tc.cuh"
+#include "kda_bwd_state_tc.cuh"
 #include "kda_post.cuh"
 
 using namespace kda;
@@ -388,10 +389,10 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   bs.dht = dht;
   bs.dE = bv.dE; bs.dQt = bv.dQt; bs.dW = bv.dW; bs.dKb = bv.dKb; bs.dM = bv.dM; bs.dGC = bv.dGC;
   bs.dh0 = dh0;
-  if ((rc = set_smem(kda_bwd_state_kernel, BwdStateSmem::END, "bwd state"))) return rc;
+  if ((rc = set_smem(kda_bwd_state_tc_kernel, BwdStateTcSmem::END, "bwd state"))) return rc;
   {
     TimedLaunch tl(K_BWD_STATE, st);
-    kda_bwd_state_kernel<<<dim3(N, H), 256, BwdStateSmem::END, st>>>(bs);
+    kda_bwd_state_tc_kernel<<<dim3(N, H), 256, BwdStateTcSmem::END, st>>>(bs);
   }
   if ((rc = launch_check("bwd state"))) return rc;
 

@@ -1,0 +1,368 @@
+// Reverse state pass of the chunked KDA backward on the fifth-generation
+// tensor cores (tcgen05 + TMEM).
+//
+// One CTA (256 threads) per (sequence, head) walks the chunks last to first,
+// carrying the gradient of the chunk-end state dS (128x128 fp32 in TMEM, one
+// lane per state row k).  Per chunk, with S0 the chunk-start state saved by
+// the forward (bf16):
+//   phase A (MMA): dE  = M^T dO + Kbar dS      (M=64, TMEM region R1, lanes +0)
+//                  dKb = E dS^T                (M=64, R1, lanes +16)
+//                  dM  = dO E^T                (M=64, N=64, R3)
+//     meanwhile:   dS <- diag(2^Gam_C) dS in TMEM; the previous chunk's dQt/dW out
+//   epilogue A:    dE out, -dE -> bf16 operand tile; dKb, tril(dM) out;
+//                  dGC = rowsum((2^Gam_C dS) o S0)
+//   phase B (MMA): dS += Qt^T dO + W^T (-dE)   (M=128, R0)
+//                  dQt = dO S0^T, dW = (-dE) S0^T (M=64, R2, lanes +0 / +16)
+//   epilogue B:    dS -> bf16 operand tile of the next chunk (dh0 after the first chunk)
+// One thread issues the MMAs; completion is tracked with mbarriers whose waits
+// are bounded: on a timeout the CTA records an error and leaves through its
+// cleanup path (TMEM is always released).  The phase-A operands (M, dO, Kbar,
+// E, 2^Gam_C) are double-buffered and loaded one chunk ahead; Qt, W and S0 are
+// loaded when phase B of the chunk before has consumed them.  All operand
+// tiles are 128B-swizzled; rows past the sequence end are zero.
+#pragma once
+
+#include "kda_bwd_state.cuh"
+#include "kda_fwd_state_tc.cuh"
+
+namespace kda {
+
+struct BwdStateTcSmem {
+  static constexpr int TILE = 16384;                    // [64][128] bf16, two 8 KB atoms
+  // stage (double-buffered): phase-A operands of one chunk
+  static constexpr int M = 0, DO = 8192, KB = DO + TILE, E = KB + TILE;
+  static constexpr int STAGE = E + TILE;                // 57344
+  static constexpr int QT = 2 * STAGE, W = QT + TILE;
+  static constexpr int S0 = W + TILE;                   // [128][128] bf16, two 16 KB atoms
+  static constexpr int DS = S0 + 32768;                 // [128][128] bf16, two 16 KB atoms
+  static constexpr int NDE = DS + 32768;                // [64][128] bf16
+  static constexpr int DC = NDE + TILE;                 // [2][128] fp32 (per stage)
+  static constexpr int GCP = DC + 1024;                 // [2][128] fp32 dGC half-row partials
+  static constexpr int MISC = GCP + 1024;               // mbarriers, TMEM slot, abort flag
+  static constexpr int END = MISC + 64;
+};
+static_assert(BwdStateTcSmem::END <= 232448, "bwd state (tcgen05) shared memory");
+
+// cp.async of a [128][128] bf16 state (contiguous rows) into two 128B-swizzled
+// 16 KB atoms (columns 0-63, 64-127).
+__device__ __forceinline__ void load_state_sw128(unsigned char* dst, const bf16* src) {
+  for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {
+    const int r = i >> 4, cc = i & 15;
+    cp_async16(dst + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4), src + r * D + cc * 8, true);
+  }
+}
+
+__global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams P) {
+  extern __shared__ __align__(1024) unsigned char tc_smem[];  // 1 KB-aligned dynamic shared memory
+  unsigned char* smem = tc_smem;
+  using S_ = BwdStateTcSmem;
+  const int n = blockIdx.x, h = blockIdx.y, H = P.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q = warp & 3, hf = warp >> 2;  // TMEM lane quarter, column half
+  const int bos = seq_bos(P.seq, n), eos = seq_eos(P.seq, n);
+  const int nchunks = seq_nchunks(P.seq, n);
+  const int cbase = seq_chunk_base(P.seq, n);
+  const int krow = 32 * q + lane;  // state row of this thread (M=128 layout)
+  const int arow = 16 * q + (lane & 15);  // chunk row of this thread (M=64 layout)
+  const bool hi = lane >= 16;             // second M=64 accumulator (lanes +16)
+
+  if (nchunks == 0) {  // empty sequence: dh0 = dht
+    if (P.dh0) {
+      const float* src = P.dht ? P.dht + ((size_t)n * H + h) * D * D : nullptr;
+      float* dst = P.dh0 + ((size_t)n * H + h) * D * D;
+      for (int i = tid; i < D * D; i += blockDim.x) dst[i] = src ? src[i] : 0.f;
+    }
+    return;
+  }
+  if (smem_u32(smem) & 1023) {  // swizzled atoms need 1 KB alignment
+    if (tid == 0) atomicExch(&g_kda_device_error, 2);
+    return;
+  }
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + S_::MISC);  // A1, A2, B1, B2
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+  unsigned char* sQt = smem + S_::QT;
+  unsigned char* sW = smem + S_::W;
+  unsigned char* sS0 = smem + S_::S0;
+  unsigned char* sDS = smem + S_::DS;
+  unsigned char* sNDE = smem + S_::NDE;
+  float* gcp = reinterpret_cast<float*>(smem + S_::GCP);
+
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) tc::mbar_init(mbar + i, 1);
+    tc::fence_mbar_init();
+    *abort_flag = 0;
+  }
+  auto stage = [&](int ci) { return smem + (ci & 1) * S_::STAGE; };
+  auto stage_dc = [&](int ci) { return reinterpret_cast<float*>(smem + S_::DC) + (ci & 1) * D; };
+  auto issue_stage = [&](int ci) {
+    unsigned char* b = stage(ci);
+    const int t0 = bos + ci * C, nv = min(C, eos - t0);
+    tc::load_tile64_sw128(b + S_::M, P.M, t0, nv, H, h);
+    tc::load_tile_sw128(b + S_::DO, P.dO, t0, nv, H, h);
+    tc::load_tile_sw128(b + S_::KB, P.Kb, t0, nv, H, h);
+    tc::load_tile_sw128(b + S_::E, P.E, t0, nv, H, h);
+    load_vec128(stage_dc(ci), P.dC + ((size_t)(cbase + ci) * H + h) * D);
+  };
+  auto issue_single = [&](int ci) {
+    const int t0 = bos + ci * C, nv = min(C, eos - t0);
+    tc::load_tile_sw128(sQt, P.Qt, t0, nv, H, h);
+    tc::load_tile_sw128(sW, P.W, t0, nv, H, h);
+    load_state_sw128(sS0, P.hs + ((size_t)(cbase + ci) * H + h) * D * D);
+  };
+  // dS row krow, columns [64 hf, 64 hf + 64) -> bf16 operand tile
+  auto store_ds = [&](const float (&v)[64]) {
+    unsigned char* atom = sDS + hf * 16384;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 pk;
+      pk.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
+      pk.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+      pk.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+      pk.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+      *reinterpret_cast<uint4*>(atom + krow * 128 + ((c ^ (krow & 7)) << 4)) = pk;
+    }
+  };
+  // 32 accumulator columns of one M=64 row -> bf16 global row segment
+  auto store_row32 = [&](bf16* dst, const float (&a)[32], bool neg) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 pk;
+      const float s = neg ? -1.f : 1.f;
+      pk.x = pack_bf16(s * a[8 * c + 0], s * a[8 * c + 1]);
+      pk.y = pack_bf16(s * a[8 * c + 2], s * a[8 * c + 3]);
+      pk.z = pack_bf16(s * a[8 * c + 4], s * a[8 * c + 5]);
+      pk.w = pack_bf16(s * a[8 * c + 6], s * a[8 * c + 7]);
+      *reinterpret_cast<uint4*>(dst + 8 * c) = pk;
+    }
+  };
+
+  const int last = nchunks - 1;
+  issue_stage(last);
+  cp_async_commit();
+  issue_single(last);
+  cp_async_commit();
+  // dht -> registers and the bf16 operand tile
+  float v[64];
+  {
+    const float* src = P.dht ? P.dht + (((size_t)n * H + h) * D + krow) * D + 64 * hf : nullptr;
+#pragma unroll
+    for (int i = 0; i < 64; i += 4) {
+      const float4 x = src ? *reinterpret_cast<const float4*>(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
+    }
+    store_ds(v);
+  }
+  cp_async_wait<1>();  // phase-A operands of the last chunk
+  tc::fence_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t tq = (uint32_t)(32 * q) << 16;
+  const uint32_t tR0 = tbase + tq + 64 * hf;         // dS (this thread's lane, its column half)
+  const uint32_t tR1 = tbase + tq + 128 + 64 * hf;   // dE / dKb
+  const uint32_t tR2 = tbase + tq + 256 + 64 * hf;   // dQt / dW
+  const uint32_t tR3 = tbase + tq + 384 + 32 * hf;   // dM
+  const uint32_t idA1 = tc::idesc_bf16(64, 128, true, true);    // M^T dO
+  const uint32_t idA2 = tc::idesc_bf16(64, 128, false, true);   // Kbar dS
+  const uint32_t idKK = tc::idesc_bf16(64, 128, false, false);  // E dS^T, dO S0^T, (-dE) S0^T
+  const uint32_t idM = tc::idesc_bf16(64, 64, false, false);    // dO E^T
+  const uint32_t idB = tc::idesc_bf16(128, 128, true, true);    // Qt^T dO, W^T (-dE)
+
+  // dQt / dW of chunk cp (R2) -> global
+  auto r2_epilogue = [&](int cp) {
+    const int t0 = bos + cp * C, nv = min(C, eos - t0);
+    bf16* dst = (hi ? P.dW : P.dQt) + ((size_t)(t0 + arow) * H + h) * D + 64 * hf;
+#pragma unroll
+    for (int c0 = 0; c0 < 64; c0 += 32) {
+      float a[32];
+      tc::tmem_ld32(tR2 + c0, a);
+      if (arow < nv) store_row32(dst + c0, a, false);
+    }
+  };
+
+  bool ok = true;
+  int it = 0;
+  for (int ci = last; ci >= 0; --ci, ++it) {
+    const int t0 = bos + ci * C, nv = min(C, eos - t0);
+    const size_t cidx = (size_t)(cbase + ci) * H + h;
+    unsigned char* st = stage(ci);
+    const float* dC = stage_dc(ci);
+    // ---- phase A MMAs
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t m0 = smem_u32(st + S_::M), do0 = smem_u32(st + S_::DO);
+      const uint32_t kb0 = smem_u32(st + S_::KB), e0 = smem_u32(st + S_::E), s0 = smem_u32(sDS);
+      // dE = M^T dO + Kbar dS
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16(tbase + 128, tc::smem_desc(m0 + ks * 2048, 8192, 1024),
+                     tc::smem_desc(do0 + ks * 2048, 8192, 1024), idA1, ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        tc::mma_bf16(tbase + 128, tc::smem_desc(kb0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
+                     tc::smem_desc(s0 + ks * 2048, 16384, 1024), idA2, true);
+      // dKb = E dS^T
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        tc::mma_bf16(tbase + (16u << 16) + 128, tc::smem_desc(e0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
+                     tc::smem_desc(s0 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024), idKK, ks > 0);
+      tc::mma_commit(mbar + 0);
+      // dM = dO E^T
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        tc::mma_bf16(tbase + 384, tc::smem_desc(do0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024),
+                     tc::smem_desc(e0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), idM, ks > 0);
+      tc::mma_commit(mbar + 1);
+    }
+    // the next chunk's phase-A operands (its stage held chunk ci+1, finished)
+    if (ci > 0) issue_stage(ci - 1);
+    cp_async_commit();
+    // dS <- diag(2^Gam_C) dS (dS is R0 = v, the chunk-end gradient)
+    {
+      const float dc = dC[krow];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) v[i] *= dc;
+      float a[32], b[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { a[i] = v[i]; b[i] = v[32 + i]; }
+      tc::tmem_st32(tR0, a);
+      tc::tmem_st32(tR0 + 32, b);
+    }
+    // dQt / dW of the chunk after this one
+    if (ci < last) {
+      if (!tc::mbar_wait(mbar + 3, (it - 1) & 1)) *abort_flag = 1;
+      tc::fence_after_sync();
+      r2_epilogue(ci + 1);
+    }
+    // ---- epilogue A
+    if (!tc::mbar_wait(mbar + 0, it & 1)) *abort_flag = 1;
+    tc::fence_after_sync();
+    {
+      bf16* gdst = (hi ? P.dKb : P.dE) + ((size_t)(t0 + arow) * H + h) * D + 64 * hf;
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 32) {
+        float a[32];
+        tc::tmem_ld32(tR1 + c0, a);
+        if (arow < nv) store_row32(gdst + c0, a, false);
+        if (!hi) {  // -dE -> operand tile (rows past the end stay zero)
+          unsigned char* atom = sNDE + hf * 8192;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int chunk = (c0 >> 3) + c;
+            uint4 pk = make_uint4(0u, 0u, 0u, 0u);
+            if (arow < nv) {
+              pk.x = pack_bf16(-a[8 * c + 0], -a[8 * c + 1]);
+              pk.y = pack_bf16(-a[8 * c + 2], -a[8 * c + 3]);
+              pk.z = pack_bf16(-a[8 * c + 4], -a[8 * c + 5]);
+              pk.w = pack_bf16(-a[8 * c + 6], -a[8 * c + 7]);
+            }
+            *reinterpret_cast<uint4*>(atom + arow * 128 + ((chunk ^ (arow & 7)) << 4)) = pk;
+          }
+        }
+      }
+    }
+    if (!tc::mbar_wait(mbar + 1, it & 1)) *abort_flag = 1;
+    tc::fence_after_sync();
+    {
+      float a[32];
+      tc::tmem_ld32(tR3, a);
+      if (!hi && arow < nv) {
+        const int cb = 32 * hf;
+        float m[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m[i] = cb + i <= arow ? a[i] : 0.f;
+        store_row32(P.dM + ((size_t)(t0 + arow) * H + h) * 64 + cb, m, false);
+      }
+    }
+    // dGC: half-row partials of rowsum((2^Gam_C dS) o S0)
+    cp_async_wait<1>();  // Qt, W, S0 of this chunk (other threads' copies too)
+    __syncthreads();
+    {
+      const unsigned char* atom = sS0 + hf * 16384;
+      float part = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 s = *reinterpret_cast<const uint4*>(atom + krow * 128 + ((c ^ (krow & 7)) << 4));
+        const float2 s0 = unpack_bf16(s.x), s1 = unpack_bf16(s.y), s2 = unpack_bf16(s.z), s3 = unpack_bf16(s.w);
+        part += v[8 * c + 0] * s0.x + v[8 * c + 1] * s0.y + v[8 * c + 2] * s1.x + v[8 * c + 3] * s1.y +
+                v[8 * c + 4] * s2.x + v[8 * c + 5] * s2.y + v[8 * c + 6] * s3.x + v[8 * c + 7] * s3.y;
+      }
+      gcp[hf * D + krow] = part;
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (*abort_flag) { ok = false; break; }
+    if (tid < D) P.dGC[cidx * D + tid] = gcp[tid] + gcp[D + tid];
+    // ---- phase B MMAs
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t do0 = smem_u32(st + S_::DO), qt0 = smem_u32(sQt), w0 = smem_u32(sW);
+      const uint32_t nde0 = smem_u32(sNDE), s00 = smem_u32(sS0);
+      // dS += Qt^T dO + W^T (-dE)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16(tbase, tc::smem_desc(qt0 + ks * 2048, 8192, 1024), tc::smem_desc(do0 + ks * 2048, 8192, 1024),
+                     idB, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_bf16(tbase, tc::smem_desc(w0 + ks * 2048, 8192, 1024), tc::smem_desc(nde0 + ks * 2048, 8192, 1024),
+                     idB, true);
+      tc::mma_commit(mbar + 2);
+      // dQt = dO S0^T, dW = (-dE) S0^T
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t bd = tc::smem_desc(s00 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+        tc::mma_bf16(tbase + 256, tc::smem_desc(do0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), bd, idKK, ks > 0);
+        tc::mma_bf16(tbase + (16u << 16) + 256, tc::smem_desc(nde0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), bd,
+                     idKK, ks > 0);
+      }
+      tc::mma_commit(mbar + 3);
+    }
+    // ---- epilogue B: dS of the chunk before -> operand tile (or dh0)
+    if (!tc::mbar_wait(mbar + 2, it & 1)) *abort_flag = 1;
+    tc::fence_after_sync();
+    {
+      float a[32], b[32];
+      tc::tmem_ld32(tR0, a);
+      tc::tmem_ld32(tR0 + 32, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = b[i]; }
+    }
+    if (ci > 0) {
+      store_ds(v);
+      // dQt/dW (phase B) still read S0: the next Qt/W/S0 wait for them
+      if (!tc::mbar_wait(mbar + 3, it & 1)) *abort_flag = 1;
+      tc::fence_after_sync();
+      issue_single(ci - 1);
+      cp_async_commit();
+      cp_async_wait<1>();  // phase-A operands of the chunk before
+    } else {
+      cp_async_commit();
+      if (P.dh0) {
+        float* dst = P.dh0 + (((size_t)n * H + h) * D + krow) * D + 64 * hf;
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      }
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (*abort_flag) { ok = false; break; }
+  }
+  if (ok) {  // dQt / dW of the first chunk
+    if (!tc::mbar_wait(mbar + 3, (it - 1) & 1)) ok = false;
+    tc::fence_after_sync();
+    if (ok) r2_epilogue(0);
+  }
+  if (!ok && tid == 0) atomicExch(&g_kda_device_error, 1);
+  cp_async_wait<0>();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
+}
+
+}  // namespace kda

@@ -39,7 +39,8 @@ struct StateTcSmem {
 };
 
 __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams P) {
-  extern __shared__ __align__(1024) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char tc_smem[];  // 1 KB-aligned dynamic shared memory
+  unsigned char* smem = tc_smem;
   const int n = blockIdx.x, h = blockIdx.y, H = P.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int sub = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
