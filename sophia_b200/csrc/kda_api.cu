@@ -55,8 +55,8 @@ SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) 
   s.M = cv.take<bf16>((size_t)TT * H * 64 * 2);
   s.dC = cv.take<float>((size_t)mc * H * D * 4);
   if (with_bwd) {
-    s.E = cv.take<bf16>(row);
-    s.hs = cv.take<bf16>((size_t)mc * H * D * D * 2);
+    s.E = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
+    s.hs = cv.take<bf16>((size_t)mc * H * STATE_ELEMS * 2);
   } else {
     s.E = nullptr;
     s.hs = nullptr;
@@ -86,14 +86,15 @@ struct BwdView {
 BwdView carve_bwd(Carver& cv, int64_t TT, int H, int64_t mc) {
   BwdView b;
   const size_t row = (size_t)TT * H * D * 2;
-  b.dE = cv.take<bf16>(row);
-  b.dQt = cv.take<bf16>(row);
-  b.dW = cv.take<bf16>(row);
-  b.dKb = cv.take<bf16>(row);
+  const size_t tile = (size_t)mc * H * TILE64_ELEMS * 2;
+  b.dE = cv.take<bf16>(tile);
+  b.dQt = cv.take<bf16>(tile);
+  b.dW = cv.take<bf16>(tile);
+  b.dKb = cv.take<bf16>(tile);
   b.dq_hat = cv.take<bf16>(row);
   b.dk_hat = cv.take<bf16>(row);
   b.dv_hat = cv.take<bf16>(row);
-  b.dM = cv.take<bf16>((size_t)TT * H * 64 * 2);
+  b.dM = cv.take<bf16>((size_t)mc * H * TILE64N64_ELEMS * 2);
   b.dGC = cv.take<float>((size_t)mc * H * D * 4);
   b.partA = cv.take<float>((size_t)mc * H * D * 4);
   b.partB = cv.take<float>((size_t)mc * H * D * 4);
@@ -145,6 +146,7 @@ int check_common(const void* q, const void* k, const void* v, const void* g, con
   pr.seq.N = N;
   pr.seq.T = T;
   pr.seq.nt = (T + C - 1) / C;
+  pr.seq.slots = (int)pr.mc;
   pr.grid_chunks = pr.packed ? (int)pr.mc : B * pr.seq.nt;
   if (pr.mc > (int64_t)INT32_MAX / 2) return fail(KDA_ERR_INVALID, "too many tokens");
   return KDA_OK;

@@ -24,11 +24,20 @@
 
 namespace kda {
 
+// cp.async of an acc64 tile into a padded [64][LD128] tile (rows >= nv zero).
+__device__ __forceinline__ void load_acc64_ld128(bf16* dst, const bf16* tile, int nv) {
+  for (int idx = threadIdx.x; idx < 64 * 16; idx += blockDim.x) {
+    int r, cc;
+    acc64_chunk(idx, r, cc);
+    cp_async16(dst + r * LD128 + cc * 8, tile + idx * 8, r < nv);
+  }
+}
+
 struct BwdIntraParams {
   PrologueIn in;
   SeqInfo seq;
   bool conv;
-  const bf16 *dE, *dW, *dQt, *dKb, *dM;
+  const bf16 *dE, *dW, *dQt, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
   const float* dGC;
   bf16 *dq_hat, *dk_hat, *dv;  // [T_total][H][128]
   bf16 *dg, *dbeta;            // [T_total][H][128], [T_total][H]
@@ -79,6 +88,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   const int nv = pos.t1 - pos.t0;
   const int tid = threadIdx.x, warp = tid >> 5;
   const size_t cidx = (size_t)c * H + h;
+  const size_t tix = tile_index(P.seq, c, h);
 
   PrologueSmem ps;
   ps.xq = reinterpret_cast<bf16*>(smem + BwdIntraSmem::RAW);
@@ -127,19 +137,20 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 
   bf16* dEs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
   bf16* dWs = dEs + 64 * LD128;
-  load_tile128(dEs, P.dE, pos.t0, nv, H, h);
-  load_tile128(dWs, P.dW, pos.t0, nv, H, h);
+  load_acc64_ld128(dEs, P.dE + tix * TILE64_ELEMS, nv);
+  load_acc64_ld128(dWs, P.dW + tix * TILE64_ELEMS, nv);
   // dQt and dKbar are only read elementwise: unpadded [64][128] tiles in the
   // (now dead) decay region, 16-byte chunks XOR-swizzled by row so that the
   // fragment-position reads below are bank-conflict free
   bf16* dQs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GAM);
   bf16* dKs = dQs + 64 * D;
   for (int i = tid; i < 2 * 64 * 16; i += blockDim.x) {
-    int which = i >> 10, r = (i >> 4) & 63, cc = i & 15;
-    bool ok = r < nv;
-    const bf16* src = which ? P.dKb : P.dQt;
+    const int which = i >> 10, idx = i & 1023;
+    int r, cc;
+    acc64_chunk(idx, r, cc);
+    const bf16* src = (which ? P.dKb : P.dQt) + tix * TILE64_ELEMS + idx * 8;
     bf16* dst = which ? dKs : dQs;
-    cp_async16(dst + r * D + ((cc ^ (r & 7)) << 3), src + (ok ? ((size_t)(pos.t0 + r) * H + h) * D + cc * 8 : 0), ok);
+    cp_async16(dst + r * D + ((cc ^ (r & 7)) << 3), src, r < nv);
   }
   cp_async_commit();
 
@@ -175,7 +186,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   }
   bf16* dMs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DMS);
   __syncthreads();
-  load_tile64(dMs, P.dM, pos.t0, nv, H, h);
+  for (int idx = tid; idx < 64 * 8; idx += blockDim.x) {
+    int r, cc;
+    acc64n64_chunk(idx, r, cc);
+    cp_async16(dMs + r * LD64 + cc * 8, P.dM + tix * TILE64N64_ELEMS + idx * 8, r < nv);
+  }
   cp_async_commit();
   cp_async_wait<1>();  // dE, dW, dQt, dKbar
   __syncthreads();

@@ -19,7 +19,9 @@
 // cleanup path (TMEM is always released).  The phase-A operands (M, dO, Kbar,
 // E, 2^Gam_C) are double-buffered and loaded one chunk ahead; Qt, W and S0 are
 // loaded when phase B of the chunk before has consumed them.  All operand
-// tiles are 128B-swizzled; rows past the sequence end are zero.
+// tiles are 128B-swizzled; rows past the sequence end are zero.  v_new and the
+// chunk-start states arrive as acc64 / st128 tiles; dE, dKb, dQt, dW (acc64)
+// and dM (acc64n64) leave as whole per-(chunk, head) tiles in epilogue order.
 #pragma once
 
 #include "kda_bwd_state.cuh"
@@ -43,13 +45,31 @@ struct BwdStateTcSmem {
 };
 static_assert(BwdStateTcSmem::END <= 232448, "bwd state (tcgen05) shared memory");
 
-// cp.async of a [128][128] bf16 state (contiguous rows) into two 128B-swizzled
-// 16 KB atoms (columns 0-63, 64-127).
-__device__ __forceinline__ void load_state_sw128(unsigned char* dst, const bf16* src) {
-  for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {
-    const int r = i >> 4, cc = i & 15;
-    cp_async16(dst + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4), src + r * D + cc * 8, true);
+// cp.async of an st128 state tile into two 128B-swizzled 16 KB atoms
+// (columns 0-63, 64-127); consecutive threads read consecutive 16-byte chunks.
+__device__ __forceinline__ void load_st128_sw128(unsigned char* dst, const bf16* tile) {
+  for (int idx = threadIdx.x; idx < 128 * 16; idx += blockDim.x) {
+    int r, cc;
+    st128_chunk(idx, r, cc);
+    cp_async16(dst + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4), tile + idx * 8, true);
   }
+}
+// Same for an acc64 tile into two 128B-swizzled 8 KB atoms.
+__device__ __forceinline__ void load_acc64_sw128(unsigned char* dst, const bf16* tile) {
+  for (int idx = threadIdx.x; idx < 64 * 16; idx += blockDim.x) {
+    int r, cc;
+    acc64_chunk(idx, r, cc);
+    cp_async16(dst + (cc >> 3) * 8192 + r * 128 + (((cc & 7) ^ (r & 7)) << 4), tile + idx * 8, true);
+  }
+}
+// Eight fp32 values -> one bf16 16-byte chunk.
+__device__ __forceinline__ void store_chunk8(bf16* dst, const float* a) {
+  uint4 pk;
+  pk.x = pack_bf16(a[0], a[1]);
+  pk.y = pack_bf16(a[2], a[3]);
+  pk.z = pack_bf16(a[4], a[5]);
+  pk.w = pack_bf16(a[6], a[7]);
+  *reinterpret_cast<uint4*>(dst) = pk;
 }
 
 __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams P) {
@@ -102,14 +122,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     tc::load_tile64_sw128(b + S_::M, P.M, t0, nv, H, h);
     tc::load_tile_sw128(b + S_::DO, P.dO, t0, nv, H, h);
     tc::load_tile_sw128(b + S_::KB, P.Kb, t0, nv, H, h);
-    tc::load_tile_sw128(b + S_::E, P.E, t0, nv, H, h);
+    load_acc64_sw128(b + S_::E, P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS);
     load_vec128(stage_dc(ci), P.dC + ((size_t)(cbase + ci) * H + h) * D);
   };
   auto issue_single = [&](int ci) {
     const int t0 = bos + ci * C, nv = min(C, eos - t0);
     tc::load_tile_sw128(sQt, P.Qt, t0, nv, H, h);
     tc::load_tile_sw128(sW, P.W, t0, nv, H, h);
-    load_state_sw128(sS0, P.hs + ((size_t)(cbase + ci) * H + h) * D * D);
+    load_st128_sw128(sS0, P.hs + tile_index(P.seq, cbase + ci, h) * STATE_ELEMS);
   };
   // dS row krow, columns [64 hf, 64 hf + 64) -> bf16 operand tile
   auto store_ds = [&](const float (&v)[64]) {
@@ -124,19 +144,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
       *reinterpret_cast<uint4*>(atom + krow * 128 + ((c ^ (krow & 7)) << 4)) = pk;
     }
   };
-  // 32 accumulator columns of one M=64 row -> bf16 global row segment
-  auto store_row32 = [&](bf16* dst, const float (&a)[32], bool neg) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint4 pk;
-      const float s = neg ? -1.f : 1.f;
-      pk.x = pack_bf16(s * a[8 * c + 0], s * a[8 * c + 1]);
-      pk.y = pack_bf16(s * a[8 * c + 2], s * a[8 * c + 3]);
-      pk.z = pack_bf16(s * a[8 * c + 4], s * a[8 * c + 5]);
-      pk.w = pack_bf16(s * a[8 * c + 6], s * a[8 * c + 7]);
-      *reinterpret_cast<uint4*>(dst + 8 * c) = pk;
-    }
-  };
+
 
   const int last = nchunks - 1;
   issue_stage(last);
@@ -171,15 +179,15 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
   const uint32_t idM = tc::idesc_bf16(64, 64, false, false);    // dO E^T
   const uint32_t idB = tc::idesc_bf16(128, 128, true, true);    // Qt^T dO, W^T (-dE)
 
-  // dQt / dW of chunk cp (R2) -> global
+  // dQt / dW of chunk cp (R2) -> acc64 tiles (whole tiles: rows past the end are zero)
   auto r2_epilogue = [&](int cp) {
-    const int t0 = bos + cp * C, nv = min(C, eos - t0);
-    bf16* dst = (hi ? P.dW : P.dQt) + ((size_t)(t0 + arow) * H + h) * D + 64 * hf;
+    bf16* tile = (hi ? P.dW : P.dQt) + tile_index(P.seq, cbase + cp, h) * TILE64_ELEMS;
 #pragma unroll
     for (int c0 = 0; c0 < 64; c0 += 32) {
       float a[32];
       tc::tmem_ld32(tR2 + c0, a);
-      if (arow < nv) store_row32(dst + c0, a, false);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64_off(arow, 64 * hf + c0 + 8 * c), a + 8 * c);
     }
   };
 
@@ -188,6 +196,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
   for (int ci = last; ci >= 0; --ci, ++it) {
     const int t0 = bos + ci * C, nv = min(C, eos - t0);
     const size_t cidx = (size_t)(cbase + ci) * H + h;
+    const size_t tix = tile_index(P.seq, cbase + ci, h);
     unsigned char* st = stage(ci);
     const float* dC = stage_dc(ci);
     // ---- phase A MMAs
@@ -241,12 +250,13 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     if (!tc::mbar_wait(mbar + 0, it & 1)) *abort_flag = 1;
     tc::fence_after_sync();
     {
-      bf16* gdst = (hi ? P.dKb : P.dE) + ((size_t)(t0 + arow) * H + h) * D + 64 * hf;
+      bf16* tile = (hi ? P.dKb : P.dE) + tix * TILE64_ELEMS;
 #pragma unroll
       for (int c0 = 0; c0 < 64; c0 += 32) {
         float a[32];
         tc::tmem_ld32(tR1 + c0, a);
-        if (arow < nv) store_row32(gdst + c0, a, false);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64_off(arow, 64 * hf + c0 + 8 * c), a + 8 * c);
         if (!hi) {  // -dE -> operand tile (rows past the end stay zero)
           unsigned char* atom = sNDE + hf * 8192;
 #pragma unroll
@@ -269,12 +279,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     {
       float a[32];
       tc::tmem_ld32(tR3, a);
-      if (!hi && arow < nv) {
+      if (!hi) {
         const int cb = 32 * hf;
         float m[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) m[i] = cb + i <= arow ? a[i] : 0.f;
-        store_row32(P.dM + ((size_t)(t0 + arow) * H + h) * 64 + cb, m, false);
+        bf16* tile = P.dM + tix * TILE64N64_ELEMS;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64n64_off(arow, cb + 8 * c), m + 8 * c);
       }
     }
     // dGC: half-row partials of rowsum((2^Gam_C dS) o S0)

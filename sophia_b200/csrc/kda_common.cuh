@@ -41,7 +41,13 @@ struct SeqInfo {
   int N;                     // number of sequences
   int T;                     // tokens per sequence when cu_seqlens == nullptr
   int nt;                    // chunks per sequence when cu_seqlens == nullptr
+  int slots;                 // chunk slots per head of the per-(chunk, head) tile arrays
 };
+
+// Tile of (global chunk c, head h) in a per-(chunk, head) tile array: head-major,
+// so one head's chunks (read by consecutive chunk-kernel CTAs, written in order
+// by one state-kernel CTA) are adjacent.
+__device__ __forceinline__ size_t tile_index(const SeqInfo& s, int c, int h) { return (size_t)h * s.slots + c; }
 
 struct ChunkPos {
   int seq;     // sequence id
@@ -225,6 +231,49 @@ __device__ __forceinline__ int acc_row(int e) { return ((threadIdx.x & 31) >> 2)
 __device__ __forceinline__ int acc_col(int j, int e) { return 8 * j + 2 * (threadIdx.x & 3) + (e & 1); }
 
 // 16-byte vector of 8 bf16
+// ---------------------------------------------------------------- tile layouts
+// Per-(chunk, head) tiles exchanged between the state kernels and the chunk
+// kernels are stored in the order their producing epilogue holds them, so that
+// every warp store is one contiguous run; consumers gather 16-byte chunks.
+// Offsets are in elements; (i, v) is row, column and every chunk of 8
+// consecutive columns is contiguous.
+//   acc64: a 64x128 tile produced from an M=64 TMEM accumulator (row i sits in
+//          lane i%16 of warp quarter i/16; each thread holds 32-column blocks):
+//          [quarter 4][column half 2][32-block 2][8-chunk 4][row lane 16][8]
+//   acc64n64: a 64x64 tile from an N=64 M=64 accumulator (32 columns/thread):
+//          [quarter 4][column half 2][8-chunk 4][row lane 16][8]
+//   st128: a 128x128 state (row k in lane k%32 of warp quarter k/32):
+//          [quarter 4][column half 2][8-chunk 8][row lane 32][8]
+constexpr int TILE64_ELEMS = 64 * 128;
+constexpr int TILE64N64_ELEMS = 64 * 64;
+constexpr int STATE_ELEMS = 128 * 128;
+__host__ __device__ __forceinline__ uint32_t acc64_off(int i, int v) {
+  return (uint32_t)((((((i >> 4) * 2 + (v >> 6)) * 2 + ((v >> 5) & 1)) * 4 + ((v >> 3) & 3)) * 16 + (i & 15)) * 8 +
+                    (v & 7));
+}
+__host__ __device__ __forceinline__ uint32_t acc64n64_off(int i, int j) {
+  return (uint32_t)(((((i >> 4) * 2 + (j >> 5)) * 4 + ((j >> 3) & 3)) * 16 + (i & 15)) * 8 + (j & 7));
+}
+__host__ __device__ __forceinline__ uint32_t st128_off(int k, int v) {
+  return (uint32_t)(((((k >> 5) * 2 + (v >> 6)) * 8 + ((v >> 3) & 7)) * 32 + (k & 31)) * 8 + (v & 7));
+}
+// Inverse maps of a 16-byte chunk index (element offset / 8) to (row, 8-chunk).
+__device__ __forceinline__ void acc64_chunk(int idx, int& row, int& cc) {
+  const int lane = idx & 15, c = (idx >> 4) & 3, c0 = (idx >> 6) & 1, hf = (idx >> 7) & 1, q = idx >> 8;
+  row = 16 * q + lane;
+  cc = hf * 8 + c0 * 4 + c;
+}
+__device__ __forceinline__ void acc64n64_chunk(int idx, int& row, int& cc) {
+  const int lane = idx & 15, c = (idx >> 4) & 3, hf = (idx >> 6) & 1, q = idx >> 7;
+  row = 16 * q + lane;
+  cc = hf * 4 + c;
+}
+__device__ __forceinline__ void st128_chunk(int idx, int& row, int& cc) {
+  const int lane = idx & 31, c = (idx >> 5) & 7, hf = (idx >> 8) & 1, q = idx >> 9;
+  row = 32 * q + lane;
+  cc = hf * 8 + c;
+}
+
 struct alignas(16) bf16x8 { uint32_t u[4]; };
 
 __device__ __forceinline__ void unpack8(const bf16x8& v, float (&f)[8]) {

@@ -5,10 +5,8 @@
 //       -> W = T (k*2^Gam), U = T v, Qt = q*2^Gam, Kbar = k*2^(Gam_C-Gam),
 //          M = Aqk (lower incl. diag), dC = 2^Gam_C
 //       with T = (I + diag(beta) L')^-1 diag(beta).
-//   kda_fwd_state_kernel  (one CTA per (sequence, head), sequential in chunks)
-//       E = U - W S,  O = Qt S + M E,  S <- diag(dC) S + Kbar^T E
-//       keeps the 128x128 fp32 state in registers, writes O, the chunk-start
-//       states h (bf16) and E (bf16) for the backward, and the final state.
+// The state pass that consumes these (E = U - W S, O = Qt S + M E,
+// S <- diag(dC) S + Kbar^T E) runs on the tensor cores: kda_fwd_state_tc.cuh.
 #pragma once
 
 #include "kda_intra.cuh"
@@ -178,17 +176,9 @@ struct FwdStateParams {
   const float* dC;
   const float* h0;       // [N][H][128][128] or null
   bf16* o;               // [T_total][H][128]
-  bf16* hs;              // [chunks][H][128][128] chunk-start states or null
-  bf16* E;               // [T_total][H][128] or null
+  bf16* hs;              // [chunks][H] st128 tiles: chunk-start states, or null
+  bf16* E;               // [chunks][H] acc64 tiles: v_new, or null
   float* ht;             // [N][H][128][128] or null
-};
-
-struct StateSmem {
-  static constexpr int TILE = 64 * LD128 * 2;               // 17408
-  static constexpr int BUF = 4 * TILE + 64 * LD64 * 2 + D * 4;  // W, Qt, Kb, U, M, dC
-  static constexpr int S = 2 * BUF;                         // 128 x LD128 bf16
-  static constexpr int E = S + 128 * LD128 * 2;             // 64 x LD128 bf16
-  static constexpr int END = E + 64 * LD128 * 2;
 };
 
 __device__ __forceinline__ void load_tile128(bf16* dst, const bf16* src, int t0, int nvalid, int H, int h) {
@@ -209,126 +199,6 @@ __device__ __forceinline__ void load_tile64(bf16* dst, const bf16* src, int t0, 
 }
 __device__ __forceinline__ void load_vec128(float* dst, const float* src) {
   for (int i = threadIdx.x; i < 32; i += blockDim.x) cp_async16(dst + 4 * i, src + 4 * i, true);
-}
-
-__global__ void __launch_bounds__(256, 1) kda_fwd_state_kernel(FwdStateParams P) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int n = blockIdx.x, h = blockIdx.y, H = P.H;
-  const int warp = threadIdx.x >> 5;
-  const int bos = seq_bos(P.seq, n), eos = seq_eos(P.seq, n);
-  const int nchunks = seq_nchunks(P.seq, n);
-  const int cbase = seq_chunk_base(P.seq, n);
-  bf16* Ssm = reinterpret_cast<bf16*>(smem + StateSmem::S);
-  bf16* Esm = reinterpret_cast<bf16*>(smem + StateSmem::E);
-
-  auto buf = [&](int b, int which) { return reinterpret_cast<bf16*>(smem + b * StateSmem::BUF + which * StateSmem::TILE); };
-  auto bufM = [&](int b) { return reinterpret_cast<bf16*>(smem + b * StateSmem::BUF + 4 * StateSmem::TILE); };
-  auto bufC = [&](int b) {
-    return reinterpret_cast<float*>(smem + b * StateSmem::BUF + 4 * StateSmem::TILE + 64 * LD64 * 2);
-  };
-  auto issue = [&](int ci, int b) {
-    int t0 = bos + ci * C;
-    int nv = min(C, eos - t0);
-    load_tile128(buf(b, 0), P.W, t0, nv, H, h);
-    load_tile128(buf(b, 1), P.Qt, t0, nv, H, h);
-    load_tile128(buf(b, 2), P.Kb, t0, nv, H, h);
-    load_tile128(buf(b, 3), P.U, t0, nv, H, h);
-    load_tile64(bufM(b), P.M, t0, nv, H, h);
-    load_vec128(bufC(b), P.dC + ((size_t)(cbase + ci) * H + h) * D);
-  };
-
-  // state: warp w owns rows 16w..16w+15, all 128 columns
-  float S[16][4];
-  const float* h0 = P.h0 ? P.h0 + ((size_t)n * H + h) * D * D : nullptr;
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int r = 16 * warp + acc_row(e), cc = acc_col(j, e);
-      S[j][e] = h0 ? h0[r * D + cc] : 0.f;
-    }
-  auto write_S_smem = [&]() {
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = 16 * warp + acc_row(e), cc = acc_col(j, e);
-        *reinterpret_cast<uint32_t*>(Ssm + r * LD128 + cc) = pack_bf16(S[j][e], S[j][e + 1]);
-      }
-  };
-  write_S_smem();
-  if (nchunks > 0) issue(0, 0);
-  cp_async_commit();
-
-  for (int ci = 0; ci < nchunks; ++ci) {
-    const int b = ci & 1;
-    if (ci + 1 < nchunks) issue(ci + 1, b ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const int t0 = bos + ci * C;
-    const int nv = min(C, eos - t0);
-    const bf16 *Wt = buf(b, 0), *Qt = buf(b, 1), *Kb = buf(b, 2), *Ut = buf(b, 3), *Mt = bufM(b);
-    const float* dC = bufC(b);
-    if (P.hs) {
-      bf16* hdst = P.hs + ((size_t)(cbase + ci) * H + h) * D * D;
-      for (int i = threadIdx.x; i < 128 * 16; i += blockDim.x) {
-        int r = i >> 4, cc = i & 15;
-        *reinterpret_cast<bf16x8*>(hdst + r * D + cc * 8) = *reinterpret_cast<const bf16x8*>(Ssm + r * LD128 + cc * 8);
-      }
-    }
-    const int m0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
-    {
-      float acc[8][4];
-      zero_acc<8>(acc);
-      warp_mma<8, false, true>(acc, Wt, LD128, m0, Ssm, LD128, n0, 0, 128);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-          float2 u = unpack_bf16(*reinterpret_cast<const uint32_t*>(Ut + r * LD128 + cc));
-          uint32_t pk = pack_bf16(u.x - acc[j][e], u.y - acc[j][e + 1]);
-          *reinterpret_cast<uint32_t*>(Esm + r * LD128 + cc) = pk;
-          if (P.E && r < nv) *reinterpret_cast<uint32_t*>(P.E + ((size_t)(t0 + r) * H + h) * D + cc) = pk;
-        }
-    }
-    __syncthreads();
-    {
-      float acc[8][4];
-      zero_acc<8>(acc);
-      warp_mma<8, false, true>(acc, Qt, LD128, m0, Ssm, LD128, n0, 0, 128);
-      warp_mma<8, false, true>(acc, Mt, LD64, m0, Esm, LD128, n0, 0, 64);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-          if (r < nv)
-            *reinterpret_cast<uint32_t*>(P.o + ((size_t)(t0 + r) * H + h) * D + cc) =
-                pack_bf16(acc[j][e], acc[j][e + 1]);
-        }
-    }
-    // S <- diag(dC) S + Kb^T E
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) S[j][e] *= dC[16 * warp + acc_row(e)];
-    warp_mma<16, true, true>(S, Kb, LD128, 16 * warp, Esm, LD128, 0, 0, 64);
-    __syncthreads();
-    write_S_smem();
-  }
-  cp_async_wait<0>();
-  if (P.ht) {
-    float* dst = P.ht + ((size_t)n * H + h) * D * D;
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = 16 * warp + acc_row(e), cc = acc_col(j, e);
-        *reinterpret_cast<float2*>(dst + r * D + cc) = make_float2(S[j][e], S[j][e + 1]);
-      }
-  }
 }
 
 }  // namespace kda

@@ -15,7 +15,9 @@
 // are bounded: on a timeout the CTA records an error and leaves through its
 // cleanup path (TMEM is always released).  Chunk inputs are double-buffered
 // with cp.async into swizzled tiles (the next chunk loads during this one);
-// rows past the sequence end are zero.
+// rows past the sequence end are zero.  v_new (E) and the chunk-start states
+// are written as per-(chunk, head) tiles in epilogue order (acc64, st128), so
+// each warp store is one contiguous run.
 #pragma once
 
 #include "kda_fwd.cuh"
@@ -103,7 +105,8 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
       pk.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
       *reinterpret_cast<uint4*>(atom + krow * 128 + ((c ^ (krow & 7)) << 4)) = pk;
       if (P.hs && chunk_for_hs >= 0)
-        *reinterpret_cast<uint4*>(P.hs + (((size_t)chunk_for_hs * H + h) * D + krow) * D + 64 * half + 8 * c) = pk;
+        *reinterpret_cast<uint4*>(P.hs + tile_index(P.seq, chunk_for_hs, h) * STATE_ELEMS +
+                                  st128_off(krow, 64 * half + 8 * c)) = pk;
     }
   };
 
@@ -180,8 +183,9 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
             e.z = pack_bf16(u2.x - acc[8 * c + 4], u2.y - acc[8 * c + 5]);
             e.w = pack_bf16(u3.x - acc[8 * c + 6], u3.y - acc[8 * c + 7]);
             *reinterpret_cast<uint4*>(eat + off) = e;
-            if (P.E && r < nv)
-              *reinterpret_cast<uint4*>(P.E + ((size_t)(t0 + r) * H + h) * D + 64 * half + 8 * chunk) = e;
+            if (P.E)  // whole tile: rows past the end are zero
+              *reinterpret_cast<uint4*>(P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS +
+                                        acc64_off(r, 64 * half + 8 * chunk)) = e;
           }
         }
       }
