@@ -170,15 +170,16 @@ def make_inputs(B, device, seed):
 
 def bench_ours(a, rank, world, local_rank):
     import torch.distributed as dist
-    from sophia_b200 import _lib, kda_layer
+    from sophia_b200 import _lib, dp, kda_layer
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    B = a.batch or (8 if a.workload == "cfg1" else 320 // world)
+    # cfg1: 8 sequences per rank (weak scaling); cfg3: rank's share of 320 (strong)
+    B = a.batch or (8 if a.workload == "cfg1" else len(range(320)[dp.shard(320, rank, world)]))
     x, w = make_inputs(B, device, 42 + rank)
     acts = {k: x[k].clone().requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
     params = {k: v.clone().requires_grad_(True) for k, v in w.items()}
-    bucket = torch.empty(H + H * D + 3 * H * D * 4, device=device, dtype=torch.float32)
+    bucket = torch.empty(dp.bucket_numel(H, D), device=device, dtype=torch.float32)
 
     def step(inputs=None):
         src = acts if inputs is None else inputs
@@ -187,10 +188,8 @@ def bench_ours(a, rank, world, local_rank):
         o, _ = kda_layer(src["q"], src["k"], src["v"], src["g"], src["beta"], params["A_log"], params["dt_bias"],
                          params["conv_q"], params["conv_k"], params["conv_v"])
         o.backward(x["do"] if inputs is None else inputs["_do"])
-        torch.cat([params[k].grad.reshape(-1) for k in ("A_log", "dt_bias", "conv_q", "conv_k", "conv_v")],
-                  out=bucket)
-        if world > 1:
-            dist.all_reduce(bucket)
+        dp.grad_bucket(params, out=bucket)
+        dp.allreduce_bucket(bucket)
         return bucket
 
     def timed(fn, steps, sampler=None):
@@ -209,12 +208,7 @@ def bench_ours(a, rank, world, local_rank):
             sampler.mark(h0, time.perf_counter())
         if world > 1:
             dist.barrier()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = t.item()
-        return ms
+        return dp.max_over_ranks(e0.elapsed_time(e1), device)
 
     for _ in range(a.warmup):
         step()
@@ -225,7 +219,8 @@ def bench_ours(a, rank, world, local_rank):
     sampler.start()
     ms = timed(step, a.steps, sampler)
     clocks = sampler.stop()
-    tokens = world * B * T * a.steps
+    global_seqs = world * B if a.workload == "cfg1" else 320
+    tokens = global_seqs * T * a.steps
     value = tokens / (ms / 1e3)
 
     # per-kernel device times (second pass, CUDA events around every launch)
@@ -279,7 +274,7 @@ def bench_ours(a, rank, world, local_rank):
     kernel_ms_per_step = {k: round(v[1] / a.steps, 4) for k, v in kern.items() if v[0]}
     return {
         "value": value, "ms": ms / a.steps, "B": B, "clocks": clocks,
-        "e2e": {"value": world * B * T * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
+        "e2e": {"value": global_seqs * T * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
@@ -317,8 +312,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    per_rank = a.batch or (8 if a.workload == "cfg1" else 320 // world)
-    config = {"workload": a.workload, "global_batch": per_rank * world,
+    config = {"workload": a.workload, "global_batch": (a.batch or 8) * world if a.workload == "cfg1" else 320,
               "seq_len": T, "heads": H, "head_dim": D, "chunk": 64,
               "parallelism": f"dp{world}", "l2": "inputs larger than L2 (128 MiB per tensor), no flush"}
     if a.impl == "reference":

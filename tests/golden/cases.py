@@ -148,3 +148,28 @@ def make_cfg0_inputs() -> dict[str, torch.Tensor]:
         "conv_q": conv[0], "conv_k": conv[1], "conv_v": conv[2],
         "A_log": torch.zeros(c["H"]), "dt_bias": torch.zeros(inner),
     }
+
+
+def cfg4_window_lengths(window: int, seed: int = 42, T: int = 4096, lo: int = 32, hi: int = 4096) -> list[int]:
+    """Document lengths of packed window `window` of configuration 4: lengths
+    log-uniform in [lo, hi] (seeded per window), drawn until the window of T
+    tokens is full; the last document is cut at the window end."""
+    gen = torch.Generator().manual_seed(seed * 1000 + window)
+    out, used = [], 0
+    while used < T:
+        u = torch.rand(1, generator=gen).item()
+        L = int(round(math.exp(math.log(lo) + u * (math.log(hi) - math.log(lo)))))
+        L = min(L, T - used)
+        out.append(L)
+        used += L
+    return out
+
+
+def cfg4_case(window: int, H: int = 16) -> Case:
+    """One packed 4096-token window of configuration 4 as a parity case."""
+    lens = cfg4_window_lengths(window)
+    cu = [0]
+    for L in lens:
+        cu.append(cu[-1] + L)
+    return Case(f"cfg4_w{window}_h{H}", B=1, T=4096, H=H, cu_seqlens=cu, h0=True, final_state_grad=True,
+                random_gate_params=True, seed=4200 + window)

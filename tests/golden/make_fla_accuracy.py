@@ -2,7 +2,7 @@
 
 Run on a GPU box (writes ``tests/golden/fla_accuracy.json``)::
 
-    python tests/golden/make_fla_accuracy.py
+    python tests/golden/make_fla_accuracy.py [--only CASE ...]
 
 For each case of ``cases.ALL_CASES`` the inputs are rounded to bf16, the float64
 oracle is run on them, and so is the reference's CUDA path: a bf16 conv1d+SiLU
@@ -36,13 +36,34 @@ from kda_cuda_runner import compare, round_inputs_bf16  # noqa: E402
 from oracle_runner import run_oracle  # noqa: E402
 
 
+def parity_cases() -> dict:
+    """Every case the GPU parity tests compare with a recorded baseline: the
+    fixture and random cases plus one configuration-4 packed window."""
+    from cases import cfg4_case
+    c4 = cfg4_case(0, H=4)
+    return {**ALL_CASES, c4.name: c4}
+
+
 def main() -> None:
+    import argparse
+
     import fla
     import numpy as np
     import torch
     from cases import CASES
-    out = {"fla_version": getattr(fla, "__version__", "unknown"), "cases": {}, "golden": {}}
-    for name, case in ALL_CASES.items():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="recompute these case names and keep the other recorded entries")
+    a = ap.parse_args()
+    path = HERE / "fla_accuracy.json"
+    if a.only is not None and path.exists():
+        with open(path) as f:
+            out = json.load(f)
+    else:
+        out = {"fla_version": getattr(fla, "__version__", "unknown"), "cases": {}, "golden": {}}
+    for name, case in parity_cases().items():
+        if a.only is not None and name not in a.only:
+            continue
         inp = round_inputs_bf16(make_case_inputs(case))
         ref = run_oracle(case, inputs=inp)
         rep = compare(run_fla(case, inputs=inp), ref)
@@ -50,12 +71,14 @@ def main() -> None:
         print(name, flush=True)
     # against the reference's own float32 outputs on the unrounded inputs
     for name, case in CASES.items():
+        if a.only is not None and name not in a.only:
+            continue
         gold = np.load(HERE / f"{name}.npz")
         ref = {k: torch.from_numpy(gold[k]) for k in gold.files if k != "input_sums"}
         rep = compare(run_fla(case), ref)
         out["golden"][name] = {k: {"viol": v[0], "rel": v[1]} for k, v in rep.items()}
         print("golden", name, flush=True)
-    with open(HERE / "fla_accuracy.json", "w") as f:
+    with open(path, "w") as f:
         json.dump(out, f, indent=1, sort_keys=True)
 
 

@@ -129,6 +129,42 @@ def run_cfg0(reference_root: str) -> dict[str, np.ndarray]:
     }
 
 
+MODULE_CFG = dict(B=2, T=70, dim=64, H=2, D=128, pad=6, seed=2024)
+
+
+def run_module(reference_root: str) -> dict[str, np.ndarray]:
+    """SophiaKDA.forward end to end (attention.py:373-420, fp32, reference
+    backend): projections, ShortConv, decay/beta logits with a left-padded row
+    (pad mask), the recurrence, gated output norm and o_proj; then the
+    backward of <out, dout> for the input and every parameter."""
+    c = MODULE_CFG
+    torch.manual_seed(c["seed"])
+    mod, _ = _module(reference_root, c["H"], c["D"], -5.0)
+    gen = torch.Generator().manual_seed(c["seed"])
+    with torch.no_grad():
+        for name in ("q_proj", "k_proj", "v_proj", "decay_down", "beta_proj"):
+            w = getattr(mod, name).weight
+            w.copy_(torch.randn(w.shape, generator=gen) * 0.15)
+        w = mod.decay_up.weight
+        w.copy_(torch.randn(w.shape, generator=gen) * 0.3)
+        for name in ("q_conv", "k_conv", "v_conv"):
+            w = getattr(mod, name).weight
+            w.copy_(torch.randn(w.shape, generator=gen) * 0.5)
+    x = torch.randn(c["B"], c["T"], c["dim"], generator=gen).requires_grad_(True)
+    mask = torch.ones(c["B"], c["T"], dtype=torch.bool)
+    mask[1, :c["pad"]] = False
+    mod._pad_mask = mask
+    out = mod(x)
+    dout = torch.randn(out.shape, generator=gen)
+    (out * dout).sum().backward()
+    res = {"x": x.detach().numpy(), "mask": mask.numpy(), "dout": dout.numpy(), "out": out.detach().numpy(),
+           "d_x": x.grad.numpy()}
+    for name, prm in mod.named_parameters():
+        res["param." + name] = prm.detach().numpy()
+        res["grad." + name] = (prm.grad if prm.grad is not None else torch.zeros_like(prm)).numpy()
+    return res
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True,
@@ -141,6 +177,8 @@ def main() -> None:
         print("wrote", name)
     np.savez_compressed(Path(a.out) / "cfg0.npz", **run_cfg0(a.reference))
     print("wrote cfg0")
+    np.savez_compressed(Path(a.out) / "module_forward.npz", **run_module(a.reference))
+    print("wrote module_forward")
 
 
 if __name__ == "__main__":

@@ -151,3 +151,107 @@ def test_errors_are_raised_on_host():
                                                                              dtype=torch.bfloat16), **kw)
     with pytest.raises(ValueError, match="chunk_size"):
         chunk_kda(q, q, q, g, b, lower_bound=-5.0, chunk_size=16, **kw)
+
+
+def _device_chunk_table(cu: list[int], total: int):
+    from sophia_b200 import _lib
+    lib = _lib.load()
+    N = len(cu) - 1
+    cu_d = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    offsets = torch.full((N + 1,), -7, dtype=torch.int32, device="cuda")
+    max_chunks = total // 64 + N
+    chunk_seq = torch.full((max(1, max_chunks),), -7, dtype=torch.int32, device="cuda")
+    err = torch.full((1,), -7, dtype=torch.int32, device="cuda")
+    rc = lib.kda_b200_chunk_table(cu_d.data_ptr(), N, total, offsets.data_ptr(), chunk_seq.data_ptr(),
+                                  err.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return offsets.cpu().numpy(), chunk_seq.cpu().numpy(), int(err.item())
+
+
+def test_chunk_table_matches_integer_oracle():
+    """The device-built packed-sequence table (offsets, sequence id per chunk)
+    equals the restated prepare_chunk_offsets / chunk index table, bit for bit,
+    including empty, one-token and chunk-aligned documents and N > 1024."""
+    from oracle.chunk_index import chunk_table_with_true_ids, prepare_chunk_offsets
+    gen = np.random.default_rng(5)
+    lens_many = gen.integers(0, 300, size=3000)
+    cases = [[0, 1, 65, 65, 200, 264, 264 + 4096], [0, 64], [0, 0, 0, 5],
+             [0] + np.cumsum(lens_many).tolist()]
+    for cu in cases:
+        total = cu[-1]
+        offsets, chunk_seq, err = _device_chunk_table(cu, total)
+        assert err == 0
+        np.testing.assert_array_equal(offsets, prepare_chunk_offsets(cu, 64))
+        table = chunk_table_with_true_ids(cu, 64)
+        np.testing.assert_array_equal(chunk_seq[:len(table)], table[:, 0])
+
+
+def test_chunk_table_rejects_malformed_cu_seqlens():
+    """A decreasing table, a nonzero start or a wrong total sets the error flag
+    and zeroes every offset, so the kernels of that call see no chunks."""
+    for cu, total in (([0, 70, 60, 100], 100), ([3, 70, 100], 100), ([0, 70, 100], 120)):
+        offsets, _, err = _device_chunk_table(cu, total)
+        assert err == 1
+        assert (offsets == 0).all()
+
+
+@pytest.mark.parametrize("window", [0, 1])
+def test_cfg4_packed_window_equals_unpacked_documents(window):
+    """Configuration 4 (packed 4096-token windows, log-uniform document
+    lengths, 16 heads): every document of the packed run is bit-identical to
+    the same document run alone -- outputs, final states and all gradients."""
+    from cases import cfg4_case
+    case = cfg4_case(window)
+    inp = round_inputs_bf16(make_case_inputs(case))
+    packed = run_cuda(case, inputs=inp)
+    cu = case.cu_seqlens
+    for n in range(len(cu) - 1):
+        one = Case("one", B=1, T=cu[n + 1] - cu[n], H=case.H, h0=True, final_state_grad=True,
+                   random_gate_params=True)
+        sub = dict(inp)
+        for k in ("q", "k", "v", "g", "beta", "do"):
+            sub[k] = inp[k][:, cu[n]:cu[n + 1]]
+        sub["h0"] = inp["h0"][n:n + 1]
+        sub["dht"] = inp["dht"][n:n + 1]
+        alone = run_cuda(one, inputs=sub)
+        sl = slice(cu[n], cu[n + 1])
+        assert torch.equal(packed["o"][:, sl], alone["o"])
+        assert torch.equal(packed["final_state"][n:n + 1], alone["final_state"])
+        for k in ("d_q", "d_k", "d_v", "d_g", "d_beta"):
+            assert torch.equal(packed[k][:, sl], alone[k]), k
+        assert torch.equal(packed["d_h0"][n:n + 1], alone["d_h0"])
+
+
+def test_cfg4_packed_window_matches_oracle():
+    """One configuration-4 window (4 heads) against the float64 oracle run per
+    document (zero conv history and the given initial state per document)."""
+    from cases import cfg4_case
+    case = cfg4_case(0, H=4)
+    rep, bad = _check(case)
+    assert not bad, "\n".join(f"{k}: viol={v[0]:.3f} rel={v[1]:.2e}" for k, v in sorted(rep.items()))
+
+
+def test_decode_steps_match_oracle():
+    """The decode seam (fused_recurrent_kda, one token per call, state carried
+    through initial_state) against the float64 oracle over the same tokens."""
+    from sophia_b200 import fused_recurrent_kda
+    case = Case("decode", B=2, T=24, H=2, conv=False, h0=True, random_gate_params=True, seed=31)
+    inp = round_inputs_bf16(make_case_inputs(case))
+    ref = run_oracle(case, inputs=inp, grads=False)
+    dev = "cuda"
+    t = {k: inp[k].to(dev, torch.bfloat16 if k in ("q", "k", "v", "g", "beta") else torch.float32)
+         for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "h0")}
+    state, outs = t["h0"], []
+    with torch.no_grad():
+        for s in range(case.T):
+            sl = slice(s, s + 1)
+            o, state = fused_recurrent_kda(t["q"][:, sl], t["k"][:, sl], t["v"][:, sl], t["g"][:, sl],
+                                           t["beta"][:, sl], A_log=t["A_log"], dt_bias=t["dt_bias"],
+                                           initial_state=state, output_final_state=True,
+                                           use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
+                                           use_beta_sigmoid_in_kernel=True, lower_bound=-5.0)
+            outs.append(o)
+    got = {"o": torch.cat(outs, dim=1).float().cpu(), "final_state": state.float().cpu()}
+    rep = compare(got, {k: ref[k] for k in ("o", "final_state")})
+    assert not failures(rep, ref), rep
