@@ -105,6 +105,23 @@ int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens,
                          int32_t* chunk_seq, int32_t* error_flag, void* stream);
 
 /*
+ * Token-by-token recurrence for decode, fp32 state and arithmetic -- replaces
+ * flash-linear-attention's fused_recurrent_kda (0.5.x, not vendored) at its
+ * Sophia call site: the single-step decode of SophiaKDA._run_kda
+ * (ml/runtime/model/attention.py:330-348, seam :296-304), with the in-kernel
+ * L2 norms, gate and beta sigmoid of that call.  q, k, v, g: [B*T][H][128],
+ * beta: [B*T][H], bf16 (fp32_inputs = 0) or fp32 (fp32_inputs = 1); o takes
+ * the same dtype.  h0 / ht: [N][H][128][128] fp32 (either may be null).  With
+ * cu_seqlens (B = 1) every sequence starts from its own h0 row.  Forward only;
+ * no workspace.  A cu_seqlens entry outside [0, B*T] makes the kernel skip that
+ * sequence and set kda_b200_device_error() to 3.
+ */
+int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                       const float* A_log, const float* dt_bias, const float* h0, const int32_t* cu_seqlens, int B,
+                       int T, int H, int D, int N, int fp32_inputs, float scale, float lower_bound, void* o,
+                       float* ht, void* stream);
+
+/*
  * Device-side failure flag of the tensor-core kernels.  Their waits on
  * asynchronous MMA completion are bounded; a wait that runs out makes the
  * kernel record a nonzero code here and return early (its outputs are then

@@ -28,6 +28,7 @@ SIGNATURES = {
                      + [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_void_p], c_int),
     "kda_b200_bwd": ([c_void_p] * 12 + [c_int] * 5 + [c_float, c_float]
                      + [c_void_p, c_size_t] + [c_void_p] * 13 + [c_void_p, c_size_t, c_void_p], c_int),
+    "kda_b200_recurrent": ([c_void_p] * 9 + [c_int] * 6 + [c_float, c_float] + [c_void_p] * 3, c_int),
     "kda_b200_chunk_table": ([c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p], c_int),
     "kda_b200_device_error": ([c_int], c_int),
     "kda_b200_fwd_noalloc": ([c_void_p] * 12 + [c_int] * 5 + [c_float, c_float] + [c_void_p, c_void_p, c_void_p],

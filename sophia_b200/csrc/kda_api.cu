@@ -10,6 +10,7 @@
 #include "kda_bwd_intra.cuh"
 #include "kda_fwd_state_tc.cuh"
 #include "kda_bwd_state_tc.cuh"
+#include "kda_recurrent.cuh"
 #include "kda_post.cuh"
 
 using namespace kda;
@@ -153,9 +154,9 @@ int check_common(const void* q, const void* k, const void* v, const void* g, con
 }
 
 // ---- optional per-launch device timing (CUDA events on the launch stream)
-enum KernelId { K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_COUNT };
+enum KernelId { K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_RECURRENT, K_COUNT };
 const char* const kKernelNames[K_COUNT] = {"chunk_table", "fwd_intra", "fwd_state", "bwd_state",
-                                           "bwd_intra",   "bwd_post",  "reduce"};
+                                           "bwd_intra",   "bwd_post",  "reduce",    "recurrent"};
 
 struct Timing {
   std::mutex mu;
@@ -275,6 +276,50 @@ int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens,
   kda_chunk_table_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(cu_seqlens, N, (long long)total_tokens,
                                                                             offsets, chunk_seq, error_flag);
   return launch_check("chunk table");
+}
+
+int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                       const float* A_log, const float* dt_bias, const float* h0, const int32_t* cu_seqlens, int B,
+                       int T, int H, int D_, int N, int fp32_inputs, float scale, float lower_bound, void* o,
+                       float* ht, void* stream) {
+  if (D_ != D) return fail(KDA_ERR_UNSUPPORTED, "head dim must be 128, got " + std::to_string(D_));
+  if (B < 1 || T < 0 || H < 1) return fail(KDA_ERR_INVALID, "B >= 1, T >= 0 and H >= 1 are required");
+  if (!(lower_bound >= -5.f && lower_bound < 0.f))
+    return fail(KDA_ERR_INVALID, "`lower_bound` must be in the safe range [-5, 0), got " + std::to_string(lower_bound));
+  if (!q || !k || !v || !g || !beta || !A_log || !dt_bias || !o) return fail(KDA_ERR_INVALID, "null pointer");
+  if (cu_seqlens) {
+    if (B != 1)
+      return fail(KDA_ERR_INVALID, "The batch size is expected to be 1 rather than " + std::to_string(B) +
+                                       " when using `cu_seqlens`.");
+    if (N < 1) return fail(KDA_ERR_INVALID, "N >= 1 sequences are required with cu_seqlens");
+  } else if (N != B) {
+    return fail(KDA_ERR_INVALID, "N must equal B without cu_seqlens");
+  }
+  RecurrentParams rp;
+  rp.seq.cu_seqlens = cu_seqlens;
+  rp.seq.chunk_offsets = nullptr;
+  rp.seq.chunk_seq = nullptr;
+  rp.seq.N = N;
+  rp.seq.T = T;
+  rp.seq.nt = (T + C - 1) / C;
+  rp.seq.slots = 0;
+  rp.H = H;
+  rp.fp32_inputs = fp32_inputs != 0;
+  rp.q = q; rp.k = k; rp.v = v; rp.g = g; rp.beta = beta;
+  rp.A_log = A_log;
+  rp.dt_bias = dt_bias;
+  rp.h0 = h0;
+  rp.scale = scale;
+  rp.lower_bound = lower_bound;
+  rp.o = o;
+  rp.ht = ht;
+  rp.total_tokens = (long long)B * T;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  {
+    TimedLaunch tl(K_RECURRENT, st);
+    kda_recurrent_kernel<<<dim3(N, H), REC_THREADS, 0, st>>>(rp);
+  }
+  return launch_check("recurrent");
 }
 
 int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, const void* beta, const float* A_log,

@@ -1,0 +1,100 @@
+// Token-by-token KDA recurrence for decode (fp32 state and arithmetic).
+//
+// One CTA (128 threads) per (sequence, head).  Thread v keeps column v of the
+// 128x128 state S[k][v] in registers for the whole sequence.  Per token, the
+// CTA builds the normalised q (times scale), the normalised k and the decay
+// alpha_k = exp(lb * sigmoid(exp(A_log) (g_k + dt_bias_k))) in shared memory,
+// then every thread runs the reference's update on its column:
+//   S <- diag(alpha) S;  pred = k^T S;  u = beta (v - pred);
+//   S <- S + k u^T;      o = q^T S
+// (ml/runtime/model/attention.py:286-292, the order of the reference loop).
+// Inputs may be bf16 or fp32; o takes v's dtype; the final state is fp32.
+#pragma once
+
+#include "kda_fwd_state_tc.cuh"  // g_kda_device_error
+
+namespace kda {
+
+constexpr int REC_THREADS = 128;
+
+struct RecurrentParams {
+  SeqInfo seq;
+  int H;
+  bool fp32_inputs;
+  const void *q, *k, *v, *g, *beta;  // [T_total][H][128] ([T_total][H] for beta)
+  const float *A_log, *dt_bias;      // [H], [H*128]
+  const float* h0;                   // [N][H][128][128] or null
+  float scale, lower_bound;
+  void* o;                           // [T_total][H][128], v's dtype
+  float* ht;                         // [N][H][128][128] or null
+  long long total_tokens;            // B*T: sequence bounds are checked against it
+};
+
+__device__ __forceinline__ float rec_load(const void* p, size_t i, bool f32) {
+  return f32 ? static_cast<const float*>(p)[i] : __bfloat162float(static_cast<const bf16*>(p)[i]);
+}
+
+// Sum over the CTA (128 threads = 4 warps); red holds 4 floats per call site.
+__device__ __forceinline__ float rec_block_sum(float x, float* red) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+__global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentParams P) {
+  __shared__ float qn[D], kn[D], alpha[D];
+  __shared__ float red[2][4];
+  const int n = blockIdx.x, h = blockIdx.y, H = P.H, vi = threadIdx.x;
+  const int bos = seq_bos(P.seq, n), eos = seq_eos(P.seq, n);
+  if (bos < 0 || eos < bos || (long long)eos > P.total_tokens) {  // malformed cu_seqlens: touch nothing
+    if (vi == 0) atomicExch(&g_kda_device_error, 3);
+    return;
+  }
+  const size_t stateoff = ((size_t)n * H + h) * D * D;
+
+  float S[D];
+#pragma unroll
+  for (int kk = 0; kk < D; ++kk) S[kk] = P.h0 ? P.h0[stateoff + (size_t)kk * D + vi] : 0.f;
+
+  const float eA = expf(P.A_log[h]);
+  const float bias = P.dt_bias[(size_t)h * D + vi];
+  for (int t = bos; t < eos; ++t) {
+    const size_t row = ((size_t)t * H + h) * D + vi;
+    const float qx = rec_load(P.q, row, P.fp32_inputs), kx = rec_load(P.k, row, P.fp32_inputs);
+    const float vx = rec_load(P.v, row, P.fp32_inputs), gx = rec_load(P.g, row, P.fp32_inputs);
+    const float bx = rec_load(P.beta, (size_t)t * H + h, P.fp32_inputs);
+    const float sq = rec_block_sum(qx * qx, red[0]);
+    const float sk = rec_block_sum(kx * kx, red[1]);
+    qn[vi] = qx / fmaxf(sqrtf(sq), 1e-12f) * P.scale;
+    kn[vi] = kx / fmaxf(sqrtf(sk), 1e-12f);
+    alpha[vi] = expf(P.lower_bound / (1.f + expf(-eA * (gx + bias))));
+    const float beta = 1.f / (1.f + expf(-bx));
+    __syncthreads();
+    float pred = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D; ++kk) {
+      S[kk] *= alpha[kk];
+      pred = fmaf(kn[kk], S[kk], pred);
+    }
+    const float u = (vx - pred) * beta;
+    float out = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D; ++kk) {
+      S[kk] = fmaf(kn[kk], u, S[kk]);
+      out = fmaf(qn[kk], S[kk], out);
+    }
+    if (P.fp32_inputs)
+      static_cast<float*>(P.o)[row] = out;
+    else
+      static_cast<bf16*>(P.o)[row] = __float2bfloat16(out);
+    __syncthreads();  // qn/kn/alpha/red are rewritten by the next token
+  }
+  if (P.ht) {
+#pragma unroll
+    for (int kk = 0; kk < D; ++kk) P.ht[stateoff + (size_t)kk * D + vi] = S[kk];
+  }
+}
+
+}  // namespace kda

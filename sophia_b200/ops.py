@@ -192,10 +192,42 @@ def kda_layer(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, *, lower
 def fused_recurrent_kda(q, k, v, g, beta, A_log=None, dt_bias=None, scale=None, initial_state=None,
                         output_final_state=False, use_qk_l2norm_in_kernel=False, use_gate_in_kernel=False,
                         use_beta_sigmoid_in_kernel=False, lower_bound=None, cu_seqlens=None, **kwargs):
-    """Decode-step seam (``attention.py:330-348``): evaluated by the chunked
-    kernels (a single partial chunk), so it returns what ``chunk_kda`` returns."""
-    return chunk_kda(q, k, v, g, beta, scale=scale, initial_state=initial_state,
-                     output_final_state=output_final_state,
-                     use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel, use_gate_in_kernel=use_gate_in_kernel,
-                     use_beta_sigmoid_in_kernel=use_beta_sigmoid_in_kernel, cu_seqlens=cu_seqlens,
-                     safe_gate=True, lower_bound=lower_bound, A_log=A_log, dt_bias=dt_bias)
+    """Decode-step seam (``attention.py:330-348``, flash-linear-attention's
+    ``fused_recurrent_kda``): the token-by-token recurrence in fp32 on the GPU
+    (``kda_b200_recurrent``), the same configuration as ``chunk_kda``.
+
+    Without gradients (decode) this runs the recurrent kernel; when autograd
+    needs gradients of the inputs it evaluates the same recurrence through the
+    chunked kernels, which have a backward.  Returns ``(o, final_state | None)``.
+    """
+    if not (use_qk_l2norm_in_kernel and use_gate_in_kernel and use_beta_sigmoid_in_kernel):
+        raise NotImplementedError(
+            "the B200 kernels implement the fused configuration: use_qk_l2norm_in_kernel, "
+            "use_gate_in_kernel and use_beta_sigmoid_in_kernel all True")
+    if A_log is None:
+        raise AssertionError("A_log must be provided when use_gate_in_kernel=True.")
+    _check_common(q, k, v, g, beta, initial_state, cu_seqlens, lower_bound)
+    if dt_bias is None:
+        dt_bias = torch.zeros(q.shape[2] * HEAD_DIM, device=q.device, dtype=torch.float32)
+    tensors = (q, k, v, g, beta, A_log, dt_bias, initial_state)
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors):
+        return chunk_kda(q, k, v, g, beta, scale=scale, initial_state=initial_state,
+                         output_final_state=output_final_state, use_qk_l2norm_in_kernel=True,
+                         use_gate_in_kernel=True, use_beta_sigmoid_in_kernel=True, cu_seqlens=cu_seqlens,
+                         safe_gate=True, lower_bound=lower_bound, A_log=A_log, dt_bias=dt_bias)
+    if scale is None:
+        scale = q.shape[-1] ** -0.5
+    fp32 = q.dtype == torch.float32
+    dt = torch.float32 if fp32 else torch.bfloat16
+    B, T, H, _ = q.shape
+    xs = [x.to(dt).contiguous() for x in (q, k, v, g, beta)]
+    o = torch.empty(B, T, H, HEAD_DIM, device=q.device, dtype=dt)
+    N = B if cu_seqlens is None else cu_seqlens.numel() - 1
+    ht = torch.empty(N, H, HEAD_DIM, HEAD_DIM, device=q.device, dtype=torch.float32) if output_final_state else None
+    cu = None if cu_seqlens is None else cu_seqlens.to(torch.int32).contiguous()
+    h0 = None if initial_state is None else initial_state.contiguous()
+    A_log32, dt_bias32 = A_log.float().contiguous(), dt_bias.float().contiguous()
+    _lib.check(_lib.load().kda_b200_recurrent(
+        *(_ptr(x) for x in xs), _ptr(A_log32), _ptr(dt_bias32), _ptr(h0), _ptr(cu),
+        B, T, H, HEAD_DIM, N, int(fp32), float(scale), float(lower_bound), _ptr(o), _ptr(ht), _stream()))
+    return o.to(v.dtype), ht

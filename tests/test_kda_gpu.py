@@ -232,19 +232,14 @@ def test_cfg4_packed_window_matches_oracle():
     assert not bad, "\n".join(f"{k}: viol={v[0]:.3f} rel={v[1]:.2e}" for k, v in sorted(rep.items()))
 
 
-def test_decode_steps_match_oracle():
-    """The decode seam (fused_recurrent_kda, one token per call, state carried
-    through initial_state) against the float64 oracle over the same tokens."""
-    from sophia_b200 import fused_recurrent_kda
-    case = Case("decode", B=2, T=24, H=2, conv=False, h0=True, random_gate_params=True, seed=31)
-    inp = round_inputs_bf16(make_case_inputs(case))
-    ref = run_oracle(case, inputs=inp, grads=False)
+def _decode(inp, T, dtype):
+    from sophia_b200 import _lib, fused_recurrent_kda
     dev = "cuda"
-    t = {k: inp[k].to(dev, torch.bfloat16 if k in ("q", "k", "v", "g", "beta") else torch.float32)
+    t = {k: inp[k].to(dev, dtype if k in ("q", "k", "v", "g", "beta") else torch.float32)
          for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "h0")}
     state, outs = t["h0"], []
     with torch.no_grad():
-        for s in range(case.T):
+        for s in range(T):
             sl = slice(s, s + 1)
             o, state = fused_recurrent_kda(t["q"][:, sl], t["k"][:, sl], t["v"][:, sl], t["g"][:, sl],
                                            t["beta"][:, sl], A_log=t["A_log"], dt_bias=t["dt_bias"],
@@ -252,6 +247,43 @@ def test_decode_steps_match_oracle():
                                            use_qk_l2norm_in_kernel=True, use_gate_in_kernel=True,
                                            use_beta_sigmoid_in_kernel=True, lower_bound=-5.0)
             outs.append(o)
-    got = {"o": torch.cat(outs, dim=1).float().cpu(), "final_state": state.float().cpu()}
+    torch.cuda.synchronize()
+    assert _lib.device_error(reset=True) == 0
+    return {"o": torch.cat(outs, dim=1).double().cpu(), "final_state": state.double().cpu()}
+
+
+def test_decode_fp32_mode_matches_oracle_to_1e5():
+    """fp32 mode of the decode kernel: fp32 inputs, state and arithmetic, one
+    token per call, against the float64 oracle within 1e-5."""
+    case = Case("decode32", B=2, T=24, H=2, conv=False, h0=True, random_gate_params=True, seed=32)
+    inp = make_case_inputs(case)
+    ref = run_oracle(case, inputs=inp, grads=False)
+    got = _decode(inp, case.T, torch.float32)
+    for key in ("o", "final_state"):
+        torch.testing.assert_close(got[key], ref[key].double(), rtol=1e-5, atol=1e-5)
+
+
+def test_decode_steps_match_oracle():
+    """The decode seam (fused_recurrent_kda, one token per call, state carried
+    through initial_state) against the float64 oracle over the same tokens."""
+    from sophia_b200 import fused_recurrent_kda
+    case = Case("decode", B=2, T=24, H=2, conv=False, h0=True, random_gate_params=True, seed=31)
+    inp = round_inputs_bf16(make_case_inputs(case))
+    ref = run_oracle(case, inputs=inp, grads=False)
+    got = _decode(inp, case.T, torch.bfloat16)
     rep = compare(got, {k: ref[k] for k in ("o", "final_state")})
     assert not failures(rep, ref), rep
+    # the same tokens through the chunked kernels when gradients are wanted
+    dev = "cuda"
+    t = {k: inp[k].to(dev, torch.bfloat16 if k in ("q", "k", "v", "g", "beta") else torch.float32)
+         for k in ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "h0")}
+    t["q"].requires_grad_(True)
+    o, ht = fused_recurrent_kda(t["q"], t["k"], t["v"], t["g"], t["beta"], A_log=t["A_log"], dt_bias=t["dt_bias"],
+                                initial_state=t["h0"], output_final_state=True, use_qk_l2norm_in_kernel=True,
+                                use_gate_in_kernel=True, use_beta_sigmoid_in_kernel=True, lower_bound=-5.0)
+    o.float().sum().backward()
+    assert t["q"].grad is not None and torch.isfinite(t["q"].grad.float()).all()
+    # (the chunked path's own accuracy is what the parity tests above check)
+    rep = compare({"o": o.detach().double().cpu(), "final_state": ht.detach().double().cpu()},
+                  {k: ref[k] for k in ("o", "final_state")})
+    assert all(rel <= 1e-2 for _, rel in rep.values()), rep
