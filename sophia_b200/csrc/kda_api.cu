@@ -44,6 +44,7 @@ struct Carver {
 struct SavedView {
   bf16 *W, *U, *Qt, *Kb, *E, *M, *hs;
   float* dC;
+  float* A;  // [slots x H] fp32 64x64 tiles of A = (I + diag(beta) L')^-1 (training only)
 };
 
 SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) {
@@ -58,9 +59,11 @@ SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) 
   if (with_bwd) {
     s.E = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.hs = cv.take<bf16>((size_t)mc * H * STATE_ELEMS * 2);
+    s.A = cv.take<float>((size_t)mc * H * TILE64N64_ELEMS * 4);
   } else {
     s.E = nullptr;
     s.hs = nullptr;
+    s.A = nullptr;
   }
   return s;
 }
@@ -358,7 +361,7 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.in = prologue_in(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, H, scale, lower_bound);
   ip.seq = pr.seq;
   ip.conv = pr.conv;
-  ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC;
+  ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A;
   if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
   {
     TimedLaunch tl(K_FWD_INTRA, st);
@@ -448,6 +451,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   bi.seq = pr.seq;
   bi.conv = pr.conv;
   bi.dE = bv.dE; bi.dW = bv.dW; bi.dQt = bv.dQt; bi.dKb = bv.dKb; bi.dM = bv.dM; bi.dGC = bv.dGC;
+  bi.A = sv.A;
   bi.dq_hat = bv.dq_hat;
   bi.dk_hat = bv.dk_hat;
   bi.dv = pr.conv ? bv.dv_hat : static_cast<bf16*>(dv);

@@ -1,7 +1,8 @@
 // Chunk-parallel backward of the chunked KDA layer.
 //
 // One CTA per (chunk, head).  Recomputes the prologue and the intra-chunk
-// quantities (operand tiles, L', A = (I + diag(beta) L')^-1, T = A diag(beta)),
+// quantities (operand tiles, L'; A = (I + diag(beta) L')^-1 is the forward's
+// saved copy, T = A diag(beta)),
 // then, from the state-pass gradient pieces (dE, dW, dQt, dKbar, dM, dGC):
 //   dv  = T^T dE                      (written out as the value gradient)
 //   dKe = T^T dW,  dT = dE v^T + dW Ke^T,  dbeta += colsum(dT o A)
@@ -38,6 +39,7 @@ struct BwdIntraParams {
   SeqInfo seq;
   bool conv;
   const bf16 *dE, *dW, *dQt, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
+  const float* A;                        // [chunks][H] fp32 64x64 tiles saved by the forward
   const float* dGC;
   bf16 *dq_hat, *dk_hat, *dv;  // [T_total][H][128]
   bf16 *dg, *dbeta;            // [T_total][H][128], [T_total][H]
@@ -59,8 +61,8 @@ struct BwdIntraSmem {
   static constexpr int END = BRAW + 64 * 2;
   // RAW aliases after the operands are built
   static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
-  static constexpr int AINV = RAW + 16640;                   // fp32 64 x LDF64
-  static constexpr int XTMP = RAW + 33280;                   // fp32 3 warps x 16 x 17
+  static constexpr int AINV = RAW + 16640;                   // fp32 [64][64] A from the forward (until the T build;
+                                                             // DMS reuses part of it afterwards)
   static constexpr int LPB = RAW + 33280;                    // bf16 64 x LD64 (after inverse)
   static constexpr int ABF = RAW;                            // bf16 64 x LD64 (after Lp fp32 is dead)
   static constexpr int TBF = RAW + 42496;                    // bf16 64 x LD64
@@ -71,7 +73,7 @@ struct BwdIntraSmem {
   static constexpr int COLS = DBL + 1024;                    // fp32 4 x 128  (sum Kbar o dKbar)
   static_assert(COLS + 2048 <= LPB, "small tiles overlap Lp bf16");
   static_assert(TBF + 64 * LD64 * 2 <= RAWSZ + RAW, "T tile overflows");
-  static_assert(XTMP + 3 * 16 * 17 * 4 <= TBF, "inverse scratch overlaps T");
+  static_assert(AINV + 64 * 64 * 4 <= LPB && AINV % 16 == 0, "A tile overlaps Lp bf16 or is misaligned");
   // DEW aliases after the WY backward
   static constexpr int DAS = DEW;                            // bf16 64 x LD64
   static constexpr int XS = DEW + 9216;                      // bf16 64 x LD64
@@ -152,14 +154,19 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     bf16* dst = which ? dKs : dQs;
     cp_async16(dst + r * D + ((cc ^ (r & 7)) << 3), src, r < nv);
   }
+  // A = (I + diag(beta) L')^-1 as the forward computed it: [64][64] fp32 in
+  // the dead raw region (clear of Lp, which l_blocks writes below)
+  float* Asm = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
+  {
+    const float* src = P.A + tix * TILE64N64_ELEMS;
+    for (int i = tid; i < 64 * 16; i += blockDim.x) cp_async16(Asm + i * 4, src + i * 4, true);
+  }
   cp_async_commit();
 
   float* Lp = reinterpret_cast<float*>(smem + BwdIntraSmem::LP);
-  float* Ainv = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
-  float* xtmp = reinterpret_cast<float*>(smem + BwdIntraSmem::XTMP);
   l_blocks(op, Lp);
+  cp_async_wait<0>();  // dE, dW, dQt, dKbar, A
   __syncthreads();
-  tri_inverse(Lp, ps.beta, Ainv, xtmp);
   bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
   for (int i = tid; i < 64 * 32; i += blockDim.x) {
     int r = i >> 5, cc = 2 * (i & 31);
@@ -171,11 +178,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   bf16* Abf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::ABF);
   bf16* Tbf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::TBF);
   {
-    // Ainv (fp32 at [16640, 33280)) -> Abf ([0, 9216)) and Tbf: Abf only overlaps the dead Lp
+    // A (fp32 at [16640, 33024)) -> Abf ([0, 9216)) and Tbf: Abf only overlaps the dead Lp
     float av[8];
     const int r = tid >> 3, c0 = (tid & 7) * 8;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Ainv[r * LDF64 + c0 + i] : 0.f;
+    for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Asm[r * 64 + c0 + i] : 0.f;
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
@@ -192,7 +199,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     cp_async16(dMs + r * LD64 + cc * 8, P.dM + tix * TILE64N64_ELEMS + idx * 8, r < nv);
   }
   cp_async_commit();
-  cp_async_wait<1>();  // dE, dW, dQt, dKbar
   __syncthreads();
 
   float dq[4][4], dk[4][4], dG[4][4];

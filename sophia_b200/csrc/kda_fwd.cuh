@@ -19,6 +19,7 @@ struct FwdIntraParams {
   bool conv;
   bf16 *W, *U, *Qt, *Kb, *M;  // [T_total][H][128] (M: [T_total][H][64])
   float* dC;                  // [chunks][H][128]
+  float* A;                   // [slots x H] fp32 64x64 tiles of A (the backward's copy), or null
 };
 
 // Shared-memory layout of the intra kernels (bytes).
@@ -138,6 +139,14 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
     float x0 = (cc <= r) ? Ainv[r * LDF64 + cc] * ps.beta[cc] : 0.f;
     float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
     *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
+  }
+  if (P.A) {  // A for the backward (entries above the diagonal are not meaningful)
+    float* dst = P.A + tile_index(P.seq, c, h) * TILE64N64_ELEMS;
+    for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
+      const int r = i >> 4, c4 = (i & 15) * 4;
+      const float* src = Ainv + r * LDF64 + c4;
+      *reinterpret_cast<float4*>(dst + r * 64 + c4) = make_float4(src[0], src[1], src[2], src[3]);
+    }
   }
   store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
   __syncthreads();

@@ -204,16 +204,26 @@ __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const Pro
     sm.beta[tid] = (tid < nvalid) ? sigmoidf_(b) : 0.f;
   }
   __syncthreads();
-  // exclusive prefix of the 16 warp totals, per channel, in place (one thread
-  // per channel walks the 16 rows)
-  if (tid < D) {
-    float acc = 0.f;
-#pragma unroll
-    for (int u = 0; u < INTRA_WARPS; ++u) {
-      float t = sm.tot[u * D + tid];
-      sm.tot[u * D + tid] = acc;
-      acc += t;
-    }
+  // exclusive prefix of the 16 warp totals, per channel, in place: warp w
+  // takes channels 8w .. 8w+7, four lanes per channel, four totals per lane,
+  // then a two-step shuffle scan over the four lanes
+  static_assert(INTRA_WARPS == 16 && INTRA_THREADS == 4 * D, "prefix layout");
+  {
+    const int ch = 8 * warp + (lane >> 2), part = lane & 3;
+    float* col = sm.tot + 4 * part * D + ch;
+    const float v0 = col[0], v1 = col[D], v2 = col[2 * D], v3 = col[3 * D];
+    const float own = (v0 + v1) + (v2 + v3);
+    float incl = own;
+    float y = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (part >= 1) incl += y;
+    y = __shfl_up_sync(0xffffffffu, incl, 2);
+    if (part >= 2) incl += y;
+    float ex = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (part == 0) ex = 0.f;
+    col[0] = ex;
+    col[D] = ex + v0;
+    col[2 * D] = (ex + v0) + v1;
+    col[3 * D] = ((ex + v0) + v1) + v2;
   }
   __syncthreads();
   float off[8];
