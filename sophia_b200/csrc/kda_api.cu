@@ -483,9 +483,10 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   {
     TimedLaunch tl(K_BWD_POST, st);
     if (pr.conv)
-      kda_bwd_post_kernel<true><<<dim3(pr.grid_chunks, H, 3), POST_THREADS, POST_DC_BYTES, st>>>(pp);
+      kda_bwd_post_conv_kernel<<<dim3((pr.grid_chunks + POST_CHUNKS_PER_CTA - 1) / POST_CHUNKS_PER_CTA, H, 3),
+                                 32 * POST_CHUNKS_PER_CTA, 0, st>>>(pp);
     else
-      kda_bwd_post_kernel<false><<<dim3(pr.grid_chunks, H, 2), POST_THREADS, 0, st>>>(pp);
+      kda_bwd_post_norm_kernel<<<dim3(pr.grid_chunks, H, 2), POST_THREADS, 0, st>>>(pp);
   }
   if ((rc = launch_check("bwd post"))) return rc;
 

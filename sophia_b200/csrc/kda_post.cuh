@@ -1,14 +1,15 @@
 // Backward epilogue: L2-norm and ShortConv(+SiLU) backward, and the final
 // deterministic reductions of the per-chunk partial sums.
 //
-//   kda_bwd_post_kernel  (one CTA per (chunk, head, tensor))
+//   kda_bwd_post_conv_kernel  (one warp per (chunk, head, tensor))
 //     given dq_hat / dk_hat (gradients of the normalised inputs) and dv from
 //     the chunk kernel, recomputes the conv output c = conv(x), y = silu(c)
 //     and the norms, then
 //       dy  = (dn - n (n . dn)) / max(|y|, eps)     (q: dn = scale dq_hat)
 //       dc  = dy * silu'(c)
 //       dx_t = sum_s w_s dc_(t+3-s),   dw_s += sum_t dc_t x_(t-3+s)
-//     Without the conv, only the L2-norm backward runs (dv passes through).
+//   kda_bwd_post_norm_kernel: without the conv, only the L2-norm backward of
+//     q and k (dv passes through).
 //   kda_reduce_kernel: dA_log, dt_bias and conv-tap gradients, summed over
 //     chunks in a fixed order.
 #pragma once
@@ -29,16 +30,10 @@ struct PostParams {
   float* partW;                                 // [chunks][3][H][128][4]
 };
 
-// One CTA per (chunk, head, tensor), 256 threads: warp w owns dc rows
-// 8w .. 8w+7 and lane l channels 4l .. 4l+3, so a warp covers whole rows (the
-// L2 norm of a row is a warp shuffle reduction) and each 8-byte load of a row
-// is part of one 256-byte coalesced access.  A thread's conv input rows (x rows
-// 8w-3 .. 8w+7) and gradient rows are loaded straight from global memory into
-// registers, all in flight together.  The fp32 dc tile goes through shared
-// memory because the conv backward of row t needs dc rows t .. t+3; rows
-// 64 .. 66 are the next chunk's first rows and are computed by warp 7.
+// Lane l of a warp owns channels 4l .. 4l+3 of a row, so a warp covers whole
+// rows (the L2 norm of a row is a warp shuffle reduction) and each 8-byte
+// load of a row is part of one 256-byte coalesced access.
 constexpr int POST_THREADS = 256;
-constexpr int POST_DC_BYTES = 67 * D * 4;
 
 struct alignas(8) bf16x4 { uint32_t u[2]; };
 
@@ -84,73 +79,33 @@ __device__ __forceinline__ void post_norm_bwd(const float (&y)[4], const float (
   }
 }
 
-// dc of one row: conv c from x rows row-3 .. row, SiLU y = c sigmoid(c) and
-// sigmoid(c) from one tanh.approx (the forward prologue's silu_fast on the
-// same c), the L2-norm backward (q, k), dc = dy sigmoid(c) (1 + c (1 - sigmoid(c)));
-// zero for rows past the sequence end.
-__device__ __forceinline__ float4 post_dc_row(const bf16x4& x0, const bf16x4& x1, const bf16x4& x2,
-                                              const bf16x4& x3, const float (&wt)[4][4], const bf16x4& gr,
-                                              bool rowok, bool norm, float dscale) {
-  float xa[4][4];
-  unpack4(x0, xa[0]); unpack4(x1, xa[1]); unpack4(x2, xa[2]); unpack4(x3, xa[3]);
-  float cv[4], y[4], sg[4], g[4], dyv[4];
-#pragma unroll
-  for (int ch = 0; ch < 4; ++ch) {
-    const float a = wt[ch][0] * xa[0][ch] + wt[ch][1] * xa[1][ch] + wt[ch][2] * xa[2][ch] + wt[ch][3] * xa[3][ch];
-    const float hh = 0.5f * a, t = tanh_fast(hh);
-    cv[ch] = a;
-    y[ch] = fmaf(hh, t, hh);
-    sg[ch] = fmaf(0.5f, t, 0.5f);
-  }
-  unpack4(gr, g);
-  if (norm) {
-    post_norm_bwd(y, g, dscale, dyv);
-  } else {
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch) dyv[ch] = g[ch];
-  }
-  float dc[4];
-#pragma unroll
-  for (int ch = 0; ch < 4; ++ch) dc[ch] = rowok ? dyv[ch] * sg[ch] * (1.f + cv[ch] * (1.f - sg[ch])) : 0.f;
-  return make_float4(dc[0], dc[1], dc[2], dc[3]);
-}
+// Conv variant, one warp per (chunk, head, tensor), four chunks per CTA.  The
+// warp walks rows r = 0 .. 66 of its chunk (rows 64 .. 66 are the next
+// chunk's first rows, whose dc the conv backward of rows 61 .. 63 needs) with
+// sliding four-row windows of x (conv inputs) and dc in registers; lane l owns
+// channels 4l .. 4l+3, so the L2 norm of a row is a warp reduction.  Per row:
+//   c = sum_s w_s x_(r-3+s), y = silu(c), dc_r = (norm backward of dy_r) silu'(c)
+//   dw_s += dc_r x_(r-3+s)                       (own rows r < 64)
+//   dx_(r-3) = sum_s w_s dc_(r-s)                (r >= 3)
+// No shared memory and no barrier; the tap-gradient partial of the chunk
+// leaves straight from the lanes.
+constexpr int POST_CHUNKS_PER_CTA = 4;
+constexpr int POST_GROUP = 4;  // rows per prefetch group
 
-template <bool CONV>
-__global__ void __launch_bounds__(POST_THREADS, 2) kda_bwd_post_kernel(PostParams P) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int c = blockIdx.x, h = blockIdx.y, X = blockIdx.z, H = P.H;
+__global__ void __launch_bounds__(32 * POST_CHUNKS_PER_CTA) kda_bwd_post_conv_kernel(PostParams P) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * POST_CHUNKS_PER_CTA + warp, h = blockIdx.y, X = blockIdx.z, H = P.H;
   const ChunkPos pos = chunk_pos(P.seq, c);
-  if (!pos.valid) return;
+  if (!pos.valid) return;  // warp-uniform
   const int eos = seq_eos(P.seq, pos.seq);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const size_t rowH = (size_t)H * D;
   const bf16* x = X == 0 ? P.q : (X == 1 ? P.k : P.v);
   const bf16* gy = X == 0 ? P.dq_hat : (X == 1 ? P.dk_hat : P.dv_hat);
   bf16* dx = X == 0 ? P.dq : (X == 1 ? P.dk : P.dv);
   const float dscale = X == 0 ? P.scale : 1.f;
-  const int r0 = 8 * warp;  // first row of this warp
+  const bool norm = X < 2;
 
-  if (!CONV) {  // L2-norm backward only (q and k)
-    bf16x4 xr[8], gr[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int t = pos.t0 + r0 + j;
-      xr[j] = post_ld(x, t, t < pos.t1, rowH, h, lane);
-      gr[j] = post_ld(gy, t, t < pos.t1, rowH, h, lane);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float y[4], g[4], dyv[4];
-      unpack4(xr[j], y);
-      unpack4(gr[j], g);
-      post_norm_bwd(y, g, dscale, dyv);
-      const int t = pos.t0 + r0 + j;
-      if (t < pos.t1) *reinterpret_cast<bf16x4*>(dx + (size_t)t * rowH + (size_t)h * D + 4 * lane) = pack4(dyv);
-    }
-    return;
-  }
-
-  float wt[4][4];
+  float wt[4][4];  // [channel][tap]
   {
     const float4* w = reinterpret_cast<const float4*>((X == 0 ? P.conv_q : (X == 1 ? P.conv_k : P.conv_v)) +
                                                       ((size_t)h * D + 4 * lane) * 4);
@@ -160,84 +115,123 @@ __global__ void __launch_bounds__(POST_THREADS, 2) kda_bwd_post_kernel(PostParam
       wt[ch][0] = t4.x; wt[ch][1] = t4.y; wt[ch][2] = t4.z; wt[ch][3] = t4.w;
     }
   }
-  const bool norm = X < 2;
-  float4* dcs = reinterpret_cast<float4*>(smem);  // [67 rows][32 lanes]
-  // x rows r0-3 .. r0+7 (zero before the sequence start and past its end)
-  bf16x4 xr[11], gr[8];
-#pragma unroll
-  for (int j = 0; j < 11; ++j) {
-    const int t = pos.t0 + r0 - 3 + j;
-    xr[j] = post_ld(x, t, t >= pos.bos && t < eos, rowH, h, lane);
+  float x0[4], x1[4], x2[4];  // x rows r-3, r-2, r-1
+  float d0[4], d1[4], d2[4];  // dc rows r-3, r-2, r-1
+  float acc[4][4];            // tap gradients [channel][tap]
+  {
+    const int t = pos.t0 - 3;
+    unpack4(post_ld(x, t, t >= pos.bos, rowH, h, lane), x0);
+    unpack4(post_ld(x, t + 1, t + 1 >= pos.bos, rowH, h, lane), x1);
+    unpack4(post_ld(x, t + 2, t + 2 >= pos.bos, rowH, h, lane), x2);
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int t = pos.t0 + r0 + j;
-    gr[j] = post_ld(gy, t, t < eos, rowH, h, lane);
+  for (int ch = 0; ch < 4; ++ch) {
+    d0[ch] = d1[ch] = d2[ch] = 0.f;
+    acc[ch][0] = acc[ch][1] = acc[ch][2] = acc[ch][3] = 0.f;
   }
+  // rows go in groups of POST_GROUP; the next group's x and dy rows are loaded
+  // before the current group is computed, so loads overlap a group of work
+  constexpr int G = POST_GROUP, NG = (C + 3 + G - 1) / G;
+  bf16x4 nx[G], ngy[G];
+  auto load_group = [&](int grp) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
-    dcs[(r0 + j) * 32 + lane] =
-        post_dc_row(xr[j], xr[j + 1], xr[j + 2], xr[j + 3], wt, gr[j], pos.t0 + r0 + j < eos, norm, dscale);
-  if (warp == 7) {  // dc rows 64 .. 66: the next chunk's first rows (x rows 61 .. 66)
-    bf16x4 xe[6], ge[3];
-#pragma unroll
-    for (int j = 0; j < 6; ++j) {
-      const int t = pos.t0 + 61 + j;
-      xe[j] = post_ld(x, t, t < eos, rowH, h, lane);
+    for (int j = 0; j < G; ++j) {
+      const int r = grp * G + j, t = pos.t0 + r;
+      const bool ok = r < C + 3 && t < eos;
+      nx[j] = post_ld(x, t, ok, rowH, h, lane);
+      ngy[j] = post_ld(gy, t, ok, rowH, h, lane);
     }
+  };
+  load_group(0);
+#pragma unroll 1
+  for (int grp = 0; grp < NG; ++grp) {
+    bf16x4 cx[G], cgy[G];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      const int t = pos.t0 + 64 + j;
-      ge[j] = post_ld(gy, t, t < eos, rowH, h, lane);
+    for (int j = 0; j < G; ++j) { cx[j] = nx[j]; cgy[j] = ngy[j]; }
+    if (grp + 1 < NG) load_group(grp + 1);
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int r = grp * G + j, t = pos.t0 + r;
+      if (r >= C + 3) break;
+      const bool rowok = t < eos;
+      float xn[4], g[4];
+      unpack4(cx[j], xn);
+      unpack4(cgy[j], g);
+      float cv[4], y[4], sg[4];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const float a = wt[ch][0] * x0[ch] + wt[ch][1] * x1[ch] + wt[ch][2] * x2[ch] + wt[ch][3] * xn[ch];
+        const float hh = 0.5f * a, th = tanh_fast(hh);
+        cv[ch] = a;
+        y[ch] = fmaf(hh, th, hh);
+        sg[ch] = fmaf(0.5f, th, 0.5f);
+      }
+      float dyv[4];
+      if (norm) {
+        post_norm_bwd(y, g, dscale, dyv);
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) dyv[ch] = g[ch];
+      }
+      float dn[4];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) dn[ch] = rowok ? dyv[ch] * sg[ch] * (1.f + cv[ch] * (1.f - sg[ch])) : 0.f;
+      if (r < C) {
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          acc[ch][0] += dn[ch] * x0[ch];
+          acc[ch][1] += dn[ch] * x1[ch];
+          acc[ch][2] += dn[ch] * x2[ch];
+          acc[ch][3] += dn[ch] * xn[ch];
+        }
+      }
+      if (r >= 3 && t - 3 < pos.t1) {
+        float dxv[4];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch)
+          dxv[ch] = wt[ch][0] * dn[ch] + wt[ch][1] * d2[ch] + wt[ch][2] * d1[ch] + wt[ch][3] * d0[ch];
+        *reinterpret_cast<bf16x4*>(dx + (size_t)(t - 3) * rowH + (size_t)h * D + 4 * lane) = pack4(dxv);
+      }
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        x0[ch] = x1[ch]; x1[ch] = x2[ch]; x2[ch] = xn[ch];
+        d0[ch] = d1[ch]; d1[ch] = d2[ch]; d2[ch] = dn[ch];
+      }
     }
-#pragma unroll
-    for (int j = 0; j < 3; ++j)
-      dcs[(64 + j) * 32 + lane] =
-          post_dc_row(xe[j], xe[j + 1], xe[j + 2], xe[j + 3], wt, ge[j], pos.t0 + 64 + j < eos, norm, dscale);
   }
-  __syncthreads();
+  float4* dst = reinterpret_cast<float4*>(P.partW + (((size_t)c * 3 + X) * H + h) * D * 4) + 4 * lane;
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) dst[ch] = make_float4(acc[ch][0], acc[ch][1], acc[ch][2], acc[ch][3]);
+}
 
-  // conv backward: dx_t = sum_s w_s dc_(t+3-s), dw_s += dc_t x_(t-3+s)
-  float acc[4][4];
-#pragma unroll
-  for (int ch = 0; ch < 4; ++ch) acc[ch][0] = acc[ch][1] = acc[ch][2] = acc[ch][3] = 0.f;
-  float4 win[4];  // dc rows t .. t+3 (ring)
-#pragma unroll
-  for (int i = 0; i < 3; ++i) win[i] = dcs[(r0 + i) * 32 + lane];
+// Without the conv: the L2-norm backward of q and k alone (dv passes
+// through).  One CTA per (chunk, head, tensor); warp w takes rows 8w .. 8w+7.
+__global__ void __launch_bounds__(POST_THREADS) kda_bwd_post_norm_kernel(PostParams P) {
+  const int c = blockIdx.x, h = blockIdx.y, X = blockIdx.z, H = P.H;
+  const ChunkPos pos = chunk_pos(P.seq, c);
+  if (!pos.valid) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const size_t rowH = (size_t)H * D;
+  const bf16* x = X == 0 ? P.q : P.k;
+  const bf16* gy = X == 0 ? P.dq_hat : P.dk_hat;
+  bf16* dx = X == 0 ? P.dq : P.dk;
+  const float dscale = X == 0 ? P.scale : 1.f;
+  const int r0 = 8 * warp;
+  bf16x4 xr[8], gr[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    win[(j + 3) & 3] = dcs[(r0 + j + 3) * 32 + lane];
-    const float4 d0 = win[j & 3], d1 = win[(j + 1) & 3], d2 = win[(j + 2) & 3], d3 = win[(j + 3) & 3];
-    const float e0[4] = {d0.x, d0.y, d0.z, d0.w}, e1[4] = {d1.x, d1.y, d1.z, d1.w};
-    const float e2[4] = {d2.x, d2.y, d2.z, d2.w}, e3[4] = {d3.x, d3.y, d3.z, d3.w};
-    float xs[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) unpack4(xr[j + i], xs[i]);
-    float dxv[4];
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      dxv[ch] = wt[ch][0] * e3[ch] + wt[ch][1] * e2[ch] + wt[ch][2] * e1[ch] + wt[ch][3] * e0[ch];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[ch][i] += e0[ch] * xs[i][ch];
-    }
     const int t = pos.t0 + r0 + j;
-    if (t < pos.t1) *reinterpret_cast<bf16x4*>(dx + (size_t)t * rowH + (size_t)h * D + 4 * lane) = pack4(dxv);
+    xr[j] = post_ld(x, t, t < pos.t1, rowH, h, lane);
+    gr[j] = post_ld(gy, t, t < pos.t1, rowH, h, lane);
   }
-  // tap-gradient partial of this chunk: the eight warps through shared memory
-  // (reusing the dc tile), added in a fixed order
-  __syncthreads();
-  float4* red = dcs;  // [8 warps][128 channels] of 4 taps
 #pragma unroll
-  for (int ch = 0; ch < 4; ++ch) red[warp * D + 4 * lane + ch] = make_float4(acc[ch][0], acc[ch][1], acc[ch][2], acc[ch][3]);
-  __syncthreads();
-  if (tid < D) {
-    float4 s4 = red[tid];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) {
-      const float4 a = red[w * D + tid];
-      s4.x += a.x; s4.y += a.y; s4.z += a.z; s4.w += a.w;
-    }
-    reinterpret_cast<float4*>(P.partW + (((size_t)c * 3 + X) * H + h) * D * 4)[tid] = s4;
+  for (int j = 0; j < 8; ++j) {
+    float y[4], g[4], dyv[4];
+    unpack4(xr[j], y);
+    unpack4(gr[j], g);
+    post_norm_bwd(y, g, dscale, dyv);
+    const int t = pos.t0 + r0 + j;
+    if (t < pos.t1) *reinterpret_cast<bf16x4*>(dx + (size_t)t * rowH + (size_t)h * D + 4 * lane) = pack4(dyv);
   }
 }
 
