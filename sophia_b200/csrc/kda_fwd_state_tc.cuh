@@ -3,14 +3,18 @@
 // One CTA (256 threads) per (sequence, head) walks the chunks in order.  The
 // 128x128 fp32 state S lives in TMEM (columns 128..255, one lane per state
 // row k); its bf16 copy in shared memory (128B-swizzled, rows k) is the B
-// operand of the chunk products.  Per chunk:
-//   MMA  E_acc = W S            (M=64 tokens, TMEM lanes 0-15 of each quarter)
-//   MMA  O_acc = Qt S           (M=64, lanes 16-31 of each quarter, same columns)
-//   epilogue: E = U - E_acc  -> bf16 tile (B operand) and v_new for the backward
-//   MMA  O_acc += M E
-//   MMA  S    += Kbar^T E       (M=128; S was pre-scaled by 2^Gam_C)
-//   epilogue: o out; S -> bf16 tile + chunk-start state for the backward, then
-//             S <- diag(2^Gam_C of the next chunk) S in TMEM.
+// operand of the chunk products.  E and O accumulate in one of two 128-column
+// TMEM buffers (E in lanes 0-15 and O in lanes 16-31 of each quarter),
+// alternating by chunk.  Per chunk, only true dependencies sit between the
+// MMAs:
+//   MMA  E_acc = W S, O_acc = Qt S       (M=64 each, from the bf16 state tile)
+//     meanwhile: S <- diag(2^Gam_C) S in TMEM from the registers of the last
+//     S epilogue, the chunk-start state out, the previous chunk's o staged in
+//     shared memory, the next chunk's loads issued
+//   epilogue: E = U - E_acc -> bf16 tile (B operand) and v_new for the backward
+//   MMA  O_acc += M E ; S += Kbar^T E    (M=64 / M=128)
+//     meanwhile: the staged o rows of the previous chunk leave, coalesced
+//   epilogue: S -> registers -> bf16 tile for the next chunk.
 // One thread issues the MMAs; completion is tracked with mbarriers whose waits
 // are bounded: on a timeout the CTA records an error and leaves through its
 // cleanup path (TMEM is always released).  Chunk inputs are double-buffered
@@ -35,9 +39,11 @@ struct StateTcSmem {
   static constexpr int NSTAGE = 2;                      // current chunk + the next one
   static constexpr int S = NSTAGE * STAGE;              // [128][128] bf16, two 16 KB atoms
   static constexpr int E = S + 32768;                   // [64][128] bf16, two 8 KB atoms
-  static constexpr int MISC = E + 16384;                // mbarriers, TMEM slot, abort flag
+  static constexpr int OST = E + 16384;                 // [64][LD128] bf16 staged o rows
+  static constexpr int MISC = OST + 64 * LD128 * 2;     // mbarriers, TMEM slot, abort flag
   static constexpr int END = MISC + 64;
   static_assert(DC + 512 <= STAGE, "stage overflow");
+  static_assert(END <= 232448, "fwd state (tcgen05) shared memory");
 };
 
 __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams P) {
@@ -60,13 +66,14 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
     if (tid == 0) atomicExch(&g_kda_device_error, 2);
     return;
   }
-  if (warp == 0) tc::tmem_alloc(tslot, 256);
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
   if (tid == 0) {
     tc::mbar_init(mbarE, 1);
     tc::mbar_init(mbarS, 1);
     tc::fence_mbar_init();
     *abort_flag = 0;
   }
+  bf16* ost = reinterpret_cast<bf16*>(smem + StateTcSmem::OST);
   auto issue = [&](int ci) {
     unsigned char* base = smem + (ci % StateTcSmem::NSTAGE) * StateTcSmem::STAGE;
     int t0 = bos + ci * C;
@@ -86,15 +93,18 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = *tslot;
-  const uint32_t tE = tbase + ((uint32_t)(32 * sub) << 16) + 64 * half;       // E (lanes <16) / O (lanes >=16)
-  const uint32_t tS = tbase + ((uint32_t)(32 * sub) << 16) + 128 + 64 * half;  // state rows
-  const int krow = 32 * sub + lane;                                            // state row of this thread
+  const uint32_t tq = (uint32_t)(32 * sub) << 16;
+  const uint32_t tS = tbase + tq + 128 + 64 * half;  // state rows
+  // E/O buffer b: lane 0 (E) / lane 16 (O) accumulators at column base 0 or 256
+  auto eo_col = [&](int b) { return b ? 256u : 0u; };
+  auto tEO = [&](int b) { return tbase + tq + eo_col(b) + 64 * half; };
+  const int krow = 32 * sub + lane;                  // state row of this thread
+  const int arow = 16 * sub + (lane & 15);           // chunk row of this thread (M=64 layout)
   const uint32_t idE = tc::idesc_bf16(64, 128, false, true);
   const uint32_t idS = tc::idesc_bf16(128, 128, true, true);
 
-  // state row krow, columns [64 half, 64 half + 64): fp32 -> bf16 operand tile,
-  // optionally the chunk-start copy for the backward
-  auto store_state = [&](const float (&v)[64], int chunk_for_hs) {
+  // state row krow, columns [64 half, 64 half + 64): fp32 -> bf16 operand tile
+  auto store_tile = [&](const float (&v)[64]) {
     unsigned char* atom = sS + half * 16384;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -104,28 +114,63 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
       pk.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
       pk.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
       *reinterpret_cast<uint4*>(atom + krow * 128 + ((c ^ (krow & 7)) << 4)) = pk;
-      if (P.hs && chunk_for_hs >= 0)
-        *reinterpret_cast<uint4*>(P.hs + tile_index(P.seq, chunk_for_hs, h) * STATE_ELEMS +
-                                  st128_off(krow, 64 * half + 8 * c)) = pk;
+    }
+  };
+  // the same row -> chunk-start state tile of the backward (st128 order)
+  auto store_hs = [&](const float (&v)[64], int chunk) {
+    if (!P.hs) return;
+    bf16* dst = P.hs + tile_index(P.seq, chunk, h) * STATE_ELEMS;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 pk;
+      pk.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
+      pk.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+      pk.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+      pk.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+      *reinterpret_cast<uint4*>(dst + st128_off(krow, 64 * half + 8 * c)) = pk;
+    }
+  };
+  // O rows of buffer b (lanes 16-31) -> staging tile
+  auto stage_o = [&](int b) {
+#pragma unroll
+    for (int c0 = 0; c0 < 64; c0 += 32) {
+      float acc[32];
+      tc::tmem_ld32(tEO(b) + c0, acc);
+      if (lane >= 16) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 pk;
+          pk.x = pack_bf16(acc[8 * c + 0], acc[8 * c + 1]);
+          pk.y = pack_bf16(acc[8 * c + 2], acc[8 * c + 3]);
+          pk.z = pack_bf16(acc[8 * c + 4], acc[8 * c + 5]);
+          pk.w = pack_bf16(acc[8 * c + 6], acc[8 * c + 7]);
+          *reinterpret_cast<uint4*>(ost + arow * LD128 + 64 * half + c0 + 8 * c) = pk;
+        }
+      }
+    }
+  };
+  // staged o rows of chunk ci -> global, 16 threads per 256-byte row
+  auto copy_o = [&](int ci) {
+    const int t0 = bos + ci * C, nv = min(C, eos - t0);
+    for (int i = tid; i < 64 * 16; i += blockDim.x) {
+      const int r = i >> 4, cc = i & 15;
+      if (r < nv)
+        *reinterpret_cast<uint4*>(P.o + ((size_t)(t0 + r) * H + h) * D + 8 * cc) =
+            *reinterpret_cast<const uint4*>(ost + r * LD128 + 8 * cc);
     }
   };
 
-  // initial state: h0 (or zeros) -> operand tile, TMEM pre-scaled by the first chunk's decay
+  // v: this thread's state row (64 columns), unscaled, from an S epilogue (or
+  // h0) to the next chunk's scaling
+  float v[64];
   if (nchunks > 0) {
-    float v[64];
     const float* h0 = P.h0 ? P.h0 + (((size_t)n * H + h) * D + krow) * D + 64 * half : nullptr;
 #pragma unroll
     for (int i = 0; i < 64; i += 4) {
       float4 x = h0 ? *reinterpret_cast<const float4*>(h0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
       v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
     }
-    store_state(v, cbase);
-    const float dc = reinterpret_cast<const float*>(smem + StateTcSmem::DC)[krow];
-    float a[32], b[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) { a[i] = v[i] * dc; b[i] = v[32 + i] * dc; }
-    tc::tmem_st32(tS, a);
-    tc::tmem_st32(tS + 32, b);
+    store_tile(v);
   } else if (P.ht) {
     // empty sequence: the final state is the initial state
     const float* h0 = P.h0 ? P.h0 + (((size_t)n * H + h) * D + krow) * D + 64 * half : nullptr;
@@ -139,37 +184,48 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
   bool ok = true;
   for (int ci = 0; ci < nchunks && ok; ++ci) {
     unsigned char* buf = smem + (ci % StateTcSmem::NSTAGE) * StateTcSmem::STAGE;
-    const int t0 = bos + ci * C;
-    const int nv = min(C, eos - t0);
     const bool last = ci + 1 == nchunks;
-    // stage (ci+1)%2 held chunk ci-1, whose MMAs and epilogues are finished
-    if (!last) issue(ci + 1);
-    cp_async_commit();
-    // E = W S, O = Qt S
+    const int eo = ci & 1;
+    // E = W S, O = Qt S into buffer eo
     if (tid == 0) {
       tc::fence_after_sync();
       const uint32_t w0 = smem_u32(buf + StateTcSmem::W), q0 = smem_u32(buf + StateTcSmem::QT);
       const uint32_t s0 = smem_u32(sS);
+      const uint32_t dE = tbase + eo_col(eo);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
         uint64_t bd = tc::smem_desc(s0 + ks * 2048, 16384, 1024);
-        tc::mma_bf16(tbase, tc::smem_desc(w0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), bd, idE, ks > 0);
-        tc::mma_bf16(tbase + (16u << 16), tc::smem_desc(q0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), bd, idE,
+        tc::mma_bf16(dE, tc::smem_desc(w0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), bd, idE, ks > 0);
+        tc::mma_bf16(dE + (16u << 16), tc::smem_desc(q0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), bd, idE,
                      ks > 0);
       }
       tc::mma_commit(mbarE);
     }
+    // S <- diag(2^Gam_C) S in TMEM from the registers; chunk-start state out
+    {
+      const float dc = reinterpret_cast<const float*>(buf + StateTcSmem::DC)[krow];
+      float a[32], b[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) { a[i] = v[i] * dc; b[i] = v[32 + i] * dc; }
+      tc::tmem_st32(tS, a);
+      tc::tmem_st32(tS + 32, b);
+      store_hs(v, cbase + ci);
+    }
+    if (ci > 0) stage_o(eo ^ 1);  // o of the previous chunk (its MMAs are complete)
+    // stage (ci+1)%2 held chunk ci-1, whose MMAs are finished
+    if (!last) issue(ci + 1);
+    cp_async_commit();
     if (!tc::mbar_wait(mbarE, ci & 1)) *abort_flag = 1;
     tc::fence_after_sync();
     // E = U - E_acc (threads holding E rows: lanes 0-15)
     {
-      const int r = 16 * sub + (lane & 15);
+      const int r = arow;
       const unsigned char* uat = buf + StateTcSmem::U + half * 8192;
       unsigned char* eat = sE + half * 8192;
 #pragma unroll
       for (int c0 = 0; c0 < 64; c0 += 32) {
         float acc[32];
-        tc::tmem_ld32(tE + c0, acc);
+        tc::tmem_ld32(tEO(eo) + c0, acc);
         if (lane < 16) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -199,50 +255,27 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
       tc::fence_after_sync();
       const uint32_t m0 = smem_u32(buf + StateTcSmem::M), k0 = smem_u32(buf + StateTcSmem::KB);
       const uint32_t e0 = smem_u32(sE);
+      const uint32_t dO = tbase + eo_col(eo) + (16u << 16);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
         uint64_t ed = tc::smem_desc(e0 + ks * 2048, 8192, 1024);
-        tc::mma_bf16(tbase + (16u << 16), tc::smem_desc(m0 + ks * 32, 16, 1024), ed, idE, true);
         tc::mma_bf16(tbase + 128, tc::smem_desc(k0 + ks * 2048, 8192, 1024), ed, idS, true);
+        tc::mma_bf16(dO, tc::smem_desc(m0 + ks * 32, 16, 1024), ed, idE, true);
       }
       tc::mma_commit(mbarS);
     }
+    if (ci > 0) copy_o(ci - 1);  // staged before the barrier above
     if (!tc::mbar_wait(mbarS, ci & 1)) *abort_flag = 1;
     tc::fence_after_sync();
-    // o (threads holding O rows: lanes 16-31)
-    {
-      const int r = 16 * sub + (lane & 15);
-#pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 32) {
-        float acc[32];
-        tc::tmem_ld32(tE + c0, acc);
-        if (lane >= 16 && r < nv) {
-          bf16* dst = P.o + ((size_t)(t0 + r) * H + h) * D + 64 * half + c0;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint4 pk;
-            pk.x = pack_bf16(acc[8 * c + 0], acc[8 * c + 1]);
-            pk.y = pack_bf16(acc[8 * c + 2], acc[8 * c + 3]);
-            pk.z = pack_bf16(acc[8 * c + 4], acc[8 * c + 5]);
-            pk.w = pack_bf16(acc[8 * c + 6], acc[8 * c + 7]);
-            *reinterpret_cast<uint4*>(dst + 8 * c) = pk;
-          }
-        }
-      }
-    }
-    // the next chunk's inputs (its decay is needed now)
+    // the next chunk's inputs (its decay and operands are needed next)
     cp_async_wait<0>();
-    __syncthreads();
-    // state: S_{ci+1} -> operand tile + chunk-start copy; pre-scale for the next update
+    // S_{ci+1} -> registers -> operand tile (or the final state)
     {
-      float v[64];
-      {
-        float a[32], bb[32];
-        tc::tmem_ld32(tS, a);
-        tc::tmem_ld32(tS + 32, bb);
+      float a[32], bb[32];
+      tc::tmem_ld32(tS, a);
+      tc::tmem_ld32(tS + 32, bb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = bb[i]; }
-      }
+      for (int i = 0; i < 32; ++i) { v[i] = a[i]; v[32 + i] = bb[i]; }
       if (last) {
         if (P.ht) {
           float* dst = P.ht + (((size_t)n * H + h) * D + krow) * D + 64 * half;
@@ -250,14 +283,7 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
           for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
         }
       } else {
-        store_state(v, cbase + ci + 1);
-        const float dc = reinterpret_cast<const float*>(smem + ((ci + 1) % StateTcSmem::NSTAGE) * StateTcSmem::STAGE +
-                                                        StateTcSmem::DC)[krow];
-        float a[32], bb[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { a[i] = v[i] * dc; bb[i] = v[32 + i] * dc; }
-        tc::tmem_st32(tS, a);
-        tc::tmem_st32(tS + 32, bb);
+        store_tile(v);
       }
     }
     tc::fence_async_smem();
@@ -265,11 +291,16 @@ __global__ void __launch_bounds__(256, 1) kda_fwd_state_tc_kernel(FwdStateParams
     __syncthreads();
     if (*abort_flag) ok = false;
   }
+  if (ok && nchunks > 0) {  // o of the last chunk
+    stage_o((nchunks - 1) & 1);
+    __syncthreads();
+    copy_o(nchunks - 1);
+  }
   if (!ok && tid == 0) atomicExch(&g_kda_device_error, 1);
   cp_async_wait<0>();
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
 }
 
 }  // namespace kda
