@@ -17,8 +17,9 @@
 // One thread issues the MMAs; completion is tracked with mbarriers whose waits
 // are bounded: on a timeout the CTA records an error and leaves through its
 // cleanup path (TMEM is always released).  The phase-A operands (M, dO, Kbar,
-// E, 2^Gam_C) are double-buffered and loaded one chunk ahead; Qt, W and S0 are
-// loaded when phase B of the chunk before has consumed them.  All operand
+// E, 2^Gam_C) are double-buffered and loaded one chunk ahead; Qt and W are
+// reloaded as soon as the dS update of the chunk before has read them, S0 once
+// its dQt/dW MMAs have; the dM epilogue runs while phase B computes.  All operand
 // tiles are 128B-swizzled; rows past the sequence end are zero.  v_new and the
 // chunk-start states arrive as acc64 / st128 tiles; dE, dKb, dQt, dW (acc64)
 // and dM (acc64n64) leave as whole per-(chunk, head) tiles in epilogue order.
@@ -125,10 +126,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     load_acc64_sw128(b + S_::E, P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS);
     load_vec128(stage_dc(ci), P.dC + ((size_t)(cbase + ci) * H + h) * D);
   };
-  auto issue_single = [&](int ci) {
+  // Qt and W: read by the dS update (free once it completes); S0: read by dGC
+  // and the dQt/dW MMAs (free once those complete)
+  auto issue_qw = [&](int ci) {
     const int t0 = bos + ci * C, nv = min(C, eos - t0);
     tc::load_tile_sw128(sQt, P.Qt, t0, nv, H, h);
     tc::load_tile_sw128(sW, P.W, t0, nv, H, h);
+  };
+  auto issue_s0 = [&](int ci) {
     load_st128_sw128(sS0, P.hs + tile_index(P.seq, cbase + ci, h) * STATE_ELEMS);
   };
   // dS row krow, columns [64 hf, 64 hf + 64) -> bf16 operand tile
@@ -147,9 +152,13 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
 
 
   const int last = nchunks - 1;
+  // cp.async groups, oldest first: per chunk ci (from the last) the loop
+  // commits [S0(ci)] and [stage(ci-1)] at its top and [Qt,W(ci-1)] in
+  // epilogue B; the prologue commits [stage(last)] and [Qt,W,S0(last)]
   issue_stage(last);
   cp_async_commit();
-  issue_single(last);
+  issue_qw(last);
+  issue_s0(last);
   cp_async_commit();
   // dht -> registers and the bf16 operand tile
   float v[64];
@@ -226,9 +235,6 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
                      tc::smem_desc(e0 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024), idM, ks > 0);
       tc::mma_commit(mbar + 1);
     }
-    // the next chunk's phase-A operands (its stage held chunk ci+1, finished)
-    if (ci > 0) issue_stage(ci - 1);
-    cp_async_commit();
     // dS <- diag(2^Gam_C) dS (dS is R0 = v, the chunk-end gradient)
     {
       const float dc = dC[krow];
@@ -240,12 +246,17 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
       tc::tmem_st32(tR0, a);
       tc::tmem_st32(tR0 + 32, b);
     }
-    // dQt / dW of the chunk after this one
+    // dQt / dW of the chunk after this one; its MMAs were the last readers of S0
     if (ci < last) {
       if (!tc::mbar_wait(mbar + 3, (it - 1) & 1)) *abort_flag = 1;
       tc::fence_after_sync();
       r2_epilogue(ci + 1);
+      issue_s0(ci);
     }
+    cp_async_commit();
+    // the next chunk's phase-A operands (its stage held chunk ci+1, finished)
+    if (ci > 0) issue_stage(ci - 1);
+    cp_async_commit();
     // ---- epilogue A
     if (!tc::mbar_wait(mbar + 0, it & 1)) *abort_flag = 1;
     tc::fence_after_sync();
@@ -272,21 +283,6 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
             *reinterpret_cast<uint4*>(atom + arow * 128 + ((chunk ^ (arow & 7)) << 4)) = pk;
           }
         }
-      }
-    }
-    if (!tc::mbar_wait(mbar + 1, it & 1)) *abort_flag = 1;
-    tc::fence_after_sync();
-    {
-      float a[32];
-      tc::tmem_ld32(tR3, a);
-      if (!hi) {
-        const int cb = 32 * hf;
-        float m[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) m[i] = cb + i <= arow ? a[i] : 0.f;
-        bf16* tile = P.dM + tix * TILE64N64_ELEMS;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64n64_off(arow, cb + 8 * c), m + 8 * c);
       }
     }
     // dGC: half-row partials of rowsum((2^Gam_C dS) o S0)
@@ -334,6 +330,22 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
       }
       tc::mma_commit(mbar + 3);
     }
+    // tril(dM) out (off the dS chain: phase B does not touch R3)
+    if (!tc::mbar_wait(mbar + 1, it & 1)) *abort_flag = 1;
+    tc::fence_after_sync();
+    {
+      float a[32];
+      tc::tmem_ld32(tR3, a);
+      if (!hi) {
+        const int cb = 32 * hf;
+        float m[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m[i] = cb + i <= arow ? a[i] : 0.f;
+        bf16* tile = P.dM + tix * TILE64N64_ELEMS;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64n64_off(arow, cb + 8 * c), m + 8 * c);
+      }
+    }
     // ---- epilogue B: dS of the chunk before -> operand tile (or dh0)
     if (!tc::mbar_wait(mbar + 2, it & 1)) *abort_flag = 1;
     tc::fence_after_sync();
@@ -346,10 +358,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     }
     if (ci > 0) {
       store_ds(v);
-      // dQt/dW (phase B) still read S0: the next Qt/W/S0 wait for them
-      if (!tc::mbar_wait(mbar + 3, it & 1)) *abort_flag = 1;
-      tc::fence_after_sync();
-      issue_single(ci - 1);
+      issue_qw(ci - 1);  // the dS update that read Qt and W is complete
       cp_async_commit();
       cp_async_wait<1>();  // phase-A operands of the chunk before
     } else {
