@@ -39,10 +39,10 @@ H, D, T = 16, 128, 4096
 # Algorithmic HBM bytes per token-head of each kernel (reads + writes of its
 # interface tensors, each once; bf16 activations, fp32 per-chunk vectors).
 KERNEL_BYTES_PER_TOKEN_HEAD = {
-    "fwd_intra": 1026 + 1160,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C out
+    "fwd_intra": 1026 + 1416,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C and A (fp32 64x64/chunk) out
     "fwd_state": 1160 + 1024,   # W,U,Qt,Kbar,M,2^Gam_C in; o, chunk states, v_new out
     "bwd_state": 1928 + 1160,   # W,Qt,Kbar,M,2^Gam_C,v_new,dO,chunk states in; dE,dQt,dW,dKbar,dM,dGam_C out
-    "bwd_intra": 2186 + 1042,   # inputs + dE,dW,dQt,dKbar,dM,dGam_C in; dq_hat,dk_hat,dv,dg,dbeta,partials out
+    "bwd_intra": 2442 + 1042,   # inputs, A + dE,dW,dQt,dKbar,dM,dGam_C in; dq_hat,dk_hat,dv,dg,dbeta,partials out
     "bwd_post": 1536 + 768,     # q,k,v and dq_hat,dk_hat,dv in; dq,dk,dv out
 }
 # Tensor-core FLOPs per token-head of each kernel (algorithmic, no recompute).
@@ -59,7 +59,7 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
 # --warmup 3 --profile` (B=2: the per-launch traffic scales with the token-heads
 # processed); summary in profiles/kda_kernels_dram_b2.md.
 NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
-    "fwd_intra": 1826.0, "fwd_state": 1824.5, "bwd_state": 2803.2, "bwd_intra": 2997.7, "bwd_post": 2141.1,
+    "fwd_intra": 2053.6, "fwd_state": 1845.4, "bwd_state": 2826.7, "bwd_intra": 3269.0, "bwd_post": 2189.9,
 }
 
 
