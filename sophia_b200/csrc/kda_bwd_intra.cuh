@@ -22,17 +22,9 @@
 #pragma once
 
 #include "kda_bwd_state.cuh"
+#include "kda_tc.cuh"
 
 namespace kda {
-
-// cp.async of an acc64 tile into a padded [64][LD128] tile (rows >= nv zero).
-__device__ __forceinline__ void load_acc64_ld128(bf16* dst, const bf16* tile, int nv) {
-  for (int idx = threadIdx.x; idx < 64 * 16; idx += blockDim.x) {
-    int r, cc;
-    acc64_chunk(idx, r, cc);
-    cp_async16(dst + r * LD128 + cc * 8, tile + idx * 8, r < nv);
-  }
-}
 
 struct BwdIntraParams {
   PrologueIn in;
@@ -58,7 +50,8 @@ struct BwdIntraSmem {
   static constexpr int EC = ER + 4 * D * 4;                  // 4 x 128 fp32
   static constexpr int BETA = EC + 4 * D * 4;                // 64 fp32
   static constexpr int BRAW = BETA + 64 * 4;                 // 64 bf16
-  static constexpr int END = BRAW + 64 * 2;
+  static constexpr int MISC = BRAW + 64 * 2;                 // mbarrier of the gradient-tile bulk copies
+  static constexpr int END = MISC + 16;
   // RAW aliases after the operands are built
   static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
   static constexpr int AINV = RAW + 16640;                   // fp32 [64][64] A from the forward (until the T build;
@@ -79,6 +72,7 @@ struct BwdIntraSmem {
   static constexpr int XS = DEW + 9216;                      // bf16 64 x LD64
   static constexpr int GRE = DEW + 18432;                    // bf16 64 x 128 gate logits (reloaded)
   static_assert(GRE + 64 * D * 2 <= RAW, "gate reload overflows");
+  static_assert(MISC % 8 == 0 && DEW % 16 == 0 && GAM % 16 == 0, "bulk-copy targets and mbarrier alignment");
 };
 
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntraParams P) {
@@ -103,6 +97,10 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   ps.tot = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS);
   ps.taps = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS + 8192);
 
+  if (tid == 0) {
+    tc::mbar_init(reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC), 1);
+    tc::fence_mbar_init();
+  }
   prologue_issue_loads(P.in, ps, pos, h, P.conv);
   cp_async_commit();
   cp_async_wait<0>();
@@ -135,37 +133,35 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       af[j][e] = ex2(G - ps.gam[m0 * LDG + col]);
       bfv[j][e] = ex2(ps.gam[(m0 + 15) * LDG + col] - G);
     }
+  tc::fence_async_smem();  // the regions below are rewritten by the bulk copies
   __syncthreads();
 
+  // The state-pass gradient tiles (acc64 order, rows past the end zero) and
+  // A = (I + diag(beta) L')^-1 as the forward computed it arrive as five bulk
+  // copies issued by one thread, so the warps go on with L' meanwhile; the
+  // tiles stay in their global order (Acc64Tile addressing).  dQt and dKbar
+  // land in the dead decay region, A in the dead raw region (clear of Lp,
+  // which l_blocks writes below).
   bf16* dEs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
   bf16* dWs = dEs + 64 * LD128;
-  load_acc64_ld128(dEs, P.dE + tix * TILE64_ELEMS, nv);
-  load_acc64_ld128(dWs, P.dW + tix * TILE64_ELEMS, nv);
-  // dQt and dKbar are only read elementwise: unpadded [64][128] tiles in the
-  // (now dead) decay region, 16-byte chunks XOR-swizzled by row so that the
-  // fragment-position reads below are bank-conflict free
   bf16* dQs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GAM);
   bf16* dKs = dQs + 64 * D;
-  for (int i = tid; i < 2 * 64 * 16; i += blockDim.x) {
-    const int which = i >> 10, idx = i & 1023;
-    int r, cc;
-    acc64_chunk(idx, r, cc);
-    const bf16* src = (which ? P.dKb : P.dQt) + tix * TILE64_ELEMS + idx * 8;
-    bf16* dst = which ? dKs : dQs;
-    cp_async16(dst + r * D + ((cc ^ (r & 7)) << 3), src, r < nv);
-  }
-  // A = (I + diag(beta) L')^-1 as the forward computed it: [64][64] fp32 in
-  // the dead raw region (clear of Lp, which l_blocks writes below)
   float* Asm = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
-  {
-    const float* src = P.A + tix * TILE64N64_ELEMS;
-    for (int i = tid; i < 64 * 16; i += blockDim.x) cp_async16(Asm + i * 4, src + i * 4, true);
+  uint64_t* tiles_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC);
+  if (tid == 0) {
+    constexpr uint32_t TB = TILE64_ELEMS * 2, AB = TILE64N64_ELEMS * 4;
+    tc::mbar_expect_tx(tiles_ready, 4 * TB + AB);
+    tc::bulk_g2s(dEs, P.dE + tix * TILE64_ELEMS, TB, tiles_ready);
+    tc::bulk_g2s(dWs, P.dW + tix * TILE64_ELEMS, TB, tiles_ready);
+    tc::bulk_g2s(dQs, P.dQt + tix * TILE64_ELEMS, TB, tiles_ready);
+    tc::bulk_g2s(dKs, P.dKb + tix * TILE64_ELEMS, TB, tiles_ready);
+    tc::bulk_g2s(Asm, P.A + tix * TILE64N64_ELEMS, AB, tiles_ready);
   }
-  cp_async_commit();
+  const Acc64Tile dEt{dEs}, dWt{dWs};
 
   float* Lp = reinterpret_cast<float*>(smem + BwdIntraSmem::LP);
   l_blocks(op, Lp);
-  cp_async_wait<0>();  // dE, dW, dQt, dKbar, A
+  if (!tc::mbar_wait(tiles_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 5);
   __syncthreads();
   bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
   for (int i = tid; i < 64 * 32; i += blockDim.x) {
@@ -206,7 +202,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   {
     float acc[4][4];
     zero_acc<4>(acc);
-    warp_mma<4, true, true>(acc, Tbf, LD64, m0, dEs, LD128, n0, 0, 64);  // dv = T^T dE
+    warp_mma_t<4, true, true>(acc, PadTile{Tbf, LD64}, m0, dEt, n0, 0, 64);  // dv = T^T dE
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -217,14 +213,14 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
               pack_bf16(acc[j][e], acc[j][e + 1]);
       }
     zero_acc<4>(acc);
-    warp_mma<4, true, true>(acc, Tbf, LD64, m0, dWs, LD128, n0, 0, 64);  // dKe = T^T dW
+    warp_mma_t<4, true, true>(acc, PadTile{Tbf, LD64}, m0, dWt, n0, 0, 64);  // dKe = T^T dW
     float colsum[4][2];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
         int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        const int sw = r * D + ((((cc >> 3) ^ (r & 7))) << 3) + (cc & 7);
+        const int sw = (int)acc64_off(r, cc);
         float2 gq = unpack_bf16(*reinterpret_cast<const uint32_t*>(dQs + sw));
         float2 gk = unpack_bf16(*reinterpret_cast<const uint32_t*>(dKs + sw));
         float2 qa = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Qa + r * LD128 + cc));
@@ -272,8 +268,8 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   {
     float acc[2][4];
     zero_acc<2>(acc);
-    warp_mma<2, false, false>(acc, dEs, LD128, m0, op.V, LD128, n1, 0, 128);
-    warp_mma<2, false, false>(acc, dWs, LD128, m0, op.Ke, LD128, n1, 0, 128);
+    warp_mma_t<2, false, false>(acc, dEt, m0, PadTile{op.V, LD128}, n1, 0, 128);
+    warp_mma_t<2, false, false>(acc, dWt, m0, PadTile{op.Ke, LD128}, n1, 0, 128);
     // dbeta_T[j] = sum_i dT_ij A_ij ; dA = dT diag(beta)
     float cs[2][2];
 #pragma unroll

@@ -220,6 +220,38 @@ __device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const bf16* A, int
   }
 }
 
+// The same fragment loads for tiles in other layouts: a tile type provides
+// at(row, col) for col a multiple of 8 (the start of a contiguous 16-byte run).
+struct PadTile {  // row-major with a padded row stride
+  const bf16* p;
+  int ld;
+  __device__ __forceinline__ const bf16* at(int r, int c) const { return p + r * ld + c; }
+};
+struct Acc64Tile;  // defined with the tile layouts below
+
+template <int NT, bool TA, bool TB, typename TAL, typename TBL>
+__device__ __forceinline__ void warp_mma_t(float (&acc)[NT][4], const TAL& A, int m0, const TBL& B, int n0, int k0,
+                                           int K) {
+  static_assert(NT % 2 == 0, "NT must be even");
+  const int l = threadIdx.x & 31, i = l >> 3, r = l & 7;
+#pragma unroll 2
+  for (int kk = 0; kk < K; kk += 16) {
+    const int k = k0 + kk;
+    uint32_t a[4];
+    if (TA) ldsm_x4_t(a, A.at(k + (i >> 1) * 8 + r, m0 + (i & 1) * 8));
+    else ldsm_x4(a, A.at(m0 + (l & 15), k + (l >> 4) * 8));
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      const int n = n0 + 8 * j;
+      if (TB) ldsm_x4_t(b, B.at(k + (i & 1) * 8 + r, n + (i >> 1) * 8));
+      else ldsm_x4(b, B.at(n + (i >> 1) * 8 + r, k + (i & 1) * 8));
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
 template <int NT>
 __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
 #pragma unroll
@@ -257,6 +289,13 @@ __host__ __device__ __forceinline__ uint32_t acc64n64_off(int i, int j) {
 __host__ __device__ __forceinline__ uint32_t st128_off(int k, int v) {
   return (uint32_t)(((((k >> 5) * 2 + (v >> 6)) * 8 + ((v >> 3) & 7)) * 32 + (k & 31)) * 8 + (v & 7));
 }
+// A 64x128 acc64 tile in shared memory, as it arrives by a plain byte copy:
+// the eight rows an ldmatrix reads (one 16-row group, one 8-column chunk) are
+// one contiguous 128-byte run, so the reads are conflict-free.
+struct Acc64Tile {
+  const bf16* p;
+  __device__ __forceinline__ const bf16* at(int r, int c) const { return p + acc64_off(r, c); }
+};
 // Inverse maps of a 16-byte chunk index (element offset / 8) to (row, 8-chunk).
 __device__ __forceinline__ void acc64_chunk(int idx, int& row, int& cc) {
   const int lane = idx & 15, c = (idx >> 4) & 3, c0 = (idx >> 6) & 1, hf = (idx >> 7) & 1, q = idx >> 8;

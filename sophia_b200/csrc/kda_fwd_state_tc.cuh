@@ -29,8 +29,6 @@
 
 namespace kda {
 
-__device__ int g_kda_device_error;  // nonzero after a bounded wait timed out
-
 struct StateTcSmem {
   static constexpr int TILE = 16384;                    // [64][128] bf16, two 8 KB atoms
   static constexpr int W = 0, QT = TILE, KB = 2 * TILE, U = 3 * TILE, M = 4 * TILE;  // M: one 8 KB atom

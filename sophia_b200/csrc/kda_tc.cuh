@@ -21,6 +21,9 @@
 #include "kda_common.cuh"
 
 namespace kda {
+
+__device__ int g_kda_device_error;  // nonzero after a bounded wait timed out
+
 namespace tc {
 
 // 16-byte chunk position of element column `col` (0..63) of row `r` inside a
@@ -101,6 +104,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint3
     if (done) return true;
   }
   return false;
+}
+
+// One thread announces `bytes` of bulk-copy traffic on the mbarrier (and
+// arrives on it); the copies complete the phase when all bytes have landed.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(mbar)), "r"(bytes)
+               : "memory");
+}
+// Bulk (TMA, non-tensor) copy of a contiguous global range into shared memory;
+// both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(mbar))
+      : "memory");
 }
 
 // 32 lanes x 32 consecutive fp32 columns: this thread gets its lane's columns
