@@ -45,6 +45,9 @@ struct SavedView {
   bf16 *W, *U, *Qt, *Kb, *E, *M, *hs;
   float* dC;
   float* A;  // [slots x H] fp32 64x64 tiles of A = (I + diag(beta) L')^-1 (training only)
+  // the forward prologue's products for the backward (training only):
+  bf16 *QN, *KN, *VN;  // [slots x H] [64][128] bf16: scaled normalised q, normalised k, post-conv v
+  float *GM, *BT;      // [slots x H] [64][LDG] fp32 in-chunk log2 decay cumsum, [slots x H][64] fp32 beta
 };
 
 SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) {
@@ -60,10 +63,17 @@ SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) 
     s.E = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.hs = cv.take<bf16>((size_t)mc * H * STATE_ELEMS * 2);
     s.A = cv.take<float>((size_t)mc * H * TILE64N64_ELEMS * 4);
+    s.QN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
+    s.KN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
+    s.VN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
+    s.GM = cv.take<float>((size_t)mc * H * 64 * LDG * 4);
+    s.BT = cv.take<float>((size_t)mc * H * 64 * 4);
   } else {
     s.E = nullptr;
     s.hs = nullptr;
     s.A = nullptr;
+    s.QN = s.KN = s.VN = nullptr;
+    s.GM = s.BT = nullptr;
   }
   return s;
 }
@@ -362,6 +372,7 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.seq = pr.seq;
   ip.conv = pr.conv;
   ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A;
+  ip.QN = sv.QN; ip.KN = sv.KN; ip.VN = sv.VN; ip.GM = sv.GM; ip.BT = sv.BT;
   if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
   {
     TimedLaunch tl(K_FWD_INTRA, st);
@@ -452,6 +463,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   bi.conv = pr.conv;
   bi.dE = bv.dE; bi.dW = bv.dW; bi.dQt = bv.dQt; bi.dKb = bv.dKb; bi.dM = bv.dM; bi.dGC = bv.dGC;
   bi.A = sv.A;
+  bi.QN = sv.QN; bi.KN = sv.KN; bi.VN = sv.VN; bi.GM = sv.GM; bi.BT = sv.BT;
   bi.dq_hat = bv.dq_hat;
   bi.dk_hat = bv.dk_hat;
   bi.dv = pr.conv ? bv.dv_hat : static_cast<bf16*>(dv);

@@ -32,6 +32,8 @@ struct BwdIntraParams {
   bool conv;
   const bf16 *dE, *dW, *dQt, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
   const float* A;                        // [chunks][H] fp32 64x64 tiles saved by the forward
+  const bf16 *QN, *KN, *VN;              // [chunks][H] [64][128] bf16 prologue products of the forward
+  const float *GM, *BT;                  // [chunks][H] [64][LDG] fp32 decay cumsum, [64] fp32 beta
   const float* dGC;
   bf16 *dq_hat, *dk_hat, *dv;  // [T_total][H][128]
   bf16 *dg, *dbeta;            // [T_total][H][128], [T_total][H]
@@ -50,7 +52,7 @@ struct BwdIntraSmem {
   static constexpr int EC = ER + 4 * D * 4;                  // 4 x 128 fp32
   static constexpr int BETA = EC + 4 * D * 4;                // 64 fp32
   static constexpr int BRAW = BETA + 64 * 4;                 // 64 bf16
-  static constexpr int MISC = BRAW + 64 * 2;                 // mbarrier of the gradient-tile bulk copies
+  static constexpr int MISC = BRAW + 64 * 2;                 // mbarriers: gradient tiles, prologue products
   static constexpr int END = MISC + 16;
   // RAW aliases after the operands are built
   static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
@@ -88,8 +90,8 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 
   PrologueSmem ps;
   ps.xq = reinterpret_cast<bf16*>(smem + BwdIntraSmem::RAW);
-  ps.xk = ps.xq + 67 * D;
-  ps.xv = ps.xk + 67 * D;
+  ps.xk = ps.xq + 64 * D;
+  ps.xv = ps.xk + 64 * D;
   ps.graw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
   ps.braw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::BRAW);
   ps.gam = reinterpret_cast<float*>(smem + BwdIntraSmem::GAM);
@@ -97,16 +99,40 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   ps.tot = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS);
   ps.taps = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS + 8192);
 
+  // The forward's prologue products (scaled normalised q, normalised k,
+  // post-conv v, the log2 decay cumsum in its padded layout, beta) arrive by
+  // five bulk copies; each thread then takes its strip.
+  uint64_t* pro_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC) + 1;
   if (tid == 0) {
     tc::mbar_init(reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC), 1);
+    tc::mbar_init(pro_ready, 1);
     tc::fence_mbar_init();
   }
-  prologue_issue_loads(P.in, ps, pos, h, P.conv);
-  cp_async_commit();
-  cp_async_wait<0>();
   __syncthreads();
+  if (tid == 0) {
+    constexpr uint32_t TB = TILE64_ELEMS * 2, GB = 64 * LDG * 4, BB = 64 * 4;
+    tc::mbar_expect_tx(pro_ready, 3 * TB + GB + BB);
+    tc::bulk_g2s(ps.xq, P.QN + tix * TILE64_ELEMS, TB, pro_ready);
+    tc::bulk_g2s(ps.xk, P.KN + tix * TILE64_ELEMS, TB, pro_ready);
+    tc::bulk_g2s(ps.xv, P.VN + tix * TILE64_ELEMS, TB, pro_ready);
+    tc::bulk_g2s(ps.gam, P.GM + tix * 64 * LDG, GB, pro_ready);
+    tc::bulk_g2s(ps.beta, P.BT + tix * 64, BB, pro_ready);
+  }
+  if (!tc::mbar_wait(pro_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 7);
   Strip s;
-  prologue_compute(P.in, ps, pos, h, P.conv, s);
+  {
+    const int tg = tid >> 4, cg = tid & 15;
+#pragma unroll
+    for (int r = 0; r < STRIP; ++r) {
+      const int t = STRIP * tg + r;
+      unpack8(*reinterpret_cast<const bf16x8*>(ps.xq + t * D + 8 * cg), s.q[r]);
+      unpack8(*reinterpret_cast<const bf16x8*>(ps.xk + t * D + 8 * cg), s.k[r]);
+      unpack8(*reinterpret_cast<const bf16x8*>(ps.xv + t * D + 8 * cg), s.v[r]);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) s.gam[r][c] = ps.gam[t * LDG + 8 * cg + c];
+    }
+  }
+  __syncthreads();
 
   Operands op;
   op.Qa = reinterpret_cast<bf16*>(smem + BwdIntraSmem::OPS);

@@ -20,6 +20,8 @@ struct FwdIntraParams {
   bf16 *W, *U, *Qt, *Kb, *M;  // [T_total][H][128] (M: [T_total][H][64])
   float* dC;                  // [chunks][H][128]
   float* A;                   // [slots x H] fp32 64x64 tiles of A (the backward's copy), or null
+  bf16 *QN, *KN, *VN;         // [slots x H] prologue products for the backward, or null
+  float *GM, *BT;
 };
 
 // Shared-memory layout of the intra kernels (bytes).
@@ -85,6 +87,22 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
 
   Strip s;
   prologue_compute(P.in, ps, pos, h, P.conv, s);
+  if (P.QN) {  // the prologue's products, so that the backward need not redo it
+    const size_t tix = tile_index(P.seq, c, h);
+    const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+#pragma unroll
+    for (int r = 0; r < STRIP; ++r) {
+      const int t = STRIP * tg + r;
+      const size_t o = tix * TILE64_ELEMS + (size_t)t * D + 8 * cg;
+      *reinterpret_cast<bf16x8*>(P.QN + o) = pack8(s.q[r]);
+      *reinterpret_cast<bf16x8*>(P.KN + o) = pack8(s.k[r]);
+      *reinterpret_cast<bf16x8*>(P.VN + o) = pack8(s.v[r]);
+      float* gd = P.GM + (tix * 64 + t) * LDG + 8 * cg;
+      *reinterpret_cast<float4*>(gd) = make_float4(s.gam[r][0], s.gam[r][1], s.gam[r][2], s.gam[r][3]);
+      *reinterpret_cast<float4*>(gd + 4) = make_float4(s.gam[r][4], s.gam[r][5], s.gam[r][6], s.gam[r][7]);
+    }
+    if (threadIdx.x < 64) P.BT[tix * 64 + threadIdx.x] = ps.beta[threadIdx.x];
+  }
 
   Operands op;
   op.Qa = reinterpret_cast<bf16*>(smem + IntraSmem::OPS);
