@@ -10,6 +10,7 @@
 #pragma once
 
 #include "kda_intra.cuh"
+#include "kda_tc.cuh"
 
 namespace kda {
 
@@ -42,6 +43,8 @@ struct IntraSmem {
   static constexpr int TBF = XTMP + 3 * 16 * 17 * 4;    // 64 x LD64 bf16
   static constexpr int MSM = GRAW;                      // 64 x LD64 bf16
   static_assert(TBF + 64 * LD64 * 2 <= GRAW, "aliases overflow the raw region");
+  static_assert(RAW % 16 == 0 && GAM % 16 == 0 && BETA % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
+                "bulk-store sources of the prologue products");
   static_assert(64 * LD64 * 2 <= GAM - GRAW, "M staging overflows");
 };
 
@@ -87,21 +90,33 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
 
   Strip s;
   prologue_compute(P.in, ps, pos, h, P.conv, s);
-  if (P.QN) {  // the prologue's products, so that the backward need not redo it
-    const size_t tix = tile_index(P.seq, c, h);
+  // the prologue's products, so that the backward need not redo it: q, k, v
+  // strips into [64][128] tiles over the dead raw inputs, then (with the decay
+  // cumsum tile and beta, already in shared memory) five bulk stores issued by
+  // one thread; they complete while the operands are built
+  const bool save_products = P.QN != nullptr;
+  if (save_products) {
     const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+    bf16* tq = reinterpret_cast<bf16*>(smem + IntraSmem::RAW);
 #pragma unroll
     for (int r = 0; r < STRIP; ++r) {
       const int t = STRIP * tg + r;
-      const size_t o = tix * TILE64_ELEMS + (size_t)t * D + 8 * cg;
-      *reinterpret_cast<bf16x8*>(P.QN + o) = pack8(s.q[r]);
-      *reinterpret_cast<bf16x8*>(P.KN + o) = pack8(s.k[r]);
-      *reinterpret_cast<bf16x8*>(P.VN + o) = pack8(s.v[r]);
-      float* gd = P.GM + (tix * 64 + t) * LDG + 8 * cg;
-      *reinterpret_cast<float4*>(gd) = make_float4(s.gam[r][0], s.gam[r][1], s.gam[r][2], s.gam[r][3]);
-      *reinterpret_cast<float4*>(gd + 4) = make_float4(s.gam[r][4], s.gam[r][5], s.gam[r][6], s.gam[r][7]);
+      *reinterpret_cast<bf16x8*>(tq + t * D + 8 * cg) = pack8(s.q[r]);
+      *reinterpret_cast<bf16x8*>(tq + TILE64_ELEMS + t * D + 8 * cg) = pack8(s.k[r]);
+      *reinterpret_cast<bf16x8*>(tq + 2 * TILE64_ELEMS + t * D + 8 * cg) = pack8(s.v[r]);
     }
-    if (threadIdx.x < 64) P.BT[tix * 64 + threadIdx.x] = ps.beta[threadIdx.x];
+    tc::fence_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const size_t tix = tile_index(P.seq, c, h);
+      constexpr uint32_t TB = TILE64_ELEMS * 2;
+      tc::bulk_s2g(P.QN + tix * TILE64_ELEMS, tq, TB);
+      tc::bulk_s2g(P.KN + tix * TILE64_ELEMS, tq + TILE64_ELEMS, TB);
+      tc::bulk_s2g(P.VN + tix * TILE64_ELEMS, tq + 2 * TILE64_ELEMS, TB);
+      tc::bulk_s2g(P.GM + tix * 64 * LDG, ps.gam, 64 * LDG * 4);
+      tc::bulk_s2g(P.BT + tix * 64, ps.beta, 64 * 4);
+      tc::bulk_commit();
+    }
   }
 
   Operands op;
@@ -130,6 +145,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
     if (threadIdx.x < D)
       P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
   }
+  if (save_products && threadIdx.x == 0) tc::bulk_wait_all();  // the raw region is reused from here on
   __syncthreads();
 
   float* Lp = reinterpret_cast<float*>(smem + IntraSmem::LP);

@@ -122,6 +122,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bulk (TMA, non-tensor) copy of a contiguous shared range to global memory,
+// tracked by this thread's bulk async-groups.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Waits until this thread's bulk groups have completed (writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
 // 32 lanes x 32 consecutive fp32 columns: this thread gets its lane's columns
 // [col, col + 32).  taddr = (lane base << 16) | column.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
