@@ -44,7 +44,7 @@ struct Carver {
 struct SavedView {
   bf16 *W, *U, *Qt, *Kb, *E, *M, *hs;
   float* dC;
-  float* A;  // [slots x H] fp32 64x64 tiles of A = (I + diag(beta) L')^-1 (training only)
+  float* A;  // [slots x H] fp32 [64][LDF64] tiles of A = (I + diag(beta) L')^-1 (training only)
   // the forward prologue's products for the backward (training only):
   bf16 *QN, *KN, *VN;  // [slots x H] [64][128] bf16: scaled normalised q, normalised k, post-conv v
   float *GM, *BT;      // [slots x H] [64][LDG] fp32 in-chunk log2 decay cumsum, [slots x H][64] fp32 beta
@@ -62,7 +62,7 @@ SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) 
   if (with_bwd) {
     s.E = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.hs = cv.take<bf16>((size_t)mc * H * STATE_ELEMS * 2);
-    s.A = cv.take<float>((size_t)mc * H * TILE64N64_ELEMS * 4);
+    s.A = cv.take<float>((size_t)mc * H * A_TILE_ELEMS * 4);
     s.QN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.KN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.VN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);

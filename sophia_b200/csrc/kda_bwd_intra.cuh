@@ -31,7 +31,7 @@ struct BwdIntraParams {
   SeqInfo seq;
   bool conv;
   const bf16 *dE, *dW, *dQt, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
-  const float* A;                        // [chunks][H] fp32 64x64 tiles saved by the forward
+  const float* A;                        // [chunks][H] fp32 [64][LDF64] tiles saved by the forward
   const bf16 *QN, *KN, *VN;              // [chunks][H] [64][128] bf16 prologue products of the forward
   const float *GM, *BT;                  // [chunks][H] [64][LDG] fp32 decay cumsum, [64] fp32 beta
   const float* dGC;
@@ -56,7 +56,7 @@ struct BwdIntraSmem {
   static constexpr int END = MISC + 16;
   // RAW aliases after the operands are built
   static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
-  static constexpr int AINV = RAW + 16640;                   // fp32 [64][64] A from the forward (until the T build;
+  static constexpr int AINV = RAW + 16640;                   // fp32 [64][LDF64] A from the forward (until the T build;
                                                              // DMS reuses part of it afterwards)
   static constexpr int LPB = RAW + 33280;                    // bf16 64 x LD64 (after inverse)
   static constexpr int ABF = RAW;                            // bf16 64 x LD64 (after Lp fp32 is dead)
@@ -68,7 +68,7 @@ struct BwdIntraSmem {
   static constexpr int COLS = DBL + 1024;                    // fp32 4 x 128  (sum Kbar o dKbar)
   static_assert(COLS + 2048 <= LPB, "small tiles overlap Lp bf16");
   static_assert(TBF + 64 * LD64 * 2 <= RAWSZ + RAW, "T tile overflows");
-  static_assert(AINV + 64 * 64 * 4 <= LPB && AINV % 16 == 0, "A tile overlaps Lp bf16 or is misaligned");
+  static_assert(AINV + A_TILE_ELEMS * 4 <= LPB && AINV % 16 == 0, "A tile overlaps Lp bf16 or is misaligned");
   // DEW aliases after the WY backward
   static constexpr int DAS = DEW;                            // bf16 64 x LD64
   static constexpr int XS = DEW + 9216;                      // bf16 64 x LD64
@@ -175,13 +175,13 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   float* Asm = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
   uint64_t* tiles_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC);
   if (tid == 0) {
-    constexpr uint32_t TB = TILE64_ELEMS * 2, AB = TILE64N64_ELEMS * 4;
+    constexpr uint32_t TB = TILE64_ELEMS * 2, AB = A_TILE_ELEMS * 4;
     tc::mbar_expect_tx(tiles_ready, 4 * TB + AB);
     tc::bulk_g2s(dEs, P.dE + tix * TILE64_ELEMS, TB, tiles_ready);
     tc::bulk_g2s(dWs, P.dW + tix * TILE64_ELEMS, TB, tiles_ready);
     tc::bulk_g2s(dQs, P.dQt + tix * TILE64_ELEMS, TB, tiles_ready);
     tc::bulk_g2s(dKs, P.dKb + tix * TILE64_ELEMS, TB, tiles_ready);
-    tc::bulk_g2s(Asm, P.A + tix * TILE64N64_ELEMS, AB, tiles_ready);
+    tc::bulk_g2s(Asm, P.A + tix * A_TILE_ELEMS, AB, tiles_ready);
   }
   const Acc64Tile dEt{dEs}, dWt{dWs};
 
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     float av[8];
     const int r = tid >> 3, c0 = (tid & 7) * 8;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Asm[r * 64 + c0 + i] : 0.f;
+    for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Asm[r * LDF64 + c0 + i] : 0.f;
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {

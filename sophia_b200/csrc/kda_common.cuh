@@ -278,6 +278,7 @@ __device__ __forceinline__ int acc_col(int j, int e) { return 8 * j + 2 * (threa
 //          [quarter 4][column half 2][8-chunk 8][row lane 32][8]
 constexpr int TILE64_ELEMS = 64 * 128;
 constexpr int TILE64N64_ELEMS = 64 * 64;
+constexpr int A_TILE_ELEMS = 64 * LDF64;  // saved A: [64][LDF64] fp32, the inverse's own padded rows
 constexpr int STATE_ELEMS = 128 * 128;
 __host__ __device__ __forceinline__ uint32_t acc64_off(int i, int v) {
   return (uint32_t)((((((i >> 4) * 2 + (v >> 6)) * 2 + ((v >> 5) & 1)) * 4 + ((v >> 3) & 3)) * 16 + (i & 15)) * 8 +

@@ -20,7 +20,7 @@ struct FwdIntraParams {
   bool conv;
   bf16 *W, *U, *Qt, *Kb, *M;  // [T_total][H][128] (M: [T_total][H][64])
   float* dC;                  // [chunks][H][128]
-  float* A;                   // [slots x H] fp32 64x64 tiles of A (the backward's copy), or null
+  float* A;                   // [slots x H] fp32 [64][LDF64] tiles of A (the backward's copy), or null
   bf16 *QN, *KN, *VN;         // [slots x H] prologue products for the backward, or null
   float *GM, *BT;
 };
@@ -43,7 +43,7 @@ struct IntraSmem {
   static constexpr int TBF = XTMP + 3 * 16 * 17 * 4;    // 64 x LD64 bf16
   static constexpr int MSM = GRAW;                      // 64 x LD64 bf16
   static_assert(TBF + 64 * LD64 * 2 <= GRAW, "aliases overflow the raw region");
-  static_assert(RAW % 16 == 0 && GAM % 16 == 0 && BETA % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
+  static_assert(RAW % 16 == 0 && GAM % 16 == 0 && BETA % 16 == 0 && AINV % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
                 "bulk-store sources of the prologue products");
   static_assert(64 * LD64 * 2 <= GAM - GRAW, "M staging overflows");
 };
@@ -174,16 +174,15 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
     float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
     *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
   }
-  if (P.A) {  // A for the backward (entries above the diagonal are not meaningful)
-    float* dst = P.A + tile_index(P.seq, c, h) * TILE64N64_ELEMS;
-    for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
-      const int r = i >> 4, c4 = (i & 15) * 4;
-      const float* src = Ainv + r * LDF64 + c4;
-      *reinterpret_cast<float4*>(dst + r * 64 + c4) = make_float4(src[0], src[1], src[2], src[3]);
-    }
-  }
   store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
+  tc::fence_async_smem();  // A (written by every thread) is read by the bulk store below
   __syncthreads();
+  // A for the backward, as it sits in shared memory (entries above the
+  // diagonal are not meaningful): one bulk store, completed before the exit
+  if (P.A && threadIdx.x == 0) {
+    tc::bulk_s2g(P.A + tile_index(P.seq, c, h) * A_TILE_ELEMS, Ainv, A_TILE_ELEMS * 4);
+    tc::bulk_commit();
+  }
 
   // W = T Ke, U = T V ; warp w -> rows 16(w&3), cols 32(w>>2)
   {
@@ -209,6 +208,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
     store_rows128(P.W, Wst, LD128, nvalid, H, h, pos.t0);
     store_rows128(P.U, Ust, LD128, nvalid, H, h, pos.t0);
   }
+  if (P.A && threadIdx.x == 0) tc::bulk_wait_all();  // the A store reads shared memory
 }
 
 // ---------------------------------------------------------------- state pass
