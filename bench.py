@@ -40,10 +40,12 @@ H, D, T = 16, 128, 4096
 # Algorithmic HBM bytes per token-head of each kernel (reads + writes of its
 # interface tensors, each once; bf16 activations, fp32 per-chunk vectors).
 KERNEL_BYTES_PER_TOKEN_HEAD = {
-    "fwd_intra": 1026 + 1416,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C and A (fp32 64x64/chunk) out
+    "fwd_intra": 1026 + 2700,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C, A (fp32 64x64/chunk) and
+                                # the saved products q_hat,k_hat,v (bf16), Gam (fp32), beta out
     "fwd_state": 1160 + 1024,   # W,U,Qt,Kbar,M,2^Gam_C in; o, chunk states, v_new out
     "bwd_state": 1928 + 1160,   # W,Qt,Kbar,M,2^Gam_C,v_new,dO,chunk states in; dE,dQt,dW,dKbar,dM,dGam_C out
-    "bwd_intra": 2442 + 1042,   # inputs, A + dE,dW,dQt,dKbar,dM,dGam_C in; dq_hat,dk_hat,dv,dg,dbeta,partials out
+    "bwd_intra": 2956 + 1042,   # saved products, g, A + dE,dW,dQt,dKbar,dM,dGam_C in;
+                                # dq_hat,dk_hat,dv,dg,dbeta,partials out
     "bwd_post": 1536 + 768,     # q,k,v and dq_hat,dk_hat,dv in; dq,dk,dv out
 }
 # Tensor-core FLOPs per token-head of each kernel (algorithmic, no recompute).
