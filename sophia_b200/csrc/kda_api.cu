@@ -2,6 +2,8 @@
 // buffer carving and kernel launches.  No allocation, no host sync.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <climits>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -210,6 +212,16 @@ int launch_check(const char* what) {
   return KDA_OK;
 }
 
+// SMs of the current device (queried once per device).
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!counts[dev] && cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    counts[dev] = 148;
+  return counts[dev];
+}
+
 template <typename K>
 int set_smem(K kernel, int bytes, const char* name) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -373,10 +385,15 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.conv = pr.conv;
   ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A;
   ip.QN = sv.QN; ip.KN = sv.KN; ip.VN = sv.VN; ip.GM = sv.GM; ip.BT = sv.BT;
+  ip.grid_chunks = pr.grid_chunks;
   if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
   {
+    // persistent: one CTA per SM (the shared-memory plan allows one) walks the items
+    const long long items = (long long)pr.grid_chunks * H;
+    if (items > INT_MAX) return fail(KDA_ERR_INVALID, "more than 2^31 (chunk, head) items");
+    const int ctas = (int)std::min<long long>(items, sm_count());
     TimedLaunch tl(K_FWD_INTRA, st);
-    kda_fwd_intra_kernel<<<dim3(pr.grid_chunks, H), INTRA_THREADS, IntraSmem::END, st>>>(ip);
+    kda_fwd_intra_kernel<<<ctas, INTRA_THREADS, IntraSmem::END, st>>>(ip);
   }
   if ((rc = launch_check("fwd intra"))) return rc;
 

@@ -96,8 +96,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   ps.braw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::BRAW);
   ps.gam = reinterpret_cast<float*>(smem + BwdIntraSmem::GAM);
   ps.beta = reinterpret_cast<float*>(smem + BwdIntraSmem::BETA);
-  ps.tot = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS);
-  ps.taps = reinterpret_cast<float*>(smem + BwdIntraSmem::OPS + 8192);
 
   // The forward's prologue products (scaled normalised q, normalised k,
   // post-conv v, the log2 decay cumsum in its padded layout, beta) arrive by

@@ -1,6 +1,7 @@
 // Forward kernels of the chunked KDA layer.
 //
-//   kda_fwd_intra_kernel  (one CTA per (chunk, head), fully parallel)
+//   kda_fwd_intra_kernel  (persistent: one CTA per SM walks the (chunk, head)
+//                          items, prefetching the next item's inputs)
 //       raw q/k/v (pre- or post-conv), gate and beta logits
 //       -> W = T (k*2^Gam), U = T v, Qt = q*2^Gam, Kbar = k*2^(Gam_C-Gam),
 //          M = Aqk (lower incl. diag), dC = 2^Gam_C
@@ -23,29 +24,37 @@ struct FwdIntraParams {
   float* A;                   // [slots x H] fp32 [64][LDF64] tiles of A (the backward's copy), or null
   bf16 *QN, *KN, *VN;         // [slots x H] prologue products for the backward, or null
   float *GM, *BT;
+  int grid_chunks;            // chunk slots per head: items are (slot, head), slot fastest
 };
 
-// Shared-memory layout of the intra kernels (bytes).
+// Shared-memory layout of the forward intra kernel (bytes).  The raw inputs,
+// taps and biases have regions of their own, so that the next item's loads can
+// land while the current item's blocks and inverse are computed.
 struct IntraSmem {
-  static constexpr int RAW = 0;                         // 3 x 67 x 128 bf16
+  static constexpr int RAW = 0;                         // 3 x 67 x 128 bf16 (then the q/k/v product tiles)
   static constexpr int GRAW = RAW + 3 * 67 * D * 2;     // 64 x 128 bf16
   static constexpr int GAM = GRAW + 64 * D * 2;         // 64 x LDG fp32
-  static constexpr int OPS = GAM + 64 * LDG * 4;        // 6 x 64 x LD128 bf16
+  static constexpr int OPS = GAM + 64 * LDG * 4;        // 6 x 64 x LD128 bf16 (cumsum scratch before)
   static constexpr int OPSZ = 64 * LD128 * 2;
   static constexpr int CVEC = OPS + 6 * OPSZ;           // 6 x 128 fp32
   static constexpr int BETA = CVEC + 6 * D * 4;         // 64 fp32
   static constexpr int BRAW = BETA + 64 * 4;            // 64 bf16
-  static constexpr int END = BRAW + 64 * 2;
-  // aliases valid after the operands are built (raw inputs are dead)
-  static constexpr int LP = RAW;                        // 64 x LDF64 fp32
-  static constexpr int AINV = LP + 64 * LDF64 * 4;      // 64 x LDF64 fp32
-  static constexpr int XTMP = AINV + 64 * LDF64 * 4;    // 3 warps x 16 x 17 fp32
+  static constexpr int TAPS = BRAW + 64 * 2;            // 3 x 128 x 4 fp32
+  static constexpr int BIAS = TAPS + 3 * D * 16;        // dt_bias [128], A_log, padding
+  static constexpr int NXT = BIAS + (D + 4) * 4;        // next item: index, bos, t0, t1
+  static constexpr int XTMP = NXT + 32;                 // 3 warps x 16 x 17 fp32
   static constexpr int TBF = XTMP + 3 * 16 * 17 * 4;    // 64 x LD64 bf16
-  static constexpr int MSM = GRAW;                      // 64 x LD64 bf16
-  static_assert(TBF + 64 * LD64 * 2 <= GRAW, "aliases overflow the raw region");
-  static_assert(RAW % 16 == 0 && GAM % 16 == 0 && BETA % 16 == 0 && AINV % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
-                "bulk-store sources of the prologue products");
-  static_assert(64 * LD64 * 2 <= GAM - GRAW, "M staging overflows");
+  static constexpr int END = TBF + 64 * LD64 * 2;
+  // aliases valid once the operands are built and the product stores completed
+  static constexpr int LP = GAM;                        // 64 x LDF64 fp32
+  static constexpr int AINV = LP + 64 * LDF64 * 4;      // 64 x LDF64 fp32
+  static constexpr int MSM = OPS + OPSZ;                // 64 x LD64 bf16 over Ka (dead once L' is formed)
+  static_assert(AINV + 64 * LDF64 * 4 <= OPS, "the inverse tiles overflow the decay tile");
+  static_assert(RAW % 16 == 0 && GAM % 16 == 0 && BETA % 16 == 0 && AINV % 16 == 0 && TAPS % 16 == 0 &&
+                    BIAS % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
+                "bulk-copy and cp.async targets");
+  static_assert(64 * LD64 * 2 <= OPSZ && 16 * D * 4 <= OPSZ, "M staging or cumsum scratch overflows a tile");
+  static_assert(END <= 232448, "shared memory");
 };
 
 __device__ __forceinline__ void store_rows128(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0) {
@@ -64,13 +73,21 @@ __device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, 
   }
 }
 
+// First valid item at or after `from` in steps of the grid (pos filled), or n_items.
+__device__ __forceinline__ int fwd_find_item(const SeqInfo& seq, int from, int n_items, int G, ChunkPos& pos) {
+  for (int it = from; it < n_items; it += gridDim.x) {
+    pos = chunk_pos(seq, it % G);
+    if (pos.valid) return it;
+  }
+  return n_items;
+}
+
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntraParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int c = blockIdx.x, h = blockIdx.y;
-  ChunkPos pos = chunk_pos(P.seq, c);
-  if (!pos.valid) return;
-  const int H = P.in.H;
-  const int nvalid = pos.t1 - pos.t0;
+  const int H = P.in.H, G = P.grid_chunks, n_items = G * H;
+  ChunkPos pos;
+  int item = fwd_find_item(P.seq, blockIdx.x, n_items, G, pos);
+  if (item >= n_items) return;
 
   PrologueSmem ps;
   ps.xq = reinterpret_cast<bf16*>(smem + IntraSmem::RAW);
@@ -81,135 +98,161 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
   ps.gam = reinterpret_cast<float*>(smem + IntraSmem::GAM);
   ps.beta = reinterpret_cast<float*>(smem + IntraSmem::BETA);
   ps.tot = reinterpret_cast<float*>(smem + IntraSmem::OPS);  // scratch, before operands
-  ps.taps = reinterpret_cast<float*>(smem + IntraSmem::OPS + 8192);
-
-  prologue_issue_loads(P.in, ps, pos, h, P.conv);
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
-
-  Strip s;
-  prologue_compute(P.in, ps, pos, h, P.conv, s);
-  // the prologue's products, so that the backward need not redo it: q, k, v
-  // strips into [64][128] tiles over the dead raw inputs, then (with the decay
-  // cumsum tile and beta, already in shared memory) five bulk stores issued by
-  // one thread; they complete while the operands are built
+  ps.taps = reinterpret_cast<float*>(smem + IntraSmem::TAPS);
+  ps.bias = reinterpret_cast<float*>(smem + IntraSmem::BIAS);
+  int* nxt = reinterpret_cast<int*>(smem + IntraSmem::NXT);
   const bool save_products = P.QN != nullptr;
-  if (save_products) {
-    const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
-    bf16* tq = reinterpret_cast<bf16*>(smem + IntraSmem::RAW);
-#pragma unroll
-    for (int r = 0; r < STRIP; ++r) {
-      const int t = STRIP * tg + r;
-      *reinterpret_cast<bf16x8*>(tq + t * D + 8 * cg) = pack8(s.q[r]);
-      *reinterpret_cast<bf16x8*>(tq + TILE64_ELEMS + t * D + 8 * cg) = pack8(s.k[r]);
-      *reinterpret_cast<bf16x8*>(tq + 2 * TILE64_ELEMS + t * D + 8 * cg) = pack8(s.v[r]);
-    }
-    tc::fence_async_smem();
-    __syncthreads();
+
+  bf16 braw = prologue_issue_loads(P.in, ps, pos, item / G, P.conv);
+  cp_async_commit();
+  for (;;) {
+    const int c = item % G, h = item / G;
+    const int nvalid = pos.t1 - pos.t0;
     if (threadIdx.x == 0) {
-      const size_t tix = tile_index(P.seq, c, h);
-      constexpr uint32_t TB = TILE64_ELEMS * 2;
-      tc::bulk_s2g(P.QN + tix * TILE64_ELEMS, tq, TB);
-      tc::bulk_s2g(P.KN + tix * TILE64_ELEMS, tq + TILE64_ELEMS, TB);
-      tc::bulk_s2g(P.VN + tix * TILE64_ELEMS, tq + 2 * TILE64_ELEMS, TB);
-      tc::bulk_s2g(P.GM + tix * 64 * LDG, ps.gam, 64 * LDG * 4);
-      tc::bulk_s2g(P.BT + tix * 64, ps.beta, 64 * 4);
+      // the next item (its table lookups overlap this item's loads)
+      ChunkPos np;
+      nxt[0] = fwd_find_item(P.seq, item + gridDim.x, n_items, G, np);
+      nxt[1] = np.bos; nxt[2] = np.t0; nxt[3] = np.t1;
+      // the previous item's A store reads the region the decay tile is rebuilt in
+      if (P.A) tc::bulk_wait_all();
+    }
+    cp_async_wait<0>();
+    if (threadIdx.x < 64) ps.braw[threadIdx.x] = braw;
+    __syncthreads();
+
+    Strip s;
+    prologue_compute(P.in, ps, pos, h, P.conv, s);
+    // the prologue's products, so that the backward need not redo it: q, k, v
+    // strips into [64][128] tiles over the dead raw inputs, then (with the decay
+    // cumsum tile and beta, already in shared memory) five bulk stores issued by
+    // one thread; they complete while the operands are built
+    if (save_products) {
+      const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+      bf16* tq = reinterpret_cast<bf16*>(smem + IntraSmem::RAW);
+#pragma unroll
+      for (int r = 0; r < STRIP; ++r) {
+        const int t = STRIP * tg + r;
+        *reinterpret_cast<bf16x8*>(tq + t * D + 8 * cg) = pack8(s.q[r]);
+        *reinterpret_cast<bf16x8*>(tq + TILE64_ELEMS + t * D + 8 * cg) = pack8(s.k[r]);
+        *reinterpret_cast<bf16x8*>(tq + 2 * TILE64_ELEMS + t * D + 8 * cg) = pack8(s.v[r]);
+      }
+      tc::fence_async_smem();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const size_t tix = tile_index(P.seq, c, h);
+        constexpr uint32_t TB = TILE64_ELEMS * 2;
+        tc::bulk_s2g(P.QN + tix * TILE64_ELEMS, tq, TB);
+        tc::bulk_s2g(P.KN + tix * TILE64_ELEMS, tq + TILE64_ELEMS, TB);
+        tc::bulk_s2g(P.VN + tix * TILE64_ELEMS, tq + 2 * TILE64_ELEMS, TB);
+        tc::bulk_s2g(P.GM + tix * 64 * LDG, ps.gam, 64 * LDG * 4);
+        tc::bulk_s2g(P.BT + tix * 64, ps.beta, 64 * 4);
+        tc::bulk_commit();
+      }
+    }
+
+    Operands op;
+    op.Qa = reinterpret_cast<bf16*>(smem + IntraSmem::OPS);
+    op.Ka = op.Qa + 64 * LD128;
+    op.Kd = op.Ka + 64 * LD128;
+    op.Kb = op.Kd + 64 * LD128;
+    op.V = op.Kb + 64 * LD128;
+    op.Ke = op.V + 64 * LD128;
+    op.cvec = reinterpret_cast<float*>(smem + IntraSmem::CVEC);
+    op.er = nullptr;
+    op.ec = nullptr;
+    {
+      float qt[STRIP][8], kbar[STRIP][8];
+      build_operands<true>(s, ps.gam, op, qt, kbar);
+      const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+#pragma unroll
+      for (int r = 0; r < STRIP; ++r) {
+        int t = STRIP * tg + r;
+        if (t < nvalid) {
+          size_t off = ((size_t)(pos.t0 + t) * H + h) * D + 8 * cg;
+          *reinterpret_cast<bf16x8*>(P.Qt + off) = pack8(qt[r]);
+          *reinterpret_cast<bf16x8*>(P.Kb + off) = pack8(kbar[r]);
+        }
+      }
+      if (threadIdx.x < D)
+        P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
+    }
+    if (save_products && threadIdx.x == 0) tc::bulk_wait_all();  // the raw region is reused from here on
+    __syncthreads();
+    // the next item's inputs stream in while this one's blocks are computed
+    const int next = nxt[0];
+    ChunkPos npos;
+    npos.valid = next < n_items;
+    npos.bos = nxt[1]; npos.t0 = nxt[2]; npos.t1 = nxt[3];
+    if (npos.valid) braw = prologue_issue_loads(P.in, ps, npos, next / G, P.conv);
+    cp_async_commit();
+
+    float* Lp = reinterpret_cast<float*>(smem + IntraSmem::LP);
+    float* Ainv = reinterpret_cast<float*>(smem + IntraSmem::AINV);
+    float* xtmp = reinterpret_cast<float*>(smem + IntraSmem::XTMP);
+    bf16* Tbf = reinterpret_cast<bf16*>(smem + IntraSmem::TBF);
+    bf16* Msm = reinterpret_cast<bf16*>(smem + IntraSmem::MSM);
+    l_blocks(op, Lp);
+    __syncthreads();
+    // the diagonal inverse (warps 0-1) overlaps the M blocks (warps 4-15)
+    {
+      const int warp = threadIdx.x >> 5;
+      if (warp < 2) {
+        tri_inverse_diag(Lp, ps.beta, Ainv);
+      } else if (warp >= 4) {
+        if (warp < 14) lm_block_task(op, 1, warp - 4, Lp, Msm);
+        zero_m_upper(Msm, 128, INTRA_THREADS - 128);
+      }
+    }
+    __syncthreads();
+    tri_inverse_offdiag(Lp, ps.beta, Ainv, xtmp);
+    // T = A diag(beta) as bf16 (A's strictly-upper part is not stored: zeros)
+    for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
+      int r = i >> 5, cc = 2 * (i & 31);
+      float x0 = (cc <= r) ? Ainv[r * LDF64 + cc] * ps.beta[cc] : 0.f;
+      float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
+      *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
+    }
+    store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
+    tc::fence_async_smem();  // A (written by every thread) is read by the bulk store below
+    __syncthreads();
+    // A for the backward, as it sits in shared memory (entries above the
+    // diagonal are not meaningful): one bulk store, completed before the exit
+    if (P.A && threadIdx.x == 0) {
+      tc::bulk_s2g(P.A + tile_index(P.seq, c, h) * A_TILE_ELEMS, Ainv, A_TILE_ELEMS * 4);
       tc::bulk_commit();
     }
-  }
 
-  Operands op;
-  op.Qa = reinterpret_cast<bf16*>(smem + IntraSmem::OPS);
-  op.Ka = op.Qa + 64 * LD128;
-  op.Kd = op.Ka + 64 * LD128;
-  op.Kb = op.Kd + 64 * LD128;
-  op.V = op.Kb + 64 * LD128;
-  op.Ke = op.V + 64 * LD128;
-  op.cvec = reinterpret_cast<float*>(smem + IntraSmem::CVEC);
-  op.er = nullptr;
-  op.ec = nullptr;
-  {
-    float qt[STRIP][8], kbar[STRIP][8];
-    build_operands<true>(s, ps.gam, op, qt, kbar);
-    const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+    // W = T Ke, U = T V ; warp w -> rows 16(w&3), cols 32(w>>2)
+    {
+      const int warp = threadIdx.x >> 5;
+      const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
+      float accW[4][4], accU[4][4];
+      zero_acc<4>(accW);
+      zero_acc<4>(accU);
+      warp_mma<4, false, true>(accW, Tbf, LD64, m0, op.Ke, LD128, n0, 0, 64);
+      warp_mma<4, false, true>(accU, Tbf, LD64, m0, op.V, LD128, n0, 0, 64);
+      __syncthreads();  // Qa/Ka are dead: reuse them as staging
+      bf16* Wst = op.Qa;
+      bf16* Ust = op.Ka;
 #pragma unroll
-    for (int r = 0; r < STRIP; ++r) {
-      int t = STRIP * tg + r;
-      if (t < nvalid) {
-        size_t off = ((size_t)(pos.t0 + t) * H + h) * D + 8 * cg;
-        *reinterpret_cast<bf16x8*>(P.Qt + off) = pack8(qt[r]);
-        *reinterpret_cast<bf16x8*>(P.Kb + off) = pack8(kbar[r]);
-      }
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
+          *reinterpret_cast<uint32_t*>(Wst + r * LD128 + cc) = pack_bf16(accW[j][e], accW[j][e + 1]);
+          *reinterpret_cast<uint32_t*>(Ust + r * LD128 + cc) = pack_bf16(accU[j][e], accU[j][e + 1]);
+        }
+      __syncthreads();
+      store_rows128(P.W, Wst, LD128, nvalid, H, h, pos.t0);
+      store_rows128(P.U, Ust, LD128, nvalid, H, h, pos.t0);
     }
-    if (threadIdx.x < D)
-      P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
-  }
-  if (save_products && threadIdx.x == 0) tc::bulk_wait_all();  // the raw region is reused from here on
-  __syncthreads();
-
-  float* Lp = reinterpret_cast<float*>(smem + IntraSmem::LP);
-  float* Ainv = reinterpret_cast<float*>(smem + IntraSmem::AINV);
-  float* xtmp = reinterpret_cast<float*>(smem + IntraSmem::XTMP);
-  bf16* Tbf = reinterpret_cast<bf16*>(smem + IntraSmem::TBF);
-  bf16* Msm = reinterpret_cast<bf16*>(smem + IntraSmem::MSM);
-  l_blocks(op, Lp);
-  __syncthreads();
-  // the diagonal inverse (warps 0-1) overlaps the M blocks (warps 4-15)
-  {
-    const int warp = threadIdx.x >> 5;
-    if (warp < 2) {
-      tri_inverse_diag(Lp, ps.beta, Ainv);
-    } else if (warp >= 4) {
-      if (warp < 14) lm_block_task(op, 1, warp - 4, Lp, Msm);
-      zero_m_upper(Msm, 128, INTRA_THREADS - 128);
-    }
-  }
-  __syncthreads();
-  tri_inverse_offdiag(Lp, ps.beta, Ainv, xtmp);
-  // T = A diag(beta) as bf16 (A's strictly-upper part is not stored: zeros)
-  for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
-    int r = i >> 5, cc = 2 * (i & 31);
-    float x0 = (cc <= r) ? Ainv[r * LDF64 + cc] * ps.beta[cc] : 0.f;
-    float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
-    *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
-  }
-  store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
-  tc::fence_async_smem();  // A (written by every thread) is read by the bulk store below
-  __syncthreads();
-  // A for the backward, as it sits in shared memory (entries above the
-  // diagonal are not meaningful): one bulk store, completed before the exit
-  if (P.A && threadIdx.x == 0) {
-    tc::bulk_s2g(P.A + tile_index(P.seq, c, h) * A_TILE_ELEMS, Ainv, A_TILE_ELEMS * 4);
-    tc::bulk_commit();
-  }
-
-  // W = T Ke, U = T V ; warp w -> rows 16(w&3), cols 32(w>>2)
-  {
-    const int warp = threadIdx.x >> 5;
-    const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
-    float accW[4][4], accU[4][4];
-    zero_acc<4>(accW);
-    zero_acc<4>(accU);
-    warp_mma<4, false, true>(accW, Tbf, LD64, m0, op.Ke, LD128, n0, 0, 64);
-    warp_mma<4, false, true>(accU, Tbf, LD64, m0, op.V, LD128, n0, 0, 64);
-    __syncthreads();  // Qa/Ka are dead: reuse them as staging
-    bf16* Wst = op.Qa;
-    bf16* Ust = op.Ka;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        *reinterpret_cast<uint32_t*>(Wst + r * LD128 + cc) = pack_bf16(accW[j][e], accW[j][e + 1]);
-        *reinterpret_cast<uint32_t*>(Ust + r * LD128 + cc) = pack_bf16(accU[j][e], accU[j][e + 1]);
-      }
-    __syncthreads();
-    store_rows128(P.W, Wst, LD128, nvalid, H, h, pos.t0);
-    store_rows128(P.U, Ust, LD128, nvalid, H, h, pos.t0);
+    if (next >= n_items) break;
+    item = next;
+    pos = npos;
   }
   if (P.A && threadIdx.x == 0) tc::bulk_wait_all();  // the A store reads shared memory
 }
+
 
 // ---------------------------------------------------------------- state pass
 struct FwdStateParams {

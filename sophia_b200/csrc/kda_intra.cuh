@@ -41,11 +41,22 @@ struct PrologueSmem {
   float* gam;                    // [64][LDG] log2 cumulative decay
   float* beta;                   // [64]
   float* tot;                    // [16][128] scratch for the cumsum (one row per warp)
-  float* taps;                   // [3][4][128] conv taps, tap-major (conflict-free reads)
+  float* taps;                   // [3][128] x 4 conv taps, channel-major 16-byte slots at tap_slot(ch)
+  float* bias;                   // [128] dt_bias of the head, then A_log of the head
 };
 
-// Issue cp.async loads of the raw chunk inputs (zero fill outside [bos, t1)).
-__device__ __forceinline__ void prologue_issue_loads(const PrologueIn& in, const PrologueSmem& sm,
+// Slot of channel ch's four taps: the eight channels a strip thread reads
+// (8*cg .. 8*cg+7) land in eight different bank quads for any eight
+// consecutive cg, so the 128-bit reads are conflict-free.
+__device__ __forceinline__ int tap_slot(int ch) { return ch ^ ((ch >> 3) & 7); }
+
+// Issues cp.async loads of one (chunk, head)'s inputs: the raw q/k/v rows
+// t0-3 .. t0+63 (zero fill outside [bos, t1)), the gate logits, the head's
+// conv taps, dt_bias and A_log.  beta is gathered with a plain load instead
+// (one bf16 per token at a stride of H elements): the value of token t0 + tid
+// is returned to threads tid < 64, which store it into sm.braw once the
+// previous chunk no longer reads it.  The caller commits the group.
+__device__ __forceinline__ bf16 prologue_issue_loads(const PrologueIn& in, const PrologueSmem& sm,
                                                      const ChunkPos& p, int h, bool conv) {
   const int tid = threadIdx.x;
   const size_t rowH = (size_t)in.H * D;
@@ -68,20 +79,30 @@ __device__ __forceinline__ void prologue_issue_loads(const PrologueIn& in, const
     const bf16* gp = in.g + (ok ? ((size_t)t * rowH + (size_t)h * D + cc * 8) : 0);
     cp_async16(sm.graw + r * D + cc * 8, gp, ok);
   }
-  if (tid < 64) {
-    int t = p.t0 + tid;
-    sm.braw[tid] = (t < p.t1) ? in.beta[(size_t)t * in.H + h] : __float2bfloat16(0.f);
+  if (conv) {
+    for (int i = tid; i < 3 * D; i += blockDim.x) {
+      int X = i >> 7, ch = i & 127;
+      const float* src = (X == 0 ? in.conv_q : (X == 1 ? in.conv_k : in.conv_v)) + ((size_t)h * D + ch) * 4;
+      cp_async16(sm.taps + (X * D + tap_slot(ch)) * 4, src, true);
+    }
   }
+  if (tid < D / 4) cp_async16(sm.bias + 4 * tid, in.dt_bias + (size_t)h * D + 4 * tid, true);
+  if (tid == D / 4) cp_async4(sm.bias + D, in.A_log + h);
+  bf16 b = __float2bfloat16(0.f);
+  if (tid < 64 && p.t0 + tid < p.t1) b = in.beta[(size_t)(p.t0 + tid) * in.H + h];
+  return b;
 }
 
-// Elementwise prologue.  On return (after the trailing __syncthreads) sm.gam
-// and sm.beta are complete and the calling thread holds its strip of the
-// normalised (q scaled) q, k, post-conv v and log2 decays.
+// Elementwise prologue, run once the loads of prologue_issue_loads have landed
+// and sm.braw is filled (the caller waits and syncs).  On return (after the
+// trailing __syncthreads) sm.gam and sm.beta are complete and the calling
+// thread holds its strip of the normalised (q scaled) q, k, post-conv v and
+// log2 decays.
 struct Strip {
   float q[STRIP][8], k[STRIP][8], v[STRIP][8], gam[STRIP][8];
 };
 
-// w: tap-major [4][128] taps of this head in shared memory.
+// w: this tensor's [128] x 4 taps in shared memory (slots at tap_slot(ch)).
 __device__ __forceinline__ void conv_strip(const bf16* x, const float* w, int tg, int cg, bool conv,
                                            float (&out)[STRIP][8]) {
   if (conv) {
@@ -92,18 +113,16 @@ __device__ __forceinline__ void conv_strip(const bf16* x, const float* w, int tg
       unpack8(v, xs[r]);
     }
 #pragma unroll
-    for (int r = 0; r < STRIP; ++r)
+    for (int c = 0; c < 8; ++c) {
+      const float4 t4 = *reinterpret_cast<const float4*>(w + 4 * tap_slot(8 * cg + c));
+      const float wt[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) out[r][c] = 0.f;
+      for (int r = 0; r < STRIP; ++r) {
+        float acc = 0.f;
 #pragma unroll
-    for (int tap = 0; tap < 4; ++tap) {
-      float4 w0 = *reinterpret_cast<const float4*>(w + tap * D + 8 * cg);
-      float4 w1 = *reinterpret_cast<const float4*>(w + tap * D + 8 * cg + 4);
-      float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-      for (int r = 0; r < STRIP; ++r)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) out[r][c] = fmaf(wv[c], xs[r + tap][c], out[r][c]);
+        for (int tap = 0; tap < 4; ++tap) acc = fmaf(wt[tap], xs[r + tap][c], acc);
+        out[r][c] = acc;
+      }
     }
 #pragma unroll
     for (int r = 0; r < STRIP; ++r)
@@ -123,17 +142,6 @@ __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const Pro
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tg = tid >> 4, cg = tid & 15;
   const int nvalid = p.t1 - p.t0;
-  if (conv) {
-    // [H*128][4] taps -> tap-major [4][128] per tensor
-    for (int i = tid; i < 3 * D; i += blockDim.x) {
-      int X = i >> 7, ch = i & 127;
-      const float* src = (X == 0 ? in.conv_q : (X == 1 ? in.conv_k : in.conv_v)) + ((size_t)h * D + ch) * 4;
-      float4 t4 = __ldg(reinterpret_cast<const float4*>(src));
-      float* dst = sm.taps + X * 4 * D + ch;
-      dst[0] = t4.x; dst[D] = t4.y; dst[2 * D] = t4.z; dst[3 * D] = t4.w;
-    }
-    __syncthreads();
-  }
   const float* wq = sm.taps;
   const float* wk = sm.taps + 4 * D;
   const float* wv = sm.taps + 8 * D;
@@ -162,11 +170,11 @@ __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const Pro
     for (int c = 0; c < 8; ++c) { s.q[r][c] *= rq; s.k[r][c] *= rk; }
   }
   // gate: g = lb * sigmoid(exp(A_log) * (x + dt_bias)), log2 units, prefix sum
-  const float eA = __expf(__ldg(in.A_log + h));
+  const float eA = __expf(sm.bias[D]);
   float bias[8];
   {
-    float4 b0 = __ldg(reinterpret_cast<const float4*>(in.dt_bias + (size_t)h * D + 8 * cg));
-    float4 b1 = __ldg(reinterpret_cast<const float4*>(in.dt_bias + (size_t)h * D + 8 * cg + 4));
+    float4 b0 = *reinterpret_cast<const float4*>(sm.bias + 8 * cg);
+    float4 b1 = *reinterpret_cast<const float4*>(sm.bias + 8 * cg + 4);
     bias[0] = b0.x; bias[1] = b0.y; bias[2] = b0.z; bias[3] = b0.w;
     bias[4] = b1.x; bias[5] = b1.y; bias[6] = b1.z; bias[7] = b1.w;
   }
