@@ -67,6 +67,9 @@ struct BwdIntraSmem {
   static constexpr int DBL = DBT + 1024;                     // fp32 4 x 64   (dbeta from L)
   static constexpr int COLS = DBL + 1024;                    // fp32 4 x 128  (sum Kbar o dKbar)
   static_assert(COLS + 2048 <= LPB, "small tiles overlap Lp bf16");
+  static constexpr int GB = COLS + 2048;                     // fp32 dGam_C [128], dt_bias [128], A_log
+                                                             // (over the dead A tile, after the T build)
+  static_assert(GB + (2 * D + 4) * 4 <= LPB && GB % 16 == 0, "gate-backward vectors overlap Lp bf16");
   static_assert(TBF + 64 * LD64 * 2 <= RAWSZ + RAW, "T tile overflows");
   static_assert(AINV + A_TILE_ELEMS * 4 <= LPB && AINV % 16 == 0, "A tile overlaps Lp bf16 or is misaligned");
   // DEW aliases after the WY backward
@@ -218,6 +221,14 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     acc64n64_chunk(idx, r, cc);
     cp_async16(dMs + r * LD64 + cc * 8, P.dM + tix * TILE64N64_ELEMS + idx * 8, r < nv);
   }
+  // the gate backward's per-channel vectors, so that the tail waits on no global load
+  float* gbv = reinterpret_cast<float*>(smem + BwdIntraSmem::GB);
+  if (tid < 32)
+    cp_async16(gbv + 4 * tid, P.dGC + cidx * D + 4 * tid, true);
+  else if (tid < 64)
+    cp_async16(gbv + D + 4 * (tid - 32), P.in.dt_bias + (size_t)h * D + 4 * (tid - 32), true);
+  else if (tid == 64)
+    cp_async4(gbv + 2 * D, P.in.A_log + h);
   cp_async_commit();
   __syncthreads();
 
@@ -540,10 +551,10 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     float* partsum = reinterpret_cast<float*>(smem + BwdIntraSmem::DAS);  // 4 x 128 fp32 (dA is dead)
     partsum[part * D + col] = own;
     __syncthreads();
-    float run = P.dGC[cidx * D + col] + cols[col] + cols[D + col] + cols[2 * D + col] + cols[3 * D + col];
+    float run = gbv[col] + cols[col] + cols[D + col] + cols[2 * D + col] + cols[3 * D + col];
     for (int p2 = part + 1; p2 < 4; ++p2) run += partsum[p2 * D + col];
-    const float eA = __expf(__ldg(P.in.A_log + h));
-    const float bias = __ldg(P.in.dt_bias + (size_t)h * D + col);
+    const float eA = __expf(gbv[2 * D]);
+    const float bias = gbv[D + col];
     float sA = 0.f, sB = 0.f;
     for (int r = 16 * part + 15; r >= 16 * part; --r) {
       run += dGs[r * LDG + col];
