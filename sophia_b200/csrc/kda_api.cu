@@ -1,5 +1,7 @@
 // C ABI of the KDA layer (declared in include/kda_b200.h): argument checks,
 // buffer carving and kernel launches.  No allocation, no host sync.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -222,6 +224,37 @@ int sm_count() {
   return counts[dev];
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// Tensor map of a [TT][H][128] bf16 activation whose boxes are `rows` tokens x
+// 128 channels of one head (no swizzle; rows outside [0, TT) read as zeros).
+int encode_rows_map(CUtensorMap* m, const void* base, int H, long long TT, int rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(KDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)TT};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)D, 1u, (cuuint32_t)rows};
+  const cuuint32_t elem[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KDA_ERR_CUDA, "tensor map encoding failed (CUresult " + std::to_string((int)r) + ")");
+  return KDA_OK;
+}
+
 template <typename K>
 int set_smem(K kernel, int bytes, const char* name) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -386,6 +419,9 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A;
   ip.QN = sv.QN; ip.KN = sv.KN; ip.VN = sv.VN; ip.GM = sv.GM; ip.BT = sv.BT;
   ip.grid_chunks = pr.grid_chunks;
+  if ((rc = encode_rows_map(&ip.maps[0], q, H, pr.TT, 67)) || (rc = encode_rows_map(&ip.maps[1], k, H, pr.TT, 67)) ||
+      (rc = encode_rows_map(&ip.maps[2], v, H, pr.TT, 67)) || (rc = encode_rows_map(&ip.maps[3], g, H, pr.TT, 64)))
+    return rc;
   if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
   {
     // persistent: one CTA per SM (the shared-memory plan allows one) walks the items

@@ -25,6 +25,7 @@ struct FwdIntraParams {
   bf16 *QN, *KN, *VN;         // [slots x H] prologue products for the backward, or null
   float *GM, *BT;
   int grid_chunks;            // chunk slots per head: items are (slot, head), slot fastest
+  CUtensorMap maps[4];        // q, k, v, g as [T_total][H][128] bf16; boxes of 67 (q/k/v) and 64 (g) rows
 };
 
 // Shared-memory layout of the forward intra kernel (bytes).  The raw inputs,
@@ -41,7 +42,8 @@ struct IntraSmem {
   static constexpr int BRAW = BETA + 64 * 4;            // 64 bf16
   static constexpr int TAPS = BRAW + 64 * 2;            // 3 x 128 x 4 fp32
   static constexpr int BIAS = TAPS + 3 * D * 16;        // dt_bias [128], A_log, padding
-  static constexpr int NXT = BIAS + (D + 4) * 4;        // next item: index, bos, t0, t1
+  static constexpr int NXT = BIAS + (D + 4) * 4;        // next item: index, bos, t0, t1; then the
+                                                        // mbarrier of the raw rows (offset 16)
   static constexpr int XTMP = NXT + 32;                 // 3 warps x 16 x 17 fp32
   static constexpr int TBF = XTMP + 3 * 16 * 17 * 4;    // 64 x LD64 bf16
   static constexpr int END = TBF + 64 * LD64 * 2;
@@ -54,6 +56,8 @@ struct IntraSmem {
                     BIAS % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
                 "bulk-copy and cp.async targets");
   static_assert(64 * LD64 * 2 <= OPSZ && 16 * D * 4 <= OPSZ, "M staging or cumsum scratch overflows a tile");
+  static_assert((RAW + 67 * D * 2) % 128 == 0 && (RAW + 2 * 67 * D * 2) % 128 == 0 && GRAW % 128 == 0,
+                "tiled TMA destinations");
   static_assert(END <= 232448, "shared memory");
 };
 
@@ -82,7 +86,7 @@ __device__ __forceinline__ int fwd_find_item(const SeqInfo& seq, int from, int n
   return n_items;
 }
 
-__global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntraParams P) {
+__global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const __grid_constant__ FwdIntraParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = P.in.H, G = P.grid_chunks, n_items = G * H;
   ChunkPos pos;
@@ -101,10 +105,17 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
   ps.taps = reinterpret_cast<float*>(smem + IntraSmem::TAPS);
   ps.bias = reinterpret_cast<float*>(smem + IntraSmem::BIAS);
   int* nxt = reinterpret_cast<int*>(smem + IntraSmem::NXT);
+  uint64_t* raw_ready = reinterpret_cast<uint64_t*>(smem + IntraSmem::NXT + 16);
   const bool save_products = P.QN != nullptr;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(raw_ready, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
 
-  bf16 braw = prologue_issue_loads(P.in, ps, pos, item / G, P.conv);
+  bf16 braw = prologue_issue_loads(P.in, ps, pos, item / G, P.conv, raw_ready, P.maps);
   cp_async_commit();
+  uint32_t raw_phase = 0;
   for (;;) {
     const int c = item % G, h = item / G;
     const int nvalid = pos.t1 - pos.t0;
@@ -116,6 +127,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
       // the previous item's A store reads the region the decay tile is rebuilt in
       if (P.A) tc::bulk_wait_all();
     }
+    if (!tc::mbar_wait(raw_ready, raw_phase) && threadIdx.x == 0) atomicExch(&g_kda_device_error, 8);
+    raw_phase ^= 1u;
+    if (P.conv) zero_foreign_halo(ps, pos);
     cp_async_wait<0>();
     if (threadIdx.x < 64) ps.braw[threadIdx.x] = braw;
     __syncthreads();
@@ -177,13 +191,14 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(FwdIntr
         P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
     }
     if (save_products && threadIdx.x == 0) tc::bulk_wait_all();  // the raw region is reused from here on
+    tc::fence_async_smem();  // this item's generic accesses of the raw rows precede the next item's bulk copies
     __syncthreads();
     // the next item's inputs stream in while this one's blocks are computed
     const int next = nxt[0];
     ChunkPos npos;
     npos.valid = next < n_items;
     npos.bos = nxt[1]; npos.t0 = nxt[2]; npos.t1 = nxt[3];
-    if (npos.valid) braw = prologue_issue_loads(P.in, ps, npos, next / G, P.conv);
+    if (npos.valid) braw = prologue_issue_loads(P.in, ps, npos, next / G, P.conv, raw_ready, P.maps);
     cp_async_commit();
 
     float* Lp = reinterpret_cast<float*>(smem + IntraSmem::LP);

@@ -17,6 +17,7 @@
 #pragma once
 
 #include "kda_common.cuh"
+#include "kda_tc.cuh"
 
 namespace kda {
 
@@ -50,34 +51,30 @@ struct PrologueSmem {
 // consecutive cg, so the 128-bit reads are conflict-free.
 __device__ __forceinline__ int tap_slot(int ch) { return ch ^ ((ch >> 3) & 7); }
 
-// Issues cp.async loads of one (chunk, head)'s inputs: the raw q/k/v rows
-// t0-3 .. t0+63 (zero fill outside [bos, t1)), the gate logits, the head's
-// conv taps, dt_bias and A_log.  beta is gathered with a plain load instead
-// (one bf16 per token at a stride of H elements): the value of token t0 + tid
-// is returned to threads tid < 64, which store it into sm.braw once the
-// previous chunk no longer reads it.  The caller commits the group.
+// Issues the loads of one (chunk, head)'s inputs.  One thread starts four
+// tiled TMA loads -- the raw q/k/v rows t0-3 .. t0+63 and the gate-logit rows
+// t0 .. t0+63 of head h, boxes of `maps` (q, k, v, g: [T_total][H][128] bf16,
+// rows outside the tensor arrive as zeros) -- and a bulk copy of the head's
+// dt_bias, all completing on `ready` (one arrival with the byte count).  Rows
+// of another sequence in the conv halo (tokens bos-3 .. bos-1) are zeroed by
+// zero_foreign_halo once `ready` has completed; rows at or past t1 are masked
+// by the prologue.  The conv taps (16-byte slots at tap_slot) and A_log go by
+// cp.async, which the caller commits.  beta is gathered with a plain load (one
+// bf16 per token at a stride of H elements): the value of token t0 + tid is
+// returned to threads tid < 64, which store it into sm.braw once the previous
+// chunk no longer reads it.
+constexpr uint32_t PROLOGUE_TMA_BYTES = (3 * 67 + 64) * D * 2 + D * 4;
 __device__ __forceinline__ bf16 prologue_issue_loads(const PrologueIn& in, const PrologueSmem& sm,
-                                                     const ChunkPos& p, int h, bool conv) {
+                                                     const ChunkPos& p, int h, bool conv, uint64_t* ready,
+                                                     const CUtensorMap* maps) {
   const int tid = threadIdx.x;
-  const size_t rowH = (size_t)in.H * D;
-  // q/k/v: 67 rows x 16 chunks of 16 bytes each
-  for (int i = tid; i < 3 * 67 * 16; i += blockDim.x) {
-    int tsel = i / (67 * 16);
-    int rem = i - tsel * 67 * 16;
-    int r = rem >> 4, cc = rem & 15;
-    int t = p.t0 - 3 + r;
-    bool ok = (t >= p.bos) && (t < p.t1) && (conv || r >= 3);
-    const bf16* src = tsel == 0 ? in.q : (tsel == 1 ? in.k : in.v);
-    bf16* dst = tsel == 0 ? sm.xq : (tsel == 1 ? sm.xk : sm.xv);
-    const bf16* gp = src + (ok ? ((size_t)t * rowH + (size_t)h * D + cc * 8) : 0);
-    cp_async16(dst + r * D + cc * 8, gp, ok);
-  }
-  for (int i = tid; i < 64 * 16; i += blockDim.x) {
-    int r = i >> 4, cc = i & 15;
-    int t = p.t0 + r;
-    bool ok = t < p.t1;
-    const bf16* gp = in.g + (ok ? ((size_t)t * rowH + (size_t)h * D + cc * 8) : 0);
-    cp_async16(sm.graw + r * D + cc * 8, gp, ok);
+  if (tid == 0) {
+    tc::mbar_expect_tx(ready, PROLOGUE_TMA_BYTES);
+    tc::tma_load_3d(sm.xq, maps + 0, 0, h, p.t0 - 3, ready);
+    tc::tma_load_3d(sm.xk, maps + 1, 0, h, p.t0 - 3, ready);
+    tc::tma_load_3d(sm.xv, maps + 2, 0, h, p.t0 - 3, ready);
+    tc::tma_load_3d(sm.graw, maps + 3, 0, h, p.t0, ready);
+    tc::bulk_g2s(sm.bias, in.dt_bias + (size_t)h * D, D * 4, ready);
   }
   if (conv) {
     for (int i = tid; i < 3 * D; i += blockDim.x) {
@@ -86,11 +83,22 @@ __device__ __forceinline__ bf16 prologue_issue_loads(const PrologueIn& in, const
       cp_async16(sm.taps + (X * D + tap_slot(ch)) * 4, src, true);
     }
   }
-  if (tid < D / 4) cp_async16(sm.bias + 4 * tid, in.dt_bias + (size_t)h * D + 4 * tid, true);
-  if (tid == D / 4) cp_async4(sm.bias + D, in.A_log + h);
+  if (tid == 64) cp_async4(sm.bias + D, in.A_log + h);
   bf16 b = __float2bfloat16(0.f);
   if (tid < 64 && p.t0 + tid < p.t1) b = in.beta[(size_t)(p.t0 + tid) * in.H + h];
   return b;
+}
+
+// Zeroes the conv-halo rows (tokens t0-3 .. t0-1) that precede the sequence
+// start: the tiled loads bring the previous sequence's rows there.  Run after
+// the loads completed and before the barrier that publishes them.
+__device__ __forceinline__ void zero_foreign_halo(const PrologueSmem& sm, const ChunkPos& p) {
+  if (p.t0 - 3 >= p.bos) return;
+  for (int i = threadIdx.x; i < 3 * 3 * 16; i += blockDim.x) {
+    const int X = i / 48, r = (i >> 4) % 3, j = i & 15;
+    if (p.t0 - 3 + r < p.bos)
+      reinterpret_cast<uint4*>((X == 0 ? sm.xq : (X == 1 ? sm.xk : sm.xv)) + r * D)[j] = make_uint4(0u, 0u, 0u, 0u);
+  }
 }
 
 // Elementwise prologue, run once the loads of prologue_issue_loads have landed

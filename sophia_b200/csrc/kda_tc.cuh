@@ -18,6 +18,8 @@
 // K) and as an MN-major operand (tokens as K).
 #pragma once
 
+#include <cuda.h>  // CUtensorMap
+
 #include "kda_common.cuh"
 
 namespace kda {
@@ -111,6 +113,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint3
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(mbar)), "r"(bytes)
                : "memory");
+}
+// Tiled TMA load of one box of a rank-3 tensor map (no swizzle, no multicast)
+// into shared memory; out-of-range elements arrive as zeros.  The map lives in
+// kernel-parameter space (__grid_constant__); the innermost coordinate c0 must
+// be a multiple of 16 bytes' worth of elements.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(mbar))
+      : "memory");
 }
 // Bulk (TMA, non-tensor) copy of a contiguous global range into shared memory;
 // both addresses 16-byte aligned, bytes a multiple of 16.
