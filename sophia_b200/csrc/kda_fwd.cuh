@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     raw_phase ^= 1u;
     if (P.conv) zero_foreign_halo(ps, pos);
     cp_async_wait<0>();
-    if (threadIdx.x < 64) ps.braw[threadIdx.x] = braw;
+    if (threadIdx.x >= LOADER_T0) ps.braw[threadIdx.x - LOADER_T0] = braw;
     __syncthreads();
 
     Strip s;

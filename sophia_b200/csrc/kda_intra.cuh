@@ -51,6 +51,11 @@ struct PrologueSmem {
 // consecutive cg, so the 128-bit reads are conflict-free.
 __device__ __forceinline__ int tap_slot(int ch) { return ch ^ ((ch >> 3) & 7); }
 
+// The last two warps issue the next chunk's loads (the TMA issuer and the 64
+// beta gatherers): they are the least loaded warps while the inverse runs.
+constexpr int LOADER_T0 = INTRA_THREADS - 64;  // beta of token t0 + i goes to thread LOADER_T0 + i
+constexpr int TMA_ISSUER = INTRA_THREADS - 32;
+
 // Issues the loads of one (chunk, head)'s inputs.  One thread starts four
 // tiled TMA loads -- the raw q/k/v rows t0-3 .. t0+63 and the gate-logit rows
 // t0 .. t0+63 of head h, boxes of `maps` (q, k, v, g: [T_total][H][128] bf16,
@@ -60,15 +65,16 @@ __device__ __forceinline__ int tap_slot(int ch) { return ch ^ ((ch >> 3) & 7); }
 // zero_foreign_halo once `ready` has completed; rows at or past t1 are masked
 // by the prologue.  The conv taps (16-byte slots at tap_slot) and A_log go by
 // cp.async, which the caller commits.  beta is gathered with a plain load (one
-// bf16 per token at a stride of H elements): the value of token t0 + tid is
-// returned to threads tid < 64, which store it into sm.braw once the previous
-// chunk no longer reads it.
+// bf16 per token at a stride of H elements): the value of token t0 + i is
+// returned to thread LOADER_T0 + i, which stores it into sm.braw once the
+// previous chunk no longer reads it.  The gather is a predicated load into a
+// zeroed register, so that nothing waits for it before that store.
 constexpr uint32_t PROLOGUE_TMA_BYTES = (3 * 67 + 64) * D * 2 + D * 4;
 __device__ __forceinline__ bf16 prologue_issue_loads(const PrologueIn& in, const PrologueSmem& sm,
                                                      const ChunkPos& p, int h, bool conv, uint64_t* ready,
                                                      const CUtensorMap* maps) {
   const int tid = threadIdx.x;
-  if (tid == 0) {
+  if (tid == TMA_ISSUER) {
     tc::mbar_expect_tx(ready, PROLOGUE_TMA_BYTES);
     tc::tma_load_3d(sm.xq, maps + 0, 0, h, p.t0 - 3, ready);
     tc::tma_load_3d(sm.xk, maps + 1, 0, h, p.t0 - 3, ready);
@@ -84,9 +90,14 @@ __device__ __forceinline__ bf16 prologue_issue_loads(const PrologueIn& in, const
     }
   }
   if (tid == 64) cp_async4(sm.bias + D, in.A_log + h);
-  bf16 b = __float2bfloat16(0.f);
-  if (tid < 64 && p.t0 + tid < p.t1) b = in.beta[(size_t)(p.t0 + tid) * in.H + h];
-  return b;
+  unsigned short b = 0;
+  if (tid >= LOADER_T0) {
+    const int t = p.t0 + (tid - LOADER_T0);
+    const bf16* src = in.beta + (t < p.t1 ? (size_t)t * in.H + h : 0);
+    asm volatile("{\n.reg .pred p;\nsetp.lt.s32 p, %2, %3;\n@p ld.global.nc.u16 %0, [%1];\n}\n"
+                 : "+h"(b) : "l"(src), "r"(t), "r"(p.t1));
+  }
+  return __ushort_as_bfloat16(b);
 }
 
 // Zeroes the conv-halo rows (tokens t0-3 .. t0-1) that precede the sequence
@@ -445,29 +456,25 @@ __device__ __forceinline__ void warp_tf32_16x16(float (&acc)[2][4], const float*
 }
 
 // Diagonal 16x16 blocks of A, threads 0..63 (one column each); no sync.
+// Column-oriented forward substitution: once x_m is final it updates every
+// later row, x_r -= beta_r L'_rm x_m, so each step is 15 - m independent FMAs
+// and the dependent chain is one FMA per step (rows above the column stay 0).
 __device__ __forceinline__ void tri_inverse_diag(const float* Lp, const float* beta, float* A) {
   const int tid = threadIdx.x;
   // (strictly-upper blocks of A are never written; readers mask them)
   if (tid < 64) {
     const int blk = tid >> 4, col = tid & 15;
     const int o = 16 * blk;
-    float x[16];
+    float x[16], nb[16];
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
-      float acc = (r == col) ? 1.f : 0.f;
-      if (r > col) {
-        const float* lrow = Lp + (o + r) * LDF64 + o;
-        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+      x[r] = (r == col) ? 1.f : 0.f;
+      nb[r] = -beta[o + r];
+    }
 #pragma unroll
-        for (int m = 0; m < 15; m += 4) {
-          if (m < r && m >= col) p0 = fmaf(lrow[m], x[m], p0);
-          if (m + 1 < r && m + 1 >= col) p1 = fmaf(lrow[m + 1], x[m + 1], p1);
-          if (m + 2 < r && m + 2 >= col) p2 = fmaf(lrow[m + 2], x[m + 2], p2);
-          if (m + 3 < 15 && m + 3 < r && m + 3 >= col) p3 = fmaf(lrow[m + 3], x[m + 3], p3);
-        }
-        acc = -beta[o + r] * ((p0 + p1) + (p2 + p3));
-      }
-      x[r] = acc;
+    for (int m = 0; m < 15; ++m) {
+#pragma unroll
+      for (int r = m + 1; r < 16; ++r) x[r] = fmaf(nb[r] * Lp[(o + r) * LDF64 + o + m], x[m], x[r]);
     }
 #pragma unroll
     for (int r = 0; r < 16; ++r) A[(o + r) * LDF64 + o + col] = x[r];
