@@ -238,15 +238,18 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     float acc[4][4];
     zero_acc<4>(acc);
     warp_mma_t<4, true, true>(acc, PadTile{Tbf, LD64}, m0, dEt, n0, 0, 64);  // dv = T^T dE
+    // 16-byte runs per lane (quad transpose) instead of scattered 4-byte stores
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int e = 0; e < 4; e += 2) {
+      uint32_t w[4];
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        if (r < nv)
-          *reinterpret_cast<uint32_t*>(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + cc) =
-              pack_bf16(acc[j][e], acc[j][e + 1]);
-      }
+      for (int j = 0; j < 4; ++j) w[j] = pack_bf16(acc[j][e], acc[j][e + 1]);
+      quad_transpose4(w);
+      const int r = m0 + acc_row(e);
+      if (r < nv)
+        *reinterpret_cast<uint4*>(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + n0 + 8 * (tid & 3)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+    }
     zero_acc<4>(acc);
     warp_mma_t<4, true, true>(acc, PadTile{Tbf, LD64}, m0, dWt, n0, 0, 64);  // dKe = T^T dW
     float colsum[4][2];
@@ -521,16 +524,22 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   }
   // ---- outputs ---------------------------------------------------------------
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
+  for (int e = 0; e < 4; e += 2) {
+    uint32_t wq[4], wk[4];
 #pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-      if (r < nv) {
-        size_t off = ((size_t)(pos.t0 + r) * H + h) * D + cc;
-        *reinterpret_cast<uint32_t*>(P.dq_hat + off) = pack_bf16(dq[j][e], dq[j][e + 1]);
-        *reinterpret_cast<uint32_t*>(P.dk_hat + off) = pack_bf16(dk[j][e], dk[j][e + 1]);
-      }
+    for (int j = 0; j < 4; ++j) {
+      wq[j] = pack_bf16(dq[j][e], dq[j][e + 1]);
+      wk[j] = pack_bf16(dk[j][e], dk[j][e + 1]);
     }
+    quad_transpose4(wq);
+    quad_transpose4(wk);
+    const int r = m0 + acc_row(e);
+    if (r < nv) {
+      const size_t off = ((size_t)(pos.t0 + r) * H + h) * D + n0 + 8 * (tid & 3);
+      *reinterpret_cast<uint4*>(P.dq_hat + off) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+      *reinterpret_cast<uint4*>(P.dk_hat + off) = make_uint4(wk[0], wk[1], wk[2], wk[3]);
+    }
+  }
   const float* cols = reinterpret_cast<const float*>(smem + BwdIntraSmem::COLS);
   float* dGs = ps.gam;  // Gam is dead: every decay factor is in registers
 #pragma unroll

@@ -262,6 +262,23 @@ __device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
 }
 
 // Row/col of accumulator element e (0..3) of n8 tile j for this lane.
+// Transposes the 4x4 matrix of 32-bit words held by a lane quad (lane t holds
+// row t) with two xor-shuffle rounds: afterwards lane t holds column t.  For
+// an accumulator row packed as w[j] = bf16 pair at columns 8j + 2t, 8j + 2t + 1
+// this leaves lane t with the eight consecutive columns 8t .. 8t + 7.
+__device__ __forceinline__ void quad_transpose4(uint32_t (&w)[4]) {
+  const int t = threadIdx.x & 3;
+  const bool hi2 = t & 2, hi1 = t & 1;
+  uint32_t a0 = hi2 ? w[0] : w[2], a1 = hi2 ? w[1] : w[3];
+  uint32_t b0 = __shfl_xor_sync(0xffffffffu, a0, 2), b1 = __shfl_xor_sync(0xffffffffu, a1, 2);
+  if (hi2) { w[0] = b0; w[1] = b1; } else { w[2] = b0; w[3] = b1; }
+  a0 = hi1 ? w[0] : w[1];
+  a1 = hi1 ? w[2] : w[3];
+  b0 = __shfl_xor_sync(0xffffffffu, a0, 1);
+  b1 = __shfl_xor_sync(0xffffffffu, a1, 1);
+  if (hi1) { w[0] = b0; w[2] = b1; } else { w[1] = b0; w[3] = b1; }
+}
+
 __device__ __forceinline__ int acc_row(int e) { return ((threadIdx.x & 31) >> 2) + ((e >> 1) << 3); }
 __device__ __forceinline__ int acc_col(int j, int e) { return 8 * j + 2 * (threadIdx.x & 3) + (e & 1); }
 
