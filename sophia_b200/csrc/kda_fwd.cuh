@@ -69,28 +69,21 @@ __device__ __forceinline__ void store_rows128(bf16* gdst, const bf16* s, int ld,
     *reinterpret_cast<bf16x8*>(gdst + ((size_t)(t0 + r) * H + h) * D + cc * 8) = v;
   }
 }
-__device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0) {
-  for (int i = threadIdx.x; i < nrows * 8; i += blockDim.x) {
+// Same for rows of 64 bf16, by threads [first, first + count) of the CTA.
+__device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0,
+                                             int first, int count) {
+  for (int i = threadIdx.x - first; i < nrows * 8; i += count) {
     int r = i >> 3, cc = i & 7;
     bf16x8 v = *reinterpret_cast<const bf16x8*>(s + r * ld + cc * 8);
     *reinterpret_cast<bf16x8*>(gdst + ((size_t)(t0 + r) * H + h) * 64 + cc * 8) = v;
   }
 }
 
-// First valid item at or after `from` in steps of the grid (pos filled), or n_items.
-__device__ __forceinline__ int fwd_find_item(const SeqInfo& seq, int from, int n_items, int G, ChunkPos& pos) {
-  for (int it = from; it < n_items; it += gridDim.x) {
-    pos = chunk_pos(seq, it % G);
-    if (pos.valid) return it;
-  }
-  return n_items;
-}
-
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const __grid_constant__ FwdIntraParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = P.in.H, G = P.grid_chunks, n_items = G * H;
   ChunkPos pos;
-  int item = fwd_find_item(P.seq, blockIdx.x, n_items, G, pos);
+  int item = next_valid_item(P.seq, blockIdx.x, n_items, G, pos);
   if (item >= n_items) return;
 
   PrologueSmem ps;
@@ -122,7 +115,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     if (threadIdx.x == 0) {
       // the next item (its table lookups overlap this item's loads)
       ChunkPos np;
-      nxt[0] = fwd_find_item(P.seq, item + gridDim.x, n_items, G, np);
+      nxt[0] = next_valid_item(P.seq, item + gridDim.x, n_items, G, np);
       nxt[1] = np.bos; nxt[2] = np.t0; nxt[3] = np.t1;
       // the previous item's A store reads the region the decay tile is rebuilt in
       if (P.A) tc::bulk_wait_all();
@@ -227,7 +220,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
       *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
     }
-    store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
+    store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0, 0, INTRA_THREADS);
     tc::fence_async_smem();  // A (written by every thread) is read by the bulk store below
     __syncthreads();
     // A for the backward, as it sits in shared memory (entries above the

@@ -34,6 +34,17 @@ struct PrologueIn {
   float scale, lower_bound;
 };
 
+// Persistent chunk kernels walk the items (chunk slot, head), slot fastest,
+// in steps of the grid.  First valid item at or after `from` (pos filled), or
+// n_items.
+__device__ __forceinline__ int next_valid_item(const SeqInfo& seq, int from, int n_items, int G, ChunkPos& pos) {
+  for (int it = from; it < n_items; it += gridDim.x) {
+    pos = chunk_pos(seq, it % G);
+    if (pos.valid) return it;
+  }
+  return n_items;
+}
+
 // Shared-memory views used by the prologue.
 struct PrologueSmem {
   bf16* xq; bf16* xk; bf16* xv;  // [67][128] raw rows t0-3 .. t0+63 (row stride 128)

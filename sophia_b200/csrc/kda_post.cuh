@@ -68,11 +68,11 @@ __device__ __forceinline__ void post_norm_bwd(const float (&y)[4], const float (
     ss += __shfl_xor_sync(0xffffffffu, ss, m);
     dot += __shfl_xor_sync(0xffffffffu, dot, m);
   }
-  const float nrm = sqrtf(ss);
-  if (nrm > 1e-12f) {
-    const float inv = 1.f / nrm, nd = dot * inv * dscale;
+  if (ss > 1e-24f) {  // |y| > eps
+    // dy = dscale g / |y| - y (dscale (y . g) / |y|^3); rsqrt.approx is within 2 ulp
+    const float inv = rsqrtf(ss), gs = dscale * inv, ys = gs * dot * inv * inv;
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) dyv[ch] = (dscale * g[ch] - y[ch] * inv * nd) * inv;
+    for (int ch = 0; ch < 4; ++ch) dyv[ch] = fmaf(g[ch], gs, -y[ch] * ys);
   } else {
 #pragma unroll
     for (int ch = 0; ch < 4; ++ch) dyv[ch] = dscale * g[ch] * 1e12f;
