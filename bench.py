@@ -62,7 +62,7 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
 # --warmup 3 --profile` (B=2: the per-launch traffic scales with the token-heads
 # processed); summary in profiles/kda_kernels_dram_b2.md.
 NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
-    "fwd_intra": 2055.3, "fwd_state": 1845.2, "bwd_state": 2826.8, "bwd_intra": 3274.1, "bwd_post": 2191.6,
+    "fwd_intra": 3305.7, "fwd_state": 1845.9, "bwd_state": 2822.4, "bwd_intra": 3829.8, "bwd_post": 2192.1,
 }
 
 
