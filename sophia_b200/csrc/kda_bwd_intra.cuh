@@ -55,11 +55,10 @@ struct BwdIntraSmem {
   static constexpr int MISC = BRAW + 64 * 2;                 // mbarriers: gradient tiles, prologue products
   static constexpr int END = MISC + 16;
   // RAW aliases after the operands are built
-  static constexpr int LP = RAW;                             // fp32 64 x LDF64 (16640)
   static constexpr int AINV = RAW + 16640;                   // fp32 [64][LDF64] A from the forward (until the T build;
                                                              // DMS reuses part of it afterwards)
   static constexpr int LPB = RAW + 33280;                    // bf16 64 x LD64 (after inverse)
-  static constexpr int ABF = RAW;                            // bf16 64 x LD64 (after Lp fp32 is dead)
+  static constexpr int ABF = RAW;                            // bf16 64 x LD64
   static constexpr int TBF = RAW + 42496;                    // bf16 64 x LD64
   static constexpr int DMS = RAW + 9216;                     // bf16 64 x LD64
   static constexpr int DLS = RAW + 18432;                    // bf16 64 x LD64
@@ -186,27 +185,18 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   }
   const Acc64Tile dEt{dEs}, dWt{dWs};
 
-  float* Lp = reinterpret_cast<float*>(smem + BwdIntraSmem::LP);
-  l_blocks(op, Lp);
-  if (!tc::mbar_wait(tiles_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 5);
-  __syncthreads();
   bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
-  for (int i = tid; i < 64 * 32; i += blockDim.x) {
-    int r = i >> 5, cc = 2 * (i & 31);
-    float x0 = cc < r ? Lp[r * LDF64 + cc] : 0.f;
-    float x1 = cc + 1 < r ? Lp[r * LDF64 + cc + 1] : 0.f;
-    *reinterpret_cast<uint32_t*>(Lpb + r * LD64 + cc) = pack_bf16(x0, x1);
-  }
+  l_blocks_bf16(op, Lpb);  // only the dbeta row sums read L', in bf16
+  if (!tc::mbar_wait(tiles_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 5);
   __syncthreads();
   bf16* Abf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::ABF);
   bf16* Tbf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::TBF);
   {
-    // A (fp32 at [16640, 33024)) -> Abf ([0, 9216)) and Tbf: Abf only overlaps the dead Lp
+    // A (fp32, [16640, 33280) of the raw region) -> Abf ([0, 9216)) and Tbf ([42496, 51712)): no overlap
     float av[8];
     const int r = tid >> 3, c0 = (tid & 7) * 8;
 #pragma unroll
     for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Asm[r * LDF64 + c0 + i] : 0.f;
-    __syncthreads();
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
       *reinterpret_cast<uint32_t*>(Abf + r * LD64 + c0 + i) = pack_bf16(av[i], av[i + 1]);

@@ -397,7 +397,8 @@ __device__ __forceinline__ void block_product(float (&acc)[2][4], const bf16* Ar
 }
 
 // One 16x16 block of L' (which == 0, strictly lower on the diagonal, fp32 into
-// Lp) or of M (which == 1, lower-inclusive on the diagonal, bf16 into Msm).
+// Lp, or bf16 into Msm when Lp is null) or of M (which == 1, lower-inclusive
+// on the diagonal, bf16 into Msm).
 // Blocks are numbered (0,0),(1,0),(1,1),(2,0),(2,1),(2,2),(3,0),...
 __device__ __forceinline__ void lm_block_task(const Operands& op, int which, int bi, float* Lp, bf16* Msm) {
   int I = bi >= 6 ? 3 : (bi >= 3 ? 2 : (bi >= 1 ? 1 : 0));
@@ -416,7 +417,10 @@ __device__ __forceinline__ void lm_block_task(const Operands& op, int which, int
         Msm[gi * LD64 + gj] = __float2bfloat16(x);
       } else {
         if (I == J && c >= r) x = 0.f;
-        Lp[gi * LDF64 + gj] = x;
+        if (Lp)
+          Lp[gi * LDF64 + gj] = x;
+        else
+          Msm[gi * LD64 + gj] = __float2bfloat16(x);
       }
     }
 }
@@ -437,14 +441,20 @@ __device__ __forceinline__ void l_blocks(const Operands& op, float* Lp) {
   const int warp = threadIdx.x >> 5;
   if (warp < 10) lm_block_task(op, 0, warp, Lp, nullptr);
 }
+// L' as a bf16 64 x LD64 tile, strictly lower, zeros above (warps 10-15 clear
+// the upper blocks while the others form the lower ones).  Caller syncs.
+__device__ __forceinline__ void l_blocks_bf16(const Operands& op, bf16* Lb) {
+  const int warp = threadIdx.x >> 5;
+  if (warp < 10)
+    lm_block_task(op, 0, warp, nullptr, Lb);
+  else
+    zero_m_upper(Lb, 320, INTRA_THREADS - 320);
+}
 
 // A = (I + diag(beta) Lp)^-1 (unit lower triangular, fp32; only the lower
-// 16x16 blocks are written).  Ends with __syncthreads().
-//   diagonal blocks: forward substitution in fp32, one column per thread;
-//   off-diagonal blocks, by distance d = I - J:
-//       X = sum_{K=J}^{I-1} L_IK A_KJ,   A_IJ = -A_II X
-//   as 16x16x16 tensor-core products (tf32 in, fp32 accumulate), one warp per
-//   block, X staged through the warp's slice of xtmp ([16 warps][16][17]).
+// 16x16 blocks are written): tri_inverse_diag (forward substitution in fp32,
+// one column per thread) for the diagonal blocks, then tri_inverse_offdiag
+// (16x16x16 tensor-core products, tf32 in, fp32 accumulate) for the rest.
 __device__ __forceinline__ void warp_tf32_16x16(float (&acc)[2][4], const float* Am, int lda, const float* rowscale,
                                                 const float* Bm, int ldb) {
   // acc[16 x 16] += diag(rowscale) Am[16 x 16] * Bm[16 x 16] (row-major fp32 tiles)
@@ -529,11 +539,5 @@ __device__ __forceinline__ void tri_inverse_offdiag(const float* Lp, const float
   }
 }
 
-// Whole inverse: diagonal blocks, sync, off-diagonal blocks.
-__device__ __forceinline__ void tri_inverse(const float* Lp, const float* beta, float* A, float* xtmp) {
-  tri_inverse_diag(Lp, beta, A);
-  __syncthreads();
-  tri_inverse_offdiag(Lp, beta, A, xtmp);
-}
 
 }  // namespace kda
