@@ -44,7 +44,7 @@ struct BwdIntraSmem {
   static constexpr int OPSZ = 64 * LD128 * 2;                // 17408
   static constexpr int OPS = 0;                              // 6 operand tiles
   static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x LDG fp32 (later dQt, dKbar, dGam)
-  static constexpr int DEW = GAM + 64 * LDG * 4;             // dE, dW tiles (graw during prologue)
+  static constexpr int DEW = GAM + 64 * LDG * 4;             // dE, dW tiles
   static constexpr int RAW = DEW + 2 * OPSZ;                 // raw q/k/v, later small tiles
   static constexpr int RAWSZ = 51712;
   static constexpr int CVEC = RAW + RAWSZ;                   // 6 x 128 fp32
@@ -94,7 +94,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   ps.xq = reinterpret_cast<bf16*>(smem + BwdIntraSmem::RAW);
   ps.xk = ps.xq + 64 * D;
   ps.xv = ps.xk + 64 * D;
-  ps.graw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
   ps.braw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::BRAW);
   ps.gam = reinterpret_cast<float*>(smem + BwdIntraSmem::GAM);
   ps.beta = reinterpret_cast<float*>(smem + BwdIntraSmem::BETA);
@@ -104,7 +103,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   // five bulk copies; each thread then takes its strip.
   uint64_t* pro_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC) + 1;
   if (tid == 0) {
-    tc::mbar_init(reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC), 1);
+    tc::mbar_init(reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC), 2);  // dE/dW, then the rest
     tc::mbar_init(pro_ready, 1);
     tc::fence_mbar_init();
   }
@@ -119,6 +118,16 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     tc::bulk_g2s(ps.beta, P.BT + tix * 64, BB, pro_ready);
   }
   if (!tc::mbar_wait(pro_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 7);
+  // dE and dW land in their own region while the operands are built; dQt,
+  // dKbar and A follow once the decay and raw regions are free
+  if (tid == 0) {
+    constexpr uint32_t TB = TILE64_ELEMS * 2;
+    uint64_t* tr = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC);
+    bf16* de = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
+    tc::mbar_expect_tx(tr, 2 * TB);
+    tc::bulk_g2s(de, P.dE + tix * TILE64_ELEMS, TB, tr);
+    tc::bulk_g2s(de + 64 * LD128, P.dW + tix * TILE64_ELEMS, TB, tr);
+  }
   Strip s;
   {
     const int tg = tid >> 4, cg = tid & 15;
@@ -163,11 +172,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   __syncthreads();
 
   // The state-pass gradient tiles (acc64 order, rows past the end zero) and
-  // A = (I + diag(beta) L')^-1 as the forward computed it arrive as five bulk
-  // copies issued by one thread, so the warps go on with L' meanwhile; the
-  // tiles stay in their global order (Acc64Tile addressing).  dQt and dKbar
-  // land in the dead decay region, A in the dead raw region (clear of Lp,
-  // which l_blocks writes below).
+  // A = (I + diag(beta) L')^-1 as the forward computed it arrive by bulk copies
+  // issued by one thread (dE and dW since the products landed, the rest now),
+  // so the warps go on with L' meanwhile; the tiles stay in their global order
+  // (Acc64Tile addressing).  dQt and dKbar land in the dead decay region, A in
+  // the dead raw region (clear of L', which l_blocks writes below).
   bf16* dEs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
   bf16* dWs = dEs + 64 * LD128;
   bf16* dQs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GAM);
@@ -176,9 +185,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   uint64_t* tiles_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC);
   if (tid == 0) {
     constexpr uint32_t TB = TILE64_ELEMS * 2, AB = A_TILE_ELEMS * 4;
-    tc::mbar_expect_tx(tiles_ready, 4 * TB + AB);
-    tc::bulk_g2s(dEs, P.dE + tix * TILE64_ELEMS, TB, tiles_ready);
-    tc::bulk_g2s(dWs, P.dW + tix * TILE64_ELEMS, TB, tiles_ready);
+    tc::mbar_expect_tx(tiles_ready, 2 * TB + AB);
     tc::bulk_g2s(dQs, P.dQt + tix * TILE64_ELEMS, TB, tiles_ready);
     tc::bulk_g2s(dKs, P.dKb + tix * TILE64_ELEMS, TB, tiles_ready);
     tc::bulk_g2s(Asm, P.A + tix * A_TILE_ELEMS, AB, tiles_ready);

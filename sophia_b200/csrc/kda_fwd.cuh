@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       nxt[0] = next_valid_item(P.seq, item + gridDim.x, n_items, G, np);
       nxt[1] = np.bos; nxt[2] = np.t0; nxt[3] = np.t1;
       // the previous item's A store reads the region the decay tile is rebuilt in
-      if (P.A) tc::bulk_wait_all();
+      if (P.A) tc::bulk_wait_read_all();
     }
     if (!tc::mbar_wait(raw_ready, raw_phase) && threadIdx.x == 0) atomicExch(&g_kda_device_error, 8);
     raw_phase ^= 1u;
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       if (threadIdx.x < D)
         P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
     }
-    if (save_products && threadIdx.x == 0) tc::bulk_wait_all();  // the raw region is reused from here on
+    if (save_products && threadIdx.x == 0) tc::bulk_wait_read_all();  // the raw region is reused from here on
     tc::fence_async_smem();  // this item's generic accesses of the raw rows precede the next item's bulk copies
     __syncthreads();
     // the next item's inputs stream in while this one's blocks are computed

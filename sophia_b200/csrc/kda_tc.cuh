@@ -146,6 +146,11 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
 // Waits until this thread's bulk groups have completed (writes performed).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+// Waits until this thread's bulk stores have finished reading their shared-memory
+// sources (the writes to global memory may still be in flight): enough to reuse the source.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+}
 
 // 32 lanes x 32 consecutive fp32 columns: this thread gets its lane's columns
 // [col, col + 32).  taddr = (lane base << 16) | column.
