@@ -1,14 +1,18 @@
 """Benchmark of the B200 KDA layer (forward + backward), one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg1|cfg3]
+                    [--workload cfg1|cfg2|cfg3]
 
 Step = one forward + backward of the KDA layer (ShortConv+SiLU, L2 norms,
 gate, beta, chunked gated delta rule) over one batch of synthetic inputs of
 configuration 1 (8 sequences x 4096 tokens x 16 heads x 128, bf16, fp32 state)
 per GPU, then one NCCL all-reduce of the layer's weight gradients when N > 1
 (weak scaling: every rank processes its own 8 sequences).  ``--workload cfg3``
-shards configuration 3's 320 sequences over the ranks instead (strong scaling).
+shards configuration 3's 320 sequences over the ranks instead (strong scaling);
+``--workload cfg2`` steps the whole mixer block of configuration 2
+(``sophia_b200.mixer.KDAMixerBlock``: input RMSNorm, fused q/k/v/gate GEMM,
+decay and beta projections, the KDA layer, gated output RMSNorm, out-
+projection; 4 x 4096 tokens, hidden 1536, bf16 autocast) per GPU.
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launch stream, max over ranks.
@@ -72,7 +76,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg1", "cfg3"], default="cfg1")
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3"], default="cfg1")
     ap.add_argument("--profile", action="store_true",
                     help="run the warm-up and K layer steps only, print nothing (command for ncu captures)")
     ap.add_argument("--batch", type=int, default=None,
@@ -342,35 +346,217 @@ def cpu_sample(tokens: int, threads: int | None = None):
     return tokens / dt, dt
 
 
+MIXER_METRIC = "KDA mixer block fwd+bwd tokens/s at B=4,T=4096,hidden 1536,H=16,D=128 (cfg2) + % roofline"
+DIM, DECAY_RANK = 1536, 128
+
+
+def mixer_flops_per_token() -> float:
+    """Algorithmic FLOPs per token of the block, fwd+bwd: its GEMMs (2 m n k
+    per token, x3 for fwd+bwd) and the KDA layer's tensor FLOPs (16 heads)."""
+    inner = H * D
+    gemm = DIM * 4 * inner + DIM * DECAY_RANK + DECAY_RANK * inner + DIM * H + inner * DIM
+    layer = sum(KERNEL_FLOPS_PER_TOKEN_HEAD.values()) * H
+    return 3 * 2 * gemm + layer
+
+
+def bench_mixer(a, rank, world, local_rank):
+    import torch.distributed as dist
+    from sophia_b200 import _lib, dp
+    from sophia_b200.mixer import KDAMixerBlock
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    B = a.batch or 4
+    gen = torch.Generator().manual_seed(42 + rank)
+    m = KDAMixerBlock(dim=DIM, heads=H, decay_rank=DECAY_RANK, generator=gen).to(device)
+    x = torch.randn(B, T, DIM, generator=gen).to(device, torch.bfloat16)
+    dout = torch.randn(B, T, DIM, generator=gen).to(device, torch.bfloat16)
+    params = list(m.parameters())
+    layer = {"A_log": m.A_log, "dt_bias": m.dt_bias, "conv_q": m.conv_q, "conv_k": m.conv_k, "conv_v": m.conv_v}
+    flat = torch.empty(sum(p.numel() for p in params), device=device, dtype=torch.float32)
+    small = torch.empty(dp.bucket_numel(H, D), device=device, dtype=torch.float32)
+
+    def step(xin=None, din=None):
+        for prm in params:
+            prm.grad = None
+        xx = (x if xin is None else xin).detach().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = m(xx)
+        out.backward(dout if din is None else din)
+        if world > 1:  # data parallel: one all-reduce of every weight gradient
+            torch.cat([prm.grad.reshape(-1) for prm in params], out=flat)
+            dist.all_reduce(flat)
+        dp.grad_bucket(layer, out=small)
+        return small
+
+    def timed(fn, steps, sampler=None):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        h0 = time.perf_counter()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        if sampler is not None:
+            sampler.mark(h0, time.perf_counter())
+        if world > 1:
+            dist.barrier()
+        return dp.max_over_ranks(e0.elapsed_time(e1), device)
+
+    for _ in range(a.warmup):
+        step()
+    if a.profile:
+        timed(step, a.steps)
+        return None
+    sampler = ClockSampler(device)
+    sampler.start()
+    ms = timed(step, a.steps, sampler)
+    clocks = sampler.stop()
+    tokens = world * B * T * a.steps
+    value = tokens / (ms / 1e3)
+
+    _lib.timing_reset()
+    _lib.timing_enable(True)
+    timed(step, a.steps)
+    _lib.timing_enable(False)
+    kern = _lib.timing_read()
+    _lib.timing_reset()
+    launches = sum(n for n, _ in kern.values())
+
+    # end to end: x and dO cross from pinned host memory every step (two
+    # alternating buffers on a copy stream), the layer's small weight
+    # gradients come back
+    host = {"x": x.detach().cpu().pin_memory(), "do": dout.detach().cpu().pin_memory()}
+    bufs = [{k: torch.empty_like(v, device=device) for k, v in host.items()} for _ in range(2)]
+    out_host = torch.empty(small.numel(), dtype=torch.float32).pin_memory()
+    copy_stream = torch.cuda.Stream(device=device)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_run(steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        copy_stream.wait_event(e0)
+
+        def issue_copy(i):
+            b = i % 2
+            with torch.cuda.stream(copy_stream):
+                if i >= 2:
+                    copy_stream.wait_event(freed[b])
+                for k in host:
+                    bufs[b][k].copy_(host[k], non_blocking=True)
+                copied[b].record(copy_stream)
+
+        issue_copy(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                issue_copy(i + 1)
+            b = i % 2
+            st.wait_event(copied[b])
+            step(bufs[b]["x"], bufs[b]["do"])
+            out_host.copy_(small, non_blocking=True)
+            freed[b].record(st)
+        e1.record(st)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return dp.max_over_ranks(e0.elapsed_time(e1), device)
+
+    e2e_run(2)
+    e2e_steps = max(3, min(a.steps, 10))
+    ms_e2e = e2e_run(e2e_steps)
+
+    hbm, tc, tc_sus, src = peaks()
+    th = B * T * H
+    dom = max((k for k in kern if k in KERNEL_BYTES_PER_TOKEN_HEAD), key=lambda k: kern[k][1])
+    n_l, tot = kern[dom]
+    achieved = KERNEL_BYTES_PER_TOKEN_HEAD[dom] * th / (tot / max(1, n_l) / 1e3) / 1e9
+    block_tflops = mixer_flops_per_token() * B * T / (ms / a.steps / 1e3) / 1e12
+    return {
+        "value": value, "ms": ms / a.steps, "B": B, "clocks": clocks,
+        "e2e": {"value": world * B * T * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host.values()),
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None, "peak_source": src,
+                     "block": {"bound": "tensor", "flops_per_token": round(mixer_flops_per_token()),
+                               "achieved_tflops": round(block_tflops, 1), "peak_tflops": tc_sus,
+                               "frac": round(block_tflops / tc_sus, 4)},
+                     "kernel_ms_per_step": {k: round(v[1] / a.steps, 4) for k, v in kern.items() if v[0]}},
+    }
+
+
+def cpu_block_sample(tokens: int):
+    """The mixer block on the CPU in fp32 (torch ops around the oracle
+    restatement of the reference recurrence), fwd+bwd on one sequence of
+    `tokens` tokens.  Returns (tokens/s, seconds)."""
+    sys.path.insert(0, ROOT)
+    from torch.nn import functional as F
+    from oracle.kda_oracle import kda_layer as oracle_layer
+    from sophia_b200.mixer import KDAMixerBlock
+    gen = torch.Generator().manual_seed(0)
+    m = KDAMixerBlock(dim=DIM, heads=H, decay_rank=DECAY_RANK, generator=gen)
+    x = torch.randn(1, tokens, DIM, generator=gen).requires_grad_(True)
+    t0 = time.perf_counter()
+    h = F.rms_norm(x, (DIM,), m.in_norm, m.eps)
+    q, k, v, gate = F.linear(h, m.w_qkvg).split(H * D, dim=-1)
+    decay = F.linear(F.linear(h, m.decay_down), m.decay_up)
+    beta = F.linear(h, m.beta_proj)
+    sh = (1, tokens, H, D)
+    o = oracle_layer(q.reshape(sh), k.reshape(sh), v.reshape(sh), decay.reshape(sh), beta, m.A_log, m.dt_bias,
+                     conv_weights=[m.conv_q, m.conv_k, m.conv_v], compute_dtype=torch.float32).o
+    y = F.rms_norm(o, (D,), m.out_norm, m.eps) * torch.sigmoid(gate.reshape(sh))
+    out = F.linear(y.reshape(1, tokens, H * D), m.o_proj)
+    out.square().mean().backward()
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    mixer = a.workload == "cfg2"
+    metric = MIXER_METRIC if mixer else METRIC
     config = {"workload": a.workload, "global_batch": (a.batch or 8) * world if a.workload == "cfg1" else 320,
               "seq_len": T, "heads": H, "head_dim": D, "chunk": 64,
               "parallelism": f"dp{world}", "l2": "inputs larger than L2 (128 MiB per tensor), no flush"}
+    if mixer:
+        config.update({"global_batch": (a.batch or 4) * world, "hidden": DIM, "decay_rank": DECAY_RANK,
+                       "l2": "activations larger than L2 (48 MiB input, 256 MiB projections), no flush"})
+    sample = cpu_block_sample if mixer else cpu_sample
+    what = "mixer block (torch fp32 ops around the oracle recurrence)" if mixer else \
+        "16 heads (oracle restatement of the reference CPU path, torch fp32 autograd)"
     if a.impl == "reference":
         if rank != 0:
             return
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
-        sample_tokens = 512
+        sample_tokens = 256 if mixer else 512
         for _ in range(a.warmup):
-            cpu_sample(64)
+            sample(64)
         rates, secs = [], 0.0
         for _ in range(a.steps):
-            r, dt = cpu_sample(sample_tokens)
+            r, dt = sample(sample_tokens)
             rates.append(r)
             secs += dt
         value = sample_tokens * a.steps / secs
-        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
+        line = {"metric": metric, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": secs / a.steps * 1e3, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                 "impl": "reference",
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                 "sample": f"1 x {sample_tokens} tokens x 16 heads fwd+bwd per step (oracle "
-                                           "restatement of the reference CPU path, torch fp32 autograd)"},
+                                 "sample": f"1 x {sample_tokens} tokens fwd+bwd per step, {what}"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -381,7 +567,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    res = bench_ours(a, rank, world, local_rank)
+    res = (bench_mixer if mixer else bench_ours)(a, rank, world, local_rank)
     if res is None:  # --profile
         if world > 1:
             import torch.distributed as dist
@@ -391,14 +577,17 @@ def main():
     cpu = None
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
-        rate, dt = cpu_sample(2048, threads)
+        if mixer:
+            torch.set_num_threads(threads)
+            rate, dt = cpu_block_sample(1024)
+        else:
+            rate, dt = cpu_sample(2048, threads)
         cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"1 x 2048 tokens x 16 heads fwd+bwd ({dt:.1f} s; oracle restatement of the reference "
-                         "CPU path, torch fp32 autograd)"}
+               "sample": f"1 x {1024 if mixer else 2048} tokens fwd+bwd ({dt:.1f} s), {what}"}
     if rank == 0:
-        line = {"metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+        line = {"metric": metric, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": res["ms"], "higher_is_better": True,
-                "scaling": "weak" if a.workload == "cfg1" else "strong", "vs_baseline": None, "dtype": "bf16",
+                "scaling": "strong" if a.workload == "cfg3" else "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic", "config": config, "roofline": res["roofline"], "cpu_baseline": cpu,
                 "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]}
         print(json.dumps(line), flush=True)

@@ -172,6 +172,28 @@ int kda_b200_fwd_noalloc(const void* q, const void* k, const void* v, const void
                          const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H,
                          int D, int N, float scale, float lower_bound, void* o, float* ht, void* stream);
 
+/*
+ * Gated output norm of the KDA mixer -- replaces, in SophiaKDA.forward
+ * (ml/runtime/model/attention.py:416-419), the output RMSNorm over each head's
+ * 128 channels (RMSNorm.forward, ml/runtime/model/ops.py:49-64, i.e.
+ * torch.nn.functional.rms_norm with a fp32 weight) followed by the product
+ * with sigmoid(gate logits):
+ *     y = o / sqrt(mean(o^2) + eps) * weight * sigmoid(g)      per row of 128
+ * o, g, y (and dy, d_o, d_g): [rows][128], all bf16 (fp32_io = 0) or all fp32
+ * (fp32_io = 1), 16-byte aligned; weight: [128] fp32; arithmetic in fp32.
+ * The backward writes d_o and d_g and stores (not accumulates) the weight
+ * gradient, summed over rows in a fixed order, into d_weight [128] fp32; it
+ * needs kda_b200_gated_norm_workspace_bytes(rows, 128) bytes of workspace.
+ * rows = 0 is a no-op (d_weight is zeroed).  Errors as the other entry points:
+ * D != 128 is KDA_ERR_UNSUPPORTED, bad shapes or pointers KDA_ERR_INVALID.
+ */
+size_t kda_b200_gated_norm_workspace_bytes(long long rows, int D);
+int kda_b200_gated_norm_fwd(const void* o, const void* g, const float* weight, long long rows, int D, float eps,
+                            int fp32_io, void* y, void* stream);
+int kda_b200_gated_norm_bwd(const void* dy, const void* o, const void* g, const float* weight, long long rows,
+                            int D, float eps, int fp32_io, void* d_o, void* d_g, float* d_weight, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

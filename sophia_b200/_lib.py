@@ -36,6 +36,11 @@ SIGNATURES = {
     "kda_b200_timing_enable": ([c_int], c_int),
     "kda_b200_timing_reset": ([], c_int),
     "kda_b200_timing_read": ([c_int, c_void_p, c_void_p, c_void_p], c_int),
+    "kda_b200_gated_norm_workspace_bytes": ([c_int64, c_int], c_size_t),
+    "kda_b200_gated_norm_fwd": ([c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int, c_void_p, c_void_p],
+                                c_int),
+    "kda_b200_gated_norm_bwd": ([c_void_p] * 4 + [c_int64, c_int, c_float, c_int] + [c_void_p] * 4
+                                + [c_size_t, c_void_p], c_int),
 }
 
 _lib = None

@@ -16,6 +16,7 @@
 #include "kda_bwd_state_tc.cuh"
 #include "kda_recurrent.cuh"
 #include "kda_post.cuh"
+#include "kda_gated_norm.cuh"
 
 using namespace kda;
 
@@ -171,9 +172,13 @@ int check_common(const void* q, const void* k, const void* v, const void* g, con
 }
 
 // ---- optional per-launch device timing (CUDA events on the launch stream)
-enum KernelId { K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_RECURRENT, K_COUNT };
-const char* const kKernelNames[K_COUNT] = {"chunk_table", "fwd_intra", "fwd_state", "bwd_state",
-                                           "bwd_intra",   "bwd_post",  "reduce",    "recurrent"};
+enum KernelId {
+  K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_RECURRENT,
+  K_GNORM_FWD, K_GNORM_BWD, K_COUNT
+};
+const char* const kKernelNames[K_COUNT] = {"chunk_table", "fwd_intra", "fwd_state",       "bwd_state",
+                                           "bwd_intra",   "bwd_post",  "reduce",          "recurrent",
+                                           "gated_norm_fwd", "gated_norm_bwd"};
 
 struct Timing {
   std::mutex mu;
@@ -294,6 +299,33 @@ PrologueIn prologue_in(const void* q, const void* k, const void* v, const void* 
   return in;
 }
 
+}  // namespace
+
+// ---- gated output norm of the mixer (attention.py:416-419, ops.py:49-64)
+namespace {
+// One wave: as many CTAs as fit on the device at once (grid-stride loops inside).
+template <typename K>
+int gn_resident(K kernel) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, GN_THREADS, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  return per_sm * sm_count();
+}
+int gn_grid(long long rows, bool bwd) {
+  const long long steps = ((rows + 1) / 2 + GN_THREADS / 32 - 1) / (GN_THREADS / 32);
+  const int resident = bwd ? gn_resident(kda_gated_norm_bwd_kernel) : gn_resident(kda_gated_norm_fwd_kernel);
+  return (int)std::max<long long>(1, std::min<long long>(steps, resident));
+}
+int gn_check(long long rows, int D_, const void* a, const void* b, const float* w, const void* c, int fp32_io) {
+  if (D_ != D) return fail(KDA_ERR_UNSUPPORTED, "head dim must be 128, got " + std::to_string(D_));
+  if (rows < 0) return fail(KDA_ERR_INVALID, "rows must be >= 0");
+  if (fp32_io != 0 && fp32_io != 1) return fail(KDA_ERR_INVALID, "fp32_io must be 0 or 1");
+  if (rows == 0) return KDA_OK;  // empty tensors may have null data
+  if (!a || !b || !w || !c) return fail(KDA_ERR_INVALID, "null pointer");
+  if (!aligned(a, 16) || !aligned(b, 16) || !aligned(c, 16) || !aligned(w, 4))
+    return fail(KDA_ERR_INVALID, "row tensors must be 16-byte aligned");
+  return KDA_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -650,6 +682,57 @@ int kda_b200_fwd_noalloc(const void* q, const void* k, const void* v, const void
   }
   return kda_b200_fwd(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, B, T, H, D_, N, scale,
                       lower_bound, o, ht, nullptr, 0, scratch, KDA_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+
+size_t kda_b200_gated_norm_workspace_bytes(long long rows, int D_) {
+  if (D_ != D || rows < 0) return 0;
+  return (size_t)gn_grid(rows, true) * D * sizeof(float);
+}
+
+int kda_b200_gated_norm_fwd(const void* o, const void* g, const float* weight, long long rows, int D_, float eps,
+                            int fp32_io, void* y, void* stream) {
+  int rc;
+  if ((rc = gn_check(rows, D_, o, g, weight, y, fp32_io))) return rc;
+  if (rows == 0) return KDA_OK;
+  GatedNormParams gp{};
+  gp.o = o; gp.g = g; gp.w = weight; gp.y = y;
+  gp.rows = rows; gp.eps = eps; gp.fp32 = fp32_io != 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  {
+    TimedLaunch tl(K_GNORM_FWD, st);
+    kda_gated_norm_fwd_kernel<<<gn_grid(rows, false), GN_THREADS, 0, st>>>(gp);
+  }
+  return launch_check("gated norm fwd");
+}
+
+int kda_b200_gated_norm_bwd(const void* dy, const void* o, const void* g, const float* weight, long long rows,
+                            int D_, float eps, int fp32_io, void* d_o, void* d_g, float* d_weight, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = gn_check(rows, D_, o, g, weight, dy, fp32_io))) return rc;
+  if (!d_weight) return fail(KDA_ERR_INVALID, "null pointer");
+  if (rows > 0 && (!d_o || !d_g)) return fail(KDA_ERR_INVALID, "null pointer");
+  if (rows > 0 && (!aligned(d_o, 16) || !aligned(d_g, 16)))
+    return fail(KDA_ERR_INVALID, "row tensors must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    cudaError_t e = cudaMemsetAsync(d_weight, 0, D * sizeof(float), st);
+    return e == cudaSuccess ? KDA_OK : fail(KDA_ERR_CUDA, cudaGetErrorString(e));
+  }
+  const int grid = gn_grid(rows, true);
+  if (!workspace || workspace_bytes < (size_t)grid * D * sizeof(float) || !aligned(workspace, 16))
+    return fail(KDA_ERR_INVALID, "workspace too small: kda_b200_gated_norm_workspace_bytes() bytes are needed");
+  GatedNormParams gp{};
+  gp.o = o; gp.g = g; gp.dy = dy; gp.w = weight;
+  gp.d_o = d_o; gp.d_g = d_g; gp.partial = static_cast<float*>(workspace);
+  gp.rows = rows; gp.eps = eps; gp.fp32 = fp32_io != 0;
+  {
+    TimedLaunch tl(K_GNORM_BWD, st);
+    kda_gated_norm_bwd_kernel<<<grid, GN_THREADS, 0, st>>>(gp);
+    kda_gated_norm_reduce_kernel<<<1, D, 0, st>>>(gp.partial, grid, d_weight);
+  }
+  return launch_check("gated norm bwd");
 }
 
 }  // extern "C"

@@ -25,7 +25,7 @@ from types import MethodType
 
 import torch
 
-from .ops import HEAD_DIM, chunk_kda, fused_recurrent_kda, kda_layer
+from .ops import HEAD_DIM, chunk_kda, fused_recurrent_kda, gated_rms_norm, kda_layer
 
 PAD_LOGIT = -1.0e4  # attention.py:17
 
@@ -67,8 +67,9 @@ def _fused_forward(self, x: torch.Tensor, *, start_pos: int = 0) -> torch.Tensor
                 self.conv_state[:bsz, index].copy_(seq.transpose(1, 2).detach().to(torch.float32))
     gate_logits = (self.output_gate(x) if self.output_gate_full_rank
                    else self.output_gate_up(self.output_gate_down(x)))
-    gate = torch.sigmoid(gate_logits).view(bsz, seqlen, H, D)
-    output = self.output_norm(output.to(dtype=x.dtype)) * gate
+    # output RMSNorm and sigmoid gate in one kernel (attention.py:416-419)
+    output = gated_rms_norm(output.to(dtype=x.dtype), gate_logits.view(bsz, seqlen, H, D),
+                            self.output_norm.weight, float(self.output_norm.eps))
     return self.o_proj(output.reshape(bsz, seqlen, inner))
 
 

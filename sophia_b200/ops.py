@@ -16,7 +16,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["chunk_kda", "kda_layer", "fused_recurrent_kda"]
+__all__ = ["chunk_kda", "kda_layer", "fused_recurrent_kda", "gated_rms_norm"]
 
 HEAD_DIM = 128
 
@@ -231,3 +231,53 @@ def fused_recurrent_kda(q, k, v, g, beta, A_log=None, dt_bias=None, scale=None, 
         *(_ptr(x) for x in xs), _ptr(A_log32), _ptr(dt_bias32), _ptr(h0), _ptr(cu),
         B, T, H, HEAD_DIM, N, int(fp32), float(scale), float(lower_bound), _ptr(o), _ptr(ht), _stream()))
     return o.to(v.dtype), ht
+
+
+class _GatedNormFunction(torch.autograd.Function):
+    """y = rms_norm(o) * weight * sigmoid(g) over the last dim (128)."""
+
+    @staticmethod
+    def forward(ctx, o, g, weight, eps):
+        io = torch.float32 if torch.float32 in (o.dtype, g.dtype) else torch.bfloat16
+        oc, gc = o.to(io).contiguous(), g.to(io).contiguous()
+        w = weight.float().contiguous()
+        rows = oc.numel() // HEAD_DIM
+        y = torch.empty_like(oc)
+        lib = _lib.load()
+        _lib.check(lib.kda_b200_gated_norm_fwd(_ptr(oc), _ptr(gc), _ptr(w), rows, HEAD_DIM, float(eps),
+                                               int(io == torch.float32), _ptr(y), _stream()))
+        ctx.save_for_backward(oc, gc, w)
+        ctx.eps = float(eps)
+        ctx.dtypes = (o.dtype, g.dtype, weight.dtype)
+        return y.to(torch.promote_types(o.dtype, g.dtype))
+
+    @staticmethod
+    def backward(ctx, dy):
+        oc, gc, w = ctx.saved_tensors
+        rows = oc.numel() // HEAD_DIM
+        dyc = dy.to(oc.dtype).contiguous()
+        d_o, d_g = torch.empty_like(oc), torch.empty_like(gc)
+        dw = torch.empty(HEAD_DIM, device=oc.device, dtype=torch.float32)
+        lib = _lib.load()
+        ws = torch.empty(max(16, lib.kda_b200_gated_norm_workspace_bytes(rows, HEAD_DIM)), device=oc.device,
+                         dtype=torch.uint8)
+        _lib.check(lib.kda_b200_gated_norm_bwd(_ptr(dyc), _ptr(oc), _ptr(gc), _ptr(w), rows, HEAD_DIM, ctx.eps,
+                                               int(oc.dtype == torch.float32), _ptr(d_o), _ptr(d_g), _ptr(dw),
+                                               _ptr(ws), ws.numel(), _stream()))
+        od, gd, wd = ctx.dtypes
+        return d_o.to(od), d_g.to(gd), dw.to(wd), None
+
+
+def gated_rms_norm(o: torch.Tensor, g: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """``rms_norm(o) * weight * sigmoid(g)`` per row of 128 channels: the output
+    norm and gate of ``SophiaKDA.forward`` (``ml/runtime/model/attention.py:
+    416-419`` with ``RMSNorm``, ``ml/runtime/model/ops.py:49-64``), fused into one
+    kernel forward and one backward.  o, g: [..., 128] CUDA tensors of the
+    same shape (bf16 or fp32); weight: [128].  Differentiable in o, g, weight.
+    """
+    if o.shape != g.shape or o.shape[-1] != HEAD_DIM or weight.shape != (HEAD_DIM,):
+        raise ValueError(f"gated_rms_norm expects o, g [..., {HEAD_DIM}] of one shape and weight [{HEAD_DIM}], "
+                         f"got {tuple(o.shape)}, {tuple(g.shape)}, {tuple(weight.shape)}")
+    if not (o.is_cuda and g.is_cuda and weight.is_cuda):
+        raise RuntimeError("gated_rms_norm runs on the CUDA kernels only: o, g and weight must be CUDA tensors")
+    return _GatedNormFunction.apply(o, g, weight, eps)
