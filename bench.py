@@ -66,7 +66,7 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
 # --warmup 3 --profile` (B=2: the per-launch traffic scales with the token-heads
 # processed); summary in profiles/kda_kernels_dram_b2.md.
 NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
-    "fwd_intra": 3305.7, "fwd_state": 1845.9, "bwd_state": 2822.4, "bwd_intra": 3829.8, "bwd_post": 2192.1,
+    "fwd_intra": 3299.9, "fwd_state": 1850.0, "bwd_state": 2824.1, "bwd_intra": 3828.0, "bwd_post": 2192.3,
 }
 
 

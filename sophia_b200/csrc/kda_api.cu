@@ -730,7 +730,7 @@ int kda_b200_gated_norm_bwd(const void* dy, const void* o, const void* g, const 
   {
     TimedLaunch tl(K_GNORM_BWD, st);
     kda_gated_norm_bwd_kernel<<<grid, GN_THREADS, 0, st>>>(gp);
-    kda_gated_norm_reduce_kernel<<<1, D, 0, st>>>(gp.partial, grid, d_weight);
+    kda_gated_norm_reduce_kernel<<<1, D * GN_REDUCE_SLICES, 0, st>>>(gp.partial, grid, d_weight);
   }
   return launch_check("gated norm bwd");
 }

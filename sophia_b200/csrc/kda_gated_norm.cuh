@@ -143,11 +143,24 @@ __global__ void __launch_bounds__(GN_THREADS) kda_gated_norm_bwd_kernel(GatedNor
   }
 }
 
-// dw[c] = sum over CTAs of partial[b][c], in CTA order.
-__global__ void __launch_bounds__(D) kda_gated_norm_reduce_kernel(const float* partial, int nparts, float* dw) {
+// dw[c] = sum over CTAs of partial[b][c]: eight strided slices of the CTAs
+// summed in order, then the eight slice sums in order (a fixed order for a
+// given CTA count).
+constexpr int GN_REDUCE_SLICES = 8;
+__global__ void __launch_bounds__(D * GN_REDUCE_SLICES) kda_gated_norm_reduce_kernel(const float* partial, int nparts,
+                                                                                     float* dw) {
+  __shared__ float part[GN_REDUCE_SLICES][D];
+  const int c = threadIdx.x % D, sl = threadIdx.x / D;
   float acc = 0.f;
-  for (int b = 0; b < nparts; ++b) acc += partial[(size_t)b * D + threadIdx.x];
-  dw[threadIdx.x] = acc;
+  for (int b = sl; b < nparts; b += GN_REDUCE_SLICES) acc += partial[(size_t)b * D + c];
+  part[sl][c] = acc;
+  __syncthreads();
+  if (sl == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < GN_REDUCE_SLICES; ++i) t += part[i][c];
+    dw[c] = t;
+  }
 }
 
 }  // namespace kda

@@ -8,7 +8,9 @@ out-projection.  It follows ``SophiaKDA`` (``ml/runtime/model/attention.py:
 ``args`` defaults (``ml/runtime/model/config.py``: decay rank 128, dt in
 [1e-3, 1e-1] floored at 1e-4, ``A_log`` = 0, norm eps 1e-5, lower bound -5)
 and adds the block's input RMSNorm in front.  The q/k/v/gate weights are one
-[4 x 2048, 1536] matrix, so the four projections are one GEMM.
+[4 x 2048, 1536] parameter; its four row blocks are four GEMMs, whose outputs
+are the contiguous [B, T, 2048] operands the kernels read (one GEMM's output
+would need four strided copies first).
 
 The projections are plain cuBLAS GEMMs (``torch.nn.functional.linear``); the
 recurrence and the output norm run on this package's kernels.  Parameters are
@@ -64,7 +66,9 @@ class KDAMixerBlock(nn.Module):
         B, T, _ = x.shape
         H, D = self.heads, HEAD_DIM
         h = F.rms_norm(x, (self.dim,), self.in_norm.to(x.dtype), self.eps)
-        q, k, v, gate = F.linear(h, self.w_qkvg).split(H * D, dim=-1)
+        # four GEMMs from row blocks of the one weight: each output is a
+        # contiguous [B, T, H*D] tensor, so the kernels read it without a copy
+        q, k, v, gate = (F.linear(h, w) for w in self.w_qkvg.split(H * D, dim=0))
         decay = F.linear(F.linear(h, self.decay_down), self.decay_up)
         beta = F.linear(h, self.beta_proj)
         o, _ = kda_layer(q.reshape(B, T, H, D), k.reshape(B, T, H, D), v.reshape(B, T, H, D),
