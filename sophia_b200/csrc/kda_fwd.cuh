@@ -69,10 +69,8 @@ __device__ __forceinline__ void store_rows128(bf16* gdst, const bf16* s, int ld,
     *reinterpret_cast<bf16x8*>(gdst + ((size_t)(t0 + r) * H + h) * D + cc * 8) = v;
   }
 }
-// Same for rows of 64 bf16, by threads [first, first + count) of the CTA.
-__device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0,
-                                             int first, int count) {
-  for (int i = threadIdx.x - first; i < nrows * 8; i += count) {
+__device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0) {
+  for (int i = threadIdx.x; i < nrows * 8; i += blockDim.x) {
     int r = i >> 3, cc = i & 7;
     bf16x8 v = *reinterpret_cast<const bf16x8*>(s + r * ld + cc * 8);
     *reinterpret_cast<bf16x8*>(gdst + ((size_t)(t0 + r) * H + h) * 64 + cc * 8) = v;
@@ -128,7 +126,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     __syncthreads();
 
     Strip s;
-    prologue_compute(P.in, ps, pos, h, P.conv, s);
+    prologue_compute(P.in, ps, pos, P.conv, s);
     // the prologue's products, so that the backward need not redo it: q, k, v
     // strips into [64][128] tiles over the dead raw inputs, then (with the decay
     // cumsum tile and beta, already in shared memory) five bulk stores issued by
@@ -220,7 +218,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
       *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
     }
-    store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0, 0, INTRA_THREADS);
+    store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
     tc::fence_async_smem();  // A (written by every thread) is read by the bulk store below
     __syncthreads();
     // A for the backward, as it sits in shared memory (entries above the

@@ -18,7 +18,6 @@
 namespace kda {
 
 constexpr int GN_THREADS = 256;
-constexpr int GN_ROWS_PER_CTA_STEP = GN_THREADS / 16;
 
 struct GatedNormParams {
   const void *o, *g, *dy;

@@ -168,7 +168,7 @@ __device__ __forceinline__ void conv_strip(const bf16* x, const float* w, int tg
 }
 
 __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const PrologueSmem& sm,
-                                                 const ChunkPos& p, int h, bool conv, Strip& s) {
+                                                 const ChunkPos& p, bool conv, Strip& s) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tg = tid >> 4, cg = tid & 15;
   const int nvalid = p.t1 - p.t0;
