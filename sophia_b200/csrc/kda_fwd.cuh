@@ -61,14 +61,6 @@ struct IntraSmem {
   static_assert(END <= 232448, "shared memory");
 };
 
-__device__ __forceinline__ void store_rows128(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0) {
-  // copies nrows rows of 128 bf16 from smem (stride ld) to token rows t0.. of a [T][H][128] tensor
-  for (int i = threadIdx.x; i < nrows * 16; i += blockDim.x) {
-    int r = i >> 4, cc = i & 15;
-    bf16x8 v = *reinterpret_cast<const bf16x8*>(s + r * ld + cc * 8);
-    *reinterpret_cast<bf16x8*>(gdst + ((size_t)(t0 + r) * H + h) * D + cc * 8) = v;
-  }
-}
 __device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0) {
   for (int i = threadIdx.x; i < nrows * 8; i += blockDim.x) {
     int r = i >> 3, cc = i & 7;
@@ -237,20 +229,24 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       zero_acc<4>(accU);
       warp_mma<4, false, true>(accW, Tbf, LD64, m0, op.Ke, LD128, n0, 0, 64);
       warp_mma<4, false, true>(accU, Tbf, LD64, m0, op.V, LD128, n0, 0, 64);
-      __syncthreads();  // Qa/Ka are dead: reuse them as staging
-      bf16* Wst = op.Qa;
-      bf16* Ust = op.Ka;
+      // straight from the fragments as 16-byte runs (quad transpose), no staging
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int e = 0; e < 4; e += 2) {
+        uint32_t ww[4], wu[4];
 #pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-          *reinterpret_cast<uint32_t*>(Wst + r * LD128 + cc) = pack_bf16(accW[j][e], accW[j][e + 1]);
-          *reinterpret_cast<uint32_t*>(Ust + r * LD128 + cc) = pack_bf16(accU[j][e], accU[j][e + 1]);
+        for (int j = 0; j < 4; ++j) {
+          ww[j] = pack_bf16(accW[j][e], accW[j][e + 1]);
+          wu[j] = pack_bf16(accU[j][e], accU[j][e + 1]);
         }
-      __syncthreads();
-      store_rows128(P.W, Wst, LD128, nvalid, H, h, pos.t0);
-      store_rows128(P.U, Ust, LD128, nvalid, H, h, pos.t0);
+        quad_transpose4(ww);
+        quad_transpose4(wu);
+        const int r = m0 + acc_row(e);
+        if (r < nvalid) {
+          const size_t off = ((size_t)(pos.t0 + r) * H + h) * D + n0 + 8 * (threadIdx.x & 3);
+          *reinterpret_cast<uint4*>(P.W + off) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
+          *reinterpret_cast<uint4*>(P.U + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+        }
+      }
     }
     if (next >= n_items) break;
     item = next;
