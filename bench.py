@@ -1,7 +1,7 @@
 """Benchmark of the B200 KDA layer (forward + backward), one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg1|cfg2|cfg3]
+                    [--workload cfg1|cfg2|cfg3|cfg4]
 
 Step = one forward + backward of the KDA layer (ShortConv+SiLU, L2 norms,
 gate, beta, chunked gated delta rule) over one batch of synthetic inputs of
@@ -12,7 +12,10 @@ shards configuration 3's 320 sequences over the ranks instead (strong scaling);
 ``--workload cfg2`` steps the whole mixer block of configuration 2
 (``sophia_b200.mixer.KDAMixerBlock``: input RMSNorm, fused q/k/v/gate GEMM,
 decay and beta projections, the KDA layer, gated output RMSNorm, out-
-projection; 4 x 4096 tokens, hidden 1536, bf16 autocast) per GPU.
+projection; 4 x 4096 tokens, hidden 1536, bf16 autocast) per GPU;
+``--workload cfg4`` steps configuration 4's packed ragged batch per GPU: 16
+windows of 4096 tokens holding documents of log-uniform length in [32, 4096]
+(seed 42), one 65,536-token sequence with ``cu_seqlens``.
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launch stream, max over ranks.
@@ -29,6 +32,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import sys
@@ -76,7 +80,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3"], default="cfg1")
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
     ap.add_argument("--profile", action="store_true",
                     help="run the warm-up and K layer steps only, print nothing (command for ncu captures)")
     ap.add_argument("--batch", type=int, default=None,
@@ -163,12 +167,32 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(inside)}
 
 
-def make_inputs(B, device, seed):
+CFG4_WINDOWS = 16
+
+
+def cfg4_cu_seqlens(windows: int = CFG4_WINDOWS, seed: int = 42) -> list[int]:
+    """Configuration 4's packed document boundaries: each 4096-token window is
+    filled with documents of log-uniform length in [32, 4096] (drawn with a
+    generator seeded per window, the last cut at the window end); the windows
+    are concatenated into one sequence of windows x 4096 tokens."""
+    cu = [0]
+    for w in range(windows):
+        gen = torch.Generator().manual_seed(seed * 1000 + w)
+        used = 0
+        while used < T:
+            u = torch.rand(1, generator=gen).item()
+            n = min(int(round(math.exp(math.log(32) + u * (math.log(4096) - math.log(32))))), T - used)
+            used += n
+            cu.append(cu[-1] + n)
+    return cu
+
+
+def make_inputs(B, device, seed, Tlen=T):
     g = torch.Generator(device=device).manual_seed(seed)
     rn = lambda *s, std=1.0: torch.randn(*s, device=device, generator=g) * std  # noqa: E731
-    x = {k: rn(B, T, H, D).to(torch.bfloat16) for k in ("q", "k", "v", "g")}
-    x["beta"] = rn(B, T, H).to(torch.bfloat16)
-    x["do"] = rn(B, T, H, D).to(torch.bfloat16)
+    x = {k: rn(B, Tlen, H, D).to(torch.bfloat16) for k in ("q", "k", "v", "g")}
+    x["beta"] = rn(B, Tlen, H).to(torch.bfloat16)
+    x["do"] = rn(B, Tlen, H, D).to(torch.bfloat16)
     w = {"A_log": torch.zeros(H, device=device), "dt_bias": torch.zeros(H * D, device=device)}
     for k in ("conv_q", "conv_k", "conv_v"):
         w[k] = rn(H * D, 4, std=0.5)
@@ -182,8 +206,14 @@ def bench_ours(a, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     # cfg1: 8 sequences per rank (weak scaling); cfg3: rank's share of 320 (strong)
-    B = a.batch or (8 if a.workload == "cfg1" else len(range(320)[dp.shard(320, rank, world)]))
-    x, w = make_inputs(B, device, 42 + rank)
+    packed = a.workload == "cfg4"
+    if packed:  # one sequence of 16 packed windows, documents reset at cu_seqlens
+        B, Tlen = 1, CFG4_WINDOWS * T
+        cu = torch.tensor(cfg4_cu_seqlens(), dtype=torch.int32, device=device)
+    else:
+        B = a.batch or (8 if a.workload == "cfg1" else len(range(320)[dp.shard(320, rank, world)]))
+        Tlen, cu = T, None
+    x, w = make_inputs(B, device, 42 + rank, Tlen)
     acts = {k: x[k].clone().requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
     params = {k: v.clone().requires_grad_(True) for k, v in w.items()}
     bucket = torch.empty(dp.bucket_numel(H, D), device=device, dtype=torch.float32)
@@ -193,7 +223,7 @@ def bench_ours(a, rank, world, local_rank):
         for t in list(src.values()) + list(params.values()):
             t.grad = None
         o, _ = kda_layer(src["q"], src["k"], src["v"], src["g"], src["beta"], params["A_log"], params["dt_bias"],
-                         params["conv_q"], params["conv_k"], params["conv_v"])
+                         params["conv_q"], params["conv_k"], params["conv_v"], cu_seqlens=cu)
         o.backward(x["do"] if inputs is None else inputs["_do"])
         dp.grad_bucket(params, out=bucket)
         dp.allreduce_bucket(bucket)
@@ -226,8 +256,9 @@ def bench_ours(a, rank, world, local_rank):
     sampler.start()
     ms = timed(step, a.steps, sampler)
     clocks = sampler.stop()
-    global_seqs = world * B if a.workload == "cfg1" else 320
-    tokens = global_seqs * T * a.steps
+    rank_tokens = B * Tlen
+    global_tokens = 320 * T if a.workload == "cfg3" else world * rank_tokens
+    tokens = global_tokens * a.steps
     value = tokens / (ms / 1e3)
 
     # per-kernel device times (second pass, CUDA events around every launch)
@@ -296,7 +327,7 @@ def bench_ours(a, rank, world, local_rank):
 
     hbm, tc, tc_sus, src = peaks()
     # dominant kernel and its roofline
-    th = B * T * H  # token-heads per launch
+    th = B * Tlen * H  # token-heads per launch
     dom = max((k for k in kern if k in KERNEL_BYTES_PER_TOKEN_HEAD), key=lambda k: kern[k][1])
     n_l, tot = kern[dom]
     per_launch_ms = tot / max(1, n_l)
@@ -313,7 +344,7 @@ def bench_ours(a, rank, world, local_rank):
     kernel_ms_per_step = {k: round(v[1] / a.steps, 4) for k, v in kern.items() if v[0]}
     return {
         "value": value, "ms": ms / a.steps, "B": B, "clocks": clocks,
-        "e2e": {"value": global_seqs * T * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
+        "e2e": {"value": global_tokens * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
@@ -531,6 +562,11 @@ def main():
     config = {"workload": a.workload, "global_batch": (a.batch or 8) * world if a.workload == "cfg1" else 320,
               "seq_len": T, "heads": H, "head_dim": D, "chunk": 64,
               "parallelism": f"dp{world}", "l2": "inputs larger than L2 (128 MiB per tensor), no flush"}
+    if a.workload == "cfg4":
+        ncu4 = len(cfg4_cu_seqlens()) - 1
+        config.update({"global_batch": world, "seq_len": CFG4_WINDOWS * T,
+                       "packing": f"{CFG4_WINDOWS} windows x {T} tokens, {ncu4} documents (log-uniform lengths in "
+                                  "[32, 4096], seed 42), cu_seqlens int32, state and conv history reset per document"})
     if mixer:
         config.update({"global_batch": (a.batch or 4) * world, "hidden": DIM, "decay_rank": DECAY_RANK,
                        "l2": "activations larger than L2 (48 MiB input, 256 MiB projections), no flush"})
