@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <mutex>
 #include <string>
@@ -221,12 +222,14 @@ int launch_check(const char* what) {
 
 // SMs of the current device (queried once per device).
 int sm_count() {
-  static int counts[64] = {0};
+  static std::atomic<int> counts[64];  // zero-initialised (static storage); concurrent first calls store the same value
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (!counts[dev] && cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    counts[dev] = 148;
-  return counts[dev];
+  int n = counts[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) n = 148;
+  counts[dev].store(n, std::memory_order_relaxed);
+  return n;
 }
 
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime
