@@ -2,7 +2,7 @@
  * kda_b200 -- C ABI of the B200 (sm_100a) Kimi Delta Attention layer.
  *
  * The reference (Sophia) reaches this path through two Python seams, and this
- * ABI is what those seams bind to (see INTEGRATION.md for the ctypes stub):
+ * ABI is what those seams bind to (sophia_b200/_lib.py is the ctypes binding):
  *
  *   SophiaKDA._fla_chunk_kda() -> chunk_kda(q, k, v, g, beta, ...)
  *       ml/runtime/model/attention.py:305-312 (seam), called at :349-365 with
@@ -22,8 +22,8 @@
  *     `workspace` buffers whose sizes the *_bytes functions return.  Nothing
  *     synchronises with the host, so calls can be captured in CUDA graphs.
  *   - q, k, v, g, o and all their gradients are bf16 [B, T, H, 128]; beta and
- *     dbeta are bf16 [B, T, H]; A_log [H], dt_bias [H*128], conv taps
- *     [H*128, 4], states [N, H, 128, 128] are fp32.
+ *     dbeta are bf16 [B, T, H] (fp32 for the *_f32 entry points); A_log [H],
+ *     dt_bias [H*128], conv taps [H*128, 4], states [N, H, 128, 128] are fp32.
  *   - cu_seqlens (int32 [N+1], device) packs N sequences along T (then B == 1);
  *     the recurrent state and the conv history restart at every boundary.
  *   - Return value: KDA_OK or an error code; kda_b200_last_error() describes
@@ -93,6 +93,36 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
                  size_t workspace_bytes, void* stream);
 
 /*
+ * fp32 mode.  Replaces chunk_kda's forward / backward (fla/ops/kda/chunk.py:
+ * 22-162) when q, k, v, g and beta arrive in float32, the precision of the
+ * reference's own recurrence (SophiaKDA._reference_kda,
+ * ml/runtime/model/attention.py:260-294, float32 inside).  Same arguments and
+ * meaning as kda_b200_fwd / kda_b200_bwd, except that every activation and
+ * gradient (q, k, v, g, beta, o, do_, dq, dk, dv, dg, dbeta) is fp32
+ * [B, T, H, 128] ([B, T, H] for beta) and the buffers are sized by the
+ * kda_b200_f32_*_bytes functions.  All arithmetic is fp32 on CUDA cores (no
+ * tensor-core rounding); the recurrence runs token by token in the
+ * reference's order, so results agree with the reference to fp32 rounding.
+ * The backward's scratch includes a per-CTA slice of 1 MiB for at most two
+ * CTAs per SM.
+ */
+size_t kda_b200_f32_saved_bytes(int64_t total_tokens, int H, int N);
+size_t kda_b200_f32_fwd_workspace_bytes(int64_t total_tokens, int H, int N, int training);
+size_t kda_b200_f32_bwd_workspace_bytes(int64_t total_tokens, int H, int N);
+int kda_b200_fwd_f32(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                     const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                     const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H, int D,
+                     int N, float scale, float lower_bound, float* o, float* ht, void* saved, size_t saved_bytes,
+                     void* workspace, size_t workspace_bytes, void* stream);
+int kda_b200_bwd_f32(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                     const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                     const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H, int D,
+                     int N, float scale, float lower_bound, const void* saved, size_t saved_bytes, const float* do_,
+                     const float* dht, float* dq, float* dk, float* dv, float* dg, float* dbeta, float* dA_log,
+                     float* ddt_bias, float* dconv_q, float* dconv_k, float* dconv_v, float* dh0, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/*
  * Packed-sequence chunk table (integer bookkeeping of prepare_chunk_indices /
  * prepare_chunk_offsets, fla/ops/utils/index.py:138-158), built on the device
  * without a host sync.  offsets: int32 [N+1]; chunk_seq: int32 [max_chunks]
@@ -122,6 +152,24 @@ int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* 
                        float* ht, void* stream);
 
 /*
+ * Decode step of a cached SophiaKDA.forward with the ShortConv fused: replaces
+ * _short_convolution with a conv history (ml/runtime/model/attention.py:226-258,
+ * CausalDepthwiseConv1d.forward with history, :32-60) followed by
+ * _run_kda's single-step decode (:330-348).  As kda_b200_recurrent, except
+ * that q, k and v are the pre-conv projections and conv_q/conv_k/conv_v
+ * ([H*128][4] fp32 taps) with conv_state ([N][3][H*128][3] fp32, the module's
+ * conv_state rows: the last three inputs of q, k and v per channel, oldest
+ * first) run the conv + SiLU in front of the recurrence; conv_state is read
+ * at the start and rewritten with the last three inputs at the end.  Any
+ * number of tokens per sequence.
+ */
+int kda_b200_decode(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                    const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                    const float* conv_v, float* conv_state, const float* h0, const int32_t* cu_seqlens, int B,
+                    int T, int H, int D, int N, int fp32_inputs, float scale, float lower_bound, void* o, float* ht,
+                    void* stream);
+
+/*
  * Device-side failure flag of the tensor-core kernels.  Their waits on
  * asynchronous MMA completion are bounded; a wait that runs out makes the
  * kernel record a nonzero code here and return early (its outputs are then
@@ -130,6 +178,26 @@ int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* 
  * has no counterpart (its kernels run in Triton without such waits).
  */
 int kda_b200_device_error(int reset);
+
+/*
+ * Codes of kda_b200_device_error():
+ *   1, 2  a tensor-core completion wait of a state kernel ran out;
+ *   3     a cu_seqlens table was malformed (does not start at 0, decreases, or
+ *         does not end at the token count): the layer call did nothing;
+ *   5, 7  a bulk-copy wait of the backward chunk kernel ran out;
+ *   8     the forward chunk kernel's wait for its prefetched inputs ran out.
+ * A kernel that records a timeout lets its copies in flight land (a second
+ * bounded wait), frees what it holds and returns; later calls are unaffected.
+ */
+
+/*
+ * Test hook of the bounded waits: the number of polls the forward chunk
+ * kernel makes for an item's prefetched inputs before it records code 8 and
+ * returns (0 restores the default, 2^26).  A test lowers it to 1 so that the
+ * wait runs out without any fault, then checks the code.  Applies to calls
+ * made after it.  No counterpart in the reference.
+ */
+int kda_b200_debug_set_input_wait_polls(unsigned int polls);
 
 /*
  * Per-kernel device timing, for benchmarks and profiling summaries.  While

@@ -18,6 +18,7 @@
 #include "kda_recurrent.cuh"
 #include "kda_post.cuh"
 #include "kda_gated_norm.cuh"
+#include "kda_f32.cuh"
 
 using namespace kda;
 
@@ -139,7 +140,8 @@ int check_common(const void* q, const void* k, const void* v, const void* g, con
   if (B < 1 || T < 0 || H < 1) return fail(KDA_ERR_INVALID, "B >= 1, T >= 0 and H >= 1 are required");
   if (!(lower_bound >= -5.f && lower_bound < 0.f))
     return fail(KDA_ERR_INVALID, "`lower_bound` must be in the safe range [-5, 0), got " + std::to_string(lower_bound));
-  if (!q || !k || !v || !g || !beta || !A_log || !dt_bias) return fail(KDA_ERR_INVALID, "null input pointer");
+  const bool empty = (int64_t)B * T == 0;  // empty tensors may have null data
+  if (!empty && (!q || !k || !v || !g || !beta || !A_log || !dt_bias)) return fail(KDA_ERR_INVALID, "null input pointer");
   const bool anyconv = cq || ck || cvv, allconv = cq && ck && cvv;
   if (anyconv && !allconv) return fail(KDA_ERR_INVALID, "conv taps must be given for all of q, k, v or none");
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(g, 16))
@@ -175,11 +177,12 @@ int check_common(const void* q, const void* k, const void* v, const void* g, con
 // ---- optional per-launch device timing (CUDA events on the launch stream)
 enum KernelId {
   K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_RECURRENT,
-  K_GNORM_FWD, K_GNORM_BWD, K_COUNT
+  K_GNORM_FWD, K_GNORM_BWD, K_F32_PREP, K_F32_FWD, K_F32_BWD, K_F32_DC, K_F32_CONV, K_COUNT
 };
 const char* const kKernelNames[K_COUNT] = {"chunk_table", "fwd_intra", "fwd_state",       "bwd_state",
                                            "bwd_intra",   "bwd_post",  "reduce",          "recurrent",
-                                           "gated_norm_fwd", "gated_norm_bwd"};
+                                           "gated_norm_fwd", "gated_norm_bwd", "f32_prep", "f32_fwd",
+                                           "f32_bwd",     "f32_dc",    "f32_conv_bwd"};
 
 struct Timing {
   std::mutex mu;
@@ -219,6 +222,11 @@ int launch_check(const char* what) {
   if (e != cudaSuccess) return fail(KDA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
   return KDA_OK;
 }
+
+// Poll limit of the forward chunk kernel's wait for its prefetched inputs
+// (kda_b200_debug_set_input_wait_polls lowers it in tests).
+constexpr uint32_t kDefaultWaitPolls = 1u << 26;
+std::atomic<uint32_t> g_input_wait_polls{kDefaultWaitPolls};
 
 // SMs of the current device (queried once per device).
 int sm_count() {
@@ -302,6 +310,68 @@ PrologueIn prologue_in(const void* q, const void* k, const void* v, const void* 
   return in;
 }
 
+// ---- fp32 mode: buffer carving
+struct F32SavedView {
+  float *qh, *kh, *alpha, *r, *bt, *ck;
+};
+
+// Training: everything the backward reads.  Inference (with_bwd = false): the
+// prep outputs only (no r, no chunk-start states).
+F32SavedView carve_f32_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) {
+  F32SavedView s;
+  const size_t row = (size_t)TT * H * D * 4;
+  s.qh = cv.take<float>(row);
+  s.kh = cv.take<float>(row);
+  s.alpha = cv.take<float>(row);
+  s.bt = cv.take<float>((size_t)TT * H * 4);
+  s.r = with_bwd ? cv.take<float>(row) : nullptr;
+  s.ck = with_bwd ? cv.take<float>((size_t)mc * H * STATE_ELEMS * 4) : nullptr;
+  return s;
+}
+
+struct F32BwdView {
+  float *dqh_p, *dkh_p, *dal_p, *dbt_p, *dvh, *dcq, *dck, *dcv, *partA, *partB, *partW, *scratch;
+};
+
+// Persistent grid of the fp32 backward recurrence (two CTAs per SM); each CTA
+// owns one F32_SCRATCH_FLOATS slice of the scratch.
+int f32_bwd_ctas(int64_t items) { return (int)std::max<int64_t>(1, std::min<int64_t>(items, 2 * (int64_t)sm_count())); }
+
+F32BwdView carve_f32_bwd(Carver& cv, int64_t TT, int H, int N, int64_t mc) {
+  F32BwdView b;
+  const size_t row = (size_t)TT * H * D * 4;
+  b.dqh_p = cv.take<float>(F32_GROUPS * row);
+  b.dkh_p = cv.take<float>(F32_GROUPS * row);
+  b.dal_p = cv.take<float>(F32_GROUPS * row);
+  b.dbt_p = cv.take<float>((size_t)F32_GROUPS * TT * H * 4);
+  b.dvh = cv.take<float>(row);
+  b.dcq = cv.take<float>(row);
+  b.dck = cv.take<float>(row);
+  b.dcv = cv.take<float>(row);
+  b.partA = cv.take<float>((size_t)mc * H * D * 4);
+  b.partB = cv.take<float>((size_t)mc * H * D * 4);
+  b.partW = cv.take<float>((size_t)mc * 3 * H * D * 4 * 4);
+  b.scratch = cv.take<float>((size_t)f32_bwd_ctas((int64_t)N * H * F32_GROUPS) * F32_SCRATCH_FLOATS * 4);
+  return b;
+}
+
+F32Inputs f32_inputs(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                     const float* A_log, const float* dt_bias, const float* cq, const float* ck, const float* cvv, int H,
+                     bool conv, float scale, float lb) {
+  F32Inputs in;
+  in.q = q; in.k = k; in.v = v; in.g = g; in.beta = beta;
+  in.A_log = A_log;
+  in.dt_bias = dt_bias;
+  in.conv_q = cq; in.conv_k = ck; in.conv_v = cvv;
+  in.H = H;
+  in.conv = conv;
+  in.scale = scale;
+  in.lower_bound = lb;
+  return in;
+}
+
+int row_grid(const Problem& pr) { return (pr.grid_chunks + F32_WARPS_PER_CTA - 1) / F32_WARPS_PER_CTA; }
+
 }  // namespace
 
 // ---- gated output norm of the mixer (attention.py:416-419, ops.py:49-64)
@@ -375,6 +445,20 @@ int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* 
                        const float* A_log, const float* dt_bias, const float* h0, const int32_t* cu_seqlens, int B,
                        int T, int H, int D_, int N, int fp32_inputs, float scale, float lower_bound, void* o,
                        float* ht, void* stream) {
+  return kda_b200_decode(q, k, v, g, beta, A_log, dt_bias, nullptr, nullptr, nullptr, nullptr, h0, cu_seqlens, B, T,
+                         H, D_, N, fp32_inputs, scale, lower_bound, o, ht, stream);
+}
+
+int kda_b200_decode(const void* q, const void* k, const void* v, const void* g, const void* beta,
+                    const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                    const float* conv_v, float* conv_state, const float* h0, const int32_t* cu_seqlens, int B,
+                    int T, int H, int D_, int N, int fp32_inputs, float scale, float lower_bound, void* o, float* ht,
+                    void* stream) {
+  const bool anyconv = conv_q || conv_k || conv_v || conv_state;
+  if (anyconv && !(conv_q && conv_k && conv_v && conv_state))
+    return fail(KDA_ERR_INVALID, "conv taps of q, k, v and the conv history must be given together or not at all");
+  if (anyconv && (!aligned(conv_q, 16) || !aligned(conv_k, 16) || !aligned(conv_v, 16)))
+    return fail(KDA_ERR_INVALID, "conv taps must be 16-byte aligned");
   if (D_ != D) return fail(KDA_ERR_UNSUPPORTED, "head dim must be 128, got " + std::to_string(D_));
   if (B < 1 || T < 0 || H < 1) return fail(KDA_ERR_INVALID, "B >= 1, T >= 0 and H >= 1 are required");
   if (!(lower_bound >= -5.f && lower_bound < 0.f))
@@ -407,6 +491,8 @@ int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* 
   rp.o = o;
   rp.ht = ht;
   rp.total_tokens = (long long)B * T;
+  rp.conv_q = conv_q; rp.conv_k = conv_k; rp.conv_v = conv_v;
+  rp.conv_state = conv_state;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   {
     TimedLaunch tl(K_RECURRENT, st);
@@ -424,7 +510,7 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   int rc = check_common(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, cu_seqlens, B, T, H, D_, N,
                         lower_bound, pr);
   if (rc) return rc;
-  if (!o) return fail(KDA_ERR_INVALID, "null output pointer");
+  if (!o && pr.TT > 0) return fail(KDA_ERR_INVALID, "null output pointer");
   if (!aligned(o, 16)) return fail(KDA_ERR_INVALID, "o must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool training = saved != nullptr;
@@ -454,6 +540,7 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A;
   ip.QN = sv.QN; ip.KN = sv.KN; ip.VN = sv.VN; ip.GM = sv.GM; ip.BT = sv.BT;
   ip.grid_chunks = pr.grid_chunks;
+  ip.wait_polls = g_input_wait_polls.load(std::memory_order_relaxed);
   if ((rc = encode_rows_map(&ip.maps[0], q, H, pr.TT, 67)) || (rc = encode_rows_map(&ip.maps[1], k, H, pr.TT, 67)) ||
       (rc = encode_rows_map(&ip.maps[2], v, H, pr.TT, 67)) || (rc = encode_rows_map(&ip.maps[3], g, H, pr.TT, 64)))
     return rc;
@@ -498,7 +585,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   if (rc) return rc;
   if (!saved || saved_bytes < kda_b200_saved_bytes(pr.TT, H, N, pr.packed))
     return fail(KDA_ERR_INVALID, "saved buffer missing or too small");
-  if (!do_ || !dq || !dk || !dv || !dg || !dbeta || !dA_log || !ddt_bias)
+  if ((pr.TT > 0 && (!do_ || !dq || !dk || !dv || !dg || !dbeta)) || !dA_log || !ddt_bias)
     return fail(KDA_ERR_INVALID, "null gradient pointer");
   if (pr.conv && (!dconv_q || !dconv_k || !dconv_v)) return fail(KDA_ERR_INVALID, "null conv gradient pointer");
   if (!aligned(do_, 16) || !aligned(dq, 16) || !aligned(dk, 16) || !aligned(dv, 16) || !aligned(dg, 4))
@@ -602,6 +689,207 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
     kda_reduce_kernel<<<dim3(2 * H + (pr.conv ? 12 * H : 0)), 256, 0, st>>>(rp);
   }
   return launch_check("reduce");
+}
+
+// ---- fp32 mode -------------------------------------------------------------
+size_t kda_b200_f32_saved_bytes(int64_t total_tokens, int H, int N) {
+  Carver cv(nullptr);
+  carve_f32_saved(cv, total_tokens, H, max_chunks(total_tokens, N), true);
+  return cv.off;
+}
+
+size_t kda_b200_f32_fwd_workspace_bytes(int64_t total_tokens, int H, int N, int training) {
+  Carver cv(nullptr);
+  const int64_t mc = max_chunks(total_tokens, N);
+  carve_table(cv, N, mc);
+  cv.take<float>((size_t)total_tokens * H * D * 4);  // post-conv v
+  if (!training) carve_f32_saved(cv, total_tokens, H, mc, false);
+  return cv.off;
+}
+
+size_t kda_b200_f32_bwd_workspace_bytes(int64_t total_tokens, int H, int N) {
+  Carver cv(nullptr);
+  const int64_t mc = max_chunks(total_tokens, N);
+  carve_table(cv, N, mc);
+  carve_f32_bwd(cv, total_tokens, H, N, mc);
+  return cv.off;
+}
+
+int kda_b200_fwd_f32(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                     const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                     const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H, int D_,
+                     int N, float scale, float lower_bound, float* o, float* ht, void* saved, size_t saved_bytes,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  Problem pr;
+  int rc = check_common(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, cu_seqlens, B, T, H, D_, N,
+                        lower_bound, pr);
+  if (rc) return rc;
+  if (!o && pr.TT > 0) return fail(KDA_ERR_INVALID, "null output pointer");
+  if (!aligned(o, 16) || !aligned(A_log, 4)) return fail(KDA_ERR_INVALID, "o must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool training = saved != nullptr;
+  const size_t need_ws = kda_b200_f32_fwd_workspace_bytes(pr.TT, H, N, training);
+  if (!workspace || workspace_bytes < need_ws)
+    return fail(KDA_ERR_INVALID, "workspace too small: need " + std::to_string(need_ws) + " bytes");
+  if (training && saved_bytes < kda_b200_f32_saved_bytes(pr.TT, H, N)) return fail(KDA_ERR_INVALID, "saved buffer too small");
+  if (pr.TT == 0) {
+    if (ht) {
+      const size_t bytes = (size_t)N * H * D * D * 4;
+      cudaError_t e = h0 ? cudaMemcpyAsync(ht, h0, bytes, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(ht, 0, bytes, st);
+      if (e != cudaSuccess) return fail(KDA_ERR_CUDA, cudaGetErrorString(e));
+    }
+    return KDA_OK;
+  }
+  Carver wcv(workspace);
+  Table tab = carve_table(wcv, N, pr.mc);
+  float* vh = wcv.take<float>((size_t)pr.TT * H * D * 4);
+  Carver scv(training ? saved : nullptr);
+  F32SavedView sv = training ? carve_f32_saved(scv, pr.TT, H, pr.mc, true) : carve_f32_saved(wcv, pr.TT, H, pr.mc, false);
+  if ((rc = build_table(pr, tab, st))) return rc;
+
+  F32PrepParams pp;
+  pp.seq = pr.seq;
+  pp.in = f32_inputs(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, H, pr.conv, scale, lower_bound);
+  pp.qh = sv.qh; pp.kh = sv.kh; pp.vh = vh; pp.alpha = sv.alpha; pp.bt = sv.bt;
+  {
+    TimedLaunch tl(K_F32_PREP, st);
+    kda_f32_prep_kernel<<<dim3(row_grid(pr), H), 32 * F32_WARPS_PER_CTA, 0, st>>>(pp);
+  }
+  if ((rc = launch_check("fp32 prep"))) return rc;
+
+  F32FwdParams fp;
+  fp.seq = pr.seq;
+  fp.H = H;
+  fp.qh = sv.qh; fp.kh = sv.kh; fp.vh = vh; fp.alpha = sv.alpha; fp.bt = sv.bt;
+  fp.h0 = h0;
+  fp.o = o;
+  fp.r = sv.r;
+  fp.ck = sv.ck;
+  fp.ht = ht;
+  fp.total_tokens = pr.TT;
+  {
+    TimedLaunch tl(K_F32_FWD, st);
+    kda_f32_fwd_kernel<<<dim3(N, H, F32_GROUPS), 32, 0, st>>>(fp);
+  }
+  return launch_check("fp32 forward");
+}
+
+int kda_b200_bwd_f32(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                     const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
+                     const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H, int D_,
+                     int N, float scale, float lower_bound, const void* saved, size_t saved_bytes, const float* do_,
+                     const float* dht, float* dq, float* dk, float* dv, float* dg, float* dbeta, float* dA_log,
+                     float* ddt_bias, float* dconv_q, float* dconv_k, float* dconv_v, float* dh0, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  (void)h0;
+  Problem pr;
+  int rc = check_common(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, cu_seqlens, B, T, H, D_, N,
+                        lower_bound, pr);
+  if (rc) return rc;
+  if (!saved || saved_bytes < kda_b200_f32_saved_bytes(pr.TT, H, N))
+    return fail(KDA_ERR_INVALID, "saved buffer missing or too small");
+  if ((pr.TT > 0 && (!do_ || !dq || !dk || !dv || !dg || !dbeta)) || !dA_log || !ddt_bias)
+    return fail(KDA_ERR_INVALID, "null gradient pointer");
+  if (pr.conv && (!dconv_q || !dconv_k || !dconv_v)) return fail(KDA_ERR_INVALID, "null conv gradient pointer");
+  if (!aligned(do_, 16) || !aligned(dq, 16) || !aligned(dk, 16) || !aligned(dv, 16) || !aligned(dg, 16) ||
+      !aligned(ddt_bias, 16) || (pr.conv && (!aligned(dconv_q, 16) || !aligned(dconv_k, 16) || !aligned(dconv_v, 16))) ||
+      (dh0 && !aligned(dh0, 16)) || (dht && !aligned(dht, 16)))
+    return fail(KDA_ERR_INVALID, "gradient tensors must be 16-byte aligned");
+  const size_t need_ws = kda_b200_f32_bwd_workspace_bytes(pr.TT, H, N);
+  if (!workspace || workspace_bytes < need_ws)
+    return fail(KDA_ERR_INVALID, "workspace too small: need " + std::to_string(need_ws) + " bytes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (pr.TT == 0) {
+    cudaMemsetAsync(dA_log, 0, (size_t)H * 4, st);
+    cudaMemsetAsync(ddt_bias, 0, (size_t)H * D * 4, st);
+    if (pr.conv) {
+      cudaMemsetAsync(dconv_q, 0, (size_t)H * D * 16, st);
+      cudaMemsetAsync(dconv_k, 0, (size_t)H * D * 16, st);
+      cudaMemsetAsync(dconv_v, 0, (size_t)H * D * 16, st);
+    }
+    if (dh0) {
+      const size_t bytes = (size_t)N * H * D * D * 4;
+      if (dht) cudaMemcpyAsync(dh0, dht, bytes, cudaMemcpyDeviceToDevice, st);
+      else cudaMemsetAsync(dh0, 0, bytes, st);
+    }
+    return launch_check("empty backward");
+  }
+  Carver wcv(workspace);
+  Table tab = carve_table(wcv, N, pr.mc);
+  F32BwdView bv = carve_f32_bwd(wcv, pr.TT, H, N, pr.mc);
+  Carver scv(const_cast<void*>(saved));
+  F32SavedView sv = carve_f32_saved(scv, pr.TT, H, pr.mc, true);
+  if ((rc = build_table(pr, tab, st))) return rc;
+
+  F32BwdParams bp;
+  bp.seq = pr.seq;
+  bp.H = H;
+  bp.qh = sv.qh; bp.kh = sv.kh; bp.alpha = sv.alpha; bp.bt = sv.bt; bp.r = sv.r; bp.ck = sv.ck;
+  bp.dO = do_;
+  bp.dht = dht;
+  bp.scratch = bv.scratch;
+  bp.dqh_p = bv.dqh_p; bp.dkh_p = bv.dkh_p; bp.dal_p = bv.dal_p; bp.dbt_p = bv.dbt_p;
+  bp.dvh = bv.dvh;
+  bp.dh0 = dh0;
+  bp.total_tokens = pr.TT;
+  bp.items = N * H * F32_GROUPS;
+  {
+    TimedLaunch tl(K_F32_BWD, st);
+    kda_f32_bwd_kernel<<<f32_bwd_ctas(bp.items), F32_BWD_THREADS, 0, st>>>(bp);
+  }
+  if ((rc = launch_check("fp32 backward"))) return rc;
+
+  const F32Inputs in = f32_inputs(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, H, pr.conv, scale,
+                                  lower_bound);
+  F32DcParams dp;
+  dp.seq = pr.seq;
+  dp.in = in;
+  dp.total_tokens = pr.TT;
+  dp.dqh_p = bv.dqh_p; dp.dkh_p = bv.dkh_p; dp.dal_p = bv.dal_p; dp.dbt_p = bv.dbt_p; dp.dvh = bv.dvh;
+  dp.alpha = sv.alpha; dp.bt = sv.bt;
+  dp.dq = pr.conv ? bv.dcq : dq;
+  dp.dk = pr.conv ? bv.dck : dk;
+  dp.dv = pr.conv ? bv.dcv : dv;
+  dp.dg = dg;
+  dp.dbeta = dbeta;
+  dp.partA = bv.partA; dp.partB = bv.partB;
+  {
+    TimedLaunch tl(K_F32_DC, st);
+    kda_f32_dc_kernel<<<dim3(row_grid(pr), H), 32 * F32_WARPS_PER_CTA, 0, st>>>(dp);
+  }
+  if ((rc = launch_check("fp32 gate/norm backward"))) return rc;
+
+  if (pr.conv) {
+    F32ConvParams cp;
+    cp.seq = pr.seq;
+    cp.in = in;
+    cp.dcq = bv.dcq; cp.dck = bv.dck; cp.dcv = bv.dcv;
+    cp.dq = dq; cp.dk = dk; cp.dv = dv;
+    cp.partW = bv.partW;
+    {
+      TimedLaunch tl(K_F32_CONV, st);
+      kda_f32_conv_bwd_kernel<<<dim3(row_grid(pr), H, 3), 32 * F32_WARPS_PER_CTA, 0, st>>>(cp);
+    }
+    if ((rc = launch_check("fp32 conv backward"))) return rc;
+  }
+
+  ReduceParams rp;
+  rp.seq = pr.seq;
+  rp.H = H;
+  rp.conv = pr.conv;
+  rp.partA = bv.partA; rp.partB = bv.partB; rp.partW = bv.partW;
+  rp.dA_log = dA_log; rp.ddt_bias = ddt_bias;
+  rp.dconv_q = dconv_q; rp.dconv_k = dconv_k; rp.dconv_v = dconv_v;
+  {
+    TimedLaunch tl(K_REDUCE, st);
+    kda_reduce_kernel<<<dim3(2 * H + (pr.conv ? 12 * H : 0)), 256, 0, st>>>(rp);
+  }
+  return launch_check("reduce");
+}
+
+int kda_b200_debug_set_input_wait_polls(unsigned int polls) {
+  g_input_wait_polls.store(polls ? polls : kDefaultWaitPolls, std::memory_order_relaxed);
+  return KDA_OK;
 }
 
 int kda_b200_device_error(int reset) {

@@ -117,7 +117,13 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     tc::bulk_g2s(ps.gam, P.GM + tix * 64 * LDG, GB, pro_ready);
     tc::bulk_g2s(ps.beta, P.BT + tix * 64, BB, pro_ready);
   }
-  if (!tc::mbar_wait(pro_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 7);
+  if (__syncthreads_or(!tc::mbar_wait(pro_ready, 0))) {
+    // the products did not arrive in time: record it, let the copies land
+    // (bounded) so none writes into a finished CTA's shared memory, and leave
+    if (tid == 0) atomicExch(&g_kda_device_error, 7);
+    tc::mbar_wait(pro_ready, 0);
+    return;
+  }
   // dE and dW land in their own region while the operands are built; dQt,
   // dKbar and A follow once the decay and raw regions are free
   if (tid == 0) {
@@ -194,8 +200,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 
   bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
   l_blocks_bf16(op, Lpb);  // only the dbeta row sums read L', in bf16
-  if (!tc::mbar_wait(tiles_ready, 0) && tid == 0) atomicExch(&g_kda_device_error, 5);
-  __syncthreads();
+  if (__syncthreads_or(!tc::mbar_wait(tiles_ready, 0))) {
+    if (tid == 0) atomicExch(&g_kda_device_error, 5);
+    tc::mbar_wait(tiles_ready, 0);
+    return;
+  }
   bf16* Abf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::ABF);
   bf16* Tbf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::TBF);
   {

@@ -26,6 +26,7 @@ struct FwdIntraParams {
   float *GM, *BT;
   int grid_chunks;            // chunk slots per head: items are (slot, head), slot fastest
   CUtensorMap maps[4];        // q, k, v, g as [T_total][H][128] bf16; boxes of 67 (q/k/v) and 64 (g) rows
+  uint32_t wait_polls;        // poll limit of the wait for an item's prefetched inputs
 };
 
 // Shared-memory layout of the forward intra kernel (bytes).  The raw inputs,
@@ -110,7 +111,16 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       // the previous item's A store reads the region the decay tile is rebuilt in
       if (P.A) tc::bulk_wait_read_all();
     }
-    if (!tc::mbar_wait(raw_ready, raw_phase) && threadIdx.x == 0) atomicExch(&g_kda_device_error, 8);
+    if (__syncthreads_or(!tc::mbar_wait(raw_ready, raw_phase, P.wait_polls))) {
+      // this item's inputs did not arrive in time: record it, let the copies in
+      // flight land (bounded wait) and leave without touching another item
+      if (threadIdx.x == 0) atomicExch(&g_kda_device_error, 8);
+      tc::mbar_wait(raw_ready, raw_phase);
+      cp_async_wait<0>();
+      if (threadIdx.x == 0) tc::bulk_wait_all();
+      __syncthreads();
+      return;
+    }
     raw_phase ^= 1u;
     if (P.conv) zero_foreign_halo(ps, pos);
     cp_async_wait<0>();

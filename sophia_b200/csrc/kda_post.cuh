@@ -15,6 +15,7 @@
 #pragma once
 
 #include "kda_common.cuh"
+#include "kda_tc.cuh"  // g_kda_device_error
 
 namespace kda {
 
@@ -293,9 +294,9 @@ __global__ void __launch_bounds__(256) kda_reduce_kernel(ReduceParams P) {
 // Builds the chunk table of packed sequences on the device (no host sync):
 // chunk_offsets[n] = sum_{m<n} ceil(len_m / 64), chunk_seq[c] = sequence of
 // chunk c.  cu_seqlens must start at 0, be non-decreasing and end at
-// total_tokens; otherwise *error_flag = 1 and every offset is 0, so all
-// kernels of the call see zero chunks and touch no token.  One CTA of 1024
-// threads.
+// total_tokens; otherwise *error_flag = 1, the device error flag
+// (kda_b200_device_error) is set to 3, and every offset is 0, so all kernels of
+// the call see zero chunks and touch no token.  One CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) kda_chunk_table_kernel(const int* cu, int N, long long total_tokens,
                                                                int* offsets, int* chunk_seq, int* error_flag) {
   __shared__ int warp_sums[32];
@@ -305,7 +306,11 @@ __global__ void __launch_bounds__(1024) kda_chunk_table_kernel(const int* cu, in
   for (int n = tid; n < N; n += 1024) bad |= (cu[n + 1] < cu[n]);
   if (tid == 0) bad |= (cu[0] != 0) || ((long long)cu[N] != total_tokens);
   bad = __syncthreads_or(bad);
-  if (tid == 0) { carry = 0; *error_flag = bad; }
+  if (tid == 0) {
+    carry = 0;
+    *error_flag = bad;
+    if (bad) atomicExch(&g_kda_device_error, 3);
+  }
   if (bad) {
     for (int n = tid; n <= N; n += 1024) offsets[n] = 0;
     return;

@@ -9,6 +9,14 @@
 //   S <- S + k u^T;      o = q^T S
 // (ml/runtime/model/attention.py:286-292, the order of the reference loop).
 // Inputs may be bf16 or fp32; o takes v's dtype; the final state is fp32.
+//
+// With conv taps and a conv history (the decode step of a cached
+// SophiaKDA.forward: _short_convolution with history, attention.py:226-258),
+// q, k and v are the pre-conv projections: thread v keeps the last three
+// inputs of channel v of q, k and v in registers, forms
+//   c = w0 x_(t-3) + w1 x_(t-2) + w2 x_(t-1) + w3 x_t,  x <- silu(c)
+// per token, and writes the history back at the end (the module's conv_state,
+// [B][3][H*128][3], oldest position first).
 #pragma once
 
 #include "kda_fwd_state_tc.cuh"  // g_kda_device_error
@@ -28,7 +36,19 @@ struct RecurrentParams {
   void* o;                           // [T_total][H][128], v's dtype
   float* ht;                         // [N][H][128][128] or null
   long long total_tokens;            // B*T: sequence bounds are checked against it
+  const float *conv_q, *conv_k, *conv_v;  // [H*128][4] taps, or null (inputs are post-conv)
+  float* conv_state;                 // [N][3][H*128][3] history in/out (with the taps)
 };
+
+// One conv step of channel `ch` given its three previous inputs (updated).
+__device__ __forceinline__ float rec_conv_silu(const float* taps, size_t ch, float (&hist)[3], float x) {
+  const float4 w = __ldg(reinterpret_cast<const float4*>(taps) + ch);
+  const float c = w.x * hist[0] + w.y * hist[1] + w.z * hist[2] + w.w * x;
+  hist[0] = hist[1];
+  hist[1] = hist[2];
+  hist[2] = x;
+  return c / (1.f + expf(-c));
+}
 
 __device__ __forceinline__ float rec_load(const void* p, size_t i, bool f32) {
   return f32 ? static_cast<const float*>(p)[i] : __bfloat162float(static_cast<const bf16*>(p)[i]);
@@ -60,10 +80,28 @@ __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentPar
 
   const float eA = expf(P.A_log[h]);
   const float bias = P.dt_bias[(size_t)h * D + vi];
+  const bool conv = P.conv_state != nullptr;
+  const size_t ch = (size_t)h * D + vi, inner = (size_t)H * D;
+  float hq[3] = {0.f, 0.f, 0.f}, hk[3] = {0.f, 0.f, 0.f}, hv[3] = {0.f, 0.f, 0.f};
+  if (conv) {
+    const float* cs = P.conv_state + (size_t)n * 3 * inner * 3 + ch * 3;
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      hq[s] = cs[s];
+      hk[s] = cs[inner * 3 + s];
+      hv[s] = cs[2 * inner * 3 + s];
+    }
+  }
   for (int t = bos; t < eos; ++t) {
     const size_t row = ((size_t)t * H + h) * D + vi;
-    const float qx = rec_load(P.q, row, P.fp32_inputs), kx = rec_load(P.k, row, P.fp32_inputs);
-    const float vx = rec_load(P.v, row, P.fp32_inputs), gx = rec_load(P.g, row, P.fp32_inputs);
+    float qx = rec_load(P.q, row, P.fp32_inputs), kx = rec_load(P.k, row, P.fp32_inputs);
+    float vx = rec_load(P.v, row, P.fp32_inputs);
+    const float gx = rec_load(P.g, row, P.fp32_inputs);
+    if (conv) {
+      qx = rec_conv_silu(P.conv_q, ch, hq, qx);
+      kx = rec_conv_silu(P.conv_k, ch, hk, kx);
+      vx = rec_conv_silu(P.conv_v, ch, hv, vx);
+    }
     const float bx = rec_load(P.beta, (size_t)t * H + h, P.fp32_inputs);
     const float sq = rec_block_sum(qx * qx, red[0]);
     const float sk = rec_block_sum(kx * kx, red[1]);
@@ -94,6 +132,15 @@ __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentPar
   if (P.ht) {
 #pragma unroll
     for (int kk = 0; kk < D; ++kk) P.ht[stateoff + (size_t)kk * D + vi] = S[kk];
+  }
+  if (conv) {
+    float* cs = P.conv_state + (size_t)n * 3 * inner * 3 + ch * 3;
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      cs[s] = hq[s];
+      cs[inner * 3 + s] = hk[s];
+      cs[2 * inner * 3 + s] = hv[s];
+    }
   }
 }
 

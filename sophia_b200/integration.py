@@ -10,10 +10,14 @@ Mirrors the reference's runtime-hook pattern
 * ``SophiaKDA.forward`` (``attention.py:373-420``) is replaced per instance by
   a version that sends the pre-conv projections straight to ``kda_layer``, so
   the ShortConv+SiLU, L2 norms, gate and beta run fused in the chunk kernels.
-  The replacement keeps the reference's pad-mask, cache and output-gate
-  semantics and defers to the original forward when a cached prefix is
-  continued (``start_pos > 0``), when the tensors are not on CUDA, or when the
-  module's ``kda_backend`` is ``"reference"``.
+  A cached continuation (``start_pos > 0`` with ``use_cache``, the decode
+  step) goes to ``kda_decode``: the conv with the module's ``conv_state``
+  history and the recurrence from ``recurrent_state`` in one kernel, both
+  states updated as the reference updates them.  The replacement keeps the
+  reference's pad-mask, cache and output-gate semantics and defers to the
+  original forward when a cached continuation needs gradients, when the
+  tensors are not on CUDA, or when the module's ``kda_backend`` is
+  ``"reference"``.
 
 The reference package is never imported here: modules are recognised by
 their class name and attributes.
@@ -25,7 +29,7 @@ from types import MethodType
 
 import torch
 
-from .ops import HEAD_DIM, chunk_kda, fused_recurrent_kda, gated_rms_norm, kda_layer
+from .ops import HEAD_DIM, chunk_kda, fused_recurrent_kda, gated_rms_norm, kda_decode, kda_layer
 
 PAD_LOGIT = -1.0e4  # attention.py:17
 
@@ -34,10 +38,43 @@ def _is_kda(m) -> bool:
     return type(m).__name__ == "SophiaKDA" and hasattr(m, "q_conv") and hasattr(m, "_run_kda")
 
 
+def _gate_out(self, x: torch.Tensor, output: torch.Tensor) -> torch.Tensor:
+    bsz, seqlen, _ = x.shape
+    gate_logits = (self.output_gate(x) if self.output_gate_full_rank
+                   else self.output_gate_up(self.output_gate_down(x)))
+    # output RMSNorm and sigmoid gate in one kernel (attention.py:416-419)
+    output = gated_rms_norm(output.to(dtype=x.dtype), gate_logits.view(bsz, seqlen, self.num_heads, self.head_dim),
+                            self.output_norm.weight, float(self.output_norm.eps))
+    return self.o_proj(output.reshape(bsz, seqlen, self.inner_dim))
+
+
+def _cached_step(self, x: torch.Tensor) -> torch.Tensor:
+    """start_pos > 0 with the cache: no pad mask (attention.py:377-380), conv
+    history from conv_state, initial state from recurrent_state, both
+    rewritten after the step (attention.py:244-257,398-410)."""
+    bsz, seqlen, _ = x.shape
+    H, D = self.num_heads, self.head_dim
+    self.ensure_batch_capacity(int(bsz))
+    qp, kp, vp = self.q_proj(x), self.k_proj(x), self.v_proj(x)
+    decay_logits = self.decay_up(self.decay_down(x)).view(bsz, seqlen, H, D)
+    beta_logits = self.beta_proj(x)
+    with torch.no_grad():
+        output, final_state = kda_decode(
+            qp.view(bsz, seqlen, H, D), kp.view(bsz, seqlen, H, D), vp.view(bsz, seqlen, H, D),
+            decay_logits, beta_logits, self.A_log, self.dt_bias, self.q_conv.weight, self.k_conv.weight,
+            self.v_conv.weight, self.conv_state[:bsz], lower_bound=self.lower_bound,
+            initial_state=self.recurrent_state[:bsz])
+        self.recurrent_state[:bsz].copy_(final_state)
+    return _gate_out(self, x, output)
+
+
 def _fused_forward(self, x: torch.Tensor, *, start_pos: int = 0) -> torch.Tensor:
-    if (int(start_pos) > 0 and self.use_cache) or not x.is_cuda or self.backend == "reference" \
-            or self.conv_kernel != 4 or self.head_dim != HEAD_DIM:
+    if not x.is_cuda or self.backend == "reference" or self.conv_kernel != 4 or self.head_dim != HEAD_DIM:
         return self._b200_reference_forward(x, start_pos=start_pos)
+    if int(start_pos) > 0 and self.use_cache:
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            return self._b200_reference_forward(x, start_pos=start_pos)
+        return _cached_step(self, x)
     bsz, seqlen, _ = x.shape
     H, D, inner = self.num_heads, self.head_dim, self.inner_dim
     if self.use_cache:
@@ -65,12 +102,7 @@ def _fused_forward(self, x: torch.Tensor, *, start_pos: int = 0) -> torch.Tensor
             for index, proj in enumerate((qp, kp, vp)):
                 seq = torch.cat((proj.new_zeros(bsz, hist, inner), proj), dim=1)[:, -hist:]
                 self.conv_state[:bsz, index].copy_(seq.transpose(1, 2).detach().to(torch.float32))
-    gate_logits = (self.output_gate(x) if self.output_gate_full_rank
-                   else self.output_gate_up(self.output_gate_down(x)))
-    # output RMSNorm and sigmoid gate in one kernel (attention.py:416-419)
-    output = gated_rms_norm(output.to(dtype=x.dtype), gate_logits.view(bsz, seqlen, H, D),
-                            self.output_norm.weight, float(self.output_norm.eps))
-    return self.o_proj(output.reshape(bsz, seqlen, inner))
+    return _gate_out(self, x, output)
 
 
 def install(model: torch.nn.Module, *, fuse_conv: bool = True) -> dict[str, object]:

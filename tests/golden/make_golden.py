@@ -16,7 +16,9 @@ runs, for every case of ``cases.py``:
 one document at a time for packed cases (state and conv history reset at each
 boundary).  Results go to ``tests/golden/<case>.npz``; configuration 0 of the
 benchmark (the full projections, T=512) goes to ``tests/golden/cfg0.npz`` as
-strided slices plus whole-tensor sums.  The fixtures are small enough to
+strided slices plus whole-tensor sums; ``SophiaKDA.forward`` end to end goes to
+``module_forward.npz`` and its cached prefill / continuation / decode path to
+``module_cache.npz``.  The fixtures are small enough to
 commit; the reference checkout is only needed to regenerate them.
 """
 
@@ -165,6 +167,69 @@ def run_module(reference_root: str) -> dict[str, np.ndarray]:
     return res
 
 
+CACHE_CFG = dict(B=2, dim=64, H=2, D=128, pad=5, prefill=70, chunk=9, decode=4, seed=2025)
+
+
+def _cache_module(reference_root: str, use_cache: bool):
+    sys.path.insert(0, reference_root)
+    from ml.runtime.model.attention import SophiaKDA
+    from ml.runtime.model.config import ModelArgs
+
+    c = CACHE_CFG
+    args = ModelArgs(dim=c["dim"], num_heads=c["H"], head_dim=c["D"], kda_decay_rank=16,
+                     kda_output_gate_rank=16, mla_q_rank=16, mla_kv_rank=16, kda_backend="reference",
+                     use_cache=use_cache, kda_decay_lower_bound=-5.0, vocab_size=128, ffn_hidden=128,
+                     n_layers=4, max_batch_size=c["B"])
+    return SophiaKDA(args)
+
+
+def run_cache(reference_root: str) -> dict[str, np.ndarray]:
+    """The cached path of SophiaKDA.forward (attention.py:373-420 with
+    use_cache): a left-padded prefill (start_pos 0, pad mask), a 9-token
+    continuation (start_pos 70: conv history from conv_state, initial state from
+    recurrent_state) and four one-token decode steps, fp32, reference backend;
+    plus the same 83 tokens in one uncached call.  Records every call's output
+    and the two cache buffers after the prefill and at the end."""
+    c = CACHE_CFG
+    torch.manual_seed(c["seed"])
+    mod = _cache_module(reference_root, True)
+    gen = torch.Generator().manual_seed(c["seed"])
+    with torch.no_grad():
+        for name, prm in mod.named_parameters():
+            if name in ("A_log", "dt_bias"):
+                continue
+            prm.copy_(torch.randn(prm.shape, generator=gen) * (0.5 if "conv" in name else 0.15))
+        mod.A_log.copy_(torch.randn(mod.A_log.shape, generator=gen) * 0.5)
+    total = c["prefill"] + c["chunk"] + c["decode"]
+    x = torch.randn(c["B"], total, c["dim"], generator=gen)
+    mask = torch.ones(c["B"], total, dtype=torch.bool)
+    mask[1, :c["pad"]] = False
+    res = {"x": x.numpy(), "mask": mask.numpy()}
+    for name, prm in mod.named_parameters():
+        res["param." + name] = prm.detach().numpy()
+    with torch.no_grad():
+        mod._pad_mask = mask
+        p0 = c["prefill"]
+        res["out.prefill"] = mod(x[:, :p0], start_pos=0).numpy()
+        res["state.prefill.recurrent"] = mod.recurrent_state.clone().numpy()
+        res["state.prefill.conv"] = mod.conv_state.clone().numpy()
+        res["out.chunk"] = mod(x[:, p0:p0 + c["chunk"]], start_pos=p0).numpy()
+        outs = []
+        for i in range(c["decode"]):
+            pos = p0 + c["chunk"] + i
+            outs.append(mod(x[:, pos:pos + 1], start_pos=pos))
+        res["out.decode"] = torch.cat(outs, dim=1).numpy()
+        res["state.final.recurrent"] = mod.recurrent_state.clone().numpy()
+        res["state.final.conv"] = mod.conv_state.clone().numpy()
+        full = _cache_module(reference_root, False)
+        full.load_state_dict(mod.state_dict(), strict=False)
+        full._pad_mask = mask
+        res["out.full"] = full(x, start_pos=0).numpy()
+    cached = np.concatenate([res["out.prefill"], res["out.chunk"], res["out.decode"]], axis=1)
+    np.testing.assert_allclose(cached, res["out.full"], rtol=1e-4, atol=1e-5)  # the reference's own invariant
+    return res
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True,
@@ -179,6 +244,8 @@ def main() -> None:
     print("wrote cfg0")
     np.savez_compressed(Path(a.out) / "module_forward.npz", **run_module(a.reference))
     print("wrote module_forward")
+    np.savez_compressed(Path(a.out) / "module_cache.npz", **run_cache(a.reference))
+    print("wrote module_cache")
 
 
 if __name__ == "__main__":

@@ -21,13 +21,14 @@ def round_inputs_bf16(inp: dict) -> dict:
     return out
 
 
-def run_cuda(case: Case, inputs: dict | None = None, grads: bool = True) -> dict:
+def run_cuda(case: Case, inputs: dict | None = None, grads: bool = True, dtype: torch.dtype = torch.bfloat16) -> dict:
+    """dtype: the activations' dtype (bf16: the bf16 kernels; float32: the fp32 kernels)."""
     from sophia_b200 import chunk_kda, kda_layer
     inp = make_inputs(case) if inputs is None else inputs
     dev = "cuda"
     t = {}
     for k in GRAD_KEYS:
-        dt = torch.bfloat16 if k in ("q", "k", "v", "g", "beta") else torch.float32
+        dt = dtype if k in ("q", "k", "v", "g", "beta") else torch.float32
         t[k] = inp[k].to(device=dev, dtype=dt).clone().requires_grad_(grads)
     cu = None if case.cu_seqlens is None else torch.tensor(case.cu_seqlens, dtype=torch.int32, device=dev)
     h0 = t["h0"] if case.h0 else None
@@ -82,7 +83,13 @@ def compare(got: dict, ref: dict, keys=None, rtol=RTOL, atol=ATOL) -> dict:
     return out
 
 
-def failures(rep: dict, ref: dict | None = None, baseline: dict | None = None) -> dict:
+# keys that passed only through the clauses relative to the reference's own CUDA
+# path ((b) and (c) of failures()), per test case; printed at the end of every
+# GPU run by conftest.py
+RELATIVE_ONLY: dict[str, dict[str, tuple[float, float]]] = {}
+
+
+def failures(rep: dict, ref: dict | None = None, baseline: dict | None = None, name: str | None = None) -> dict:
     """Keys that fail.  A key passes when
       (a) viol <= 1, and rel <= REL_FRO unless the tensor sits in the
           atol-dominated regime (rms(ref) <= atol / rtol, where a Frobenius
@@ -103,6 +110,27 @@ def failures(rep: dict, ref: dict | None = None, baseline: dict | None = None) -
             b = baseline[k]
             ok = viol <= 1.25 * max(b["viol"], 1.0) and rel <= 1.25 * max(b["rel"], REL_FRO)
             ok = ok or (rel <= max(b["rel"], REL_FRO) and viol <= 1.5 * max(b["viol"], 1.0))
+            if ok and name is not None:
+                RELATIVE_ONLY.setdefault(name, {})[k] = (viol, rel)
         if not ok:
             bad[k] = (viol, rel)
+    return bad
+
+
+FP32_TOL = 1e-5  # fp32 mode: rtol = atol = 1e-5
+
+
+def fp32_failures(got: dict, ref: dict) -> dict:
+    """Keys of the fp32 path outside |got - ref| <= 1e-5 + 1e-5 |ref|
+    (elementwise, torch.testing.assert_close semantics); value: the largest
+    ratio of error to allowance."""
+    bad = {}
+    for k in got:
+        if k not in ref or not got[k].numel():
+            continue
+        a = got[k].double()
+        b = ref[k].double().reshape(a.shape)
+        ratio = ((a - b).abs() / (FP32_TOL + FP32_TOL * b.abs())).max().item()
+        if not ratio <= 1.0:
+            bad[k] = ratio
     return bad

@@ -103,3 +103,25 @@ def test_chunk_index_restatement_known_answers():
     cu = [0, 10, 10, 80]
     np.testing.assert_array_equal(prepare_chunk_indices(cu, 64), [[0, 0], [1, 0], [1, 1]])
     np.testing.assert_array_equal(chunk_table_with_true_ids(cu, 64), [[0, 0], [2, 0], [2, 1]])
+
+
+def test_chunk_index_restatement_matches_fla():
+    """The restated integer bookkeeping equals flash-linear-attention's own
+    prepare_chunk_indices / prepare_chunk_offsets (fla/ops/utils/index.py:
+    138-158, the reference's pinned CUDA dependency) element for element, on
+    hand-made tables (empty, one-token, chunk-aligned documents) and random
+    ones, for chunk sizes 64 and 32."""
+    index = pytest.importorskip("fla.ops.utils.index")
+    rng = np.random.default_rng(11)
+    tables = [[0, 37, 101, 150, 214], [0, 64, 65, 200], [0, 10, 10, 80], [0, 1], [0, 64], [0, 0, 0, 5],
+              [0, 1, 65, 65, 200, 264, 264 + 4096]]
+    for _ in range(20):
+        lens = rng.integers(0, 300, size=int(rng.integers(1, 60)))
+        tables.append([0] + np.cumsum(lens).tolist())
+    for cu in tables:
+        cu_t = torch.tensor(cu, dtype=torch.long)
+        for chunk in (64, 32):
+            np.testing.assert_array_equal(prepare_chunk_offsets(cu, chunk),
+                                          index.prepare_chunk_offsets(cu_t, chunk).numpy())
+            np.testing.assert_array_equal(prepare_chunk_indices(cu, chunk).reshape(-1, 2),
+                                          index.prepare_chunk_indices(cu_t, chunk).numpy().reshape(-1, 2))
