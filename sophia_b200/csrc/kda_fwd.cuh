@@ -111,21 +111,20 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       // the previous item's A store reads the region the decay tile is rebuilt in
       if (P.A) tc::bulk_wait_read_all();
     }
-    if (__syncthreads_or(!tc::mbar_wait(raw_ready, raw_phase, P.wait_polls))) {
+    const bool arrived = tc::mbar_wait(raw_ready, raw_phase, P.wait_polls);
+    if (P.conv) zero_foreign_halo(ps, pos);
+    cp_async_wait<0>();
+    if (threadIdx.x >= LOADER_T0) ps.braw[threadIdx.x - LOADER_T0] = braw;
+    if (__syncthreads_or(!arrived)) {
       // this item's inputs did not arrive in time: record it, let the copies in
       // flight land (bounded wait) and leave without touching another item
       if (threadIdx.x == 0) atomicExch(&g_kda_device_error, 8);
       tc::mbar_wait(raw_ready, raw_phase);
-      cp_async_wait<0>();
       if (threadIdx.x == 0) tc::bulk_wait_all();
       __syncthreads();
       return;
     }
     raw_phase ^= 1u;
-    if (P.conv) zero_foreign_halo(ps, pos);
-    cp_async_wait<0>();
-    if (threadIdx.x >= LOADER_T0) ps.braw[threadIdx.x - LOADER_T0] = braw;
-    __syncthreads();
 
     Strip s;
     prologue_compute(P.in, ps, pos, P.conv, s);

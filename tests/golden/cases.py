@@ -75,6 +75,13 @@ RANDOM_CASES = {
 
 ALL_CASES = {**CASES, **RANDOM_CASES}
 
+# Full-length sequence: 64 chunks of state carried forward and back (checked
+# against the oracle on the GPU box; its oracle run takes seconds).
+LONG_CASES = {
+    "t4096_h2": Case("t4096_h2", B=1, T=4096, H=2, h0=True, final_state_grad=True, random_gate_params=True,
+                     seed=4096),
+}
+
 
 def make_case_inputs(case: Case) -> dict[str, torch.Tensor]:
     """make_inputs plus the case's gate-logit shift (saturation cases)."""

@@ -39,9 +39,9 @@ from oracle_runner import run_oracle  # noqa: E402
 def parity_cases() -> dict:
     """Every case the GPU parity tests compare with a recorded baseline: the
     fixture and random cases plus one configuration-4 packed window."""
-    from cases import cfg4_case
+    from cases import LONG_CASES, cfg4_case
     c4 = cfg4_case(0, H=4)
-    return {**ALL_CASES, c4.name: c4}
+    return {**ALL_CASES, c4.name: c4, **LONG_CASES}
 
 
 def main() -> None:
