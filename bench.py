@@ -7,8 +7,14 @@ Step = one forward + backward of the KDA layer (ShortConv+SiLU, L2 norms,
 gate, beta, chunked gated delta rule) over one batch of synthetic inputs of
 configuration 1 (8 sequences x 4096 tokens x 16 heads x 128, bf16, fp32 state)
 per GPU, then one NCCL all-reduce of the layer's weight gradients when N > 1
-(weak scaling: every rank processes its own 8 sequences).  ``--workload cfg3``
-shards configuration 3's 320 sequences over the ranks instead (strong scaling);
+(weak scaling: every rank processes its own 8 sequences).  The all-reduce is
+asynchronous: it runs on NCCL's stream while the next step computes, and the
+timed region ends after the last one completes.  ``--workload cfg3`` is one
+optimizer update of configuration 3: its 320 sequences sharded over the ranks
+(strong scaling), each rank running its share as micro-batches of at most
+40 sequences with the weight gradients accumulated, then one all-reduce (320
+sequences fwd+bwd need about 181 GB of activations, saved products and
+workspace at once, more than one GPU holds);
 ``--workload cfg2`` steps the whole mixer block of configuration 2
 (``sophia_b200.mixer.KDAMixerBlock``: input RMSNorm, fused q/k/v/gate GEMM,
 decay and beta projections, the KDA layer, gated output RMSNorm, out-
@@ -25,7 +31,11 @@ API with the step's inputs copied from pinned host memory and the weight
 gradients read back each step (the input copies run on a second stream, so
 step i+1's inputs cross PCIe while step i computes).  ``--impl reference`` times the reference's CPU
 implementation (the oracle restatement of ``SophiaKDA._reference_kda`` +
-``CausalDepthwiseConv1d`` with autograd) on the host cores instead.
+``CausalDepthwiseConv1d`` with autograd) on the host cores instead.  Both CPU
+figures (that arm, and the ``cpu_baseline`` of this one) time the same sample:
+one sequence of ``CPU_SAMPLE_TOKENS`` tokens x 16 heads, fwd+bwd (the
+reference's loop costs the same per token at any length, so the rate stands
+for configuration 1's sequences).
 """
 
 from __future__ import annotations
@@ -44,6 +54,8 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "KDA layer fwd+bwd tokens/s at H=16,D=128,T=4096 (1/2/4/8 B200) + % roofline"
 H, D, T = 16, 128, 4096
+CFG3_SEQS, CFG3_MICRO = 320, 40  # configuration 3: sequences per update, sequences per micro-batch
+CPU_SAMPLE_TOKENS = 1024         # tokens of the timed CPU sample (both CPU figures)
 
 # Algorithmic HBM bytes per token-head of each kernel (reads + writes of its
 # interface tensors, each once; bf16 activations, fp32 per-chunk vectors).
@@ -211,22 +223,40 @@ def bench_ours(a, rank, world, local_rank):
         B, Tlen = 1, CFG4_WINDOWS * T
         cu = torch.tensor(cfg4_cu_seqlens(), dtype=torch.int32, device=device)
     else:
-        B = a.batch or (8 if a.workload == "cfg1" else len(range(320)[dp.shard(320, rank, world)]))
+        B = a.batch or (8 if a.workload == "cfg1" else len(range(CFG3_SEQS)[dp.shard(CFG3_SEQS, rank, world)]))
         Tlen, cu = T, None
-    x, w = make_inputs(B, device, 42 + rank, Tlen)
+    # cfg3: the rank's B sequences run as micro-batches of at most CFG3_MICRO
+    # (the same synthetic micro-batch each time), gradients accumulated
+    micro = min(B, CFG3_MICRO) if a.workload == "cfg3" else B
+    n_micro = -(-B // micro)
+    x, w = make_inputs(micro, device, 42 + rank, Tlen)
     acts = {k: x[k].clone().requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
     params = {k: v.clone().requires_grad_(True) for k, v in w.items()}
     bucket = torch.empty(dp.bucket_numel(H, D), device=device, dtype=torch.float32)
+    pending = []  # the in-flight all-reduce of the previous step
+
+    def drain():
+        while pending:
+            pending.pop().wait()
 
     def step(inputs=None):
         src = acts if inputs is None else inputs
-        for t in list(src.values()) + list(params.values()):
+        for t in list(params.values()):
             t.grad = None
-        o, _ = kda_layer(src["q"], src["k"], src["v"], src["g"], src["beta"], params["A_log"], params["dt_bias"],
-                         params["conv_q"], params["conv_k"], params["conv_v"], cu_seqlens=cu)
-        o.backward(x["do"] if inputs is None else inputs["_do"])
+        for mb in range(n_micro):
+            rows = min(micro, B - mb * micro)
+            for t in src.values():
+                t.grad = None
+            sl = (lambda t: t) if rows == micro else (lambda t: t[:rows])  # noqa: E731
+            o, _ = kda_layer(sl(src["q"]), sl(src["k"]), sl(src["v"]), sl(src["g"]), sl(src["beta"]),
+                             params["A_log"], params["dt_bias"], params["conv_q"], params["conv_k"],
+                             params["conv_v"], cu_seqlens=cu)
+            o.backward(sl(x["do"] if inputs is None else inputs["_do"]))
+        drain()  # the previous step's reduction reads the bucket
         dp.grad_bucket(params, out=bucket)
-        dp.allreduce_bucket(bucket)
+        h = dp.allreduce_bucket_async(bucket)
+        if h is not None:
+            pending.append(h)
         return bucket
 
     def timed(fn, steps, sampler=None):
@@ -239,6 +269,7 @@ def bench_ours(a, rank, world, local_rank):
         e0.record(st)
         for _ in range(steps):
             fn()
+        drain()
         e1.record(st)
         torch.cuda.synchronize()
         if sampler is not None:
@@ -257,7 +288,7 @@ def bench_ours(a, rank, world, local_rank):
     ms = timed(step, a.steps, sampler)
     clocks = sampler.stop()
     rank_tokens = B * Tlen
-    global_tokens = 320 * T if a.workload == "cfg3" else world * rank_tokens
+    global_tokens = CFG3_SEQS * T if a.workload == "cfg3" else world * rank_tokens
     tokens = global_tokens * a.steps
     value = tokens / (ms / 1e3)
 
@@ -309,6 +340,7 @@ def bench_ours(a, rank, world, local_rank):
             inp = {k: bufs[b][k].requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
             inp["_do"] = bufs[b]["do"]
             step(inp)
+            drain()
             out_host.copy_(bucket, non_blocking=True)
             for k in ("q", "k", "v", "g", "beta"):
                 bufs[b][k].requires_grad_(False)
@@ -327,7 +359,7 @@ def bench_ours(a, rank, world, local_rank):
 
     hbm, tc, tc_sus, src = peaks()
     # dominant kernel and its roofline
-    th = B * Tlen * H  # token-heads per launch
+    th = micro * Tlen * H  # token-heads per launch
     dom = max((k for k in kern if k in KERNEL_BYTES_PER_TOKEN_HEAD), key=lambda k: kern[k][1])
     n_l, tot = kern[dom]
     per_launch_ms = tot / max(1, n_l)
@@ -343,7 +375,7 @@ def bench_ours(a, rank, world, local_rank):
         roof_ms += max(f / (tc_sus * 1e12), bpt * th / (hbm * 1e9)) * 1e3
     kernel_ms_per_step = {k: round(v[1] / a.steps, 4) for k, v in kern.items() if v[0]}
     return {
-        "value": value, "ms": ms / a.steps, "B": B, "clocks": clocks,
+        "value": value, "ms": ms / a.steps, "B": B, "micro": micro, "n_micro": n_micro, "clocks": clocks,
         "e2e": {"value": global_tokens * e2e_steps / (ms_e2e / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
@@ -552,6 +584,11 @@ def cpu_block_sample(tokens: int):
     return tokens / dt, dt
 
 
+def dp_shard(n, rank, world):
+    from sophia_b200.dp import shard
+    return shard(n, rank, world)
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -567,6 +604,13 @@ def main():
         config.update({"global_batch": world, "seq_len": CFG4_WINDOWS * T,
                        "packing": f"{CFG4_WINDOWS} windows x {T} tokens, {ncu4} documents (log-uniform lengths in "
                                   "[32, 4096], seed 42), cu_seqlens int32, state and conv history reset per document"})
+    if a.workload == "cfg3":
+        per_rank = len(range(CFG3_SEQS)[dp_shard(CFG3_SEQS, rank, world)])
+        config.update({"global_batch": CFG3_SEQS, "micro_batch": min(per_rank, CFG3_MICRO),
+                       "update": f"{CFG3_SEQS} sequences per update, {per_rank} on rank 0 in micro-batches of at most "
+                                 f"{CFG3_MICRO}, weight gradients accumulated, one all-reduce"})
+    if world > 1:
+        config["all_reduce"] = "asynchronous: overlaps the next step's compute; the timed region waits for the last"
     if mixer:
         config.update({"global_batch": (a.batch or 4) * world, "hidden": DIM, "decay_rank": DECAY_RANK,
                        "l2": "activations larger than L2 (48 MiB input, 256 MiB projections), no flush"})
@@ -578,7 +622,7 @@ def main():
             return
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
-        sample_tokens = 256 if mixer else 512
+        sample_tokens = 256 if mixer else CPU_SAMPLE_TOKENS
         for _ in range(a.warmup):
             sample(64)
         rates, secs = [], 0.0
@@ -587,12 +631,13 @@ def main():
             rates.append(r)
             secs += dt
         value = sample_tokens * a.steps / secs
+        config["cpu_sample"] = f"each step: 1 sequence x {sample_tokens} tokens x {H} heads fwd+bwd on the host"
         line = {"metric": metric, "value": value, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": secs / a.steps * 1e3, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                 "impl": "reference",
                 "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                 "sample": f"1 x {sample_tokens} tokens fwd+bwd per step, {what}"},
+                                 "sample": f"1 sequence x {sample_tokens} tokens fwd+bwd per step, {what}"},
                 "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -616,10 +661,19 @@ def main():
         if mixer:
             torch.set_num_threads(threads)
             rate, dt = cpu_block_sample(1024)
+            n_s, tok = 1, 1024
         else:
-            rate, dt = cpu_sample(2048, threads)
+            cpu_sample(64, threads)  # warm-up
+            n_s, tok, dt = 0, CPU_SAMPLE_TOKENS, 0.0
+            while n_s < 3 or dt < 10.0:  # 10-30 s of CPU work
+                _, d = cpu_sample(tok, threads)
+                dt += d
+                n_s += 1
+                if dt > 30.0:
+                    break
+            rate = n_s * tok / dt
         cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"1 x {1024 if mixer else 2048} tokens fwd+bwd ({dt:.1f} s), {what}"}
+               "sample": f"{n_s} x (1 sequence x {tok} tokens fwd+bwd) ({dt:.1f} s), {what}"}
     if rank == 0:
         line = {"metric": metric, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": res["ms"], "higher_is_better": True,

@@ -135,6 +135,24 @@ int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens,
                          int32_t* chunk_seq, int32_t* error_flag, void* stream);
 
 /*
+ * Document boundaries of packed pretraining windows -> cu_seqlens, on the
+ * device with no host synchronisation, so that it can sit inside a captured
+ * CUDA graph.  Sophia's data path packs documents into fixed windows and runs
+ * each window as one sequence with no reset at document ends
+ * (ml/training/pretrain/engine/sm120_graph_runner.py:244-259); this entry
+ * point gives the packed layer the boundaries instead.  tokens: int32
+ * [total_tokens], windows of `window` tokens back to back.  A document starts
+ * at every window start and after every token equal to eos_id.  cu_seqlens:
+ * int32 [capacity + 1]: the first min(count, capacity) document starts in
+ * order, then total_tokens in every later entry (empty sequences), so the
+ * layer is called with N = capacity.  n_docs: int32 [1], the true document
+ * count; when it exceeds the capacity the later boundaries are dropped (those
+ * documents continue their predecessor's state, as the reference does).
+ */
+int kda_b200_doc_cu_seqlens(const int32_t* tokens, int64_t total_tokens, int window, int eos_id, int capacity,
+                            int32_t* cu_seqlens, int32_t* n_docs, void* stream);
+
+/*
  * Token-by-token recurrence for decode, fp32 state and arithmetic -- replaces
  * flash-linear-attention's fused_recurrent_kda (0.5.x, not vendored) at its
  * Sophia call site: the single-step decode of SophiaKDA._run_kda

@@ -37,6 +37,7 @@ SIGNATURES = {
                          + [c_void_p, c_size_t] + [c_void_p] * 13 + [c_void_p, c_size_t, c_void_p], c_int),
     "kda_b200_recurrent": ([c_void_p] * 9 + [c_int] * 6 + [c_float, c_float] + [c_void_p] * 3, c_int),
     "kda_b200_decode": ([c_void_p] * 13 + [c_int] * 6 + [c_float, c_float] + [c_void_p] * 3, c_int),
+    "kda_b200_doc_cu_seqlens": ([c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p], c_int),
     "kda_b200_chunk_table": ([c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p], c_int),
     "kda_b200_device_error": ([c_int], c_int),
     "kda_b200_debug_set_input_wait_polls": ([ctypes.c_uint], c_int),

@@ -19,6 +19,7 @@
 #include "kda_post.cuh"
 #include "kda_gated_norm.cuh"
 #include "kda_f32.cuh"
+#include "kda_pack.cuh"
 
 using namespace kda;
 
@@ -439,6 +440,18 @@ int kda_b200_chunk_table(const int32_t* cu_seqlens, int N, int64_t total_tokens,
   kda_chunk_table_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(cu_seqlens, N, (long long)total_tokens,
                                                                             offsets, chunk_seq, error_flag);
   return launch_check("chunk table");
+}
+
+int kda_b200_doc_cu_seqlens(const int32_t* tokens, int64_t total_tokens, int window, int eos_id, int capacity,
+                            int32_t* cu_seqlens, int32_t* n_docs, void* stream) {
+  if (total_tokens < 0 || total_tokens > INT32_MAX) return fail(KDA_ERR_INVALID, "total_tokens must be in [0, 2^31)");
+  if (window < 1) return fail(KDA_ERR_INVALID, "window must be >= 1");
+  if (capacity < 1) return fail(KDA_ERR_INVALID, "capacity must be >= 1");
+  if (!cu_seqlens || !n_docs || (total_tokens > 0 && !tokens))
+    return fail(KDA_ERR_INVALID, "doc_cu_seqlens needs tokens, cu_seqlens and n_docs");
+  kda_doc_bounds_kernel<<<1, PACK_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      tokens, (long long)total_tokens, window, eos_id, capacity, cu_seqlens, n_docs);
+  return launch_check("doc cu_seqlens");
 }
 
 int kda_b200_recurrent(const void* q, const void* k, const void* v, const void* g, const void* beta,

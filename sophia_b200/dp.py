@@ -57,6 +57,18 @@ def allreduce_bucket(bucket: torch.Tensor) -> torch.Tensor:
     return bucket
 
 
+def allreduce_bucket_async(bucket: torch.Tensor):
+    """Starts the sum all-reduce of the bucket on the collective's own stream
+    and returns its handle (``None`` without a multi-rank group).  The
+    caller's stream keeps issuing work (the next micro-batch computes while
+    the gradients cross NVLink); ``handle.wait()`` makes the current stream
+    wait for the reduction before anything reads or rewrites the bucket."""
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        return dist.all_reduce(bucket, op=dist.ReduceOp.SUM, async_op=True)
+    return None
+
+
 def scatter_bucket(bucket: torch.Tensor, params: dict) -> None:
     """Writes the (reduced) bucket back into the parameters' ``.grad``."""
     off = 0
