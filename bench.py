@@ -240,10 +240,12 @@ def bench_ours(a, rank, world, local_rank):
             pending.pop().wait()
 
     def step(inputs=None):
-        src = acts if inputs is None else inputs
+        """inputs: None (the resident micro-batch every time) or a function of
+        the micro-batch index returning that micro-batch's inputs."""
         for t in list(params.values()):
             t.grad = None
         for mb in range(n_micro):
+            src = acts if inputs is None else inputs(mb)
             rows = min(micro, B - mb * micro)
             for t in src.values():
                 t.grad = None
@@ -251,7 +253,7 @@ def bench_ours(a, rank, world, local_rank):
             o, _ = kda_layer(sl(src["q"]), sl(src["k"]), sl(src["v"]), sl(src["g"]), sl(src["beta"]),
                              params["A_log"], params["dt_bias"], params["conv_q"], params["conv_k"],
                              params["conv_v"], cu_seqlens=cu)
-            o.backward(sl(x["do"] if inputs is None else inputs["_do"]))
+            o.backward(sl(x["do"] if inputs is None else src["_do"]))
         drain()  # the previous step's reduction reads the bucket
         dp.grad_bucket(params, out=bucket)
         h = dp.allreduce_bucket_async(bucket)
@@ -301,11 +303,11 @@ def bench_ours(a, rank, world, local_rank):
     _lib.timing_reset()
     launches = sum(n for n, _ in kern.values())
 
-    # end to end through the public API: every step copies its inputs from
-    # pinned host memory and reads the weight gradients back.  The copies run
-    # on a second stream into two alternating device buffers, so step i+1's
-    # inputs cross PCIe while step i computes; all copies are inside the
-    # timed region.
+    # end to end through the public API: every micro-batch of every step
+    # copies its inputs from pinned host memory, and every step reads the
+    # weight gradients back.  The copies run on a second stream into two
+    # alternating device buffers, so micro-batch i+1's inputs cross PCIe while
+    # micro-batch i computes; all copies are inside the timed region.
     host = {k: x[k].cpu().pin_memory() for k in ("q", "k", "v", "g", "beta", "do")}
     bufs = [{k: torch.empty_like(x[k]) for k in host} for _ in range(2)]
     out_host = torch.empty(bucket.numel(), dtype=torch.float32).pin_memory()
@@ -331,20 +333,30 @@ def bench_ours(a, rank, world, local_rank):
                     bufs[b][k].copy_(host[k], non_blocking=True)
                 copied[b].record(copy_stream)
 
+        total = steps * n_micro
         issue_copy(0)
-        for i in range(steps):
-            if i + 1 < steps:
+        state = {"i": 0}
+
+        def micro_inputs(_mb):
+            i = state["i"]
+            if i > 0:  # the previous micro-batch's buffer is free once its kernels ran
+                pb = (i - 1) % 2
+                for k in ("q", "k", "v", "g", "beta"):
+                    bufs[pb][k].requires_grad_(False)
+                freed[pb].record(st)
+            if i + 1 < total:
                 issue_copy(i + 1)
             b = i % 2
             st.wait_event(copied[b])
             inp = {k: bufs[b][k].requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
             inp["_do"] = bufs[b]["do"]
-            step(inp)
+            state["i"] = i + 1
+            return inp
+
+        for _ in range(steps):
+            step(micro_inputs)
             drain()
             out_host.copy_(bucket, non_blocking=True)
-            for k in ("q", "k", "v", "g", "beta"):
-                bufs[b][k].requires_grad_(False)
-            freed[b].record(st)
         e1.record(st)
         torch.cuda.synchronize()
         if world > 1:
@@ -354,7 +366,7 @@ def bench_ours(a, rank, world, local_rank):
     e2e_run(2)
     e2e_steps = max(3, min(a.steps, 10))
     ms_e2e = e2e_run(e2e_steps)
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    h2d = n_micro * sum(t.numel() * t.element_size() for t in host.values())
     d2h = out_host.numel() * out_host.element_size()
 
     hbm, tc, tc_sus, src = peaks()
@@ -373,6 +385,7 @@ def bench_ours(a, rank, world, local_rank):
     for k, bpt in KERNEL_BYTES_PER_TOKEN_HEAD.items():
         f = KERNEL_FLOPS_PER_TOKEN_HEAD[k] * th
         roof_ms += max(f / (tc_sus * 1e12), bpt * th / (hbm * 1e9)) * 1e3
+    roof_ms *= n_micro  # launches of each kernel per step
     kernel_ms_per_step = {k: round(v[1] / a.steps, 4) for k, v in kern.items() if v[0]}
     return {
         "value": value, "ms": ms / a.steps, "B": B, "micro": micro, "n_micro": n_micro, "clocks": clocks,
