@@ -80,7 +80,7 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per token-head of
 # each kernel from one ncu capture of `python bench.py --batch 2 --steps 1
 # --warmup 3 --profile` (B=2: the per-launch traffic scales with the token-heads
-# processed); summary in profiles/kda_kernels_dram_b2.md.
+# processed).
 NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
     "fwd_intra": 3299.9, "fwd_state": 1850.0, "bwd_state": 2824.1, "bwd_intra": 3828.0, "bwd_post": 2192.3,
 }

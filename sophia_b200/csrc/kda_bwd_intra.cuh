@@ -1,8 +1,9 @@
 // Chunk-parallel backward of the chunked KDA layer.
 //
-// One CTA per (chunk, head).  Recomputes the prologue and the intra-chunk
-// quantities (operand tiles, L'; A = (I + diag(beta) L')^-1 is the forward's
-// saved copy, T = A diag(beta)),
+// One CTA per (chunk, head).  Loads the forward's saved prologue products
+// (normalised q and k, post-conv v, the decay cumsum, beta) and its A =
+// (I + diag(beta) L')^-1, rebuilds the decayed operand tiles and L' from them
+// (T = A diag(beta)),
 // then, from the state-pass gradient pieces (dE, dW, dQt, dKbar, dM, dGC):
 //   dv  = T^T dE                      (written out as the value gradient)
 //   dKe = T^T dW,  dT = dE v^T + dW Ke^T,  dbeta += colsum(dT o A)
@@ -21,7 +22,7 @@
 // decay factors of that tile stay in registers for the whole kernel.
 #pragma once
 
-#include "kda_bwd_state.cuh"
+#include "kda_fwd.cuh"
 #include "kda_tc.cuh"
 
 namespace kda {

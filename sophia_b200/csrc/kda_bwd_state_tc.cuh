@@ -25,10 +25,22 @@
 // and dM (acc64n64) leave as whole per-(chunk, head) tiles in epilogue order.
 #pragma once
 
-#include "kda_bwd_state.cuh"
+#include "kda_fwd.cuh"
 #include "kda_fwd_state_tc.cuh"
 
 namespace kda {
+
+struct BwdStateParams {
+  SeqInfo seq;
+  int H;
+  const bf16 *W, *Qt, *Kb, *M, *dO;  // [T_total][H][128] (M: [T_total][H][64])
+  const bf16 *E, *hs;                // [chunks][H] acc64 / st128 tiles
+  const float* dC;
+  const float* dht;  // [N][H][128][128] or null
+  bf16 *dE, *dQt, *dW, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
+  float* dGC;        // [chunks][H][128]
+  float* dh0;        // [N][H][128][128] or null
+};
 
 struct BwdStateTcSmem {
   static constexpr int TILE = 16384;                    // [64][128] bf16, two 8 KB atoms

@@ -225,6 +225,26 @@ __device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const bf16* A, int
 
 // The same fragment loads for tiles in other layouts: a tile type provides
 // at(row, col) for col a multiple of 8 (the start of a contiguous 16-byte run).
+// As warp_mma with A negated (sign bits of the bf16 A fragments flipped).
+template <int NT, bool TA, bool TB>
+__device__ __forceinline__ void warp_mma_neg(float (&acc)[NT][4], const bf16* A, int lda, int m0,
+                                             const bf16* B, int ldb, int n0, int k0, int K) {
+#pragma unroll 2
+  for (int kk = 0; kk < K; kk += 16) {
+    uint32_t a[4];
+    if (TA) load_AT(a, A, lda, m0, k0 + kk); else load_A(a, A, lda, m0, k0 + kk);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] ^= 0x80008000u;
+#pragma unroll
+    for (int j = 0; j < NT; j += 2) {
+      uint32_t b[4];
+      if (TB) load_B_kn(b, B, ldb, n0 + 8 * j, k0 + kk); else load_B_nk(b, B, ldb, n0 + 8 * j, k0 + kk);
+      mma16816(acc[j], a, b[0], b[1]);
+      mma16816(acc[j + 1], a, b[2], b[3]);
+    }
+  }
+}
+
 struct PadTile {  // row-major with a padded row stride
   const bf16* p;
   int ld;
