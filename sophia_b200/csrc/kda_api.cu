@@ -52,7 +52,8 @@ struct Carver {
 struct SavedView {
   bf16 *W, *U, *Qt, *Kb, *E, *M, *hs;
   float* dC;
-  float* A;  // [slots x H] fp32 [64][LDF64] tiles of A = (I + diag(beta) L')^-1 (training only)
+  bf16* A;   // [slots x H] bf16 64x64 swizzled tiles of A = (I + diag(beta) L')^-1 (training only)
+  bf16* LP;  // [slots x H] bf16 64x64 swizzled tiles of L' (training only)
   // the forward prologue's products for the backward (training only):
   bf16 *QN, *KN, *VN;  // [slots x H] [64][128] bf16: scaled normalised q, normalised k, post-conv v
   float *GM, *BT;      // [slots x H] [64][LDG] fp32 in-chunk log2 decay cumsum, [slots x H][64] fp32 beta
@@ -70,7 +71,8 @@ SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) 
   if (with_bwd) {
     s.E = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.hs = cv.take<bf16>((size_t)mc * H * STATE_ELEMS * 2);
-    s.A = cv.take<float>((size_t)mc * H * A_TILE_ELEMS * 4);
+    s.A = cv.take<bf16>((size_t)mc * H * TILE64N64_ELEMS * 2);
+    s.LP = cv.take<bf16>((size_t)mc * H * TILE64N64_ELEMS * 2);
     s.QN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.KN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
     s.VN = cv.take<bf16>((size_t)mc * H * TILE64_ELEMS * 2);
@@ -80,6 +82,7 @@ SavedView carve_saved(Carver& cv, int64_t TT, int H, int64_t mc, bool with_bwd) 
     s.E = nullptr;
     s.hs = nullptr;
     s.A = nullptr;
+    s.LP = nullptr;
     s.QN = s.KN = s.VN = nullptr;
     s.GM = s.BT = nullptr;
   }
@@ -550,7 +553,7 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.in = prologue_in(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, H, scale, lower_bound);
   ip.seq = pr.seq;
   ip.conv = pr.conv;
-  ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A;
+  ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A; ip.LP = sv.LP;
   ip.QN = sv.QN; ip.KN = sv.KN; ip.VN = sv.VN; ip.GM = sv.GM; ip.BT = sv.BT;
   ip.grid_chunks = pr.grid_chunks;
   ip.wait_polls = g_input_wait_polls.load(std::memory_order_relaxed);
@@ -651,6 +654,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   bi.conv = pr.conv;
   bi.dE = bv.dE; bi.dW = bv.dW; bi.dQt = bv.dQt; bi.dKb = bv.dKb; bi.dM = bv.dM; bi.dGC = bv.dGC;
   bi.A = sv.A;
+  bi.LP = sv.LP;
   bi.QN = sv.QN; bi.KN = sv.KN; bi.VN = sv.VN; bi.GM = sv.GM; bi.BT = sv.BT;
   bi.dq_hat = bv.dq_hat;
   bi.dk_hat = bv.dk_hat;

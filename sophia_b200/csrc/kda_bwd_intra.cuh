@@ -1,25 +1,51 @@
-// Chunk-parallel backward of the chunked KDA layer.
+// Chunk-parallel backward of the chunked KDA layer on the fifth-generation
+// tensor cores (tcgen05 + TMEM).
 //
-// One CTA per (chunk, head).  Loads the forward's saved prologue products
-// (normalised q and k, post-conv v, the decay cumsum, beta) and its A =
-// (I + diag(beta) L')^-1, rebuilds the decayed operand tiles and L' from them
-// (T = A diag(beta)),
-// then, from the state-pass gradient pieces (dE, dW, dQt, dKbar, dM, dGC):
-//   dv  = T^T dE                      (written out as the value gradient)
-//   dKe = T^T dW,  dT = dE v^T + dW Ke^T,  dbeta += colsum(dT o A)
-//   dA  = dT diag(beta),  dL = -A^T dA A^T (strictly lower)
-//   dbeta += rowsum(dL o L'),  dL' = diag(beta) dL
-//   block products of dM and dL' against the decayed q/k operands give the
-//   gradients through M (Aqk) and L'
-//   dGam collects q o dq + k o dk terms; dg = reverse cumsum of dGam inside
+// One CTA of 512 threads per (chunk, head).  The forward's saved products --
+// normalised q and k, post-conv v (bf16, in the 128B-swizzled operand layout),
+// the decay cumsum, beta, and A = (I + diag(beta) L')^-1 and L' as bf16
+// operand tiles -- arrive by bulk copies; the state pass's gradient tiles dE,
+// dW and dM by cp.async straight into swizzled operand tiles.  With T =
+// A diag(beta) and the decayed operands Qa = q a, Ka = k a, Kd = k / a,
+// Ke = k 2^Gam built in shared memory, every block product is a tcgen05 MMA
+// with M = 64 (a 64 x 128 result is two N = 64 halves at TMEM lane offsets
+// 0 and 16, sharing 64 columns):
+//   G1  dv = T^T dE,  dKe = T^T dW,  dT = dE V^T + dW Ke^T
+//   G2  P_J = dM[:, J] Kd[J]          (row side of the gradient through M, J = 0..3)
+//   G3  X = dA A^T                    (dA = dT diag(beta))
+//   G4  R_I = dM[I, :]^T Qa[I]        (column side through M)
+//   G5  -dL = A^T X                   (then dL' = diag(beta) tril(dL))
+//   G6  P_J = dL'[:, J] Kd[J]         (row side through L')
+//   G7  R_I = dL'[I, :]^T Ka[I]       (column side through L')
+// One thread issues each group and commits it to its own mbarrier; the other
+// groups' epilogues run while it computes (G1+G2, then G3 during the row-M
+// epilogue, G4 during X, ...).  TMEM holds 512 columns in eight 64-column
+// units: G1 in units 0-2, X in 3, dL in 0, the row side of L' in 0-3, the
+// row side of M and both column sides in 4-7.
+//
+// Epilogues run in the TMEM row layout: warp w reads lane quarter w % 4 (rows
+// 16 (w % 4) .. +15 = sub-chunk block I), lanes 0-15 the first half of the
+// columns and lanes 16-31 the second, 16 columns per thread.  Each thread
+// keeps its 16 elements of dq, dk, dGam and of the decay factor
+//   af = 2^(Gam - Gam_r(I)) <= 1   (and bf = 2^(Gam_e(I) - Gam) = rev_I / af <= 1,
+//                                   rev_I = 2^(Gam_e(I) - Gam_r(I)))
+// in registers for the whole kernel.  The sub-chunk factorisation is that of
+// the chunk kernels (kda_intra.cuh): the row side scales P_J (J < I) by
+// 2^(Gam_r(I) - Gam_r(J)) and then by af, the column side scales R_Ib (Ib > I)
+// by 2^(Gam_r(Ib) - Gam_e(I)) and then by bf, the diagonal blocks by af and
+// 1/af; every factor is bounded, and one that underflows only does so where
+// the exact product is negligible.
+// Per element then:
+//   dq  = dQt 2^Gam + af (row side through M)
+//   dk  = dKe 2^Gam + dKbar 2^(Gam_C - Gam) + af (row side through L')
+//         + 1/af (diagonal) + bf (off-diagonal column sides)
+//   dGam collects q o dq - k o dk terms; dg = reverse cumsum of dGam inside
 //   the chunk; the gate and beta sigmoids are differentiated last.
 // Outputs: dq_hat, dk_hat (gradients of the normalised, scaled q and of the
 // normalised k; the L2-norm and conv backward run in the post kernel), dv,
 // dg_logits, dbeta_logits and per-chunk partial sums for dA_log and dt_bias.
-//
-// 512 threads.  Accumulator layout "F": warp w owns rows 16*(w&3) .. +15 and
-// columns 32*(w>>2) .. +31 of every 64x128 per-chunk gradient; the per-element
-// decay factors of that tile stay in registers for the whole kernel.
+// Every wait is bounded; on a timeout the CTA records an error, lets its
+// copies and MMAs in flight finish (bounded), frees TMEM and leaves.
 #pragma once
 
 #include "kda_fwd.cuh"
@@ -32,8 +58,8 @@ struct BwdIntraParams {
   SeqInfo seq;
   bool conv;
   const bf16 *dE, *dW, *dQt, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
-  const float* A;                        // [chunks][H] fp32 [64][LDF64] tiles saved by the forward
-  const bf16 *QN, *KN, *VN;              // [chunks][H] [64][128] bf16 prologue products of the forward
+  const bf16 *A, *LP;                    // [chunks][H] bf16 64x64 swizzled tiles of A and L' from the forward
+  const bf16 *QN, *KN, *VN;              // [chunks][H] bf16 64x128 swizzled prologue products of the forward
   const float *GM, *BT;                  // [chunks][H] [64][LDG] fp32 decay cumsum, [64] fp32 beta
   const float* dGC;
   bf16 *dq_hat, *dk_hat, *dv;  // [T_total][H][128]
@@ -42,529 +68,550 @@ struct BwdIntraParams {
 };
 
 struct BwdIntraSmem {
-  static constexpr int OPSZ = 64 * LD128 * 2;                // 17408
-  static constexpr int OPS = 0;                              // 6 operand tiles
-  static constexpr int GAM = OPS + 6 * OPSZ;                 // 64 x LDG fp32 (later dQt, dKbar, dGam)
-  static constexpr int DEW = GAM + 64 * LDG * 4;             // dE, dW tiles
-  static constexpr int RAW = DEW + 2 * OPSZ;                 // raw q/k/v, later small tiles
-  static constexpr int RAWSZ = 51712;
-  static constexpr int CVEC = RAW + RAWSZ;                   // 6 x 128 fp32
-  static constexpr int ER = CVEC + 6 * D * 4;                // 4 x 128 fp32
-  static constexpr int EC = ER + 4 * D * 4;                  // 4 x 128 fp32
-  static constexpr int BETA = EC + 4 * D * 4;                // 64 fp32
-  static constexpr int BRAW = BETA + 64 * 4;                 // 64 bf16
-  static constexpr int MISC = BRAW + 64 * 2;                 // mbarriers: gradient tiles, prologue products
-  static constexpr int END = MISC + 16;
-  // RAW aliases after the operands are built
-  static constexpr int AINV = RAW + 16640;                   // fp32 [64][LDF64] A from the forward (until the T build;
-                                                             // DMS reuses part of it afterwards)
-  static constexpr int LPB = RAW + 33280;                    // bf16 64 x LD64 (after inverse)
-  static constexpr int ABF = RAW;                            // bf16 64 x LD64
-  static constexpr int TBF = RAW + 42496;                    // bf16 64 x LD64
-  static constexpr int DMS = RAW + 9216;                     // bf16 64 x LD64
-  static constexpr int DLS = RAW + 18432;                    // bf16 64 x LD64
-  static constexpr int DBT = RAW + 27648;                    // fp32 4 x 64   (dbeta from T)
-  static constexpr int DBL = DBT + 1024;                     // fp32 4 x 64   (dbeta from L)
-  static constexpr int COLS = DBL + 1024;                    // fp32 4 x 128  (sum Kbar o dKbar)
-  static_assert(COLS + 2048 <= LPB, "small tiles overlap Lp bf16");
-  static constexpr int GB = COLS + 2048;                     // fp32 dGam_C [128], dt_bias [128], A_log
-                                                             // (over the dead A tile, after the T build)
-  static_assert(GB + (2 * D + 4) * 4 <= LPB && GB % 16 == 0, "gate-backward vectors overlap Lp bf16");
-  static_assert(TBF + 64 * LD64 * 2 <= RAWSZ + RAW, "T tile overflows");
-  static_assert(AINV + A_TILE_ELEMS * 4 <= LPB && AINV % 16 == 0, "A tile overlaps Lp bf16 or is misaligned");
-  // DEW aliases after the WY backward
-  static constexpr int DAS = DEW;                            // bf16 64 x LD64
-  static constexpr int XS = DEW + 9216;                      // bf16 64 x LD64
-  static constexpr int GRE = DEW + 18432;                    // bf16 64 x 128 gate logits (reloaded)
-  static_assert(GRE + 64 * D * 2 <= RAW, "gate reload overflows");
-  static_assert(MISC % 8 == 0 && DEW % 16 == 0 && GAM % 16 == 0, "bulk-copy targets and mbarrier alignment");
+  static constexpr int T128 = 16384, T64 = 8192;  // swizzled bf16 tiles of 64 x 128 / 64 x 64
+  static constexpr int QA = 0, KA = QA + T128, KD = KA + T128, KE = KD + T128, V = KE + T128;
+  static constexpr int DE = V + T128, DW = DE + T128;
+  static constexpr int QN = DW + T128, KN = QN + T128;
+  static constexpr int AT = KN + T128, LPT = AT + T64, DM = LPT + T64, TT = DM + T64;
+  static constexpr int GAM = TT + T64;  // 64 x LDG fp32; then the dQt | dKbar acc64 tiles; then dGam
+  static constexpr int VEC = GAM + 64 * LDG * 4;
+  static constexpr int CP = VEC;                    // [6][128] 2^(Gam_r(I) - Gam_r(J)), pair I(I-1)/2 + J
+  static constexpr int CC = CP + 6 * D * 4;         // [6][128] 2^(Gam_r(I) - Gam_e(J))
+  static constexpr int ER = CC + 6 * D * 4;         // [4][128] 2^Gam_r(J)
+  static constexpr int EC = ER + 4 * D * 4;         // [4][128] 2^(Gam_C - Gam_e(J))
+  static constexpr int REV = EC + 4 * D * 4;        // [4][128] 2^(Gam_e(J) - Gam_r(J))
+  static constexpr int BETA = REV + 4 * D * 4;      // [64] fp32
+  static constexpr int MISC = BETA + 64 * 4;        // 9 mbarriers, TMEM slot, issued mask
+  static constexpr int END = MISC + 128;
+  // aliases (regions dead by then)
+  static constexpr int DA = QN, XS = QN + T64;      // dA, X tiles (after the operand build)
+  static constexpr int DLP = KN;                    // dL' tile
+  static constexpr int DBT = KN + T64;              // fp32 [4][64] dbeta from T
+  static constexpr int DBL = DBT + 1024;            // fp32 [4][64] dbeta from L'
+  static constexpr int COLS = DBL + 1024;           // fp32 [4][128] column sums of Kbar o dKbar
+  static constexpr int GRE = DE;                    // bf16 [64][128] gate logits (after G1)
+  static constexpr int GBV = DW;                    // fp32 dGam_C [128], dt_bias [128], A_log (after G1)
+  static constexpr int PSUM = DW + 2048;            // fp32 [8][128] partial sums of the gate tail
+  static constexpr int DQT = GAM, DKB = GAM + T128; // acc64 state-pass tiles (after the decay factors)
+  static_assert(COLS + 4 * D * 4 <= KN + T128, "small arrays overflow the dL' region");
+  static_assert(PSUM + 8 * D * 4 <= DW + T128 && GBV + (2 * D + 4) * 4 <= PSUM, "gate-tail arrays overflow");
+  static_assert(DKB + T128 <= VEC, "gradient tiles overflow the decay region");
+  static_assert(END <= 232448, "shared memory");
+  static_assert(GAM % 1024 == 0 && MISC % 8 == 0, "alignment");
 };
 
+// Bytes of the products arriving by bulk copy at the start.
+constexpr uint32_t BWD_PRODUCT_BYTES = 3 * BwdIntraSmem::T128 + 64 * LDG * 4 + 64 * 4 + 2 * BwdIntraSmem::T64;
+
+__device__ __forceinline__ uint4 lds_chunk(const unsigned char* tile, int r, int c8) {
+  return *reinterpret_cast<const uint4*>(tile + 2 * sw64_chunk(r, c8));
+}
+__device__ __forceinline__ void unpack16(const uint4& a, const uint4& b, float (&f)[16]) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 p = unpack_bf16(w[i]);
+    f[2 * i] = p.x;
+    f[2 * i + 1] = p.y;
+  }
+}
+// 16 consecutive columns of row r of a swizzled tile (two 16-byte chunks).
+__device__ __forceinline__ void lds_row16(const unsigned char* tile, int r, int col0, float (&f)[16]) {
+  unpack16(lds_chunk(tile, r, col0 >> 3), lds_chunk(tile, r, (col0 >> 3) + 1), f);
+}
+__device__ __forceinline__ void pack16(const float (&f)[16], uint4& a, uint4& b) {
+  a.x = pack_bf16(f[0], f[1]); a.y = pack_bf16(f[2], f[3]); a.z = pack_bf16(f[4], f[5]); a.w = pack_bf16(f[6], f[7]);
+  b.x = pack_bf16(f[8], f[9]); b.y = pack_bf16(f[10], f[11]); b.z = pack_bf16(f[12], f[13]);
+  b.w = pack_bf16(f[14], f[15]);
+}
+__device__ __forceinline__ void sts_row16(unsigned char* tile, int r, int col0, const float (&f)[16]) {
+  uint4 a, b;
+  pack16(f, a, b);
+  *reinterpret_cast<uint4*>(tile + 2 * sw64_chunk(r, col0 >> 3)) = a;
+  *reinterpret_cast<uint4*>(tile + 2 * sw64_chunk(r, (col0 >> 3) + 1)) = b;
+}
+// 16 consecutive columns of row r of an acc64 tile (two 16-byte chunks).
+__device__ __forceinline__ void lds_acc64_16(const bf16* tile, int r, int col0, float (&f)[16]) {
+  unpack16(*reinterpret_cast<const uint4*>(tile + acc64_off(r, col0)),
+           *reinterpret_cast<const uint4*>(tile + acc64_off(r, col0 + 8)), f);
+}
+__device__ __forceinline__ void ld_vec16(const float* v, float (&f)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    const float4 x = *reinterpret_cast<const float4*>(v + i);
+    f[i] = x.x; f[i + 1] = x.y; f[i + 2] = x.z; f[i + 3] = x.w;
+  }
+}
+__device__ __forceinline__ void st_global16(bf16* dst, const float (&f)[16]) {
+  uint4 a, b;
+  pack16(f, a, b);
+  reinterpret_cast<uint4*>(dst)[0] = a;
+  reinterpret_cast<uint4*>(dst)[1] = b;
+}
+// Sum over the 16 lanes of this lane half (rows of one sub-chunk block).
+__device__ __forceinline__ float half_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  x += __shfl_xor_sync(0xffffffffu, x, 8);
+  return x;
+}
+
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntraParams P) {
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char bwi_smem[];  // 1 KB-aligned dynamic shared memory
+  unsigned char* smem = bwi_smem;
+  using S = BwdIntraSmem;
   const int c = blockIdx.x, h = blockIdx.y;
-  ChunkPos pos = chunk_pos(P.seq, c);
+  const ChunkPos pos = chunk_pos(P.seq, c);
   if (!pos.valid) return;
   const int H = P.in.H;
   const int nv = pos.t1 - pos.t0;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t cidx = (size_t)c * H + h;
   const size_t tix = tile_index(P.seq, c, h);
-
-  PrologueSmem ps;
-  ps.xq = reinterpret_cast<bf16*>(smem + BwdIntraSmem::RAW);
-  ps.xk = ps.xq + 64 * D;
-  ps.xv = ps.xk + 64 * D;
-  ps.braw = reinterpret_cast<bf16*>(smem + BwdIntraSmem::BRAW);
-  ps.gam = reinterpret_cast<float*>(smem + BwdIntraSmem::GAM);
-  ps.beta = reinterpret_cast<float*>(smem + BwdIntraSmem::BETA);
-
-  // The forward's prologue products (scaled normalised q, normalised k,
-  // post-conv v, the log2 decay cumsum in its padded layout, beta) arrive by
-  // five bulk copies; each thread then takes its strip.
-  uint64_t* pro_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC) + 1;
+  uint64_t* mb = reinterpret_cast<uint64_t*>(smem + S::MISC);  // 0 products, 1 dQt/dKbar, 2..8 MMA groups G1..G7
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mb + 9);
+  volatile uint32_t* issued = tslot + 1;  // bit i: mbarrier i has work in flight
+  float* gam = reinterpret_cast<float*>(smem + S::GAM);
+  float* beta = reinterpret_cast<float*>(smem + S::BETA);
+  if (smem_u32(smem) & 1023) {  // swizzled tiles need 1 KB alignment (block-uniform)
+    if (tid == 0) atomicExch(&g_kda_device_error, 9);
+    return;
+  }
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
   if (tid == 0) {
-    tc::mbar_init(reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC), 2);  // dE/dW, then the rest
-    tc::mbar_init(pro_ready, 1);
+    for (int i = 0; i < 9; ++i) tc::mbar_init(mb + i, 1);
     tc::fence_mbar_init();
+    *issued = 0u;
   }
+  // the state pass's gradient tiles, straight into their swizzled operand slots
+  {
+    const bf16* gE = P.dE + tix * TILE64_ELEMS;
+    const bf16* gW = P.dW + tix * TILE64_ELEMS;
+    for (int idx = tid; idx < 64 * 16; idx += blockDim.x) {
+      int row, cc;
+      acc64_chunk(idx, row, cc);
+      const uint32_t so = 2 * sw64_chunk(row, cc);
+      cp_async16(smem + S::DE + so, gE + idx * 8, true);
+      cp_async16(smem + S::DW + so, gW + idx * 8, true);
+    }
+    for (int idx = tid; idx < 64 * 8; idx += blockDim.x) {
+      int row, cc;
+      acc64n64_chunk(idx, row, cc);
+      cp_async16(smem + S::DM + 2 * sw64_chunk(row, cc), P.dM + tix * TILE64N64_ELEMS + idx * 8, row < nv);
+    }
+    cp_async_commit();
+  }
+  tc::fence_before_sync();
   __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
   if (tid == 0) {
-    constexpr uint32_t TB = TILE64_ELEMS * 2, GB = 64 * LDG * 4, BB = 64 * 4;
-    tc::mbar_expect_tx(pro_ready, 3 * TB + GB + BB);
-    tc::bulk_g2s(ps.xq, P.QN + tix * TILE64_ELEMS, TB, pro_ready);
-    tc::bulk_g2s(ps.xk, P.KN + tix * TILE64_ELEMS, TB, pro_ready);
-    tc::bulk_g2s(ps.xv, P.VN + tix * TILE64_ELEMS, TB, pro_ready);
-    tc::bulk_g2s(ps.gam, P.GM + tix * 64 * LDG, GB, pro_ready);
-    tc::bulk_g2s(ps.beta, P.BT + tix * 64, BB, pro_ready);
+    constexpr uint32_t TB = S::T128, GB = 64 * LDG * 4, BB = 64 * 4, AB = S::T64;
+    tc::mbar_expect_tx(mb + 0, BWD_PRODUCT_BYTES);
+    tc::bulk_g2s(smem + S::QN, P.QN + tix * TILE64_ELEMS, TB, mb + 0);
+    tc::bulk_g2s(smem + S::KN, P.KN + tix * TILE64_ELEMS, TB, mb + 0);
+    tc::bulk_g2s(smem + S::V, P.VN + tix * TILE64_ELEMS, TB, mb + 0);
+    tc::bulk_g2s(gam, P.GM + tix * 64 * LDG, GB, mb + 0);
+    tc::bulk_g2s(beta, P.BT + tix * 64, BB, mb + 0);
+    tc::bulk_g2s(smem + S::AT, P.A + tix * TILE64N64_ELEMS, AB, mb + 0);
+    tc::bulk_g2s(smem + S::LPT, P.LP + tix * TILE64N64_ELEMS, AB, mb + 0);
+    *issued = 1u;
   }
-  if (__syncthreads_or(!tc::mbar_wait(pro_ready, 0))) {
-    // the products did not arrive in time: record it, let the copies land
-    // (bounded) so none writes into a finished CTA's shared memory, and leave
-    if (tid == 0) atomicExch(&g_kda_device_error, 7);
-    tc::mbar_wait(pro_ready, 0);
-    return;
-  }
-  // dE and dW land in their own region while the operands are built; dQt,
-  // dKbar and A follow once the decay and raw regions are free
-  if (tid == 0) {
-    constexpr uint32_t TB = TILE64_ELEMS * 2;
-    uint64_t* tr = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC);
-    bf16* de = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
-    tc::mbar_expect_tx(tr, 2 * TB);
-    tc::bulk_g2s(de, P.dE + tix * TILE64_ELEMS, TB, tr);
-    tc::bulk_g2s(de + 64 * LD128, P.dW + tix * TILE64_ELEMS, TB, tr);
-  }
-  Strip s;
-  {
-    const int tg = tid >> 4, cg = tid & 15;
-#pragma unroll
-    for (int r = 0; r < STRIP; ++r) {
-      const int t = STRIP * tg + r;
-      unpack8(*reinterpret_cast<const bf16x8*>(ps.xq + t * D + 8 * cg), s.q[r]);
-      unpack8(*reinterpret_cast<const bf16x8*>(ps.xk + t * D + 8 * cg), s.k[r]);
-      unpack8(*reinterpret_cast<const bf16x8*>(ps.xv + t * D + 8 * cg), s.v[r]);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) s.gam[r][c] = ps.gam[t * LDG + 8 * cg + c];
-    }
-  }
-  __syncthreads();
 
-  Operands op;
-  op.Qa = reinterpret_cast<bf16*>(smem + BwdIntraSmem::OPS);
-  op.Ka = op.Qa + 64 * LD128;
-  op.Kd = op.Ka + 64 * LD128;
-  op.Kb = op.Kd + 64 * LD128;
-  op.V = op.Kb + 64 * LD128;
-  op.Ke = op.V + 64 * LD128;
-  op.cvec = reinterpret_cast<float*>(smem + BwdIntraSmem::CVEC);
-  op.er = reinterpret_cast<float*>(smem + BwdIntraSmem::ER);
-  op.ec = reinterpret_cast<float*>(smem + BwdIntraSmem::EC);
-  build_operands<false>(s, ps.gam, op, nullptr, nullptr);
+  // epilogue mapping: rows 16 s .. 16 s + 15 (block I = s), 16 columns from c0
+  const int s = warp & 3, qd = warp >> 2, hh = lane >> 4;
+  const int r = 16 * s + (lane & 15);
+  const int c0 = 64 * hh + 16 * qd;
+  const uint32_t trow = tbase + ((uint32_t)(32 * s) << 16);
+  const uint32_t idMM = tc::idesc_bf16(64, 64, true, true);    // A MN-major, B MN-major
+  const uint32_t idKM = tc::idesc_bf16(64, 64, false, true);   // A K-major,  B MN-major
+  const uint32_t idKK = tc::idesc_bf16(64, 64, false, false);  // A K-major,  B K-major
+  const uint32_t sb = smem_u32(smem);
+  // K-major operand at byte offset `off`: K step ks (16 elements) of a tile of 64-element atoms
+  auto kdesc = [&](int off, int ks) { return tc::smem_desc(sb + off + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024); };
+  // MN-major operand: K step ks (16 rows)
+  auto mdesc = [&](int off, int ks) { return tc::smem_desc(sb + off + ks * 2048, 8192, 1024); };
 
-  // F layout of this warp and its per-element decay factors
-  const int I = warp & 3;             // row block
-  const int m0 = 16 * I, n0 = 32 * (warp >> 2);
-  float af[4][4], bfv[4][4];          // a = 2^(Gam - Gam_r(I)), b = 2^(Gam_e(I) - Gam)
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int r = m0 + acc_row(e), col = n0 + acc_col(j, e);
-      float G = ps.gam[r * LDG + col];
-      af[j][e] = ex2(G - ps.gam[m0 * LDG + col]);
-      bfv[j][e] = ex2(ps.gam[(m0 + 15) * LDG + col] - G);
-    }
-  tc::fence_async_smem();  // the regions below are rewritten by the bulk copies
-  __syncthreads();
+  float dq[16], dk[16], dG[16], af[16];
+  bool ok = true;
+  for (int once = 0; once < 1; ++once) {
+    ok = tc::mbar_wait(mb + 0, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 7); break; }
 
-  // The state-pass gradient tiles (acc64 order, rows past the end zero) and
-  // A = (I + diag(beta) L')^-1 as the forward computed it arrive by bulk copies
-  // issued by one thread (dE and dW since the products landed, the rest now),
-  // so the warps go on with L' meanwhile; the tiles stay in their global order
-  // (Acc64Tile addressing).  dQt and dKbar land in the dead decay region, A in
-  // the dead raw region (clear of L', which l_blocks writes below).
-  bf16* dEs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DEW);
-  bf16* dWs = dEs + 64 * LD128;
-  bf16* dQs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GAM);
-  bf16* dKs = dQs + 64 * D;
-  float* Asm = reinterpret_cast<float*>(smem + BwdIntraSmem::AINV);
-  uint64_t* tiles_ready = reinterpret_cast<uint64_t*>(smem + BwdIntraSmem::MISC);
-  if (tid == 0) {
-    constexpr uint32_t TB = TILE64_ELEMS * 2, AB = A_TILE_ELEMS * 4;
-    tc::mbar_expect_tx(tiles_ready, 2 * TB + AB);
-    tc::bulk_g2s(dQs, P.dQt + tix * TILE64_ELEMS, TB, tiles_ready);
-    tc::bulk_g2s(dKs, P.dKb + tix * TILE64_ELEMS, TB, tiles_ready);
-    tc::bulk_g2s(Asm, P.A + tix * A_TILE_ELEMS, AB, tiles_ready);
-  }
-  const Acc64Tile dEt{dEs}, dWt{dWs};
-
-  bf16* Lpb = reinterpret_cast<bf16*>(smem + BwdIntraSmem::LPB);
-  l_blocks_bf16(op, Lpb);  // only the dbeta row sums read L', in bf16
-  if (__syncthreads_or(!tc::mbar_wait(tiles_ready, 0))) {
-    if (tid == 0) atomicExch(&g_kda_device_error, 5);
-    tc::mbar_wait(tiles_ready, 0);
-    return;
-  }
-  bf16* Abf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::ABF);
-  bf16* Tbf = reinterpret_cast<bf16*>(smem + BwdIntraSmem::TBF);
-  {
-    // A (fp32, [16640, 33280) of the raw region) -> Abf ([0, 9216)) and Tbf ([42496, 51712)): no overlap
-    float av[8];
-    const int r = tid >> 3, c0 = (tid & 7) * 8;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) av[i] = (c0 + i <= r) ? Asm[r * LDF64 + c0 + i] : 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      *reinterpret_cast<uint32_t*>(Abf + r * LD64 + c0 + i) = pack_bf16(av[i], av[i + 1]);
-      *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + c0 + i) =
-          pack_bf16(av[i] * ps.beta[c0 + i], av[i + 1] * ps.beta[c0 + i + 1]);
-    }
-  }
-  bf16* dMs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DMS);
-  __syncthreads();
-  for (int idx = tid; idx < 64 * 8; idx += blockDim.x) {
-    int r, cc;
-    acc64n64_chunk(idx, r, cc);
-    cp_async16(dMs + r * LD64 + cc * 8, P.dM + tix * TILE64N64_ELEMS + idx * 8, r < nv);
-  }
-  // the gate backward's per-channel vectors, so that the tail waits on no global load
-  float* gbv = reinterpret_cast<float*>(smem + BwdIntraSmem::GB);
-  if (tid < 32)
-    cp_async16(gbv + 4 * tid, P.dGC + cidx * D + 4 * tid, true);
-  else if (tid < 64)
-    cp_async16(gbv + D + 4 * (tid - 32), P.in.dt_bias + (size_t)h * D + 4 * (tid - 32), true);
-  else if (tid == 64)
-    cp_async4(gbv + 2 * D, P.in.A_log + h);
-  cp_async_commit();
-  __syncthreads();
-
-  float dq[4][4], dk[4][4], dG[4][4];
-  // ---- WY backward and the state-side pieces --------------------------------
-  {
-    float acc[4][4];
-    zero_acc<4>(acc);
-    warp_mma_t<4, true, true>(acc, PadTile{Tbf, LD64}, m0, dEt, n0, 0, 64);  // dv = T^T dE
-    // 16-byte runs per lane (quad transpose) instead of scattered 4-byte stores
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) w[j] = pack_bf16(acc[j][e], acc[j][e + 1]);
-      quad_transpose4(w);
-      const int r = m0 + acc_row(e);
-      if (r < nv)
-        *reinterpret_cast<uint4*>(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + n0 + 8 * (tid & 3)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    zero_acc<4>(acc);
-    warp_mma_t<4, true, true>(acc, PadTile{Tbf, LD64}, m0, dWt, n0, 0, 64);  // dKe = T^T dW
-    float colsum[4][2];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        const int sw = (int)acc64_off(r, cc);
-        float2 gq = unpack_bf16(*reinterpret_cast<const uint32_t*>(dQs + sw));
-        float2 gk = unpack_bf16(*reinterpret_cast<const uint32_t*>(dKs + sw));
-        float2 qa = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Qa + r * LD128 + cc));
-        float2 kb = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kb + r * LD128 + cc));
-        float2 ke = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Ke + r * LD128 + cc));
-        float2 er = *reinterpret_cast<const float2*>(op.er + I * D + cc);
-        float2 ec = *reinterpret_cast<const float2*>(op.ec + I * D + cc);
-        float qav[2] = {qa.x, qa.y}, kbv[2] = {kb.x, kb.y}, kev[2] = {ke.x, ke.y};
-        float gqv[2] = {gq.x, gq.y}, gkv[2] = {gk.x, gk.y}, erv[2] = {er.x, er.y}, ecv[2] = {ec.x, ec.y};
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          float eg = af[j][e + u] * erv[u];
-          float egc = bfv[j][e + u] * ecv[u];
-          float dke = acc[j][e + u];
-          dq[j][e + u] = gqv[u] * eg;
-          dk[j][e + u] = dke * eg + gkv[u] * egc;
-          float kbar = kbv[u] * ecv[u];
-          float qt = qav[u] * erv[u];
-          dG[j][e + u] = kev[u] * dke + qt * gqv[u] - kbar * gkv[u];
-          if (e == 0) colsum[j][u] = kbar * gkv[u]; else colsum[j][u] += kbar * gkv[u];
-        }
-      }
-    }
-    // column sums of Kbar o dKbar over the chunk (lanes sharing a column differ in bits 2..4)
-    float* cols = reinterpret_cast<float*>(smem + BwdIntraSmem::COLS);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float x = colsum[j][u];
-        x += __shfl_xor_sync(0xffffffffu, x, 4);
-        x += __shfl_xor_sync(0xffffffffu, x, 8);
-        x += __shfl_xor_sync(0xffffffffu, x, 16);
-        colsum[j][u] = x;
-      }
-    if ((tid & 31) < 4) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int u = 0; u < 2; ++u) cols[I * D + n0 + acc_col(j, u)] = colsum[j][u];
-    }
-  }
-  // dT = dE V^T + dW Ke^T (64x64), warp tile rows m0, cols n1 (two n8 tiles)
-  const int n1 = 16 * (warp >> 2);
-  {
-    float acc[2][4];
-    zero_acc<2>(acc);
-    warp_mma_t<2, false, false>(acc, dEt, m0, PadTile{op.V, LD128}, n1, 0, 128);
-    warp_mma_t<2, false, false>(acc, dWt, m0, PadTile{op.Ke, LD128}, n1, 0, 128);
-    // dbeta_T[j] = sum_i dT_ij A_ij ; dA = dT diag(beta)
-    float cs[2][2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float sum = 0.f;
-#pragma unroll
-        for (int e = u; e < 4; e += 2) {
-          int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
-          sum += acc[j][e] * __bfloat162float(Abf[r * LD64 + cc]);
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-        cs[j][u] = sum;
-      }
-    float* dbt = reinterpret_cast<float*>(smem + BwdIntraSmem::DBT);
-    if ((tid & 31) < 4) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int u = 0; u < 2; ++u) dbt[I * 64 + n1 + acc_col(j, u)] = cs[j][u];
-    }
-    __syncthreads();  // all reads of dE / dW are done
-    bf16* dAs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DAS);
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
-        *reinterpret_cast<uint32_t*>(dAs + r * LD64 + cc) =
-            pack_bf16(acc[j][e] * ps.beta[cc], acc[j][e + 1] * ps.beta[cc + 1]);
-      }
-  }
-  __syncthreads();
-  // X = dA A^T ; dL = -A^T X (strictly lower)
-  {
-    bf16* dAs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DAS);
-    bf16* Xs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::XS);
-    float acc[2][4];
-    zero_acc<2>(acc);
-    warp_mma<2, false, false>(acc, dAs, LD64, m0, Abf, LD64, n1, 0, 64);
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
-        *reinterpret_cast<uint32_t*>(Xs + r * LD64 + cc) = pack_bf16(acc[j][e], acc[j][e + 1]);
-      }
-    __syncthreads();
-    zero_acc<2>(acc);
-    warp_mma_neg<2, true, true>(acc, Abf, LD64, m0, Xs, LD64, n1, 0, 64);
-    bf16* dLs = reinterpret_cast<bf16*>(smem + BwdIntraSmem::DLS);
-    float rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n1 + acc_col(j, e);
-        float x0 = cc < r ? acc[j][e] : 0.f;
-        float x1 = cc + 1 < r ? acc[j][e + 1] : 0.f;
-        float2 lp = unpack_bf16(*reinterpret_cast<const uint32_t*>(Lpb + r * LD64 + cc));
-        rs[e >> 1] += x0 * lp.x + x1 * lp.y;
-        float br = ps.beta[r];
-        *reinterpret_cast<uint32_t*>(dLs + r * LD64 + cc) = pack_bf16(x0 * br, x1 * br);
-      }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 1);
-      rs[i] += __shfl_xor_sync(0xffffffffu, rs[i], 2);
-    }
-    float* dbl = reinterpret_cast<float*>(smem + BwdIntraSmem::DBL);
-    if ((tid & 3) == 0) {
-      dbl[(warp >> 2) * 64 + m0 + acc_row(0)] = rs[0];
-      dbl[(warp >> 2) * 64 + m0 + acc_row(2)] = rs[1];
-    }
-  }
-  // the gate logits are needed again at the end: fetch them now (region free)
-  bf16* gre = reinterpret_cast<bf16*>(smem + BwdIntraSmem::GRE);
-  for (int i = tid; i < 64 * 16; i += blockDim.x) {
-    int r = i >> 4, cc = i & 15;
-    bool ok = r < nv;
-    cp_async16(gre + r * D + cc * 8,
-               P.in.g + (ok ? ((size_t)(pos.t0 + r) * H + h) * D + cc * 8 : 0), ok);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();  // dM and the gate logits
-  __syncthreads();
-
-  const bf16* dLs = reinterpret_cast<const bf16*>(smem + BwdIntraSmem::DLS);
-  // ---- gradients through M (Aqk) and L' -------------------------------------
-  // row side: rows of block I, reduction over j <= i
-#pragma unroll 1
-  for (int which = 0; which < 2; ++which) {
-    const bf16* dX = which == 0 ? dMs : dLs;
-    const bf16* rowop = which == 0 ? op.Qa : op.Ka;
-    float acc[4][4];
-    zero_acc<4>(acc);
+    // ---- operands (strip mapping: tokens 2 tg, 2 tg + 1, channels 8 cg .. +7)
     {
-      uint32_t a[4];
-      load_A(a, dX, LD64, m0, 16 * I);
+      const int tg = tid >> 4, cg = tid & 15;
+      const int J = (STRIP * tg) >> 4;
+      float Gr[8], erv[8];
 #pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        uint32_t b[4];
-        load_B_kn(b, op.Kd, LD128, n0 + 8 * j, 16 * I);
-        mma16816(acc[j], a, b[0], b[1]);
-        mma16816(acc[j + 1], a, b[2], b[3]);
-      }
-    }
-    for (int J = 0; J < I; ++J) {
-      float tmp[4][4];
-      zero_acc<4>(tmp);
-      uint32_t a[4];
-      load_A(a, dX, LD64, m0, 16 * J);
-#pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        uint32_t b[4];
-        load_B_kn(b, op.Kb, LD128, n0 + 8 * j, 16 * J);
-        mma16816(tmp[j], a, b[0], b[1]);
-        mma16816(tmp[j + 1], a, b[2], b[3]);
-      }
-      const float* cv = op.cvec + pair_index(I, J) * D;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 c2 = *reinterpret_cast<const float2*>(cv + n0 + acc_col(j, 0));
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] += ((e & 1) ? c2.y : c2.x) * tmp[j][e];
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        float2 ro = unpack_bf16(*reinterpret_cast<const uint32_t*>(rowop + r * LD128 + cc));
-        float rov[2] = {ro.x, ro.y};
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          float gval = acc[j][e + u];
-          if (which == 0) dq[j][e + u] += af[j][e + u] * gval; else dk[j][e + u] += af[j][e + u] * gval;
-          dG[j][e + u] += rov[u] * gval;
-        }
-      }
-  }
-  // column side: rows j of block I (as the column block), reduction over i >= j
-#pragma unroll 1
-  for (int which = 0; which < 2; ++which) {
-    const bf16* dX = which == 0 ? dMs : dLs;
-    const bf16* rowop = which == 0 ? op.Qa : op.Ka;
-    float acc[4][4];
-    zero_acc<4>(acc);
-    {
-      uint32_t a[4];
-      load_AT(a, dX, LD64, m0, 16 * I);
-#pragma unroll
-      for (int j = 0; j < 4; j += 2) {
-        uint32_t b[4];
-        load_B_kn(b, rowop, LD128, n0 + 8 * j, 16 * I);
-        mma16816(acc[j], a, b[0], b[1]);
-        mma16816(acc[j + 1], a, b[2], b[3]);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-        float2 kd = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kd + r * LD128 + cc));
-        float kdv[2] = {kd.x, kd.y};
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          float ia = rcp(af[j][e + u]);
-          dk[j][e + u] += ia * acc[j][e + u];
-          dG[j][e + u] -= kdv[u] * acc[j][e + u];
-        }
-      }
-    if (I < 3) {
-      zero_acc<4>(acc);
-      for (int Ib = I + 1; Ib < 4; ++Ib) {
-        float tmp[4][4];
-        zero_acc<4>(tmp);
-        uint32_t a[4];
-        load_AT(a, dX, LD64, m0, 16 * Ib);
-#pragma unroll
-        for (int j = 0; j < 4; j += 2) {
-          uint32_t b[4];
-          load_B_kn(b, rowop, LD128, n0 + 8 * j, 16 * Ib);
-          mma16816(tmp[j], a, b[0], b[1]);
-          mma16816(tmp[j + 1], a, b[2], b[3]);
-        }
-        const float* cv = op.cvec + pair_index(Ib, I) * D;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 c2 = *reinterpret_cast<const float2*>(cv + n0 + acc_col(j, 0));
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[j][e] += ((e & 1) ? c2.y : c2.x) * tmp[j][e];
-        }
+      for (int u = 0; u < 8; ++u) {
+        Gr[u] = gam[(16 * J) * LDG + 8 * cg + u];
+        erv[u] = ex2(Gr[u]);
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int rr = 0; rr < STRIP; ++rr) {
+        const int t = STRIP * tg + rr;
+        float qv[8], kv[8], qa[8], ka[8], kd[8], ke[8];
+        {
+          const uint4 qx = lds_chunk(smem + S::QN, t, cg), kx = lds_chunk(smem + S::KN, t, cg);
+          const uint32_t qw[4] = {qx.x, qx.y, qx.z, qx.w}, kw[4] = {kx.x, kx.y, kx.z, kx.w};
 #pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-          float2 kb = unpack_bf16(*reinterpret_cast<const uint32_t*>(op.Kb + r * LD128 + cc));
-          float kbv[2] = {kb.x, kb.y};
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            dk[j][e + u] += bfv[j][e + u] * acc[j][e + u];
-            dG[j][e + u] -= kbv[u] * acc[j][e + u];
+          for (int i = 0; i < 4; ++i) {
+            const float2 a = unpack_bf16(qw[i]), b = unpack_bf16(kw[i]);
+            qv[2 * i] = a.x; qv[2 * i + 1] = a.y; kv[2 * i] = b.x; kv[2 * i + 1] = b.y;
           }
         }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float G = gam[t * LDG + 8 * cg + u];
+          const float a = ex2(G - Gr[u]), ia = ex2(Gr[u] - G);
+          qa[u] = qv[u] * a;
+          ka[u] = kv[u] * a;
+          kd[u] = kv[u] * ia;
+          ke[u] = ka[u] * erv[u];
+        }
+        const uint32_t so = 2 * sw64_chunk(t, cg);
+        *reinterpret_cast<bf16x8*>(smem + S::QA + so) = pack8(qa);
+        *reinterpret_cast<bf16x8*>(smem + S::KA + so) = pack8(ka);
+        *reinterpret_cast<bf16x8*>(smem + S::KD + so) = pack8(kd);
+        *reinterpret_cast<bf16x8*>(smem + S::KE + so) = pack8(ke);
+      }
+      // T = A diag(beta): row k, columns i
+      {
+        const int k = tid >> 3, c8 = tid & 7;
+        float tv[8];
+        const uint4 ax = lds_chunk(smem + S::AT, k, c8);
+        const uint32_t aw[4] = {ax.x, ax.y, ax.z, ax.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 p = unpack_bf16(aw[i]);
+          tv[2 * i] = p.x * beta[8 * c8 + 2 * i];
+          tv[2 * i + 1] = p.y * beta[8 * c8 + 2 * i + 1];
+        }
+        *reinterpret_cast<bf16x8*>(smem + S::TT + 2 * sw64_chunk(k, c8)) = pack8(tv);
+      }
+      // per-pair and per-sub-chunk channel vectors
+      float* cpv = reinterpret_cast<float*>(smem + S::CP);
+      float* ccv = reinterpret_cast<float*>(smem + S::CC);
+      for (int i = tid; i < 6 * D; i += blockDim.x) {
+        const int p = i / D, d = i - p * D;
+        const int I = p >= 3 ? 3 : (p >= 1 ? 2 : 1);
+        const int Jp = p - pair_index(I, 0);
+        cpv[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp) * LDG + d]);
+        ccv[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
+      }
+      {
+        float* erw = reinterpret_cast<float*>(smem + S::ER);
+        float* ecw = reinterpret_cast<float*>(smem + S::EC);
+        float* rvw = reinterpret_cast<float*>(smem + S::REV);
+        const int Jp = tid >> 7, d = tid & 127;
+        const float gr = gam[(16 * Jp) * LDG + d], ge = gam[(16 * Jp + 15) * LDG + d];
+        erw[tid] = ex2(gr);
+        ecw[tid] = ex2(gam[63 * LDG + d] - ge);
+        rvw[tid] = ex2(ge - gr);
+      }
+      // the decay factor of this thread's epilogue elements
+#pragma unroll
+      for (int u = 0; u < 16; ++u) af[u] = ex2(gam[r * LDG + c0 + u] - gam[(16 * s) * LDG + c0 + u]);
     }
+    cp_async_wait<0>();      // dE, dW, dM
+    tc::fence_async_smem();  // operand tiles -> tensor cores; the decay region -> the bulk copy below
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      // dQt and dKbar (acc64) land over the dead decay region while the MMAs run
+      tc::mbar_expect_tx(mb + 1, 2 * S::T128);
+      tc::bulk_g2s(smem + S::DQT, P.dQt + tix * TILE64_ELEMS, S::T128, mb + 1);
+      tc::bulk_g2s(smem + S::DKB, P.dKb + tix * TILE64_ELEMS, S::T128, mb + 1);
+      // G1: dv = T^T dE (unit 0), dKe = T^T dW (unit 1), dT = dE V^T + dW Ke^T (unit 2)
+      for (int hf = 0; hf < 2; ++hf) {
+        const uint32_t lo = (uint32_t)(16 * hf) << 16;
+        for (int ks = 0; ks < 4; ++ks) {
+          tc::mma_bf16(tbase + lo + 0, mdesc(S::TT, ks), mdesc(S::DE + hf * 8192, ks), idMM, ks > 0);
+          tc::mma_bf16(tbase + lo + 64, mdesc(S::TT, ks), mdesc(S::DW + hf * 8192, ks), idMM, ks > 0);
+        }
+      }
+      for (int ks = 0; ks < 8; ++ks) tc::mma_bf16(tbase + 128, kdesc(S::DE, ks), kdesc(S::V, ks), idKK, ks > 0);
+      for (int ks = 0; ks < 8; ++ks) tc::mma_bf16(tbase + 128, kdesc(S::DW, ks), kdesc(S::KE, ks), idKK, true);
+      tc::mma_commit(mb + 2);
+      // G2: row side through M, P_J = dM[:, J] Kd[J] (units 4 + J)
+      for (int J = 0; J < 4; ++J)
+        for (int hf = 0; hf < 2; ++hf)
+          tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * J, kdesc(S::DM, J),
+                       mdesc(S::KD + hf * 8192, J), idKM, false);
+      tc::mma_commit(mb + 3);
+      *issued = 0xFu;
+    }
+
+    // ---- E1: dv out; dq, dk, dGam from dKe and the state-pass tiles; dT -> dbeta, dA
+    ok = tc::mbar_wait(mb + 2, 0) && tc::mbar_wait(mb + 1, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    // the gate logits and the gate backward's vectors, for the tail (dE / dW are dead)
+    {
+      bf16* gre = reinterpret_cast<bf16*>(smem + S::GRE);
+      for (int i = tid; i < 64 * 16; i += blockDim.x) {
+        const int rr = i >> 4, cc = i & 15;
+        const bool okr = rr < nv;
+        cp_async16(gre + rr * D + cc * 8, P.in.g + (okr ? ((size_t)(pos.t0 + rr) * H + h) * D + cc * 8 : 0), okr);
+      }
+      float* gbv = reinterpret_cast<float*>(smem + S::GBV);
+      if (tid < 32)
+        cp_async16(gbv + 4 * tid, P.dGC + cidx * D + 4 * tid, true);
+      else if (tid < 64)
+        cp_async16(gbv + D + 4 * (tid - 32), P.in.dt_bias + (size_t)h * D + 4 * (tid - 32), true);
+      else if (tid == 64)
+        cp_async4(gbv + 2 * D, P.in.A_log + h);
+      cp_async_commit();
+    }
+    {
+      float acc[16];
+      tc::tmem_ld16(trow + 0 + 16 * qd, acc);  // dv
+      if (r < nv) st_global16(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + c0, acc);
+      tc::tmem_ld16(trow + 64 + 16 * qd, acc);  // dKe
+      const bf16* tq = reinterpret_cast<const bf16*>(smem + S::DQT);
+      const bf16* tk = reinterpret_cast<const bf16*>(smem + S::DKB);
+      const float* erp = reinterpret_cast<const float*>(smem + S::ER) + s * D + c0;
+      const float* ecp = reinterpret_cast<const float*>(smem + S::EC) + s * D + c0;
+      const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
+      float* cols = reinterpret_cast<float*>(smem + S::COLS) + s * D + c0;
+#pragma unroll
+      for (int hb = 0; hb < 16; hb += 8) {  // two 8-column chunks
+        float gq[8], gk[8], qa[8], ka[8], kd[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(tq + acc64_off(r, c0 + hb)), gq);
+        unpack8(*reinterpret_cast<const bf16x8*>(tk + acc64_off(r, c0 + hb)), gk);
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::QA + 2 * sw64_chunk(r, (c0 + hb) >> 3)), qa);
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KA + 2 * sw64_chunk(r, (c0 + hb) >> 3)), ka);
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, (c0 + hb) >> 3)), kd);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const int u = hb + v;
+          const float er = erp[u], ec = ecp[u], rv = rvp[u];
+          const float eg = af[u] * er, egc = rv * rcp(af[u]) * ec;
+          const float kbar = kd[v] * rv * ec;
+          dq[u] = gq[v] * eg;
+          dk[u] = acc[u] * eg + gk[v] * egc;
+          dG[u] = ka[v] * er * acc[u] + qa[v] * er * gq[v] - kbar * gk[v];
+          const float cs = half_sum(kbar * gk[v]);  // column sum over the 16 rows of this lane half
+          if ((lane & 15) == 0) cols[u] = cs;
+        }
+      }
+      // dT (64 x 64, lanes 0-15): dbeta_T[j] = sum_i dT_ij A_ij, dA = dT diag(beta)
+      tc::tmem_ld16(trow + 128 + 16 * qd, acc);
+      float av[16], cs[16];
+      lds_row16(smem + S::AT, r, 16 * qd, av);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) cs[u] = half_sum(hh == 0 ? acc[u] * av[u] : 0.f);
+      if (lane == 0) {
+        float* dbt = reinterpret_cast<float*>(smem + S::DBT) + s * 64 + 16 * qd;
+#pragma unroll
+        for (int u = 0; u < 16; u += 4)
+          *reinterpret_cast<float4*>(dbt + u) = make_float4(cs[u], cs[u + 1], cs[u + 2], cs[u + 3]);
+      }
+      if (hh == 0) {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc[u] *= beta[16 * qd + u];
+        sts_row16(smem + S::DA, r, 16 * qd, acc);
+      }
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G3: X = dA A^T (unit 3)
+      tc::fence_after_sync();
+      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 192, kdesc(S::DA, ks), kdesc(S::AT, ks), idKK, ks > 0);
+      tc::mma_commit(mb + 4);
+      *issued = 0x1Fu;
+    }
+
+    // ---- E2: row side through M: dq += af (P_I + sum_J<I c'_IJ P_J), dGam += Qa o (...)
+    ok = tc::mbar_wait(mb + 3, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    {
+      float out[16], pj[16], cp[16], qa[16];
+      tc::tmem_ld16(trow + 256 + 64 * s + 16 * qd, out);
+      for (int J = 0; J < s; ++J) {
+        tc::tmem_ld16(trow + 256 + 64 * J + 16 * qd, pj);
+        ld_vec16(reinterpret_cast<const float*>(smem + S::CP) + pair_index(s, J) * D + c0, cp);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) out[u] = fmaf(cp[u], pj[u], out[u]);
+      }
+      lds_row16(smem + S::QA, r, c0, qa);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        dq[u] = fmaf(af[u], out[u], dq[u]);
+        dG[u] = fmaf(qa[u], out[u], dG[u]);
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G4: column side through M, R_I = dM[I, :]^T Qa[I] (units 4 + I)
+      tc::fence_after_sync();
+      for (int I = 0; I < 4; ++I)
+        for (int hf = 0; hf < 2; ++hf)
+          tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DM, I),
+                       mdesc(S::QA + hf * 8192, I), idMM, false);
+      tc::mma_commit(mb + 5);
+      *issued = 0x3Fu;
+    }
+
+    // ---- E3: X -> bf16 tile
+    ok = tc::mbar_wait(mb + 4, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    {
+      float acc[16];
+      tc::tmem_ld16(trow + 192 + 16 * qd, acc);
+      if (hh == 0) sts_row16(smem + S::XS, r, 16 * qd, acc);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G5: -dL = A^T X (unit 0)
+      tc::fence_after_sync();
+      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 0, mdesc(S::AT, ks), mdesc(S::XS, ks), idMM, ks > 0);
+      tc::mma_commit(mb + 6);
+      *issued = 0x7Fu;
+    }
+
+    // ---- E4: dL = -(A^T X), strictly lower: dbeta_L = rowsum(dL o L'), dL' = diag(beta) dL
+    ok = tc::mbar_wait(mb + 6, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    {
+      float acc[16], lp[16];
+      tc::tmem_ld16(trow + 0 + 16 * qd, acc);
+      lds_row16(smem + S::LPT, r, 16 * qd, lp);
+      float rs = 0.f;
+      const float br = beta[r];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const float x = (16 * qd + u < r) ? -acc[u] : 0.f;
+        rs = fmaf(x, lp[u], rs);
+        acc[u] = x * br;
+      }
+      if (hh == 0) {
+        reinterpret_cast<float*>(smem + S::DBL)[qd * 64 + r] = rs;
+        sts_row16(smem + S::DLP, r, 16 * qd, acc);
+      }
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G6: row side through L', P_J = dL'[:, J] Kd[J] (units J)
+      tc::fence_after_sync();
+      for (int J = 0; J < 4; ++J)
+        for (int hf = 0; hf < 2; ++hf)
+          tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 64 * J, kdesc(S::DLP, J), mdesc(S::KD + hf * 8192, J),
+                       idKM, false);
+      tc::mma_commit(mb + 7);
+      *issued = 0xFFu;
+    }
+
+    // ---- E5 / E7: column sides (M, then L') into dk and dGam
+    // tot = R_I + rev_I sum_{Ib > I} c_{Ib,I} R_Ib; then dk += tot / af (the
+    // diagonal's 1/af and the off-diagonal bf = rev_I / af at once), dGam -= Kd o tot
+    auto column_side = [&](uint32_t unit0) {
+      float tot[16], R[16], cc[16];
+      tc::tmem_ld16(trow + unit0 + 64 * s + 16 * qd, tot);  // diagonal block: R_I
+      const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
+      for (int Ib = s + 1; Ib < 4; ++Ib) {
+        tc::tmem_ld16(trow + unit0 + 64 * Ib + 16 * qd, R);
+        ld_vec16(reinterpret_cast<const float*>(smem + S::CC) + pair_index(Ib, s) * D + c0, cc);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) tot[u] = fmaf(rvp[u] * cc[u], R[u], tot[u]);
+      }
+      float kd[16];
+      lds_row16(smem + S::KD, r, c0, kd);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        dk[u] = fmaf(rcp(af[u]), tot[u], dk[u]);
+        dG[u] = fmaf(-kd[u], tot[u], dG[u]);
+      }
+    };
+    ok = tc::mbar_wait(mb + 5, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    column_side(256);
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G7: column side through L', R_I = dL'[I, :]^T Ka[I] (units 4 + I)
+      tc::fence_after_sync();
+      for (int I = 0; I < 4; ++I)
+        for (int hf = 0; hf < 2; ++hf)
+          tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DLP, I),
+                       mdesc(S::KA + hf * 8192, I), idMM, false);
+      tc::mma_commit(mb + 8);
+      *issued = 0x1FFu;
+    }
+
+    // ---- E6: row side through L': dk += af (...), dGam += Ka o (...)
+    ok = tc::mbar_wait(mb + 7, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    {
+      float out[16], pj[16], cp[16], ka[16];
+      tc::tmem_ld16(trow + 64 * s + 16 * qd, out);
+      for (int J = 0; J < s; ++J) {
+        tc::tmem_ld16(trow + 64 * J + 16 * qd, pj);
+        ld_vec16(reinterpret_cast<const float*>(smem + S::CP) + pair_index(s, J) * D + c0, cp);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) out[u] = fmaf(cp[u], pj[u], out[u]);
+      }
+      lds_row16(smem + S::KA, r, c0, ka);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        dk[u] = fmaf(af[u], out[u], dk[u]);
+        dG[u] = fmaf(ka[u], out[u], dG[u]);
+      }
+    }
+    ok = tc::mbar_wait(mb + 8, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    column_side(256);
   }
-  // ---- outputs ---------------------------------------------------------------
-#pragma unroll
-  for (int e = 0; e < 4; e += 2) {
-    uint32_t wq[4], wk[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      wq[j] = pack_bf16(dq[j][e], dq[j][e + 1]);
-      wk[j] = pack_bf16(dk[j][e], dk[j][e + 1]);
-    }
-    quad_transpose4(wq);
-    quad_transpose4(wk);
-    const int r = m0 + acc_row(e);
-    if (r < nv) {
-      const size_t off = ((size_t)(pos.t0 + r) * H + h) * D + n0 + 8 * (tid & 3);
-      *reinterpret_cast<uint4*>(P.dq_hat + off) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
-      *reinterpret_cast<uint4*>(P.dk_hat + off) = make_uint4(wk[0], wk[1], wk[2], wk[3]);
-    }
+
+  if (!ok) {
+    // let what is in flight finish (bounded), then release TMEM and leave
+    const uint32_t iss = *issued;
+    for (int i = 0; i < 9; ++i)
+      if (iss & (1u << i)) tc::mbar_wait(mb + i, 0, 1u << 22);
+    cp_async_wait<0>();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tbase, 512);
+    return;
   }
-  const float* cols = reinterpret_cast<const float*>(smem + BwdIntraSmem::COLS);
-  float* dGs = ps.gam;  // Gam is dead: every decay factor is in registers
+
+  // ---- outputs: dq_hat, dk_hat; dGam -> shared memory for the gate tail
+  if (r < nv) {
+    const size_t off = ((size_t)(pos.t0 + r) * H + h) * D + c0;
+    st_global16(P.dq_hat + off, dq);
+    st_global16(P.dk_hat + off, dk);
+  }
+  float* dGs = gam;  // the dQt / dKbar tiles there are dead
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      int r = m0 + acc_row(e), cc = n0 + acc_col(j, e);
-      *reinterpret_cast<float2*>(dGs + r * LDG + cc) = make_float2(dG[j][e], dG[j][e + 1]);
-    }
+  for (int u = 0; u < 16; u += 4)
+    *reinterpret_cast<float4*>(dGs + r * LDG + c0 + u) = make_float4(dG[u], dG[u + 1], dG[u + 2], dG[u + 3]);
+  cp_async_wait<0>();  // gate logits and vectors
   __syncthreads();
   // reverse cumsum over the chunk and the gate backward: thread (part, col)
   // with col = tid % 128 owns rows 16*part .. 16*part+15 of one channel
   {
+    const float* gbv = reinterpret_cast<const float*>(smem + S::GBV);
+    const float* cols = reinterpret_cast<const float*>(smem + S::COLS);
+    const bf16* gre = reinterpret_cast<const bf16*>(smem + S::GRE);
+    float* partsum = reinterpret_cast<float*>(smem + S::PSUM);
     const int col = tid & 127, part = tid >> 7;
     float own = 0.f;
 #pragma unroll 4
-    for (int r = 16 * part; r < 16 * part + 16; ++r) own += dGs[r * LDG + col];
-    float* partsum = reinterpret_cast<float*>(smem + BwdIntraSmem::DAS);  // 4 x 128 fp32 (dA is dead)
+    for (int rr = 16 * part; rr < 16 * part + 16; ++rr) own += dGs[rr * LDG + col];
     partsum[part * D + col] = own;
     __syncthreads();
     float run = gbv[col] + cols[col] + cols[D + col] + cols[2 * D + col] + cols[3 * D + col];
@@ -572,15 +619,15 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     const float eA = __expf(gbv[2 * D]);
     const float bias = gbv[D + col];
     float sA = 0.f, sB = 0.f;
-    for (int r = 16 * part + 15; r >= 16 * part; --r) {
-      run += dGs[r * LDG + col];
-      if (r < nv) {
-        size_t off = ((size_t)(pos.t0 + r) * H + h) * D + col;
-        float x = __bfloat162float(gre[r * D + col]) + bias;
-        float z = eA * x;
-        float sg = sigmoidf_(z);
-        float dz = run * P.in.lower_bound * sg * (1.f - sg);
-        float dx = dz * eA;
+    for (int rr = 16 * part + 15; rr >= 16 * part; --rr) {
+      run += dGs[rr * LDG + col];
+      if (rr < nv) {
+        const size_t off = ((size_t)(pos.t0 + rr) * H + h) * D + col;
+        const float x = __bfloat162float(gre[rr * D + col]) + bias;
+        const float z = eA * x;
+        const float sg = sigmoidf_(z);
+        const float dz = run * P.in.lower_bound * sg * (1.f - sg);
+        const float dx = dz * eA;
         P.dg[off] = __float2bfloat16(dx);
         sA += dz * z;
         sB += dx;
@@ -597,14 +644,14 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     }
   }
   if (tid < 64) {
-    int r = tid;
-    if (r < nv) {
-      const float* dbt = reinterpret_cast<const float*>(smem + BwdIntraSmem::DBT);
-      const float* dbl = reinterpret_cast<const float*>(smem + BwdIntraSmem::DBL);
-      float db = dbt[r] + dbt[64 + r] + dbt[128 + r] + dbt[192 + r] + dbl[r] + dbl[64 + r] + dbl[128 + r] +
-                 dbl[192 + r];
-      float bt = ps.beta[r];
-      P.dbeta[(size_t)(pos.t0 + r) * H + h] = __float2bfloat16(db * bt * (1.f - bt));
+    const int rr = tid;
+    if (rr < nv) {
+      const float* dbt = reinterpret_cast<const float*>(smem + S::DBT);
+      const float* dbl = reinterpret_cast<const float*>(smem + S::DBL);
+      const float db = dbt[rr] + dbt[64 + rr] + dbt[128 + rr] + dbt[192 + rr] + dbl[rr] + dbl[64 + rr] +
+                       dbl[128 + rr] + dbl[192 + rr];
+      const float bt = beta[rr];
+      P.dbeta[(size_t)(pos.t0 + rr) * H + h] = __float2bfloat16(db * bt * (1.f - bt));
     }
   }
 }

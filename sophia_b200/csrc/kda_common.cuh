@@ -354,6 +354,14 @@ __device__ __forceinline__ void st128_chunk(int idx, int& row, int& cc) {
   cc = hf * 8 + c;
 }
 
+// Element offset of 16-byte chunk c8 (columns 8*c8 .. 8*c8+7) of row r in a
+// 128B-swizzled bf16 tile of 64 rows: 64-column atoms of 64 x 128 bytes one
+// after the other, chunk position c8 ^ (r & 7) inside a row (the tcgen05
+// operand layout of kda_tc.cuh).
+__host__ __device__ __forceinline__ uint32_t sw64_chunk(int r, int c8) {
+  return (uint32_t)((c8 >> 3) * 4096 + r * 64 + (((c8 & 7) ^ (r & 7)) << 3));
+}
+
 struct alignas(16) bf16x8 { uint32_t u[4]; };
 
 __device__ __forceinline__ void unpack8(const bf16x8& v, float (&f)[8]) {

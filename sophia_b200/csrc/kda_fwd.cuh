@@ -21,7 +21,8 @@ struct FwdIntraParams {
   bool conv;
   bf16 *W, *U, *Qt, *Kb, *M;  // [T_total][H][128] (M: [T_total][H][64])
   float* dC;                  // [chunks][H][128]
-  float* A;                   // [slots x H] fp32 [64][LDF64] tiles of A (the backward's copy), or null
+  bf16* A;                    // [slots x H] 64x64 bf16 tiles of A = (I + diag(beta) L')^-1 (swizzled), or null
+  bf16* LP;                   // [slots x H] 64x64 bf16 tiles of L' (swizzled), with A
   bf16 *QN, *KN, *VN;         // [slots x H] prologue products for the backward, or null
   float *GM, *BT;
   int grid_chunks;            // chunk slots per head: items are (slot, head), slot fastest
@@ -138,9 +139,10 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
 #pragma unroll
       for (int r = 0; r < STRIP; ++r) {
         const int t = STRIP * tg + r;
-        *reinterpret_cast<bf16x8*>(tq + t * D + 8 * cg) = pack8(s.q[r]);
-        *reinterpret_cast<bf16x8*>(tq + TILE64_ELEMS + t * D + 8 * cg) = pack8(s.k[r]);
-        *reinterpret_cast<bf16x8*>(tq + 2 * TILE64_ELEMS + t * D + 8 * cg) = pack8(s.v[r]);
+        const uint32_t so = sw64_chunk(t, cg);  // the backward's tcgen05 operand layout
+        *reinterpret_cast<bf16x8*>(tq + so) = pack8(s.q[r]);
+        *reinterpret_cast<bf16x8*>(tq + TILE64_ELEMS + so) = pack8(s.k[r]);
+        *reinterpret_cast<bf16x8*>(tq + 2 * TILE64_ELEMS + so) = pack8(s.v[r]);
       }
       tc::fence_async_smem();
       __syncthreads();
@@ -219,13 +221,32 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
       *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
     }
+    // A and L' for the backward, as bf16 tiles in its tcgen05 operand layout
+    // (zeros above the diagonal), over the dead Qa and Kd operand tiles
+    bf16* Asw = op.Qa;
+    bf16* Lsw = op.Kd;
+    if (P.A) {
+      for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+        const int r = i >> 3, c8 = i & 7;
+        float av[8], lv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int cc = 8 * c8 + u;
+          av[u] = cc <= r ? Ainv[r * LDF64 + cc] : 0.f;
+          lv[u] = cc < r ? Lp[r * LDF64 + cc] : 0.f;
+        }
+        *reinterpret_cast<bf16x8*>(Asw + sw64_chunk(r, c8)) = pack8(av);
+        *reinterpret_cast<bf16x8*>(Lsw + sw64_chunk(r, c8)) = pack8(lv);
+      }
+    }
     store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
-    tc::fence_async_smem();  // A (written by every thread) is read by the bulk store below
+    tc::fence_async_smem();  // A and L' (written by every thread) are read by the bulk stores below
     __syncthreads();
-    // A for the backward, as it sits in shared memory (entries above the
-    // diagonal are not meaningful): one bulk store, completed before the exit
+    // one bulk store each, completed before the exit
     if (P.A && threadIdx.x == 0) {
-      tc::bulk_s2g(P.A + tile_index(P.seq, c, h) * A_TILE_ELEMS, Ainv, A_TILE_ELEMS * 4);
+      const size_t tix = tile_index(P.seq, c, h);
+      tc::bulk_s2g(P.A + tix * TILE64N64_ELEMS, Asw, TILE64N64_ELEMS * 2);
+      tc::bulk_s2g(P.LP + tix * TILE64N64_ELEMS, Lsw, TILE64N64_ELEMS * 2);
       tc::bulk_commit();
     }
 

@@ -47,10 +47,10 @@ def test_version_and_sizes(lib):
     tt, H, N = 8 * 4096, 16, 8
     saved = lib.kda_b200_saved_bytes(tt, H, N, 0)
     # W, U, Qt, Kb (bf16 token rows x128), M (x64); per chunk slot: v_new (64x128 tile),
-    # the chunk-start state, the decays, A (fp32 64x65) and the prologue products
-    # (q, k, v bf16 64x128, the decay cumsum fp32 64x132, beta)
+    # the chunk-start state, the decays, A and L' (bf16 64x64 each) and the prologue
+    # products (q, k, v bf16 64x128, the decay cumsum fp32 64x132, beta)
     mc = tt // 64 + N
-    lower = tt * H * (4 * 128 + 64) * 2 + mc * H * (64 * 128 * 2 + 128 * 128 * 2 + 128 * 4 + 64 * 65 * 4 +
+    lower = tt * H * (4 * 128 + 64) * 2 + mc * H * (64 * 128 * 2 + 128 * 128 * 2 + 128 * 4 + 2 * 64 * 64 * 2 +
                                                     3 * 64 * 128 * 2 + 64 * 132 * 4 + 64 * 4)
     assert lower <= saved <= lower + 64 * 256
     assert lib.kda_b200_fwd_workspace_bytes(tt, H, N, 0, 1) < lib.kda_b200_fwd_workspace_bytes(tt, H, N, 0, 0)
