@@ -330,6 +330,7 @@ def bench_ours(a, rank, world, local_rank):
                 if i >= 2:
                     copy_stream.wait_event(freed[b])  # step i-2 is done with this buffer
                 for k in host:
+                    bufs[b][k].requires_grad_(False)
                     bufs[b][k].copy_(host[k], non_blocking=True)
                 copied[b].record(copy_stream)
 
@@ -340,10 +341,7 @@ def bench_ours(a, rank, world, local_rank):
         def micro_inputs(_mb):
             i = state["i"]
             if i > 0:  # the previous micro-batch's buffer is free once its kernels ran
-                pb = (i - 1) % 2
-                for k in ("q", "k", "v", "g", "beta"):
-                    bufs[pb][k].requires_grad_(False)
-                freed[pb].record(st)
+                freed[(i - 1) % 2].record(st)
             if i + 1 < total:
                 issue_copy(i + 1)
             b = i % 2
