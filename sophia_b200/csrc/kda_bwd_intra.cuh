@@ -313,7 +313,14 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       }
       // the decay factor of this thread's epilogue elements
 #pragma unroll
-      for (int u = 0; u < 16; ++u) af[u] = ex2(gam[r * LDG + c0 + u] - gam[(16 * s) * LDG + c0 + u]);
+      for (int u = 0; u < 16; u += 4) {
+        const float4 g = *reinterpret_cast<const float4*>(gam + r * LDG + c0 + u);
+        const float4 g0 = *reinterpret_cast<const float4*>(gam + (16 * s) * LDG + c0 + u);
+        af[u] = ex2(g.x - g0.x);
+        af[u + 1] = ex2(g.y - g0.y);
+        af[u + 2] = ex2(g.z - g0.z);
+        af[u + 3] = ex2(g.w - g0.w);
+      }
     }
     cp_async_wait<0>();      // dE, dW, dM
     tc::fence_async_smem();  // operand tiles -> tensor cores; the decay region -> the bulk copy below
@@ -367,10 +374,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       cp_async_commit();
     }
     {
-      float acc[16];
-      tc::tmem_ld16(trow + 0 + 16 * qd, acc);  // dv
-      if (r < nv) st_global16(P.dv + ((size_t)(pos.t0 + r) * H + h) * D + c0, acc);
-      tc::tmem_ld16(trow + 64 + 16 * qd, acc);  // dKe
+      bf16* dvrow = P.dv + ((size_t)(pos.t0 + r) * H + h) * D + c0;
       const bf16* tq = reinterpret_cast<const bf16*>(smem + S::DQT);
       const bf16* tk = reinterpret_cast<const bf16*>(smem + S::DKB);
       const float* erp = reinterpret_cast<const float*>(smem + S::ER) + s * D + c0;
@@ -378,13 +382,18 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
       float* cols = reinterpret_cast<float*>(smem + S::COLS) + s * D + c0;
 #pragma unroll
-      for (int hb = 0; hb < 16; hb += 8) {  // two 8-column chunks
+      for (int hb = 0; hb < 16; hb += 8) {  // two 8-column passes
+        float acc[8];
+        tc::tmem_ld8(trow + 0 + 16 * qd + hb, acc);  // dv
+        if (r < nv) *reinterpret_cast<bf16x8*>(dvrow + hb) = pack8(acc);
+        tc::tmem_ld8(trow + 64 + 16 * qd + hb, acc);  // dKe
         float gq[8], gk[8], qa[8], ka[8], kd[8];
+        const int c8 = (c0 + hb) >> 3;
         unpack8(*reinterpret_cast<const bf16x8*>(tq + acc64_off(r, c0 + hb)), gq);
         unpack8(*reinterpret_cast<const bf16x8*>(tk + acc64_off(r, c0 + hb)), gk);
-        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::QA + 2 * sw64_chunk(r, (c0 + hb) >> 3)), qa);
-        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KA + 2 * sw64_chunk(r, (c0 + hb) >> 3)), ka);
-        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, (c0 + hb) >> 3)), kd);
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::QA + 2 * sw64_chunk(r, c8)), qa);
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KA + 2 * sw64_chunk(r, c8)), ka);
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, c8)), kd);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const int u = hb + v;
@@ -392,28 +401,27 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           const float eg = af[u] * er, egc = rv * rcp(af[u]) * ec;
           const float kbar = kd[v] * rv * ec;
           dq[u] = gq[v] * eg;
-          dk[u] = acc[u] * eg + gk[v] * egc;
-          dG[u] = ka[v] * er * acc[u] + qa[v] * er * gq[v] - kbar * gk[v];
+          dk[u] = acc[v] * eg + gk[v] * egc;
+          dG[u] = ka[v] * er * acc[v] + qa[v] * er * gq[v] - kbar * gk[v];
           const float cs = half_sum(kbar * gk[v]);  // column sum over the 16 rows of this lane half
           if ((lane & 15) == 0) cols[u] = cs;
         }
       }
       // dT (64 x 64, lanes 0-15): dbeta_T[j] = sum_i dT_ij A_ij, dA = dT diag(beta)
-      tc::tmem_ld16(trow + 128 + 16 * qd, acc);
-      float av[16], cs[16];
-      lds_row16(smem + S::AT, r, 16 * qd, av);
 #pragma unroll
-      for (int u = 0; u < 16; ++u) cs[u] = half_sum(hh == 0 ? acc[u] * av[u] : 0.f);
-      if (lane == 0) {
-        float* dbt = reinterpret_cast<float*>(smem + S::DBT) + s * 64 + 16 * qd;
+      for (int hb = 0; hb < 16; hb += 8) {
+        float acc[8], av[8];
+        tc::tmem_ld8(trow + 128 + 16 * qd + hb, acc);
+        const int c8 = (16 * qd + hb) >> 3;
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::AT + 2 * sw64_chunk(r, c8)), av);
+        float* dbt = reinterpret_cast<float*>(smem + S::DBT) + s * 64 + 16 * qd + hb;
 #pragma unroll
-        for (int u = 0; u < 16; u += 4)
-          *reinterpret_cast<float4*>(dbt + u) = make_float4(cs[u], cs[u + 1], cs[u + 2], cs[u + 3]);
-      }
-      if (hh == 0) {
-#pragma unroll
-        for (int u = 0; u < 16; ++u) acc[u] *= beta[16 * qd + u];
-        sts_row16(smem + S::DA, r, 16 * qd, acc);
+        for (int v = 0; v < 8; ++v) {
+          const float cs = half_sum(hh == 0 ? acc[v] * av[v] : 0.f);
+          if (lane == 0) dbt[v] = cs;
+          acc[v] *= beta[16 * qd + hb + v];
+        }
+        if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DA + 2 * sw64_chunk(r, c8)) = pack8(acc);
       }
     }
     tc::fence_async_smem();
@@ -426,26 +434,56 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       *issued = 0x1Fu;
     }
 
-    // ---- E2: row side through M: dq += af (P_I + sum_J<I c'_IJ P_J), dGam += Qa o (...)
+    // row sides: dX += af (P_I + sum_J<I c'_IJ P_J), dGam += rowop o (...)
+    auto row_side = [&](uint32_t unit0, int rowop, float (&dx)[16]) {
+      const float* cpb = reinterpret_cast<const float*>(smem + S::CP) + c0;
+#pragma unroll
+      for (int hb = 0; hb < 16; hb += 8) {
+        float out[8], pj[8], ro[8];
+        tc::tmem_ld8(trow + unit0 + 64 * s + 16 * qd + hb, out);
+        for (int J = 0; J < s; ++J) {
+          tc::tmem_ld8(trow + unit0 + 64 * J + 16 * qd + hb, pj);
+          const float* cp = cpb + pair_index(s, J) * D + hb;
+#pragma unroll
+          for (int v = 0; v < 8; ++v) out[v] = fmaf(cp[v], pj[v], out[v]);
+        }
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + rowop + 2 * sw64_chunk(r, (c0 + hb) >> 3)), ro);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          dx[hb + v] = fmaf(af[hb + v], out[v], dx[hb + v]);
+          dG[hb + v] = fmaf(ro[v], out[v], dG[hb + v]);
+        }
+      }
+    };
+    // column sides: tot = R_I + rev_I sum_{Ib > I} c_{Ib,I} R_Ib; then dk += tot / af
+    // (the diagonal's 1/af and the off-diagonal bf = rev_I / af at once), dGam -= Kd o tot
+    auto column_side = [&](uint32_t unit0) {
+      const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
+      const float* ccb = reinterpret_cast<const float*>(smem + S::CC) + c0;
+#pragma unroll
+      for (int hb = 0; hb < 16; hb += 8) {
+        float tot[8], R[8], kd[8];
+        tc::tmem_ld8(trow + unit0 + 64 * s + 16 * qd + hb, tot);  // diagonal block: R_I
+        for (int Ib = s + 1; Ib < 4; ++Ib) {
+          tc::tmem_ld8(trow + unit0 + 64 * Ib + 16 * qd + hb, R);
+          const float* cc = ccb + pair_index(Ib, s) * D + hb;
+#pragma unroll
+          for (int v = 0; v < 8; ++v) tot[v] = fmaf(rvp[hb + v] * cc[v], R[v], tot[v]);
+        }
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, (c0 + hb) >> 3)), kd);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          dk[hb + v] = fmaf(rcp(af[hb + v]), tot[v], dk[hb + v]);
+          dG[hb + v] = fmaf(-kd[v], tot[v], dG[hb + v]);
+        }
+      }
+    };
+
+    // ---- E2: row side through M
     ok = tc::mbar_wait(mb + 3, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();
-    {
-      float out[16], pj[16], cp[16], qa[16];
-      tc::tmem_ld16(trow + 256 + 64 * s + 16 * qd, out);
-      for (int J = 0; J < s; ++J) {
-        tc::tmem_ld16(trow + 256 + 64 * J + 16 * qd, pj);
-        ld_vec16(reinterpret_cast<const float*>(smem + S::CP) + pair_index(s, J) * D + c0, cp);
-#pragma unroll
-        for (int u = 0; u < 16; ++u) out[u] = fmaf(cp[u], pj[u], out[u]);
-      }
-      lds_row16(smem + S::QA, r, c0, qa);
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        dq[u] = fmaf(af[u], out[u], dq[u]);
-        dG[u] = fmaf(qa[u], out[u], dG[u]);
-      }
-    }
+    row_side(256, S::QA, dq);
     tc::fence_before_sync();
     __syncthreads();
     if (tid == 0) {  // G4: column side through M, R_I = dM[I, :]^T Qa[I] (units 4 + I)
@@ -462,10 +500,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     ok = tc::mbar_wait(mb + 4, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();
-    {
-      float acc[16];
-      tc::tmem_ld16(trow + 192 + 16 * qd, acc);
-      if (hh == 0) sts_row16(smem + S::XS, r, 16 * qd, acc);
+#pragma unroll
+    for (int hb = 0; hb < 16; hb += 8) {
+      float acc[8];
+      tc::tmem_ld8(trow + 192 + 16 * qd + hb, acc);
+      if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::XS + 2 * sw64_chunk(r, (16 * qd + hb) >> 3)) = pack8(acc);
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
@@ -477,69 +516,47 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       *issued = 0x7Fu;
     }
 
+    // ---- E5: column side through M (runs while G5 computes)
+    ok = tc::mbar_wait(mb + 5, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    tc::fence_after_sync();
+    column_side(256);
+
     // ---- E4: dL = -(A^T X), strictly lower: dbeta_L = rowsum(dL o L'), dL' = diag(beta) dL
     ok = tc::mbar_wait(mb + 6, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();
     {
-      float acc[16], lp[16];
-      tc::tmem_ld16(trow + 0 + 16 * qd, acc);
-      lds_row16(smem + S::LPT, r, 16 * qd, lp);
       float rs = 0.f;
       const float br = beta[r];
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const float x = (16 * qd + u < r) ? -acc[u] : 0.f;
-        rs = fmaf(x, lp[u], rs);
-        acc[u] = x * br;
+      for (int hb = 0; hb < 16; hb += 8) {
+        float acc[8], lp[8];
+        tc::tmem_ld8(trow + 0 + 16 * qd + hb, acc);
+        const int c8 = (16 * qd + hb) >> 3;
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::LPT + 2 * sw64_chunk(r, c8)), lp);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float x = (16 * qd + hb + v < r) ? -acc[v] : 0.f;
+          rs = fmaf(x, lp[v], rs);
+          acc[v] = x * br;
+        }
+        if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DLP + 2 * sw64_chunk(r, c8)) = pack8(acc);
       }
-      if (hh == 0) {
-        reinterpret_cast<float*>(smem + S::DBL)[qd * 64 + r] = rs;
-        sts_row16(smem + S::DLP, r, 16 * qd, acc);
-      }
+      if (hh == 0) reinterpret_cast<float*>(smem + S::DBL)[qd * 64 + r] = rs;
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {  // G6: row side through L', P_J = dL'[:, J] Kd[J] (units J)
+    if (tid == 0) {
       tc::fence_after_sync();
+      // G6: row side through L', P_J = dL'[:, J] Kd[J] (units J)
       for (int J = 0; J < 4; ++J)
         for (int hf = 0; hf < 2; ++hf)
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 64 * J, kdesc(S::DLP, J), mdesc(S::KD + hf * 8192, J),
                        idKM, false);
       tc::mma_commit(mb + 7);
-      *issued = 0xFFu;
-    }
-
-    // ---- E5 / E7: column sides (M, then L') into dk and dGam
-    // tot = R_I + rev_I sum_{Ib > I} c_{Ib,I} R_Ib; then dk += tot / af (the
-    // diagonal's 1/af and the off-diagonal bf = rev_I / af at once), dGam -= Kd o tot
-    auto column_side = [&](uint32_t unit0) {
-      float tot[16], R[16], cc[16];
-      tc::tmem_ld16(trow + unit0 + 64 * s + 16 * qd, tot);  // diagonal block: R_I
-      const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
-      for (int Ib = s + 1; Ib < 4; ++Ib) {
-        tc::tmem_ld16(trow + unit0 + 64 * Ib + 16 * qd, R);
-        ld_vec16(reinterpret_cast<const float*>(smem + S::CC) + pair_index(Ib, s) * D + c0, cc);
-#pragma unroll
-        for (int u = 0; u < 16; ++u) tot[u] = fmaf(rvp[u] * cc[u], R[u], tot[u]);
-      }
-      float kd[16];
-      lds_row16(smem + S::KD, r, c0, kd);
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        dk[u] = fmaf(rcp(af[u]), tot[u], dk[u]);
-        dG[u] = fmaf(-kd[u], tot[u], dG[u]);
-      }
-    };
-    ok = tc::mbar_wait(mb + 5, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
-    tc::fence_after_sync();
-    column_side(256);
-    tc::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {  // G7: column side through L', R_I = dL'[I, :]^T Ka[I] (units 4 + I)
-      tc::fence_after_sync();
+      // G7: column side through L', R_I = dL'[I, :]^T Ka[I] (units 4 + I)
       for (int I = 0; I < 4; ++I)
         for (int hf = 0; hf < 2; ++hf)
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DLP, I),
@@ -548,26 +565,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       *issued = 0x1FFu;
     }
 
-    // ---- E6: row side through L': dk += af (...), dGam += Ka o (...)
+    // ---- E6: row side through L'; E7: column side through L'
     ok = tc::mbar_wait(mb + 7, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();
-    {
-      float out[16], pj[16], cp[16], ka[16];
-      tc::tmem_ld16(trow + 64 * s + 16 * qd, out);
-      for (int J = 0; J < s; ++J) {
-        tc::tmem_ld16(trow + 64 * J + 16 * qd, pj);
-        ld_vec16(reinterpret_cast<const float*>(smem + S::CP) + pair_index(s, J) * D + c0, cp);
-#pragma unroll
-        for (int u = 0; u < 16; ++u) out[u] = fmaf(cp[u], pj[u], out[u]);
-      }
-      lds_row16(smem + S::KA, r, c0, ka);
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        dk[u] = fmaf(af[u], out[u], dk[u]);
-        dG[u] = fmaf(ka[u], out[u], dG[u]);
-      }
-    }
+    row_side(0, S::KA, dk);
     ok = tc::mbar_wait(mb + 8, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();

@@ -67,18 +67,11 @@ def _empty(like: Tensor, dtype=torch.float32) -> Tensor:
     return like.new_empty((0,), dtype=dtype)
 
 
-def _opt(t: Tensor) -> Tensor | None:
-    return None if t.numel() == 0 else t
-
-
 # --------------------------------------------------------------------------- layer
 
 
-@torch.library.custom_op("sophia_b200::kda_fwd", mutates_args=(), device_types="cuda")
-def _kda_fwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
-             conv_q: Optional[Tensor], conv_k: Optional[Tensor], conv_v: Optional[Tensor],
-             h0: Optional[Tensor], cu_seqlens: Optional[Tensor], scale: float, lower_bound: float,
-             output_final_state: bool, training: bool) -> tuple[Tensor, Tensor, Tensor]:
+def _kda_fwd_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, scale, lower_bound,
+                  output_final_state, training):
     """Returns (o in the compute dtype, final state or empty, saved buffer or empty)."""
     with torch.autocast("cuda", enabled=False):
         lib = _lib.load()
@@ -111,6 +104,15 @@ def _kda_fwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Te
         return o, ht, saved
 
 
+@torch.library.custom_op("sophia_b200::kda_fwd", mutates_args=(), device_types="cuda")
+def _kda_fwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
+             conv_q: Optional[Tensor], conv_k: Optional[Tensor], conv_v: Optional[Tensor],
+             h0: Optional[Tensor], cu_seqlens: Optional[Tensor], scale: float, lower_bound: float,
+             output_final_state: bool, training: bool) -> tuple[Tensor, Tensor, Tensor]:
+    return _kda_fwd_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, scale,
+                         lower_bound, output_final_state, training)
+
+
 @_kda_fwd.register_fake
 def _(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, scale, lower_bound,
       output_final_state, training):
@@ -123,12 +125,8 @@ def _(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, 
     return o, ht, q.new_empty((nbytes,), dtype=torch.uint8)
 
 
-@torch.library.custom_op("sophia_b200::kda_bwd", mutates_args=(), device_types="cuda")
-def _kda_bwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
-             conv_q: Optional[Tensor], conv_k: Optional[Tensor], conv_v: Optional[Tensor],
-             h0: Optional[Tensor], cu_seqlens: Optional[Tensor], saved: Tensor, do: Tensor,
-             dht: Optional[Tensor], scale: float, lower_bound: float, want_dh0: bool
-             ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+def _kda_bwd_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, saved, do, dht, scale,
+                  lower_bound, want_dh0):
     """Returns (dq, dk, dv, dg, dbeta, dA_log, ddt_bias, dconv_q, dconv_k, dconv_v, dh0); absent ones empty."""
     with torch.autocast("cuda", enabled=False):
         lib = _lib.load()
@@ -166,6 +164,16 @@ def _kda_bwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Te
         return dq, dk, dv, dg, dbeta, dA, ddt, dconvs[0], dconvs[1], dconvs[2], dh0
 
 
+@torch.library.custom_op("sophia_b200::kda_bwd", mutates_args=(), device_types="cuda")
+def _kda_bwd(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
+             conv_q: Optional[Tensor], conv_k: Optional[Tensor], conv_v: Optional[Tensor],
+             h0: Optional[Tensor], cu_seqlens: Optional[Tensor], saved: Tensor, do: Tensor,
+             dht: Optional[Tensor], scale: float, lower_bound: float, want_dh0: bool
+             ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    return _kda_bwd_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, saved, do, dht,
+                         scale, lower_bound, want_dh0)
+
+
 @_kda_bwd.register_fake
 def _(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, saved, do, dht, scale,
       lower_bound, want_dh0):
@@ -189,11 +197,13 @@ def _kda_setup_context(ctx, inputs, output):
     ctx.scale, ctx.lower_bound = scale, lower_bound
 
 
-def _kda_backward(ctx, do, dht, _dsaved):
+def _kda_grads(ctx, do, dht, bwd):
     q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu, saved = ctx.saved_tensors
     dht = None if dht is None or dht.numel() == 0 else dht
-    grads = _kda_bwd(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu, saved, do, dht,
-                     ctx.scale, ctx.lower_bound, h0 is not None)
+    if do is None:
+        do = torch.zeros(q.shape, device=q.device, dtype=torch.float32 if _fp32_mode(q, k, v) else torch.bfloat16)
+    grads = bwd(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu, saved, do, dht,
+                ctx.scale, ctx.lower_bound, h0 is not None)
     dq, dk, dv, dg, dbeta, dA, ddt, dcq, dck, dcv, dh0 = grads
     cast = lambda d, x: None if x is None else d.to(x.dtype)  # noqa: E731
     return (cast(dq, q), cast(dk, k), cast(dv, v), cast(dg, g), cast(dbeta, beta), cast(dA, A_log),
@@ -202,7 +212,33 @@ def _kda_backward(ctx, do, dht, _dsaved):
             None if h0 is None else dh0.to(h0.dtype), None, None, None, None, None)
 
 
+def _kda_backward(ctx, do, dht, _dsaved):
+    return _kda_grads(ctx, do, dht, _kda_bwd)
+
+
 _kda_fwd.register_autograd(_kda_backward, setup_context=_kda_setup_context)
+
+
+class _KdaEager(torch.autograd.Function):
+    """The eager path: the same implementation as the ``sophia_b200::kda_fwd``
+    / ``kda_bwd`` custom ops without the custom-op dispatch, and with the saved
+    buffer held by the autograd context instead of returned."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, scale, lower_bound,
+                output_final_state):
+        training = any(ctx.needs_input_grad)
+        o, ht, saved = _kda_fwd_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens,
+                                     scale, lower_bound, output_final_state, training)
+        if training:
+            ctx.save_for_backward(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, saved)
+            ctx.scale, ctx.lower_bound = scale, lower_bound
+        ctx.set_materialize_grads(False)
+        return o, ht
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        return _kda_grads(ctx, do, dht, _kda_bwd_impl)[:15]
 
 
 def _needs_grad(*tensors) -> bool:
@@ -211,9 +247,13 @@ def _needs_grad(*tensors) -> bool:
 
 def _layer(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, scale, lower_bound,
            output_final_state):
-    training = _needs_grad(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0)
-    o, ht, _ = _kda_fwd(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, float(scale),
-                        float(lower_bound), bool(output_final_state), training)
+    if torch.compiler.is_compiling():  # traced: the custom op, an opaque node with a fake
+        training = _needs_grad(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0)
+        o, ht, _ = _kda_fwd(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, float(scale),
+                            float(lower_bound), bool(output_final_state), training)
+    else:
+        o, ht = _KdaEager.apply(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens,
+                                float(scale), float(lower_bound), bool(output_final_state))
     return o.to(q.dtype), (ht if output_final_state else None)
 
 
@@ -315,10 +355,7 @@ def kda_layer(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, *, lower
 # --------------------------------------------------------------------------- decode
 
 
-@torch.library.custom_op("sophia_b200::kda_recurrent", mutates_args=(), device_types="cuda")
-def _kda_recurrent(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
-                   h0: Optional[Tensor], cu_seqlens: Optional[Tensor], scale: float, lower_bound: float,
-                   output_final_state: bool) -> tuple[Tensor, Tensor]:
+def _kda_recurrent_impl(q, k, v, g, beta, A_log, dt_bias, h0, cu_seqlens, scale, lower_bound, output_final_state):
     with torch.autocast("cuda", enabled=False):
         fp32 = q.dtype == torch.float32
         dt = torch.float32 if fp32 else torch.bfloat16
@@ -337,6 +374,14 @@ def _kda_recurrent(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_l
         return o, ht
 
 
+@torch.library.custom_op("sophia_b200::kda_recurrent", mutates_args=(), device_types="cuda")
+def _kda_recurrent(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
+                   h0: Optional[Tensor], cu_seqlens: Optional[Tensor], scale: float, lower_bound: float,
+                   output_final_state: bool) -> tuple[Tensor, Tensor]:
+    return _kda_recurrent_impl(q, k, v, g, beta, A_log, dt_bias, h0, cu_seqlens, scale, lower_bound,
+                               output_final_state)
+
+
 @_kda_recurrent.register_fake
 def _(q, k, v, g, beta, A_log, dt_bias, h0, cu_seqlens, scale, lower_bound, output_final_state):
     B, T, H, _ = q.shape
@@ -345,10 +390,7 @@ def _(q, k, v, g, beta, A_log, dt_bias, h0, cu_seqlens, scale, lower_bound, outp
     return o, q.new_empty((N, H, HEAD_DIM, HEAD_DIM) if output_final_state else (0,), dtype=torch.float32)
 
 
-@torch.library.custom_op("sophia_b200::kda_decode", mutates_args=("conv_state",), device_types="cuda")
-def _kda_decode(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
-                conv_q: Tensor, conv_k: Tensor, conv_v: Tensor, conv_state: Tensor, h0: Optional[Tensor],
-                scale: float, lower_bound: float) -> tuple[Tensor, Tensor]:
+def _kda_decode_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, conv_state, h0, scale, lower_bound):
     with torch.autocast("cuda", enabled=False):
         if conv_state.dtype != torch.float32 or not conv_state.is_contiguous():
             raise ValueError("conv_state must be a contiguous float32 tensor [B, 3, H*128, 3]")
@@ -366,6 +408,14 @@ def _kda_decode(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log:
             _ptr(h0c), None, B, T, H, HEAD_DIM, B, int(fp32), float(scale), float(lower_bound), _ptr(o), _ptr(ht),
             _stream()))
         return o, ht
+
+
+@torch.library.custom_op("sophia_b200::kda_decode", mutates_args=("conv_state",), device_types="cuda")
+def _kda_decode(q: Tensor, k: Tensor, v: Tensor, g: Tensor, beta: Tensor, A_log: Tensor, dt_bias: Tensor,
+                conv_q: Tensor, conv_k: Tensor, conv_v: Tensor, conv_state: Tensor, h0: Optional[Tensor],
+                scale: float, lower_bound: float) -> tuple[Tensor, Tensor]:
+    return _kda_decode_impl(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, conv_state, h0, scale,
+                            lower_bound)
 
 
 @_kda_decode.register_fake
@@ -389,8 +439,9 @@ def kda_decode(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, conv_st
         raise NotImplementedError("kda_decode has no backward; use kda_layer / chunk_kda for training")
     if scale is None:
         scale = q.shape[-1] ** -0.5
-    o, ht = _kda_decode(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, conv_state, initial_state,
-                        float(scale), float(lower_bound))
+    fn = _kda_decode if torch.compiler.is_compiling() else _kda_decode_impl
+    o, ht = fn(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, conv_state, initial_state, float(scale),
+               float(lower_bound))
     return o.to(v.dtype), ht
 
 
@@ -421,8 +472,9 @@ def fused_recurrent_kda(q, k, v, g, beta, A_log=None, dt_bias=None, scale=None, 
                          safe_gate=True, lower_bound=lower_bound, A_log=A_log, dt_bias=dt_bias)
     if scale is None:
         scale = q.shape[-1] ** -0.5
-    o, ht = _kda_recurrent(q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, float(scale),
-                           float(lower_bound), bool(output_final_state))
+    fn = _kda_recurrent if torch.compiler.is_compiling() else _kda_recurrent_impl
+    o, ht = fn(q, k, v, g, beta, A_log, dt_bias, initial_state, cu_seqlens, float(scale), float(lower_bound),
+               bool(output_final_state))
     return o.to(v.dtype), (ht if output_final_state else None)
 
 
@@ -433,8 +485,7 @@ def _gn_io(o: Tensor, g: Tensor) -> torch.dtype:
     return torch.float32 if torch.float32 in (o.dtype, g.dtype) else torch.bfloat16
 
 
-@torch.library.custom_op("sophia_b200::gated_norm_fwd", mutates_args=(), device_types="cuda")
-def _gated_norm_fwd(o: Tensor, g: Tensor, weight: Tensor, eps: float) -> Tensor:
+def _gated_norm_fwd_impl(o, g, weight, eps):
     with torch.autocast("cuda", enabled=False):
         io = _gn_io(o, g)
         oc, gc = o.to(io).contiguous(), g.to(io).contiguous()
@@ -446,13 +497,17 @@ def _gated_norm_fwd(o: Tensor, g: Tensor, weight: Tensor, eps: float) -> Tensor:
         return y
 
 
+@torch.library.custom_op("sophia_b200::gated_norm_fwd", mutates_args=(), device_types="cuda")
+def _gated_norm_fwd(o: Tensor, g: Tensor, weight: Tensor, eps: float) -> Tensor:
+    return _gated_norm_fwd_impl(o, g, weight, eps)
+
+
 @_gated_norm_fwd.register_fake
 def _(o, g, weight, eps):
     return o.new_empty(o.shape, dtype=_gn_io(o, g))
 
 
-@torch.library.custom_op("sophia_b200::gated_norm_bwd", mutates_args=(), device_types="cuda")
-def _gated_norm_bwd(dy: Tensor, o: Tensor, g: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor, Tensor]:
+def _gated_norm_bwd_impl(dy, o, g, weight, eps):
     with torch.autocast("cuda", enabled=False):
         io = _gn_io(o, g)
         oc, gc = o.to(io).contiguous(), g.to(io).contiguous()
@@ -470,6 +525,11 @@ def _gated_norm_bwd(dy: Tensor, o: Tensor, g: Tensor, weight: Tensor, eps: float
         return d_o, d_g, dw
 
 
+@torch.library.custom_op("sophia_b200::gated_norm_bwd", mutates_args=(), device_types="cuda")
+def _gated_norm_bwd(dy: Tensor, o: Tensor, g: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor, Tensor]:
+    return _gated_norm_bwd_impl(dy, o, g, weight, eps)
+
+
 @_gated_norm_bwd.register_fake
 def _(dy, o, g, weight, eps):
     io = _gn_io(o, g)
@@ -483,13 +543,31 @@ def _gn_setup_context(ctx, inputs, output):
     ctx.eps = eps
 
 
-def _gn_backward(ctx, dy):
+def _gn_grads(ctx, dy, bwd):
     o, g, weight = ctx.saved_tensors
-    d_o, d_g, dw = _gated_norm_bwd(dy, o, g, weight, ctx.eps)
+    d_o, d_g, dw = bwd(dy, o, g, weight, ctx.eps)
     return d_o.to(o.dtype), d_g.to(g.dtype), dw.to(weight.dtype), None
 
 
+def _gn_backward(ctx, dy):
+    return _gn_grads(ctx, dy, _gated_norm_bwd)
+
+
 _gated_norm_fwd.register_autograd(_gn_backward, setup_context=_gn_setup_context)
+
+
+class _GnEager(torch.autograd.Function):
+    """Eager path of the gated norm: the custom ops' implementation without their dispatch."""
+
+    @staticmethod
+    def forward(ctx, o, g, weight, eps):
+        ctx.save_for_backward(o, g, weight)
+        ctx.eps = eps
+        return _gated_norm_fwd_impl(o, g, weight, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        return _gn_grads(ctx, dy, _gated_norm_bwd_impl)
 
 
 def gated_rms_norm(o: Tensor, g: Tensor, weight: Tensor, eps: float = 1e-5) -> Tensor:
@@ -504,4 +582,5 @@ def gated_rms_norm(o: Tensor, g: Tensor, weight: Tensor, eps: float = 1e-5) -> T
                          f"got {tuple(o.shape)}, {tuple(g.shape)}, {tuple(weight.shape)}")
     if not (o.is_cuda and g.is_cuda and weight.is_cuda):
         raise RuntimeError("gated_rms_norm runs on the CUDA kernels only: o, g and weight must be CUDA tensors")
-    return _gated_norm_fwd(o, g, weight, float(eps)).to(torch.promote_types(o.dtype, g.dtype))
+    fn = _gated_norm_fwd if torch.compiler.is_compiling() else _GnEager.apply
+    return fn(o, g, weight, float(eps)).to(torch.promote_types(o.dtype, g.dtype))

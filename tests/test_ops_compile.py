@@ -1,9 +1,10 @@
-"""The custom-op boundary of the layer, without a GPU: every kernel call is a
-``torch.library.custom_op`` with a fake implementation and an autograd
-formula, so shapes, dtypes and gradients propagate on meta tensors, and
-``torch.compile(fullgraph=True)`` traces through the seam without a graph
-break (Sophia compiles its training model,
-``ml/training/pretrain/engine/sm120_graph_runner.py:71-75``)."""
+"""The custom-op boundary of the layer, without a GPU: under ``torch.compile``
+every kernel call is a ``torch.library.custom_op`` with a fake implementation
+and an autograd formula, so the seam traces with ``fullgraph=True`` (no graph
+break) and shapes, dtypes and gradients propagate on meta tensors (Sophia
+compiles its training model, ``ml/training/pretrain/engine/
+sm120_graph_runner.py:71-75``).  Eager calls take a plain autograd.Function
+over the same implementation (checked on the GPU)."""
 
 from __future__ import annotations
 
@@ -33,10 +34,14 @@ def _inputs(dt=torch.bfloat16):
 ARGS = ("q", "k", "v", "g", "beta", "A_log", "dt_bias", "conv_q", "conv_k", "conv_v", "h0")
 
 
+def _traced(fn):
+    return torch.compile(fn, backend="eager", fullgraph=True)
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 def test_layer_shapes_and_gradients_propagate(dt):
     x = _inputs(dt)
-    o, ht = ops._layer(*(x[n] for n in ARGS), None, D ** -0.5, -5.0, True)
+    o, ht = _traced(lambda *a: ops._layer(*a, None, D ** -0.5, -5.0, True))(*(x[n] for n in ARGS))
     assert o.shape == (B, T, H, D) and o.dtype == dt
     assert ht.shape == (B, H, D, D) and ht.dtype == torch.float32
     (o.float().sum() + ht.sum()).backward()
@@ -49,13 +54,14 @@ def test_packed_and_inference_calls():
     q1 = {n: _mk(1, 150, H, D) for n in ("q", "k", "v", "g")}
     cu = torch.empty(4, device="meta", dtype=torch.int32)
     h0 = _mk(3, H, D, D, dt=torch.float32)
-    o, ht = ops._layer(q1["q"], q1["k"], q1["v"], q1["g"], _mk(1, 150, H), x["A_log"], x["dt_bias"],
-                       None, None, None, h0, cu, D ** -0.5, -5.0, True)
+    packed = _traced(lambda q, k, v, g, b, A, dtb, h, c: ops._layer(q, k, v, g, b, A, dtb, None, None, None, h, c,
+                                                                    D ** -0.5, -5.0, True))
+    o, ht = packed(q1["q"], q1["k"], q1["v"], q1["g"], _mk(1, 150, H), x["A_log"], x["dt_bias"], h0, cu)
     assert ht.shape == (3, H, D, D)
     o.float().sum().backward()
     assert h0.grad.shape == h0.shape and q1["q"].grad.shape == q1["q"].shape
     with torch.no_grad():  # no saved buffer when nothing needs gradients
-        o, ht = ops._layer(*(x[n] for n in ARGS), None, D ** -0.5, -5.0, False)
+        o, ht = _traced(lambda *a: ops._layer(*a, None, D ** -0.5, -5.0, False))(*(x[n] for n in ARGS))
     assert ht is None and o.shape == (B, T, H, D)
 
 
@@ -78,5 +84,5 @@ def test_decode_op_shapes():
     b = torch.empty(3, 1, H, device="meta", dtype=torch.float32)
     A = torch.empty(H, device="meta")
     dtb = torch.empty(H * D, device="meta")
-    o, ht = ops._kda_recurrent(q, q, q, q, b, A, dtb, None, None, D ** -0.5, -5.0, True)
+    o, ht = ops._kda_recurrent(q, q, q, q, b, A, dtb, None, None, D ** -0.5, -5.0, True)  # the custom op itself
     assert o.shape == q.shape and o.dtype == torch.float32 and ht.shape == (3, H, D, D)
