@@ -93,6 +93,8 @@ struct BwdIntraSmem {
   static constexpr int GBV = DW;                    // fp32 dGam_C [128], dt_bias [128], A_log (after G1)
   static constexpr int PSUM = DW + 2048;            // fp32 [8][128] partial sums of the gate tail
   static constexpr int DQT = GAM, DKB = GAM + T128; // acc64 state-pass tiles (after the decay factors)
+  static constexpr int DGAM = KE;                   // fp32 [64][128] dGam over Ke and V (after G1)
+  static_assert(V == KE + T128, "dGam needs Ke and V adjacent");
   static_assert(COLS + 4 * D * 4 <= KN + T128, "small arrays overflow the dL' region");
   static_assert(PSUM + 8 * D * 4 <= DW + T128 && GBV + (2 * D + 4) * 4 <= PSUM, "gate-tail arrays overflow");
   static_assert(DKB + T128 <= VEC, "gradient tiles overflow the decay region");
@@ -148,13 +150,59 @@ __device__ __forceinline__ void st_global16(bf16* dst, const float (&f)[16]) {
   reinterpret_cast<uint4*>(dst)[0] = a;
   reinterpret_cast<uint4*>(dst)[1] = b;
 }
-// Sum over the 16 lanes of this lane half (rows of one sub-chunk block).
-__device__ __forceinline__ float half_sum(float x) {
-  x += __shfl_xor_sync(0xffffffffu, x, 1);
-  x += __shfl_xor_sync(0xffffffffu, x, 2);
-  x += __shfl_xor_sync(0xffffffffu, x, 4);
-  x += __shfl_xor_sync(0xffffffffu, x, 8);
-  return x;
+// Column sums over the 16 lanes of this lane half (the rows of one sub-chunk
+// block): lane L of the half returns sum over the half's lanes of v[L].
+// Recursive halving, 8 + 4 + 2 + 1 shuffles.
+__device__ __forceinline__ float half_reduce_scatter(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 8, n = 8; m >= 1; m >>= 1, n >>= 1) {
+    const bool up = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = up ? v[i] : v[i + n];
+      const float keep = up ? v[i + n] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+    }
+  }
+  return v[0];
+}
+// The same for 8 values: lanes L and L ^ 1 of the half both return the column
+// sum of v[(L & 15) >> 1].
+__device__ __forceinline__ float half_reduce_scatter8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 8, n = 4; m >= 2; m >>= 1, n >>= 1) {
+    const bool up = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float send = up ? v[i] : v[i + n];
+      const float keep = up ? v[i + n] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+// dGam as fp32 [64][128] over the dead V and Ke tiles: 16-byte chunk k of row
+// r at position k ^ (r & 7), so the 16 rows a warp half touches hit distinct banks.
+__device__ __forceinline__ float4* dg_chunk(unsigned char* base, int r, int col) {
+  return reinterpret_cast<float4*>(base + r * 512 + ((((col >> 2) ^ (r & 7))) << 4));
+}
+__device__ __forceinline__ void ld_dg16(unsigned char* base, int r, int col0, float (&f)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) {
+    const float4 x = *dg_chunk(base, r, col0 + i);
+    f[i] = x.x; f[i + 1] = x.y; f[i + 2] = x.z; f[i + 3] = x.w;
+  }
+}
+__device__ __forceinline__ void st_dg16(unsigned char* base, int r, int col0, const float (&f)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 4) *dg_chunk(base, r, col0 + i) = make_float4(f[i], f[i + 1], f[i + 2], f[i + 3]);
+}
+__device__ __forceinline__ void st_dg8(unsigned char* base, int r, int col0, const float (&f)[8]) {
+  *dg_chunk(base, r, col0) = make_float4(f[0], f[1], f[2], f[3]);
+  *dg_chunk(base, r, col0 + 4) = make_float4(f[4], f[5], f[6], f[7]);
 }
 
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntraParams P) {
@@ -233,7 +281,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   // MN-major operand: K step ks (16 rows)
   auto mdesc = [&](int off, int ks) { return tc::smem_desc(sb + off + ks * 2048, 8192, 1024); };
 
-  float dq[16], dk[16], dG[16], af[16];
+  // dq, dk and the decay factor stay in registers; dGam lives in shared memory
+  // over the V and Ke tiles once G1 has read them (each thread owns its 16
+  // elements there: no synchronisation needed).
+  float dq[16], dk[16], af[16];
+  unsigned char* dgb = smem + S::DGAM;
   bool ok = true;
   for (int once = 0; once < 1; ++once) {
     ok = tc::mbar_wait(mb + 0, 0);
@@ -362,7 +414,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       for (int i = tid; i < 64 * 16; i += blockDim.x) {
         const int rr = i >> 4, cc = i & 15;
         const bool okr = rr < nv;
-        cp_async16(gre + rr * D + cc * 8, P.in.g + (okr ? ((size_t)(pos.t0 + rr) * H + h) * D + cc * 8 : 0), okr);
+        cp_async16(gre + sw64_chunk(rr, cc), P.in.g + (okr ? ((size_t)(pos.t0 + rr) * H + h) * D + cc * 8 : 0), okr);
       }
       float* gbv = reinterpret_cast<float*>(smem + S::GBV);
       if (tid < 32)
@@ -380,14 +432,13 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       const float* erp = reinterpret_cast<const float*>(smem + S::ER) + s * D + c0;
       const float* ecp = reinterpret_cast<const float*>(smem + S::EC) + s * D + c0;
       const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
-      float* cols = reinterpret_cast<float*>(smem + S::COLS) + s * D + c0;
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {  // two 8-column passes
         float acc[8];
         tc::tmem_ld8(trow + 0 + 16 * qd + hb, acc);  // dv
         if (r < nv) *reinterpret_cast<bf16x8*>(dvrow + hb) = pack8(acc);
         tc::tmem_ld8(trow + 64 + 16 * qd + hb, acc);  // dKe
-        float gq[8], gk[8], qa[8], ka[8], kd[8];
+        float gq[8], gk[8], qa[8], ka[8], kd[8], colsum[8], g8[8];
         const int c8 = (c0 + hb) >> 3;
         unpack8(*reinterpret_cast<const bf16x8*>(tq + acc64_off(r, c0 + hb)), gq);
         unpack8(*reinterpret_cast<const bf16x8*>(tk + acc64_off(r, c0 + hb)), gk);
@@ -402,26 +453,29 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           const float kbar = kd[v] * rv * ec;
           dq[u] = gq[v] * eg;
           dk[u] = acc[v] * eg + gk[v] * egc;
-          dG[u] = ka[v] * er * acc[v] + qa[v] * er * gq[v] - kbar * gk[v];
-          const float cs = half_sum(kbar * gk[v]);  // column sum over the 16 rows of this lane half
-          if ((lane & 15) == 0) cols[u] = cs;
+          g8[v] = ka[v] * er * acc[v] + qa[v] * er * gq[v] - kbar * gk[v];
+          colsum[v] = kbar * gk[v];
         }
+        st_dg8(dgb, r, c0 + hb, g8);
+        // column sums over the 16 rows of this lane half
+        const float cs = half_reduce_scatter8(colsum);
+        if ((lane & 1) == 0) reinterpret_cast<float*>(smem + S::COLS)[s * D + c0 + hb + ((lane & 15) >> 1)] = cs;
       }
       // dT (64 x 64, lanes 0-15): dbeta_T[j] = sum_i dT_ij A_ij, dA = dT diag(beta)
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {
-        float acc[8], av[8];
+        float acc[8], av[8], cs[8];
         tc::tmem_ld8(trow + 128 + 16 * qd + hb, acc);
         const int c8 = (16 * qd + hb) >> 3;
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::AT + 2 * sw64_chunk(r, c8)), av);
-        float* dbt = reinterpret_cast<float*>(smem + S::DBT) + s * 64 + 16 * qd + hb;
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
-          const float cs = half_sum(hh == 0 ? acc[v] * av[v] : 0.f);
-          if (lane == 0) dbt[v] = cs;
+          cs[v] = acc[v] * av[v];
           acc[v] *= beta[16 * qd + hb + v];
         }
         if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DA + 2 * sw64_chunk(r, c8)) = pack8(acc);
+        const float dbt = half_reduce_scatter8(cs);
+        if (hh == 0 && (lane & 1) == 0) reinterpret_cast<float*>(smem + S::DBT)[s * 64 + 16 * qd + hb + (lane >> 1)] = dbt;
       }
     }
     tc::fence_async_smem();
@@ -437,6 +491,8 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     // row sides: dX += af (P_I + sum_J<I c'_IJ P_J), dGam += rowop o (...)
     auto row_side = [&](uint32_t unit0, int rowop, float (&dx)[16]) {
       const float* cpb = reinterpret_cast<const float*>(smem + S::CP) + c0;
+      float g16[16];
+      ld_dg16(dgb, r, c0, g16);
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {
         float out[8], pj[8], ro[8];
@@ -451,15 +507,18 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           dx[hb + v] = fmaf(af[hb + v], out[v], dx[hb + v]);
-          dG[hb + v] = fmaf(ro[v], out[v], dG[hb + v]);
+          g16[hb + v] = fmaf(ro[v], out[v], g16[hb + v]);
         }
       }
+      st_dg16(dgb, r, c0, g16);
     };
     // column sides: tot = R_I + rev_I sum_{Ib > I} c_{Ib,I} R_Ib; then dk += tot / af
     // (the diagonal's 1/af and the off-diagonal bf = rev_I / af at once), dGam -= Kd o tot
     auto column_side = [&](uint32_t unit0) {
       const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
       const float* ccb = reinterpret_cast<const float*>(smem + S::CC) + c0;
+      float g16[16];
+      ld_dg16(dgb, r, c0, g16);
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {
         float tot[8], R[8], kd[8];
@@ -474,9 +533,10 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           dk[hb + v] = fmaf(rcp(af[hb + v]), tot[v], dk[hb + v]);
-          dG[hb + v] = fmaf(-kd[v], tot[v], dG[hb + v]);
+          g16[hb + v] = fmaf(-kd[v], tot[v], g16[hb + v]);
         }
       }
+      st_dg16(dgb, r, c0, g16);
     };
 
     // ---- E2: row side through M
@@ -484,6 +544,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();
     row_side(256, S::QA, dq);
+    if (r < nv) st_global16(P.dq_hat + ((size_t)(pos.t0 + r) * H + h) * D + c0, dq);  // dq is complete
     tc::fence_before_sync();
     __syncthreads();
     if (tid == 0) {  // G4: column side through M, R_I = dM[I, :]^T Qa[I] (units 4 + I)
@@ -588,65 +649,71 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     return;
   }
 
-  // ---- outputs: dq_hat, dk_hat; dGam -> shared memory for the gate tail
-  if (r < nv) {
-    const size_t off = ((size_t)(pos.t0 + r) * H + h) * D + c0;
-    st_global16(P.dq_hat + off, dq);
-    st_global16(P.dk_hat + off, dk);
-  }
-  float* dGs = gam;  // the dQt / dKbar tiles there are dead
+  // ---- outputs: dk_hat (dq_hat left after the row side through M)
+  if (r < nv) st_global16(P.dk_hat + ((size_t)(pos.t0 + r) * H + h) * D + c0, dk);
+  float dG[16];
+  ld_dg16(dgb, r, c0, dG);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tbase, 512);
+
+  // ---- the gate backward, in the same row layout.  dg_r = f(r) (C + sum_{r' >= r} dGam_r'),
+  // C = dGam_C + sum over the chunk of Kbar o dKbar: a suffix scan over the 16 rows of
+  // this lane half, plus the totals of the later sub-chunk blocks.
+  float* qtot = reinterpret_cast<float*>(smem + S::PSUM);  // [4][128] block totals, then [2][4][128] sums
 #pragma unroll
-  for (int u = 0; u < 16; u += 4)
-    *reinterpret_cast<float4*>(dGs + r * LDG + c0 + u) = make_float4(dG[u], dG[u + 1], dG[u + 2], dG[u + 3]);
+  for (int u = 0; u < 16; ++u) {
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+      const float y = __shfl_down_sync(0xffffffffu, dG[u], o, 16);
+      if ((lane & 15) + o < 16) dG[u] += y;
+    }
+  }
+  if ((lane & 15) == 0) {
+#pragma unroll
+    for (int u = 0; u < 16; u += 4)
+      *reinterpret_cast<float4*>(qtot + s * D + c0 + u) = make_float4(dG[u], dG[u + 1], dG[u + 2], dG[u + 3]);
+  }
   cp_async_wait<0>();  // gate logits and vectors
   __syncthreads();
-  // reverse cumsum over the chunk and the gate backward: thread (part, col)
-  // with col = tid % 128 owns rows 16*part .. 16*part+15 of one channel
   {
     const float* gbv = reinterpret_cast<const float*>(smem + S::GBV);
     const float* cols = reinterpret_cast<const float*>(smem + S::COLS);
-    const bf16* gre = reinterpret_cast<const bf16*>(smem + S::GRE);
-    float* partsum = reinterpret_cast<float*>(smem + S::PSUM);
-    const int col = tid & 127, part = tid >> 7;
-    float own = 0.f;
-#pragma unroll 4
-    for (int rr = 16 * part; rr < 16 * part + 16; ++rr) own += dGs[rr * LDG + col];
-    partsum[part * D + col] = own;
-    __syncthreads();
-    float run = gbv[col] + cols[col] + cols[D + col] + cols[2 * D + col] + cols[3 * D + col];
-    for (int p2 = part + 1; p2 < 4; ++p2) run += partsum[p2 * D + col];
     const float eA = __expf(gbv[2 * D]);
-    const float bias = gbv[D + col];
-    float sA = 0.f, sB = 0.f;
-    for (int rr = 16 * part + 15; rr >= 16 * part; --rr) {
-      run += dGs[rr * LDG + col];
-      if (rr < nv) {
-        const size_t off = ((size_t)(pos.t0 + rr) * H + h) * D + col;
-        const float x = __bfloat162float(gre[rr * D + col]) + bias;
-        const float z = eA * x;
-        const float sg = sigmoidf_(z);
-        const float dz = run * P.in.lower_bound * sg * (1.f - sg);
-        const float dx = dz * eA;
-        P.dg[off] = __float2bfloat16(dx);
-        sA += dz * z;
-        sB += dx;
-      }
+    float gl[16];
+    lds_row16(smem + S::GRE, r, c0, gl);
+    float sA[16], sB[16];
+    const bool okr = r < nv;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int cc = c0 + u;
+      float run = dG[u] + gbv[cc] + cols[cc] + cols[D + cc] + cols[2 * D + cc] + cols[3 * D + cc];
+      for (int s2 = s + 1; s2 < 4; ++s2) run += qtot[s2 * D + cc];
+      const float z = eA * (gl[u] + gbv[D + cc]);
+      const float sg = sigmoidf_(z);
+      const float dz = run * P.in.lower_bound * sg * (1.f - sg);
+      const float dx = dz * eA;
+      gl[u] = dx;
+      sA[u] = okr ? dz * z : 0.f;
+      sB[u] = okr ? dx : 0.f;
     }
+    if (okr) st_global16(P.dg + ((size_t)(pos.t0 + r) * H + h) * D + c0, gl);
+    const float a = half_reduce_scatter(sA);
+    const float b = half_reduce_scatter(sB);
+    __syncthreads();  // the block totals are read
+    qtot[s * D + c0 + (lane & 15)] = a;
+    qtot[4 * D + s * D + c0 + (lane & 15)] = b;
     __syncthreads();
-    partsum[part * D + col] = sA;
-    partsum[4 * D + part * D + col] = sB;
-    __syncthreads();
-    if (part == 0) {
-      P.partA[cidx * D + col] = partsum[col] + partsum[D + col] + partsum[2 * D + col] + partsum[3 * D + col];
-      P.partB[cidx * D + col] = partsum[4 * D + col] + partsum[5 * D + col] + partsum[6 * D + col] +
-                                partsum[7 * D + col];
+    if (tid < D) {
+      P.partA[cidx * D + tid] = (qtot[tid] + qtot[D + tid]) + (qtot[2 * D + tid] + qtot[3 * D + tid]);
+    } else if (tid < 2 * D) {
+      const int cc = tid - D;
+      const float* q2 = qtot + 4 * D;
+      P.partB[cidx * D + cc] = (q2[cc] + q2[D + cc]) + (q2[2 * D + cc] + q2[3 * D + cc]);
     }
   }
-  if (tid < 64) {
-    const int rr = tid;
+  if (tid >= 2 * D && tid < 2 * D + 64) {
+    const int rr = tid - 2 * D;
     if (rr < nv) {
       const float* dbt = reinterpret_cast<const float*>(smem + S::DBT);
       const float* dbl = reinterpret_cast<const float*>(smem + S::DBL);
