@@ -184,6 +184,12 @@ __device__ __forceinline__ float half_reduce_scatter8(float (&v)[8]) {
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
+// 8 consecutive floats of a 16-byte-aligned shared vector (two LDS.128).
+__device__ __forceinline__ void ld8f(const float* p, float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
 // dGam as fp32 [64][128] over the dead V and Ke tiles: 16-byte chunk k of row
 // r at position k ^ (r & 7), so the 16 rows a warp half touches hit distinct banks.
 __device__ __forceinline__ float4* dg_chunk(unsigned char* base, int r, int col) {
@@ -276,10 +282,13 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   const uint32_t idKM = tc::idesc_bf16(64, 64, false, true);   // A K-major,  B MN-major
   const uint32_t idKK = tc::idesc_bf16(64, 64, false, false);  // A K-major,  B K-major
   const uint32_t sb = smem_u32(smem);
+  // Descriptors: the address field (bits 0-13, address / 16) of a base descriptor
+  // plus the operand's offset / 16 (every address stays below 256 KB).
+  const uint64_t kbase = tc::smem_desc(sb, 16, 1024), mbase = tc::smem_desc(sb, 8192, 1024);
   // K-major operand at byte offset `off`: K step ks (16 elements) of a tile of 64-element atoms
-  auto kdesc = [&](int off, int ks) { return tc::smem_desc(sb + off + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024); };
+  auto kdesc = [&](int off, int ks) { return kbase + (uint64_t)((off + (ks >> 2) * 8192 + (ks & 3) * 32) >> 4); };
   // MN-major operand: K step ks (16 rows)
-  auto mdesc = [&](int off, int ks) { return tc::smem_desc(sb + off + ks * 2048, 8192, 1024); };
+  auto mdesc = [&](int off, int ks) { return mbase + (uint64_t)((off + ks * 2048) >> 4); };
 
   // dq, dk and the decay factor stay in registers; dGam lives in shared memory
   // over the V and Ke tiles once G1 has read them (each thread owns its 16
@@ -378,12 +387,21 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     tc::fence_async_smem();  // operand tiles -> tensor cores; the decay region -> the bulk copy below
     tc::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {
-      tc::fence_after_sync();
+    if (tid == 64) {
       // dQt and dKbar (acc64) land over the dead decay region while the MMAs run
       tc::mbar_expect_tx(mb + 1, 2 * S::T128);
       tc::bulk_g2s(smem + S::DQT, P.dQt + tix * TILE64_ELEMS, S::T128, mb + 1);
       tc::bulk_g2s(smem + S::DKB, P.dKb + tix * TILE64_ELEMS, S::T128, mb + 1);
+    } else if (tid == 32) {
+      tc::fence_after_sync();
+      // G2: row side through M, P_J = dM[:, J] Kd[J] (units 4 + J)
+      for (int J = 0; J < 4; ++J)
+        for (int hf = 0; hf < 2; ++hf)
+          tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * J, kdesc(S::DM, J),
+                       mdesc(S::KD + hf * 8192, J), idKM, false);
+      tc::mma_commit(mb + 3);
+    } else if (tid == 0) {
+      tc::fence_after_sync();
       // G1: dv = T^T dE (unit 0), dKe = T^T dW (unit 1), dT = dE V^T + dW Ke^T (unit 2)
       for (int hf = 0; hf < 2; ++hf) {
         const uint32_t lo = (uint32_t)(16 * hf) << 16;
@@ -395,12 +413,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       for (int ks = 0; ks < 8; ++ks) tc::mma_bf16(tbase + 128, kdesc(S::DE, ks), kdesc(S::V, ks), idKK, ks > 0);
       for (int ks = 0; ks < 8; ++ks) tc::mma_bf16(tbase + 128, kdesc(S::DW, ks), kdesc(S::KE, ks), idKK, true);
       tc::mma_commit(mb + 2);
-      // G2: row side through M, P_J = dM[:, J] Kd[J] (units 4 + J)
-      for (int J = 0; J < 4; ++J)
-        for (int hf = 0; hf < 2; ++hf)
-          tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * J, kdesc(S::DM, J),
-                       mdesc(S::KD + hf * 8192, J), idKM, false);
-      tc::mma_commit(mb + 3);
       *issued = 0xFu;
     }
 
@@ -445,13 +457,16 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::QA + 2 * sw64_chunk(r, c8)), qa);
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KA + 2 * sw64_chunk(r, c8)), ka);
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, c8)), kd);
+        float erv[8], ecv[8], rvv[8];
+        ld8f(erp + hb, erv);
+        ld8f(ecp + hb, ecv);
+        ld8f(rvp + hb, rvv);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const int u = hb + v;
-          const float er = erp[u], ec = ecp[u], rv = rvp[u];
+          const float er = erv[v], ec = ecv[v], rv = rvv[v];
           const float eg = af[u] * er, egc = rv * rcp(af[u]) * ec;
           const float kbar = kd[v] * rv * ec;
-          dq[u] = gq[v] * eg;
           dk[u] = acc[v] * eg + gk[v] * egc;
           g8[v] = ka[v] * er * acc[v] + qa[v] * er * gq[v] - kbar * gk[v];
           colsum[v] = kbar * gk[v];
@@ -464,14 +479,15 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       // dT (64 x 64, lanes 0-15): dbeta_T[j] = sum_i dT_ij A_ij, dA = dT diag(beta)
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {
-        float acc[8], av[8], cs[8];
+        float acc[8], av[8], cs[8], bv[8];
         tc::tmem_ld8(trow + 128 + 16 * qd + hb, acc);
         const int c8 = (16 * qd + hb) >> 3;
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::AT + 2 * sw64_chunk(r, c8)), av);
+        ld8f(beta + 16 * qd + hb, bv);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           cs[v] = acc[v] * av[v];
-          acc[v] *= beta[16 * qd + hb + v];
+          acc[v] *= bv[v];
         }
         if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DA + 2 * sw64_chunk(r, c8)) = pack8(acc);
         const float dbt = half_reduce_scatter8(cs);
@@ -498,8 +514,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         float out[8], pj[8], ro[8];
         tc::tmem_ld8(trow + unit0 + 64 * s + 16 * qd + hb, out);
         for (int J = 0; J < s; ++J) {
+          float cp[8];
           tc::tmem_ld8(trow + unit0 + 64 * J + 16 * qd + hb, pj);
-          const float* cp = cpb + pair_index(s, J) * D + hb;
+          ld8f(cpb + pair_index(s, J) * D + hb, cp);
 #pragma unroll
           for (int v = 0; v < 8; ++v) out[v] = fmaf(cp[v], pj[v], out[v]);
         }
@@ -523,11 +540,20 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       for (int hb = 0; hb < 16; hb += 8) {
         float tot[8], R[8], kd[8];
         tc::tmem_ld8(trow + unit0 + 64 * s + 16 * qd + hb, tot);  // diagonal block: R_I
-        for (int Ib = s + 1; Ib < 4; ++Ib) {
-          tc::tmem_ld8(trow + unit0 + 64 * Ib + 16 * qd + hb, R);
-          const float* cc = ccb + pair_index(Ib, s) * D + hb;
+        if (s < 3) {
+          float off[8], rv[8];
 #pragma unroll
-          for (int v = 0; v < 8; ++v) tot[v] = fmaf(rvp[hb + v] * cc[v], R[v], tot[v]);
+          for (int v = 0; v < 8; ++v) off[v] = 0.f;
+          for (int Ib = s + 1; Ib < 4; ++Ib) {
+            float cc[8];
+            tc::tmem_ld8(trow + unit0 + 64 * Ib + 16 * qd + hb, R);
+            ld8f(ccb + pair_index(Ib, s) * D + hb, cc);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) off[v] = fmaf(cc[v], R[v], off[v]);
+          }
+          ld8f(rvp + hb, rv);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) tot[v] = fmaf(rv[v], off[v], tot[v]);
         }
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, (c0 + hb) >> 3)), kd);
 #pragma unroll
@@ -543,6 +569,18 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     ok = tc::mbar_wait(mb + 3, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
     tc::fence_after_sync();
+    {  // dq = dQt 2^Gam, then the row side through M adds to it
+      const bf16* tq = reinterpret_cast<const bf16*>(smem + S::DQT);
+      const float* erp = reinterpret_cast<const float*>(smem + S::ER) + s * D + c0;
+#pragma unroll
+      for (int hb = 0; hb < 16; hb += 8) {
+        float gq[8], er[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(tq + acc64_off(r, c0 + hb)), gq);
+        ld8f(erp + hb, er);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) dq[hb + v] = gq[v] * af[hb + v] * er[v];
+      }
+    }
     row_side(256, S::QA, dq);
     if (r < nv) st_global16(P.dq_hat + ((size_t)(pos.t0 + r) * H + h) * D + c0, dq);  // dq is complete
     tc::fence_before_sync();
@@ -676,33 +714,51 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   }
   cp_async_wait<0>();  // gate logits and vectors
   __syncthreads();
+  float* coff = qtot + 4 * D;  // [4][128]: what the rows of block s add to their suffix sums
   {
+    const int sb2 = tid >> 7, cc = tid & 127;
     const float* gbv = reinterpret_cast<const float*>(smem + S::GBV);
     const float* cols = reinterpret_cast<const float*>(smem + S::COLS);
+    float o = gbv[cc] + ((cols[cc] + cols[D + cc]) + (cols[2 * D + cc] + cols[3 * D + cc]));
+    for (int s2 = sb2 + 1; s2 < 4; ++s2) o += qtot[s2 * D + cc];
+    coff[sb2 * D + cc] = o;
+  }
+  __syncthreads();
+  {
+    const float* gbv = reinterpret_cast<const float*>(smem + S::GBV);
     const float eA = __expf(gbv[2 * D]);
-    float gl[16];
-    lds_row16(smem + S::GRE, r, c0, gl);
-    float sA[16], sB[16];
     const bool okr = r < nv;
+    bf16* dgrow = P.dg + ((size_t)(pos.t0 + r) * H + h) * D + c0;
+    float a2[2], b2[2];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int cc = c0 + u;
-      float run = dG[u] + gbv[cc] + cols[cc] + cols[D + cc] + cols[2 * D + cc] + cols[3 * D + cc];
-      for (int s2 = s + 1; s2 < 4; ++s2) run += qtot[s2 * D + cc];
-      const float z = eA * (gl[u] + gbv[D + cc]);
-      const float sg = sigmoidf_(z);
-      const float dz = run * P.in.lower_bound * sg * (1.f - sg);
-      const float dx = dz * eA;
-      gl[u] = dx;
-      sA[u] = okr ? dz * z : 0.f;
-      sB[u] = okr ? dx : 0.f;
+    for (int hb = 0; hb < 16; hb += 8) {
+      float gl[8], ofs[8], bias[8], sA[8], sB[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(smem + S::GRE + 2 * sw64_chunk(r, (c0 + hb) >> 3)), gl);
+      ld8f(coff + s * D + c0 + hb, ofs);
+      ld8f(gbv + D + c0 + hb, bias);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float run = dG[hb + v] + ofs[v];
+        const float z = eA * (gl[v] + bias[v]);
+        const float sg = sigmoidf_(z);
+        const float dz = run * P.in.lower_bound * sg * (1.f - sg);
+        const float dx = dz * eA;
+        gl[v] = dx;
+        sA[v] = okr ? dz * z : 0.f;
+        sB[v] = okr ? dx : 0.f;
+      }
+      if (okr) *reinterpret_cast<bf16x8*>(dgrow + hb) = pack8(gl);
+      a2[hb >> 3] = half_reduce_scatter8(sA);
+      b2[hb >> 3] = half_reduce_scatter8(sB);
     }
-    if (okr) st_global16(P.dg + ((size_t)(pos.t0 + r) * H + h) * D + c0, gl);
-    const float a = half_reduce_scatter(sA);
-    const float b = half_reduce_scatter(sB);
-    __syncthreads();  // the block totals are read
-    qtot[s * D + c0 + (lane & 15)] = a;
-    qtot[4 * D + s * D + c0 + (lane & 15)] = b;
+    __syncthreads();  // the block totals and offsets are read
+    if ((lane & 1) == 0) {
+      const int cc = c0 + ((lane & 15) >> 1);
+      qtot[s * D + cc] = a2[0];
+      qtot[s * D + cc + 8] = a2[1];
+      qtot[4 * D + s * D + cc] = b2[0];
+      qtot[4 * D + s * D + cc + 8] = b2[1];
+    }
     __syncthreads();
     if (tid < D) {
       P.partA[cidx * D + tid] = (qtot[tid] + qtot[D + tid]) + (qtot[2 * D + tid] + qtot[3 * D + tid]);
