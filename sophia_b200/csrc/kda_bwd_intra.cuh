@@ -17,11 +17,13 @@
 //   G5  -dL = A^T X                   (then dL' = diag(beta) tril(dL))
 //   G6  P_J = dL'[:, J] Kd[J]         (row side through L')
 //   G7  R_I = dL'[I, :]^T Ka[I]       (column side through L')
-// One thread issues each group and commits it to its own mbarrier; the other
-// groups' epilogues run while it computes (G1+G2, then G3 during the row-M
-// epilogue, G4 during X, ...).  TMEM holds 512 columns in eight 64-column
-// units: G1 in units 0-2, X in 3, dL in 0, the row side of L' in 0-3, the
-// row side of M and both column sides in 4-7.
+// One thread issues each group and commits it to its own mbarrier.  The
+// epilogues on the chain G1 -> dA -> G3 -> X -> G5 -> dL' -> G6/G7 run first;
+// the others (dv and dKe, the row and column sides through M) run while the
+// chain's MMAs compute.  TMEM holds 512 columns in eight 64-column units: G1 in
+// units 0-2, X in 3, dL in 0, the row side of L' in 0-3, the row side of M and
+// both column sides in 4-7.  Accumulator slices a phase needs are loaded
+// together and waited for once.
 //
 // Epilogues run in the TMEM row layout: warp w reads lane quarter w % 4 (rows
 // 16 (w % 4) .. +15 = sub-chunk block I), lanes 0-15 the first half of the
@@ -416,10 +418,54 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       *issued = 0xFu;
     }
 
-    // ---- E1: dv out; dq, dk, dGam from dKe and the state-pass tiles; dT -> dbeta, dA
-    ok = tc::mbar_wait(mb + 2, 0) && tc::mbar_wait(mb + 1, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    // Order of the epilogues: the chain G1 -> dA -> G3 -> X -> G5 -> dL' -> G6/G7 first,
+    // the other epilogues while its MMAs run.
+    auto fail_if = [&](bool bad) {
+      if (__syncthreads_or(bad)) {
+        if (tid == 0) atomicExch(&g_kda_device_error, 5);
+        return true;
+      }
+      return false;
+    };
+
+    // ---- E1a: dT (64 x 64, lanes 0-15): dbeta_T[j] = sum_i dT_ij A_ij, dA = dT diag(beta)
+    ok = tc::mbar_wait(mb + 2, 0);
+    if (fail_if(!ok)) { ok = false; break; }
     tc::fence_after_sync();
+    {
+      float a0[8], a1[8];
+      tc::tmem_ld8_async(trow + 128 + 16 * qd, a0);
+      tc::tmem_ld8_async(trow + 128 + 16 * qd + 8, a1);
+      tc::tmem_wait8(a0);
+      tc::tmem_wait8(a1);
+      auto pass = [&](float (&acc)[8], int hb) {
+        float av[8], cs[8], bv[8];
+        const int c8 = (16 * qd + hb) >> 3;
+        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::AT + 2 * sw64_chunk(r, c8)), av);
+        ld8f(beta + 16 * qd + hb, bv);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          cs[v] = acc[v] * av[v];
+          acc[v] *= bv[v];
+        }
+        if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DA + 2 * sw64_chunk(r, c8)) = pack8(acc);
+        const float dbt = half_reduce_scatter8(cs);
+        if (hh == 0 && (lane & 1) == 0) reinterpret_cast<float*>(smem + S::DBT)[s * 64 + 16 * qd + hb + (lane >> 1)] = dbt;
+      };
+      pass(a0, 0);
+      pass(a1, 8);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G3: X = dA A^T (unit 3)
+      tc::fence_after_sync();
+      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 192, kdesc(S::DA, ks), kdesc(S::AT, ks), idKK, ks > 0);
+      tc::mma_commit(mb + 4);
+      *issued = 0x1Fu;
+    }
+
+    // ---- E1b (while G3 runs): dv out; dk and dGam from dKe and the state-pass tiles
     // the gate logits and the gate backward's vectors, for the tail (dE / dW are dead)
     {
       bf16* gre = reinterpret_cast<bf16*>(smem + S::GRE);
@@ -437,6 +483,8 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         cp_async4(gbv + 2 * D, P.in.A_log + h);
       cp_async_commit();
     }
+    ok = tc::mbar_wait(mb + 1, 0);
+    if (fail_if(!ok)) { ok = false; break; }
     {
       bf16* dvrow = P.dv + ((size_t)(pos.t0 + r) * H + h) * D + c0;
       const bf16* tq = reinterpret_cast<const bf16*>(smem + S::DQT);
@@ -446,10 +494,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {  // two 8-column passes
-        float acc[8];
-        tc::tmem_ld8(trow + 0 + 16 * qd + hb, acc);  // dv
-        if (r < nv) *reinterpret_cast<bf16x8*>(dvrow + hb) = pack8(acc);
-        tc::tmem_ld8(trow + 64 + 16 * qd + hb, acc);  // dKe
+        float dv8[8], acc[8];
+        tc::tmem_ld8_async(trow + 0 + 16 * qd + hb, dv8);   // dv
+        tc::tmem_ld8_async(trow + 64 + 16 * qd + hb, acc);  // dKe
         float gq[8], gk[8], qa[8], ka[8], kd[8], colsum[8], g8[8];
         const int c8 = (c0 + hb) >> 3;
         unpack8(*reinterpret_cast<const bf16x8*>(tq + acc64_off(r, c0 + hb)), gq);
@@ -461,6 +508,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         ld8f(erp + hb, erv);
         ld8f(ecp + hb, ecv);
         ld8f(rvp + hb, rvv);
+        tc::tmem_wait8(dv8);
+        tc::tmem_wait8(acc);
+        if (r < nv) *reinterpret_cast<bf16x8*>(dvrow + hb) = pack8(dv8);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const int u = hb + v;
@@ -476,100 +526,133 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         const float cs = half_reduce_scatter8(colsum);
         if ((lane & 1) == 0) reinterpret_cast<float*>(smem + S::COLS)[s * D + c0 + hb + ((lane & 15) >> 1)] = cs;
       }
-      // dT (64 x 64, lanes 0-15): dbeta_T[j] = sum_i dT_ij A_ij, dA = dT diag(beta)
-#pragma unroll
-      for (int hb = 0; hb < 16; hb += 8) {
-        float acc[8], av[8], cs[8], bv[8];
-        tc::tmem_ld8(trow + 128 + 16 * qd + hb, acc);
-        const int c8 = (16 * qd + hb) >> 3;
-        unpack8(*reinterpret_cast<const bf16x8*>(smem + S::AT + 2 * sw64_chunk(r, c8)), av);
-        ld8f(beta + 16 * qd + hb, bv);
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          cs[v] = acc[v] * av[v];
-          acc[v] *= bv[v];
-        }
-        if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DA + 2 * sw64_chunk(r, c8)) = pack8(acc);
-        const float dbt = half_reduce_scatter8(cs);
-        if (hh == 0 && (lane & 1) == 0) reinterpret_cast<float*>(smem + S::DBT)[s * 64 + 16 * qd + hb + (lane >> 1)] = dbt;
-      }
-    }
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {  // G3: X = dA A^T (unit 3)
-      tc::fence_after_sync();
-      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 192, kdesc(S::DA, ks), kdesc(S::AT, ks), idKK, ks > 0);
-      tc::mma_commit(mb + 4);
-      *issued = 0x1Fu;
     }
 
-    // row sides: dX += af (P_I + sum_J<I c'_IJ P_J), dGam += rowop o (...)
+    // row sides: dX += af (P_I + sum_J<I c'_IJ P_J), dGam += rowop o (...); the block's
+    // accumulator slices load together (one wait)
     auto row_side = [&](uint32_t unit0, int rowop, float (&dx)[16]) {
       const float* cpb = reinterpret_cast<const float*>(smem + S::CP) + c0;
-      float g16[16];
-      ld_dg16(dgb, r, c0, g16);
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {
-        float out[8], pj[8], ro[8];
-        tc::tmem_ld8(trow + unit0 + 64 * s + 16 * qd + hb, out);
-        for (int J = 0; J < s; ++J) {
-          float cp[8];
-          tc::tmem_ld8(trow + unit0 + 64 * J + 16 * qd + hb, pj);
-          ld8f(cpb + pair_index(s, J) * D + hb, cp);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) out[v] = fmaf(cp[v], pj[v], out[v]);
-        }
+        float out[8], p0[8], p1[8], p2[8];
+        const uint32_t col = trow + unit0 + 16 * qd + hb;
+        tc::tmem_ld8_async(col + 64 * s, out);
+        if (s > 0) tc::tmem_ld8_async(col + 0, p0);
+        if (s > 1) tc::tmem_ld8_async(col + 64, p1);
+        if (s > 2) tc::tmem_ld8_async(col + 128, p2);
+        float ro[8], g8[8], cp[8];
         unpack8(*reinterpret_cast<const bf16x8*>(smem + rowop + 2 * sw64_chunk(r, (c0 + hb) >> 3)), ro);
+        {
+          const float4 a = *dg_chunk(dgb, r, c0 + hb), b = *dg_chunk(dgb, r, c0 + hb + 4);
+          g8[0] = a.x; g8[1] = a.y; g8[2] = a.z; g8[3] = a.w; g8[4] = b.x; g8[5] = b.y; g8[6] = b.z; g8[7] = b.w;
+        }
+        tc::tmem_wait8(out);
+        if (s > 0) {
+          tc::tmem_wait8(p0);
+          ld8f(cpb + pair_index(s, 0) * D + hb, cp);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) out[v] = fmaf(cp[v], p0[v], out[v]);
+        }
+        if (s > 1) {
+          tc::tmem_wait8(p1);
+          ld8f(cpb + pair_index(s, 1) * D + hb, cp);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) out[v] = fmaf(cp[v], p1[v], out[v]);
+        }
+        if (s > 2) {
+          tc::tmem_wait8(p2);
+          ld8f(cpb + pair_index(s, 2) * D + hb, cp);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) out[v] = fmaf(cp[v], p2[v], out[v]);
+        }
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           dx[hb + v] = fmaf(af[hb + v], out[v], dx[hb + v]);
-          g16[hb + v] = fmaf(ro[v], out[v], g16[hb + v]);
+          g8[v] = fmaf(ro[v], out[v], g8[v]);
         }
+        st_dg8(dgb, r, c0 + hb, g8);
       }
-      st_dg16(dgb, r, c0, g16);
     };
     // column sides: tot = R_I + rev_I sum_{Ib > I} c_{Ib,I} R_Ib; then dk += tot / af
     // (the diagonal's 1/af and the off-diagonal bf = rev_I / af at once), dGam -= Kd o tot
     auto column_side = [&](uint32_t unit0) {
       const float* rvp = reinterpret_cast<const float*>(smem + S::REV) + s * D + c0;
       const float* ccb = reinterpret_cast<const float*>(smem + S::CC) + c0;
-      float g16[16];
-      ld_dg16(dgb, r, c0, g16);
 #pragma unroll
       for (int hb = 0; hb < 16; hb += 8) {
-        float tot[8], R[8], kd[8];
-        tc::tmem_ld8(trow + unit0 + 64 * s + 16 * qd + hb, tot);  // diagonal block: R_I
-        if (s < 3) {
-          float off[8], rv[8];
-#pragma unroll
-          for (int v = 0; v < 8; ++v) off[v] = 0.f;
-          for (int Ib = s + 1; Ib < 4; ++Ib) {
-            float cc[8];
-            tc::tmem_ld8(trow + unit0 + 64 * Ib + 16 * qd + hb, R);
-            ld8f(ccb + pair_index(Ib, s) * D + hb, cc);
-#pragma unroll
-            for (int v = 0; v < 8; ++v) off[v] = fmaf(cc[v], R[v], off[v]);
-          }
-          ld8f(rvp + hb, rv);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) tot[v] = fmaf(rv[v], off[v], tot[v]);
-        }
+        float tot[8], r1[8], r2[8], r3[8];
+        const uint32_t col = trow + unit0 + 16 * qd + hb;
+        tc::tmem_ld8_async(col + 64 * s, tot);  // diagonal block: R_I
+        if (s < 3) tc::tmem_ld8_async(col + 192, r3);
+        if (s < 2) tc::tmem_ld8_async(col + 128, r2);
+        if (s < 1) tc::tmem_ld8_async(col + 64, r1);
+        float kd[8], g8[8], cc[8], off[8];
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::KD + 2 * sw64_chunk(r, (c0 + hb) >> 3)), kd);
+        {
+          const float4 a = *dg_chunk(dgb, r, c0 + hb), b = *dg_chunk(dgb, r, c0 + hb + 4);
+          g8[0] = a.x; g8[1] = a.y; g8[2] = a.z; g8[3] = a.w; g8[4] = b.x; g8[5] = b.y; g8[6] = b.z; g8[7] = b.w;
+        }
+        tc::tmem_wait8(tot);
+        if (s < 3) {
+          tc::tmem_wait8(r3);
+          ld8f(ccb + pair_index(3, s) * D + hb, cc);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) off[v] = cc[v] * r3[v];
+          if (s < 2) {
+            tc::tmem_wait8(r2);
+            ld8f(ccb + pair_index(2, s) * D + hb, cc);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) off[v] = fmaf(cc[v], r2[v], off[v]);
+          }
+          if (s < 1) {
+            tc::tmem_wait8(r1);
+            ld8f(ccb + pair_index(1, s) * D + hb, cc);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) off[v] = fmaf(cc[v], r1[v], off[v]);
+          }
+          ld8f(rvp + hb, cc);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) tot[v] = fmaf(cc[v], off[v], tot[v]);
+        }
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           dk[hb + v] = fmaf(rcp(af[hb + v]), tot[v], dk[hb + v]);
-          g16[hb + v] = fmaf(-kd[v], tot[v], g16[hb + v]);
+          g8[v] = fmaf(-kd[v], tot[v], g8[v]);
         }
+        st_dg8(dgb, r, c0 + hb, g8);
       }
-      st_dg16(dgb, r, c0, g16);
     };
 
-    // ---- E2: row side through M
-    ok = tc::mbar_wait(mb + 3, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    // ---- E3: X -> bf16 tile
+    ok = tc::mbar_wait(mb + 4, 0);
+    if (fail_if(!ok)) { ok = false; break; }
     tc::fence_after_sync();
-    {  // dq = dQt 2^Gam, then the row side through M adds to it
+    {
+      float x0[8], x1[8];
+      tc::tmem_ld8_async(trow + 192 + 16 * qd, x0);
+      tc::tmem_ld8_async(trow + 192 + 16 * qd + 8, x1);
+      tc::tmem_wait8(x0);
+      tc::tmem_wait8(x1);
+      if (hh == 0) {
+        *reinterpret_cast<bf16x8*>(smem + S::XS + 2 * sw64_chunk(r, (16 * qd) >> 3)) = pack8(x0);
+        *reinterpret_cast<bf16x8*>(smem + S::XS + 2 * sw64_chunk(r, (16 * qd + 8) >> 3)) = pack8(x1);
+      }
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G5: -dL = A^T X (unit 0; dv was read in E1b)
+      tc::fence_after_sync();
+      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 0, mdesc(S::AT, ks), mdesc(S::XS, ks), idMM, ks > 0);
+      tc::mma_commit(mb + 6);
+      *issued = 0x5Fu;
+    }
+
+    // ---- E2 (while G5 runs): dq = dQt 2^Gam + row side through M; dq out
+    ok = tc::mbar_wait(mb + 3, 0);
+    if (fail_if(!ok)) { ok = false; break; }
+    tc::fence_after_sync();
+    {
       const bf16* tq = reinterpret_cast<const bf16*>(smem + S::DQT);
       const float* erp = reinterpret_cast<const float*>(smem + S::ER) + s * D + c0;
 #pragma unroll
@@ -582,7 +665,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       }
     }
     row_side(256, S::QA, dq);
-    if (r < nv) st_global16(P.dq_hat + ((size_t)(pos.t0 + r) * H + h) * D + c0, dq);  // dq is complete
+    if (r < nv) st_global16(P.dq_hat + ((size_t)(pos.t0 + r) * H + h) * D + c0, dq);
     tc::fence_before_sync();
     __syncthreads();
     if (tid == 0) {  // G4: column side through M, R_I = dM[I, :]^T Qa[I] (units 4 + I)
@@ -592,46 +675,23 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DM, I),
                        mdesc(S::QA + hf * 8192, I), idMM, false);
       tc::mma_commit(mb + 5);
-      *issued = 0x3Fu;
-    }
-
-    // ---- E3: X -> bf16 tile
-    ok = tc::mbar_wait(mb + 4, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
-    tc::fence_after_sync();
-#pragma unroll
-    for (int hb = 0; hb < 16; hb += 8) {
-      float acc[8];
-      tc::tmem_ld8(trow + 192 + 16 * qd + hb, acc);
-      if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::XS + 2 * sw64_chunk(r, (16 * qd + hb) >> 3)) = pack8(acc);
-    }
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {  // G5: -dL = A^T X (unit 0)
-      tc::fence_after_sync();
-      for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 0, mdesc(S::AT, ks), mdesc(S::XS, ks), idMM, ks > 0);
-      tc::mma_commit(mb + 6);
       *issued = 0x7Fu;
     }
 
-    // ---- E5: column side through M (runs while G5 computes)
-    ok = tc::mbar_wait(mb + 5, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
-    tc::fence_after_sync();
-    column_side(256);
-
     // ---- E4: dL = -(A^T X), strictly lower: dbeta_L = rowsum(dL o L'), dL' = diag(beta) dL
     ok = tc::mbar_wait(mb + 6, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    if (fail_if(!ok)) { ok = false; break; }
     tc::fence_after_sync();
     {
       float rs = 0.f;
       const float br = beta[r];
-#pragma unroll
-      for (int hb = 0; hb < 16; hb += 8) {
-        float acc[8], lp[8];
-        tc::tmem_ld8(trow + 0 + 16 * qd + hb, acc);
+      float l0[8], l1[8];
+      tc::tmem_ld8_async(trow + 0 + 16 * qd, l0);
+      tc::tmem_ld8_async(trow + 0 + 16 * qd + 8, l1);
+      tc::tmem_wait8(l0);
+      tc::tmem_wait8(l1);
+      auto pass = [&](float (&acc)[8], int hb) {
+        float lp[8];
         const int c8 = (16 * qd + hb) >> 3;
         unpack8(*reinterpret_cast<const bf16x8*>(smem + S::LPT + 2 * sw64_chunk(r, c8)), lp);
 #pragma unroll
@@ -641,21 +701,33 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           acc[v] = x * br;
         }
         if (hh == 0) *reinterpret_cast<bf16x8*>(smem + S::DLP + 2 * sw64_chunk(r, c8)) = pack8(acc);
-      }
+      };
+      pass(l0, 0);
+      pass(l1, 8);
       if (hh == 0) reinterpret_cast<float*>(smem + S::DBL)[qd * 64 + r] = rs;
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0) {  // G6: row side through L', P_J = dL'[:, J] Kd[J] (units J)
       tc::fence_after_sync();
-      // G6: row side through L', P_J = dL'[:, J] Kd[J] (units J)
       for (int J = 0; J < 4; ++J)
         for (int hf = 0; hf < 2; ++hf)
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 64 * J, kdesc(S::DLP, J), mdesc(S::KD + hf * 8192, J),
                        idKM, false);
       tc::mma_commit(mb + 7);
-      // G7: column side through L', R_I = dL'[I, :]^T Ka[I] (units 4 + I)
+      *issued = 0xFFu;
+    }
+
+    // ---- E5 (while G6 runs): column side through M
+    ok = tc::mbar_wait(mb + 5, 0);
+    if (fail_if(!ok)) { ok = false; break; }
+    tc::fence_after_sync();
+    column_side(256);
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {  // G7: column side through L', R_I = dL'[I, :]^T Ka[I] (units 4 + I)
+      tc::fence_after_sync();
       for (int I = 0; I < 4; ++I)
         for (int hf = 0; hf < 2; ++hf)
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DLP, I),
@@ -666,11 +738,11 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 
     // ---- E6: row side through L'; E7: column side through L'
     ok = tc::mbar_wait(mb + 7, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    if (fail_if(!ok)) { ok = false; break; }
     tc::fence_after_sync();
     row_side(0, S::KA, dk);
     ok = tc::mbar_wait(mb + 8, 0);
-    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 5); break; }
+    if (fail_if(!ok)) { ok = false; break; }
     tc::fence_after_sync();
     column_side(256);
   }
