@@ -105,7 +105,8 @@ struct BwdIntraSmem {
 };
 
 // Bytes of the products arriving by bulk copy at the start.
-constexpr uint32_t BWD_PRODUCT_BYTES = 3 * BwdIntraSmem::T128 + 64 * LDG * 4 + 64 * 4 + 2 * BwdIntraSmem::T64;
+constexpr uint32_t BWD_DECAY_BYTES = 64 * LDG * 4 + 64 * 4;                      // Gam, beta
+constexpr uint32_t BWD_TILE_BYTES = 3 * BwdIntraSmem::T128 + 2 * BwdIntraSmem::T64;  // q, k, v, A, L'
 
 __device__ __forceinline__ uint4 lds_chunk(const unsigned char* tile, int r, int c8) {
   return *reinterpret_cast<const uint4*>(tile + 2 * sw64_chunk(r, c8));
@@ -225,8 +226,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t cidx = (size_t)c * H + h;
   const size_t tix = tile_index(P.seq, c, h);
-  uint64_t* mb = reinterpret_cast<uint64_t*>(smem + S::MISC);  // 0 products, 1 dQt/dKbar, 2..8 MMA groups G1..G7
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mb + 9);
+  // mbarriers: 0 decay cumsum and beta, 1 dQt/dKbar, 2..8 MMA groups G1..G7, 9 product tiles
+  uint64_t* mb = reinterpret_cast<uint64_t*>(smem + S::MISC);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mb + 10);
   volatile uint32_t* issued = tslot + 1;  // bit i: mbarrier i has work in flight
   float* gam = reinterpret_cast<float*>(smem + S::GAM);
   float* beta = reinterpret_cast<float*>(smem + S::BETA);
@@ -236,7 +238,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   }
   if (warp == 0) tc::tmem_alloc(tslot, 512);
   if (tid == 0) {
-    for (int i = 0; i < 9; ++i) tc::mbar_init(mb + i, 1);
+    for (int i = 0; i < 10; ++i) tc::mbar_init(mb + i, 1);
     tc::fence_mbar_init();
     *issued = 0u;
   }
@@ -264,15 +266,17 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   const uint32_t tbase = *tslot;
   if (tid == 0) {
     constexpr uint32_t TB = S::T128, GB = 64 * LDG * 4, BB = 64 * 4, AB = S::T64;
-    tc::mbar_expect_tx(mb + 0, BWD_PRODUCT_BYTES);
-    tc::bulk_g2s(smem + S::QN, P.QN + tix * TILE64_ELEMS, TB, mb + 0);
-    tc::bulk_g2s(smem + S::KN, P.KN + tix * TILE64_ELEMS, TB, mb + 0);
-    tc::bulk_g2s(smem + S::V, P.VN + tix * TILE64_ELEMS, TB, mb + 0);
+    // the decay cumsum first: the channel vectors and decay factors need only it
+    tc::mbar_expect_tx(mb + 0, BWD_DECAY_BYTES);
     tc::bulk_g2s(gam, P.GM + tix * 64 * LDG, GB, mb + 0);
     tc::bulk_g2s(beta, P.BT + tix * 64, BB, mb + 0);
-    tc::bulk_g2s(smem + S::AT, P.A + tix * TILE64N64_ELEMS, AB, mb + 0);
-    tc::bulk_g2s(smem + S::LPT, P.LP + tix * TILE64N64_ELEMS, AB, mb + 0);
-    *issued = 1u;
+    tc::mbar_expect_tx(mb + 9, BWD_TILE_BYTES);
+    tc::bulk_g2s(smem + S::QN, P.QN + tix * TILE64_ELEMS, TB, mb + 9);
+    tc::bulk_g2s(smem + S::KN, P.KN + tix * TILE64_ELEMS, TB, mb + 9);
+    tc::bulk_g2s(smem + S::V, P.VN + tix * TILE64_ELEMS, TB, mb + 9);
+    tc::bulk_g2s(smem + S::AT, P.A + tix * TILE64N64_ELEMS, AB, mb + 9);
+    tc::bulk_g2s(smem + S::LPT, P.LP + tix * TILE64N64_ELEMS, AB, mb + 9);
+    *issued = 0x201u;
   }
 
   // epilogue mapping: rows 16 s .. 16 s + 15 (block I = s), 16 columns from c0
@@ -300,6 +304,42 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   bool ok = true;
   for (int once = 0; once < 1; ++once) {
     ok = tc::mbar_wait(mb + 0, 0);
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 7); break; }
+
+    // ---- from the decay cumsum alone (the product tiles are still arriving)
+    {
+      // per-pair and per-sub-chunk channel vectors
+      float* cpv = reinterpret_cast<float*>(smem + S::CP);
+      float* ccv = reinterpret_cast<float*>(smem + S::CC);
+      for (int i = tid; i < 6 * D; i += blockDim.x) {
+        const int p = i / D, d = i - p * D;
+        const int I = p >= 3 ? 3 : (p >= 1 ? 2 : 1);
+        const int Jp = p - pair_index(I, 0);
+        cpv[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp) * LDG + d]);
+        ccv[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
+      }
+      {
+        float* erw = reinterpret_cast<float*>(smem + S::ER);
+        float* ecw = reinterpret_cast<float*>(smem + S::EC);
+        float* rvw = reinterpret_cast<float*>(smem + S::REV);
+        const int Jp = tid >> 7, d = tid & 127;
+        const float gr = gam[(16 * Jp) * LDG + d], ge = gam[(16 * Jp + 15) * LDG + d];
+        erw[tid] = ex2(gr);
+        ecw[tid] = ex2(gam[63 * LDG + d] - ge);
+        rvw[tid] = ex2(ge - gr);
+      }
+      // the decay factor of this thread's epilogue elements
+#pragma unroll
+      for (int u = 0; u < 16; u += 4) {
+        const float4 g = *reinterpret_cast<const float4*>(gam + r * LDG + c0 + u);
+        const float4 g0 = *reinterpret_cast<const float4*>(gam + (16 * s) * LDG + c0 + u);
+        af[u] = ex2(g.x - g0.x);
+        af[u + 1] = ex2(g.y - g0.y);
+        af[u + 2] = ex2(g.z - g0.z);
+        af[u + 3] = ex2(g.w - g0.w);
+      }
+    }
+    ok = tc::mbar_wait(mb + 9, 0);
     if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 7); break; }
 
     // ---- operands (strip mapping: tokens 2 tg, 2 tg + 1, channels 8 cg .. +7)
@@ -354,36 +394,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         }
         *reinterpret_cast<bf16x8*>(smem + S::TT + 2 * sw64_chunk(k, c8)) = pack8(tv);
       }
-      // per-pair and per-sub-chunk channel vectors
-      float* cpv = reinterpret_cast<float*>(smem + S::CP);
-      float* ccv = reinterpret_cast<float*>(smem + S::CC);
-      for (int i = tid; i < 6 * D; i += blockDim.x) {
-        const int p = i / D, d = i - p * D;
-        const int I = p >= 3 ? 3 : (p >= 1 ? 2 : 1);
-        const int Jp = p - pair_index(I, 0);
-        cpv[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp) * LDG + d]);
-        ccv[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
-      }
-      {
-        float* erw = reinterpret_cast<float*>(smem + S::ER);
-        float* ecw = reinterpret_cast<float*>(smem + S::EC);
-        float* rvw = reinterpret_cast<float*>(smem + S::REV);
-        const int Jp = tid >> 7, d = tid & 127;
-        const float gr = gam[(16 * Jp) * LDG + d], ge = gam[(16 * Jp + 15) * LDG + d];
-        erw[tid] = ex2(gr);
-        ecw[tid] = ex2(gam[63 * LDG + d] - ge);
-        rvw[tid] = ex2(ge - gr);
-      }
-      // the decay factor of this thread's epilogue elements
-#pragma unroll
-      for (int u = 0; u < 16; u += 4) {
-        const float4 g = *reinterpret_cast<const float4*>(gam + r * LDG + c0 + u);
-        const float4 g0 = *reinterpret_cast<const float4*>(gam + (16 * s) * LDG + c0 + u);
-        af[u] = ex2(g.x - g0.x);
-        af[u + 1] = ex2(g.y - g0.y);
-        af[u + 2] = ex2(g.z - g0.z);
-        af[u + 3] = ex2(g.w - g0.w);
-      }
     }
     cp_async_wait<0>();      // dE, dW, dM
     tc::fence_async_smem();  // operand tiles -> tensor cores; the decay region -> the bulk copy below
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       for (int ks = 0; ks < 8; ++ks) tc::mma_bf16(tbase + 128, kdesc(S::DE, ks), kdesc(S::V, ks), idKK, ks > 0);
       for (int ks = 0; ks < 8; ++ks) tc::mma_bf16(tbase + 128, kdesc(S::DW, ks), kdesc(S::KE, ks), idKK, true);
       tc::mma_commit(mb + 2);
-      *issued = 0xFu;
+      *issued = 0x20Fu;
     }
 
     // Order of the epilogues: the chain G1 -> dA -> G3 -> X -> G5 -> dL' -> G6/G7 first,
@@ -462,7 +472,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       tc::fence_after_sync();
       for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 192, kdesc(S::DA, ks), kdesc(S::AT, ks), idKK, ks > 0);
       tc::mma_commit(mb + 4);
-      *issued = 0x1Fu;
+      *issued = 0x21Fu;
     }
 
     // ---- E1b (while G3 runs): dv out; dk and dGam from dKe and the state-pass tiles
@@ -645,7 +655,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
       tc::fence_after_sync();
       for (int ks = 0; ks < 4; ++ks) tc::mma_bf16(tbase + 0, mdesc(S::AT, ks), mdesc(S::XS, ks), idMM, ks > 0);
       tc::mma_commit(mb + 6);
-      *issued = 0x5Fu;
+      *issued = 0x25Fu;
     }
 
     // ---- E2 (while G5 runs): dq = dQt 2^Gam + row side through M; dq out
@@ -675,7 +685,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DM, I),
                        mdesc(S::QA + hf * 8192, I), idMM, false);
       tc::mma_commit(mb + 5);
-      *issued = 0x7Fu;
+      *issued = 0x27Fu;
     }
 
     // ---- E4: dL = -(A^T X), strictly lower: dbeta_L = rowsum(dL o L'), dL' = diag(beta) dL
@@ -716,7 +726,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 64 * J, kdesc(S::DLP, J), mdesc(S::KD + hf * 8192, J),
                        idKM, false);
       tc::mma_commit(mb + 7);
-      *issued = 0xFFu;
+      *issued = 0x2FFu;
     }
 
     // ---- E5 (while G6 runs): column side through M
@@ -733,7 +743,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
           tc::mma_bf16(tbase + ((uint32_t)(16 * hf) << 16) + 256 + 64 * I, mdesc(S::DLP, I),
                        mdesc(S::KA + hf * 8192, I), idMM, false);
       tc::mma_commit(mb + 8);
-      *issued = 0x1FFu;
+      *issued = 0x3FFu;
     }
 
     // ---- E6: row side through L'; E7: column side through L'
@@ -750,7 +760,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   if (!ok) {
     // let what is in flight finish (bounded), then release TMEM and leave
     const uint32_t iss = *issued;
-    for (int i = 0; i < 9; ++i)
+    for (int i = 0; i < 10; ++i)
       if (iss & (1u << i)) tc::mbar_wait(mb + i, 0, 1u << 22);
     cp_async_wait<0>();
     tc::fence_before_sync();
