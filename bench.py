@@ -60,11 +60,11 @@ CPU_SAMPLE_TOKENS = 1024         # tokens of the timed CPU sample (both CPU figu
 # Algorithmic HBM bytes per token-head of each kernel (reads + writes of its
 # interface tensors, each once; bf16 activations, fp32 per-chunk vectors).
 KERNEL_BYTES_PER_TOKEN_HEAD = {
-    "fwd_intra": 1026 + 2700,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C, A (fp32 64x64/chunk) and
-                                # the saved products q_hat,k_hat,v (bf16), Gam (fp32), beta out
+    "fwd_intra": 1026 + 2700,   # q,k,v,g,beta in; W,U,Qt,Kbar,M,2^Gam_C, A and L' (bf16 64x64 per chunk)
+                                # and the saved products q_hat,k_hat,v (bf16), Gam (fp32), beta out
     "fwd_state": 1160 + 1024,   # W,U,Qt,Kbar,M,2^Gam_C in; o, chunk states, v_new out
     "bwd_state": 1928 + 1160,   # W,Qt,Kbar,M,2^Gam_C,v_new,dO,chunk states in; dE,dQt,dW,dKbar,dM,dGam_C out
-    "bwd_intra": 2956 + 1042,   # saved products, g, A + dE,dW,dQt,dKbar,dM,dGam_C in;
+    "bwd_intra": 2956 + 1042,   # saved products, g, A, L' + dE,dW,dQt,dKbar,dM,dGam_C in;
                                 # dq_hat,dk_hat,dv,dg,dbeta,partials out
     "bwd_post": 1536 + 768,     # q,k,v and dq_hat,dk_hat,dv in; dq,dk,dv out
 }
@@ -82,8 +82,22 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
 # --warmup 3 --profile` (B=2: the per-launch traffic scales with the token-heads
 # processed).
 NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
-    "fwd_intra": 3299.9, "fwd_state": 1850.0, "bwd_state": 2824.1, "bwd_intra": 3828.0, "bwd_post": 2192.3,
+    "fwd_intra": 3322.3, "fwd_state": 1882.8, "bwd_state": 2844.1, "bwd_intra": 3847.0, "bwd_post": 2221.6,
 }
+# Hash of the kernel sources (sophia_b200/csrc/*.cu, *.cuh) that capture ran on: the
+# line says whether the traffic figures describe the kernels being timed.
+NCU_SOURCE_HASH = "001ec4bcd229231a"
+
+
+def kernel_source_hash() -> str:
+    import glob
+    import hashlib
+    h = hashlib.sha256()
+    for f in sorted(glob.glob(os.path.join(ROOT, "sophia_b200", "csrc", "*"))):
+        if f.endswith((".cu", ".cuh")):
+            with open(f, "rb") as fh:
+                h.update(fh.read())
+    return h.hexdigest()[:16]
 
 
 def parse():
@@ -378,6 +392,7 @@ def bench_ours(a, rank, world, local_rank):
     traffic = None
     if dom in NCU_DRAM_BYTES_PER_TOKEN_HEAD:
         traffic = round(NCU_DRAM_BYTES_PER_TOKEN_HEAD[dom] * th)
+    traffic_current = kernel_source_hash() == NCU_SOURCE_HASH
     # per-kernel roofline of the whole step: sum_k max(F_k/P, B_k/BW)
     roof_ms = 0.0
     for k, bpt in KERNEL_BYTES_PER_TOKEN_HEAD.items():
@@ -392,6 +407,8 @@ def bench_ours(a, rank, world, local_rank):
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "traffic_source": "ncu dram bytes at B=2 scaled to this launch; current kernel sources: "
+                                       + ("yes" if traffic_current else "no (stale)"),
                      "peak_source": src,
                      "per_kernel_roofline_ms": round(roof_ms, 4),
                      "per_kernel_roofline_frac": round(roof_ms / (ms_prof / a.steps), 4),

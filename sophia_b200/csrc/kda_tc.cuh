@@ -114,7 +114,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(mbar)), "r"(bytes)
                : "memory");
 }
-// Tiled TMA load of one box of a rank-3 tensor map (no swizzle, no multicast)
+// Tiled TMA load of one box of a rank-3 tensor map (no swizzle; this CTA only)
 // into shared memory; out-of-range elements arrive as zeros.  The map lives in
 // kernel-parameter space (__grid_constant__); the innermost coordinate c0 must
 // be a multiple of 16 bytes' worth of elements.
