@@ -242,10 +242,11 @@ int kda_b200_timing_read(int max_kernels, const char** names, int* launches, flo
  * until the process exits.
  *   - A call whose kda_b200_fwd_workspace_bytes(B*T, H, N, packed, 0) exceeds
  *     that size returns KDA_ERR_INVALID (no kernel runs).
- *   - The first call on a device does a one-time set-up: it resolves the
- *     array's device address on the current device (cudaGetSymbolAddress);
- *     later calls reuse it.  Make that first call before any stream capture
- *     begins.
+ *   - Every call resolves the array's device address on the current device
+ *     (cudaGetSymbolAddress, which the CUDA runtime keeps per context), so the
+ *     address stays valid across cudaDeviceReset and context re-creation.  The
+ *     first call on a device may load the module: make it before any stream
+ *     capture begins.
  *   - All calls share the one array and it keeps the last call's contents;
  *     nothing in it has to start at zero (every call writes what it reads).
  *     Calls that overlap on the GPU (other streams, other host threads) race on

@@ -963,8 +963,6 @@ int kda_b200_fwd_noalloc(const void* q, const void* k, const void* v, const void
                          const float* A_log, const float* dt_bias, const float* conv_q, const float* conv_k,
                          const float* conv_v, const float* h0, const int32_t* cu_seqlens, int B, int T, int H,
                          int D_, int N, float scale, float lower_bound, void* o, float* ht, void* stream) {
-  static std::mutex mu;
-  static void* dev_ptr[128] = {nullptr};
   if (B < 1 || T < 0 || H < 1 || N < 1) return fail(KDA_ERR_INVALID, "B >= 1, T >= 0, H >= 1 and N >= 1 are required");
   const size_t need = kda_b200_fwd_workspace_bytes((int64_t)B * T, H, N, cu_seqlens != nullptr, 0);
   if (need > KDA_NOALLOC_SCRATCH_BYTES)
@@ -972,22 +970,12 @@ int kda_b200_fwd_noalloc(const void* q, const void* k, const void* v, const void
                                      " bytes of scratch but the static scratch holds " +
                                      std::to_string(KDA_NOALLOC_SCRATCH_BYTES) +
                                      "; call kda_b200_fwd with a caller-provided workspace instead");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(KDA_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-  if (dev < 0 || dev >= 128) return fail(KDA_ERR_INVALID, "device ordinal out of range");
+  // The address is resolved on every call (the runtime keeps it per context), so it
+  // stays valid across cudaDeviceReset and context re-creation.
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!dev_ptr[dev]) {
-      // set-up, once per device, with that device current
-      e = cudaGetSymbolAddress(&scratch, kda_noalloc_scratch);
-      if (e != cudaSuccess || !scratch)
-        return fail(KDA_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
-      dev_ptr[dev] = scratch;
-    }
-    scratch = dev_ptr[dev];
-  }
+  const cudaError_t e = cudaGetSymbolAddress(&scratch, kda_noalloc_scratch);
+  if (e != cudaSuccess || !scratch)
+    return fail(KDA_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
   return kda_b200_fwd(q, k, v, g, beta, A_log, dt_bias, conv_q, conv_k, conv_v, h0, cu_seqlens, B, T, H, D_, N, scale,
                       lower_bound, o, ht, nullptr, 0, scratch, KDA_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -72,3 +72,32 @@ def test_noalloc_rejects_problems_beyond_the_static_scratch():
     rc = lib.kda_b200_fwd_noalloc(*args, x["q"].data_ptr(), None, torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.KDA_ERR_INVALID
     assert b"static scratch" in lib.kda_b200_last_error()
+
+
+def test_noalloc_packed_forward_matches_workspace_forward_twice():
+    # B = 1 with cu_seqlens over three unequal documents: the chunk table and the
+    # chunk-to-sequence map are carved from the static scratch as well
+    from sophia_b200 import _lib
+    lib = _lib.load()
+    H, bounds = 4, [0, 37, 150, 290]
+    N, T = len(bounds) - 1, bounds[-1]
+    x = _inputs(1, T, H, seed=7)
+    x["h0"] = (torch.randn(N, H, 128, 128, device="cuda", generator=torch.Generator(device="cuda").manual_seed(8))
+               * 0.1)
+    cu = torch.tensor(bounds, device="cuda", dtype=torch.int32)
+    args = _args(x, 1, T, H)
+    args[11], args[16] = cu.data_ptr(), N
+    stream = torch.cuda.current_stream().cuda_stream
+    o_ref = torch.empty_like(x["q"])
+    ht_ref = torch.empty(N, H, 128, 128, device="cuda")
+    ws = torch.empty(lib.kda_b200_fwd_workspace_bytes(T, H, N, 1, 0), device="cuda", dtype=torch.uint8)
+    _lib.check(lib.kda_b200_fwd(*args, o_ref.data_ptr(), ht_ref.data_ptr(), None, 0, ws.data_ptr(), ws.numel(),
+                                stream))
+    for _ in range(2):
+        o = torch.full_like(x["q"], float("nan"))
+        ht = torch.full((N, H, 128, 128), float("nan"), device="cuda")
+        _lib.check(lib.kda_b200_fwd_noalloc(*args, o.data_ptr(), ht.data_ptr(), stream))
+        torch.cuda.synchronize()
+        _close(o, o_ref)
+        _close(ht, ht_ref)
+    assert _lib.device_error(reset=True) == 0
