@@ -337,9 +337,13 @@ struct F32BwdView {
   float *dqh_p, *dkh_p, *dal_p, *dbt_p, *dvh, *dcq, *dck, *dcv, *partA, *partB, *partW, *scratch;
 };
 
-// Persistent grid of the fp32 backward recurrence (two CTAs per SM); each CTA
-// owns one F32_SCRATCH_FLOATS slice of the scratch.
-int f32_bwd_ctas(int64_t items) { return (int)std::max<int64_t>(1, std::min<int64_t>(items, 2 * (int64_t)sm_count())); }
+// Persistent grid of the fp32 backward recurrence: up to four CTAs per SM (the
+// register limit of its 128-thread CTAs), so that up to 4 x SMs items run at once;
+// each CTA owns one F32_SCRATCH_FLOATS slice of the scratch.
+constexpr int F32_BWD_CTAS_PER_SM = 4;
+int f32_bwd_ctas(int64_t items) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>(items, F32_BWD_CTAS_PER_SM * (int64_t)sm_count()));
+}
 
 F32BwdView carve_f32_bwd(Carver& cv, int64_t TT, int H, int N, int64_t mc) {
   F32BwdView b;
@@ -786,7 +790,7 @@ int kda_b200_fwd_f32(const float* q, const float* k, const float* v, const float
   fp.total_tokens = pr.TT;
   {
     TimedLaunch tl(K_F32_FWD, st);
-    kda_f32_fwd_kernel<<<dim3(N, H, F32_GROUPS), 32, 0, st>>>(fp);
+    kda_f32_fwd_kernel<<<dim3(N, H, F32_FWD_GROUPS), 32, 0, st>>>(fp);
   }
   return launch_check("fp32 forward");
 }

@@ -11,8 +11,10 @@
 //                         taps are given), L2 norms (q times scale), decay
 //                         alpha = exp(lb * sigmoid(exp(A_log) (g + dt_bias))),
 //                         beta = sigmoid(b).  Lane l owns channels 4l..4l+3.
-//   kda_f32_fwd_kernel    one warp per (sequence, head, 32-column group); lane j
-//                         keeps column j of the 128x128 state in registers:
+//   kda_f32_fwd_kernel    one warp per (sequence, head, 16-column group); lanes
+//                         j and j + 16 keep rows 0-63 and 64-127 of column j of
+//                         the 128x128 state in registers (the row sums of the
+//                         two halves meet in one shuffle):
 //                           S <- diag(alpha) S; r = v - k^T S; S <- S + k (beta r)^T;
 //                           o = q^T S
 //                         and saves r, plus the state at every chunk start
@@ -45,7 +47,9 @@
 
 namespace kda {
 
-constexpr int F32_COLS = 32;                  // state columns per recurrence item
+constexpr int F32_COLS = 32;                  // state columns per backward recurrence item
+constexpr int F32_FWD_COLS = 16;              // state columns per forward warp (two lanes per column)
+constexpr int F32_FWD_GROUPS = D / F32_FWD_COLS;
 constexpr int F32_GROUPS = D / F32_COLS;      // column groups per (sequence, head)
 constexpr int F32_WARPS_PER_CTA = 4;          // chunks per CTA of the row kernels
 constexpr int F32_BWD_THREADS = 128;          // one thread per state row
@@ -165,16 +169,17 @@ struct F32FwdParams {
 
 __global__ void __launch_bounds__(32) kda_f32_fwd_kernel(F32FwdParams P) {
   __shared__ float4 sq[2][32], sk[2][32], sa[2][32];
-  const int n = blockIdx.x, h = blockIdx.y, lane = threadIdx.x, col = blockIdx.z * F32_COLS + lane, H = P.H;
+  const int n = blockIdx.x, h = blockIdx.y, lane = threadIdx.x, H = P.H;
+  const int col = blockIdx.z * F32_FWD_COLS + (lane & 15), r0 = 64 * (lane >> 4);  // column, first row
   const int bos = seq_bos(P.seq, n), eos = seq_eos(P.seq, n);
   if (bos < 0 || eos < bos || (long long)eos > P.total_tokens) {  // malformed cu_seqlens: touch nothing
     if (lane == 0) atomicExch(&g_kda_device_error, 3);
     return;
   }
   const size_t rowH = (size_t)H * D, stateoff = ((size_t)n * H + h) * D * D;
-  float S[D];
+  float S[64];  // rows r0 .. r0 + 63 of column col
 #pragma unroll
-  for (int i = 0; i < D; ++i) S[i] = P.h0 ? P.h0[stateoff + (size_t)i * D + col] : 0.f;
+  for (int i = 0; i < 64; ++i) S[i] = P.h0 ? P.h0[stateoff + (size_t)(r0 + i) * D + col] : 0.f;
   const int cbase = seq_chunk_base(P.seq, n);
   // register prefetch of the next token's vectors
   float4 nq = make_float4(0.f, 0.f, 0.f, 0.f), nk = nq, na = nq;
@@ -191,9 +196,9 @@ __global__ void __launch_bounds__(32) kda_f32_fwd_kernel(F32FwdParams P) {
   for (int t = bos; t < eos; ++t) {
     const int m = t - bos, buf = t & 1;
     if (P.ck && (m & (C - 1)) == 0) {
-      float* dst = P.ck + tile_index(P.seq, cbase + m / C, h) * (size_t)STATE_ELEMS + col;
+      float* dst = P.ck + tile_index(P.seq, cbase + m / C, h) * (size_t)STATE_ELEMS + (size_t)r0 * D + col;
 #pragma unroll
-      for (int i = 0; i < D; ++i) dst[(size_t)i * D] = S[i];
+      for (int i = 0; i < 64; ++i) dst[(size_t)i * D] = S[i];
     }
     sq[buf][lane] = nq;
     sk[buf][lane] = nk;
@@ -201,12 +206,12 @@ __global__ void __launch_bounds__(32) kda_f32_fwd_kernel(F32FwdParams P) {
     const float beta = nb, vx = nv;
     if (t + 1 < eos) fetch(t + 1);
     __syncwarp();
-    const float* qv = reinterpret_cast<const float*>(sq[buf]);
-    const float* kv = reinterpret_cast<const float*>(sk[buf]);
-    const float* av = reinterpret_cast<const float*>(sa[buf]);
+    const float* qv = reinterpret_cast<const float*>(sq[buf]) + r0;
+    const float* kv = reinterpret_cast<const float*>(sk[buf]) + r0;
+    const float* av = reinterpret_cast<const float*>(sa[buf]) + r0;
     float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-    for (int i = 0; i < D; i += 4) {
+    for (int i = 0; i < 64; i += 4) {
       S[i] *= av[i];
       S[i + 1] *= av[i + 1];
       S[i + 2] *= av[i + 2];
@@ -216,11 +221,13 @@ __global__ void __launch_bounds__(32) kda_f32_fwd_kernel(F32FwdParams P) {
       p2 = fmaf(kv[i + 2], S[i + 2], p2);
       p3 = fmaf(kv[i + 3], S[i + 3], p3);
     }
-    const float rr = vx - ((p0 + p1) + (p2 + p3));
+    float pr = (p0 + p1) + (p2 + p3);
+    pr += __shfl_xor_sync(0xffffffffu, pr, 16);  // the other row half of the column
+    const float rr = vx - pr;
     const float e = rr * beta;
     float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
 #pragma unroll
-    for (int i = 0; i < D; i += 4) {
+    for (int i = 0; i < 64; i += 4) {
       S[i] = fmaf(kv[i], e, S[i]);
       S[i + 1] = fmaf(kv[i + 1], e, S[i + 1]);
       S[i + 2] = fmaf(kv[i + 2], e, S[i + 2]);
@@ -230,14 +237,18 @@ __global__ void __launch_bounds__(32) kda_f32_fwd_kernel(F32FwdParams P) {
       o2 = fmaf(qv[i + 2], S[i + 2], o2);
       o3 = fmaf(qv[i + 3], S[i + 3], o3);
     }
-    const size_t off = (size_t)t * rowH + (size_t)h * D + col;
-    P.o[off] = (o0 + o1) + (o2 + o3);
-    if (P.r) P.r[off] = rr;
+    float ov = (o0 + o1) + (o2 + o3);
+    ov += __shfl_xor_sync(0xffffffffu, ov, 16);
+    if (lane < 16) {
+      const size_t off = (size_t)t * rowH + (size_t)h * D + col;
+      P.o[off] = ov;
+      if (P.r) P.r[off] = rr;
+    }
     __syncwarp();  // buffer `buf` is rewritten two tokens later
   }
   if (P.ht) {
 #pragma unroll
-    for (int i = 0; i < D; ++i) P.ht[stateoff + (size_t)i * D + col] = S[i];
+    for (int i = 0; i < 64; ++i) P.ht[stateoff + (size_t)(r0 + i) * D + col] = S[i];
   }
 }
 
@@ -256,8 +267,25 @@ struct F32BwdParams {
   int items;                                   // N * H * F32_GROUPS
 };
 
+// Sum over the 32 lanes of v[j], j = 0..31, ending with lane l holding the sum for
+// j = l: five halving steps, each lane keeping the half of its values whose index
+// bit matches its lane bit and adding its partner's copy of that half.
+__device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int half = 16; half >= 1; half >>= 1) {
+    const bool up = lane & half;
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float send = up ? v[j] : v[j + half];
+      const float keep = up ? v[j + half] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+    }
+  }
+  return v[0];
+}
+
 struct F32BwdSmem {
-  float red[D][F32_COLS + 1];      // k_i dS[i][j] for the reduction over rows
   float part[4][F32_COLS];         // per-warp partial sums of de
   float dov[2][F32_COLS];          // dO_t of this group's columns
   float rv[2][F32_COLS];           // r_t of this group's columns
@@ -319,30 +347,37 @@ __global__ void __launch_bounds__(F32_BWD_THREADS) kda_f32_bwd_kernel(F32BwdPara
         }
       }
       __syncthreads();  // scratch written by all rows (each thread reads only its own row, but keep order simple)
-      // ---- reverse over the chunk's tokens
+      // ---- reverse over the chunk's tokens; each token's inputs are loaded while
+      //      the token after it computes
+      float nx = 0.f, nq, nk, na, nb;  // token m's dO / r column (threads < 64), q, k, alpha of row i, beta
+      auto load_token = [&](int m) {
+        const size_t off = (size_t)(t0 + m) * rowH + (size_t)h * D;
+        if (tid < F32_COLS) nx = P.dO[off + col0 + tid];
+        else if (tid < 2 * F32_COLS) nx = P.r[off + col0 + tid - F32_COLS];
+        nq = P.qh[off + i];
+        nk = P.kh[off + i];
+        na = P.alpha[off + i];
+        nb = P.bt[(size_t)(t0 + m) * H + h];
+      };
+      load_token(L - 1);
       for (int m = L - 1; m >= 0; --m) {
         const int t = t0 + m, b = m & 1;
         const size_t off = (size_t)t * rowH + (size_t)h * D;
-        if (tid < F32_COLS) sm.dov[b][tid] = P.dO[off + col0 + tid];
-        else if (tid < 2 * F32_COLS) sm.rv[b][tid - F32_COLS] = P.r[off + col0 + tid - F32_COLS];
-        const float qi = P.qh[off + i], ki = P.kh[off + i], ai = P.alpha[off + i];
-        const float beta = P.bt[(size_t)t * H + h];
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < F32_COLS; ++j) {
-          dS[j] = fmaf(qi, sm.dov[b][j], dS[j]);
-          sm.red[i][j] = ki * dS[j];
-        }
+        if (tid < F32_COLS) sm.dov[b][tid] = nx;
+        else if (tid < 2 * F32_COLS) sm.rv[b][tid - F32_COLS] = nx;
+        const float qi = nq, ki = nk, ai = na, beta = nb;
+        if (m > 0) load_token(m - 1);
         __syncthreads();
         {
-          // warp w sums rows 32w .. 32w+31 of column `lane`
-          float s0 = 0.f, s1 = 0.f;
+          // de_j = sum_i k_i dS[i][j]: warp w's rows 32w .. 32w+31 in registers (lane
+          // `lane` ends with column `lane`), then the four warps' sums
+          float kd[F32_COLS];
 #pragma unroll
-          for (int ii = 0; ii < 32; ii += 2) {
-            s0 += sm.red[warp * 32 + ii][lane];
-            s1 += sm.red[warp * 32 + ii + 1][lane];
+          for (int j = 0; j < F32_COLS; ++j) {
+            dS[j] = fmaf(qi, sm.dov[b][j], dS[j]);
+            kd[j] = ki * dS[j];
           }
-          sm.part[warp][lane] = s0 + s1;
+          sm.part[warp][lane] = warp_reduce_scatter32(kd);
         }
         __syncthreads();
         if (warp == 0) {
