@@ -84,19 +84,20 @@ KERNEL_FLOPS_PER_TOKEN_HEAD = {
 NCU_DRAM_BYTES_PER_TOKEN_HEAD: dict[str, float] = {
     "fwd_intra": 3322.3, "fwd_state": 1882.8, "bwd_state": 2844.1, "bwd_intra": 3847.0, "bwd_post": 2221.6,
 }
-# Hash of the device code (sophia_b200/csrc/*.cuh) that capture ran on: the line says
-# whether the traffic figures describe the kernels being timed.
-NCU_SOURCE_HASH = "f0e00e6692d0e2f5"
+# The device code of the layer's kernels (the headers they are built from) and its
+# hash when that capture ran: the line says whether the traffic figures describe
+# the kernels being timed.
+LAYER_KERNEL_SOURCES = ("kda_bwd_intra.cuh", "kda_bwd_state_tc.cuh", "kda_common.cuh", "kda_fwd.cuh",
+                        "kda_fwd_state_tc.cuh", "kda_intra.cuh", "kda_post.cuh", "kda_tc.cuh")
+NCU_SOURCE_HASH = "6fe6036efae3f399"
 
 
 def kernel_source_hash() -> str:
-    import glob
     import hashlib
     h = hashlib.sha256()
-    for f in sorted(glob.glob(os.path.join(ROOT, "sophia_b200", "csrc", "*"))):
-        if f.endswith(".cuh"):
-            with open(f, "rb") as fh:
-                h.update(fh.read())
+    for f in LAYER_KERNEL_SOURCES:
+        with open(os.path.join(ROOT, "sophia_b200", "csrc", f), "rb") as fh:
+            h.update(fh.read())
     return h.hexdigest()[:16]
 
 
