@@ -103,7 +103,7 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
  * kda_b200_f32_*_bytes functions.  All arithmetic is fp32 on CUDA cores (no
  * tensor-core rounding); the recurrence runs token by token in the
  * reference's order, so results agree with the reference to fp32 rounding.
- * The backward's scratch includes a per-CTA slice of 1 MiB for at most four
+ * The backward's scratch includes a per-CTA slice of 256 KiB for at most four
  * CTAs per SM (and at most one per (sequence, head, 32-column group)).
  */
 size_t kda_b200_f32_saved_bytes(int64_t total_tokens, int H, int N);

@@ -22,9 +22,12 @@
 //   kda_f32_bwd_kernel    persistent, one CTA of 128 threads per (sequence,
 //                         head, 32-column group) item; thread i keeps row i of
 //                         this group's columns of dS.  Chunks run last to first:
-//                         the chunk's states are recomputed from its checkpoint
-//                         into a per-CTA scratch (bit-identical to the
-//                         forward's), then the tokens run in reverse:
+//                         the states at every 8th token are recomputed from the
+//                         chunk's checkpoint into a per-CTA scratch, then per
+//                         block of 8 tokens (last first) that block's states
+//                         (bit-identical to the forward's, 256 KB of scratch
+//                         per CTA, so it stays in L2), and the tokens run in
+//                         reverse:
 //                           dS += q dO^T;  de = k^T dS (CTA reduction over rows);
 //                           dv = beta de;  dbeta = de . r;  dpred = -beta de;
 //                           dq = alpha (S_prev dO) + k (e . dO)
@@ -53,7 +56,10 @@ constexpr int F32_FWD_GROUPS = D / F32_FWD_COLS;
 constexpr int F32_GROUPS = D / F32_COLS;      // column groups per (sequence, head)
 constexpr int F32_WARPS_PER_CTA = 4;          // chunks per CTA of the row kernels
 constexpr int F32_BWD_THREADS = 128;          // one thread per state row
-constexpr size_t F32_SCRATCH_FLOATS = (size_t)C * F32_COLS * D;  // per backward CTA: 64 states x 32 cols x 128 rows
+constexpr int F32_SUB = 8;                    // tokens per recompute block of the backward
+// per backward CTA: the states at every F32_SUB-th token of a chunk, then the
+// F32_SUB states of one block (each 32 columns x 128 rows)
+constexpr size_t F32_SCRATCH_FLOATS = (size_t)(C / F32_SUB + F32_SUB) * F32_COLS * D;
 constexpr float F32_NORM_EPS = 1e-12f;        // F.normalize's eps
 
 struct F32Inputs {
@@ -258,7 +264,7 @@ struct F32BwdParams {
   const float *qh, *kh, *alpha, *bt, *r, *ck;  // saved by the forward
   const float* dO;                             // [TT][H][128]
   const float* dht;                            // [N][H][128][128] or null
-  float* scratch;                              // [gridDim.x][64][32][128]
+  float* scratch;                              // [gridDim.x][8 + 8][32][128]
   float *dqh_p, *dkh_p, *dal_p;                // [F32_GROUPS][TT][H][128] partials
   float* dbt_p;                                // [F32_GROUPS][TT][H]
   float* dvh;                                  // [TT][H][128]
@@ -293,7 +299,7 @@ struct F32BwdSmem {
   float ed[2];                     // e_t . dO_t over this group's columns
 };
 
-__global__ void __launch_bounds__(F32_BWD_THREADS) kda_f32_bwd_kernel(F32BwdParams P) {
+__global__ void __launch_bounds__(F32_BWD_THREADS, 4) kda_f32_bwd_kernel(F32BwdParams P) {
   __shared__ F32BwdSmem sm;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, H = P.H;
   const int i = tid;  // state row of this thread
@@ -317,8 +323,34 @@ __global__ void __launch_bounds__(F32_BWD_THREADS) kda_f32_bwd_kernel(F32BwdPara
     const int nchunks = (eos - bos + C - 1) / C, cbase = seq_chunk_base(P.seq, n);
     for (int ci = nchunks - 1; ci >= 0; --ci) {
       const int t0 = bos + ci * C, t1 = min(t0 + C, eos), L = t1 - t0;
-      // ---- recompute this chunk's states (row i, this group's columns) into the scratch:
-      //      slot m holds the state before token t0 + m, in [m][j][i] order
+      // ---- states of row i, this group's columns, in [slot][j][i] order: the one
+      //      before token t0 + 8 b in slot b of the block-start area, then the ones
+      //      before the tokens of one block in the block area
+      float* const sblk = scr + (size_t)(C / F32_SUB) * F32_COLS * D;
+      // S <- the state after token t (the forward's update, bit for bit)
+      auto step = [&](float (&S)[F32_COLS], int t) {
+        const size_t off = (size_t)t * rowH + (size_t)h * D;
+        const float a = P.alpha[off + i], kk = P.kh[off + i], beta = P.bt[(size_t)t * H + h];
+        const float4* rr = reinterpret_cast<const float4*>(P.r + off + col0);
+#pragma unroll
+        for (int j = 0; j < F32_COLS; j += 4) {
+          const float4 r4 = __ldg(rr + j / 4);
+          S[j] = fmaf(kk, r4.x * beta, a * S[j]);
+          S[j + 1] = fmaf(kk, r4.y * beta, a * S[j + 1]);
+          S[j + 2] = fmaf(kk, r4.z * beta, a * S[j + 2]);
+          S[j + 3] = fmaf(kk, r4.w * beta, a * S[j + 3]);
+        }
+      };
+      auto put = [&](float* area, int slot, const float (&S)[F32_COLS]) {
+        float* dst = area + (size_t)slot * F32_COLS * D + i;
+#pragma unroll
+        for (int j = 0; j < F32_COLS; ++j) dst[(size_t)j * D] = S[j];
+      };
+      auto get = [&](const float* area, int slot, float (&S)[F32_COLS]) {
+        const float* src = area + (size_t)slot * F32_COLS * D + i;
+#pragma unroll
+        for (int j = 0; j < F32_COLS; ++j) S[j] = src[(size_t)j * D];
+      };
       {
         float S[F32_COLS];
         const float* src = P.ck + tile_index(P.seq, cbase + ci, h) * (size_t)STATE_ELEMS + (size_t)i * D + col0;
@@ -327,95 +359,94 @@ __global__ void __launch_bounds__(F32_BWD_THREADS) kda_f32_bwd_kernel(F32BwdPara
           const float4 v = *reinterpret_cast<const float4*>(src + j);
           S[j] = v.x; S[j + 1] = v.y; S[j + 2] = v.z; S[j + 3] = v.w;
         }
-        for (int m = 0; m < L; ++m) {
-          const int t = t0 + m;
-          float* dst = scr + (size_t)m * F32_COLS * D + i;
-#pragma unroll
-          for (int j = 0; j < F32_COLS; ++j) dst[(size_t)j * D] = S[j];
-          if (m + 1 == L) break;
-          const size_t off = (size_t)t * rowH + (size_t)h * D;
-          const float a = P.alpha[off + i], kk = P.kh[off + i], beta = P.bt[(size_t)t * H + h];
-          const float4* rr = reinterpret_cast<const float4*>(P.r + off + col0);
-#pragma unroll
-          for (int j = 0; j < F32_COLS; j += 4) {
-            const float4 r4 = __ldg(rr + j / 4);
-            S[j] = fmaf(kk, r4.x * beta, a * S[j]);
-            S[j + 1] = fmaf(kk, r4.y * beta, a * S[j + 1]);
-            S[j + 2] = fmaf(kk, r4.z * beta, a * S[j + 2]);
-            S[j + 3] = fmaf(kk, r4.w * beta, a * S[j + 3]);
-          }
+        const int mlast = ((L - 1) / F32_SUB) * F32_SUB;  // the last block's first token
+        for (int m = 0; m < mlast; ++m) {
+          if (m % F32_SUB == 0) put(scr, m / F32_SUB, S);
+          step(S, t0 + m);
         }
+        put(scr, mlast / F32_SUB, S);
       }
-      __syncthreads();  // scratch written by all rows (each thread reads only its own row, but keep order simple)
-      // ---- reverse over the chunk's tokens; each token's inputs are loaded while
-      //      the token after it computes
-      float nx = 0.f, nq, nk, na, nb;  // token m's dO / r column (threads < 64), q, k, alpha of row i, beta
-      auto load_token = [&](int m) {
-        const size_t off = (size_t)(t0 + m) * rowH + (size_t)h * D;
-        if (tid < F32_COLS) nx = P.dO[off + col0 + tid];
-        else if (tid < 2 * F32_COLS) nx = P.r[off + col0 + tid - F32_COLS];
-        nq = P.qh[off + i];
-        nk = P.kh[off + i];
-        na = P.alpha[off + i];
-        nb = P.bt[(size_t)(t0 + m) * H + h];
-      };
-      load_token(L - 1);
-      for (int m = L - 1; m >= 0; --m) {
-        const int t = t0 + m, b = m & 1;
-        const size_t off = (size_t)t * rowH + (size_t)h * D;
-        if (tid < F32_COLS) sm.dov[b][tid] = nx;
-        else if (tid < 2 * F32_COLS) sm.rv[b][tid - F32_COLS] = nx;
-        const float qi = nq, ki = nk, ai = na, beta = nb;
-        if (m > 0) load_token(m - 1);
-        __syncthreads();
+      for (int blk = (L - 1) / F32_SUB; blk >= 0; --blk) {
+        const int mb0 = blk * F32_SUB, mb1 = min(mb0 + F32_SUB, L);
         {
-          // de_j = sum_i k_i dS[i][j]: warp w's rows 32w .. 32w+31 in registers (lane
-          // `lane` ends with column `lane`), then the four warps' sums
-          float kd[F32_COLS];
-#pragma unroll
-          for (int j = 0; j < F32_COLS; ++j) {
-            dS[j] = fmaf(qi, sm.dov[b][j], dS[j]);
-            kd[j] = ki * dS[j];
+          float S[F32_COLS];
+          get(scr, blk, S);
+          for (int m = mb0; m < mb1; ++m) {
+            put(sblk, m - mb0, S);
+            if (m + 1 < mb1) step(S, t0 + m);
           }
-          sm.part[warp][lane] = warp_reduce_scatter32(kd);
         }
-        __syncthreads();
-        if (warp == 0) {
-          const float de = (sm.part[0][lane] + sm.part[1][lane]) + (sm.part[2][lane] + sm.part[3][lane]);
-          const float rj = sm.rv[b][lane];
-          P.dvh[off + col0 + lane] = beta * de;
-          const float db = warp_sum(de * rj);
-          const float ed = warp_sum(rj * beta * sm.dov[b][lane]);
-          if (lane == 0) {
-            P.dbt_p[((size_t)grp * P.total_tokens + t) * H + h] = db;
-            sm.ed[b] = ed;
-          }
-          sm.de[b][lane] = de;
-        }
-        __syncthreads();
-        const float* sp = scr + (size_t)m * F32_COLS * D + i;
-        float dq0 = 0.f, dq1 = 0.f, dk0 = 0.f, dk1 = 0.f, da0 = 0.f, da1 = 0.f;
+        __syncthreads();  // (each thread reads back only its own row; keeps the order simple)
+        // ---- reverse over the block's tokens; each token's inputs are loaded while
+        //      the token after it computes
+        float nx = 0.f, nq, nk, na, nb;  // token m's dO / r column (threads < 64), q, k, alpha of row i, beta
+        auto load_token = [&](int m) {
+          const size_t off = (size_t)(t0 + m) * rowH + (size_t)h * D;
+          if (tid < F32_COLS) nx = P.dO[off + col0 + tid];
+          else if (tid < 2 * F32_COLS) nx = P.r[off + col0 + tid - F32_COLS];
+          nq = P.qh[off + i];
+          nk = P.kh[off + i];
+          na = P.alpha[off + i];
+          nb = P.bt[(size_t)(t0 + m) * H + h];
+        };
+        load_token(mb1 - 1);
+        for (int m = mb1 - 1; m >= mb0; --m) {
+          const int t = t0 + m, b = m & 1;
+          const size_t off = (size_t)t * rowH + (size_t)h * D;
+          if (tid < F32_COLS) sm.dov[b][tid] = nx;
+          else if (tid < 2 * F32_COLS) sm.rv[b][tid - F32_COLS] = nx;
+          const float qi = nq, ki = nk, ai = na, beta = nb;
+          if (m > mb0) load_token(m - 1);
+          __syncthreads();
+          {
+            // de_j = sum_i k_i dS[i][j]: warp w's rows 32w .. 32w+31 in registers (lane
+            // `lane` ends with column `lane`), then the four warps' sums
+            float kd[F32_COLS];
 #pragma unroll
-        for (int j = 0; j < F32_COLS; j += 2) {
-          const float sp0 = sp[(size_t)j * D], sp1 = sp[(size_t)(j + 1) * D];
-          const float dp0 = -beta * sm.de[b][j], dp1 = -beta * sm.de[b][j + 1];
-          const float e0 = sm.rv[b][j] * beta, e1 = sm.rv[b][j + 1] * beta;
-          dq0 = fmaf(sp0, sm.dov[b][j], dq0);
-          dq1 = fmaf(sp1, sm.dov[b][j + 1], dq1);
-          dk0 = fmaf(dS[j], e0, fmaf(dp0, ai * sp0, dk0));
-          dk1 = fmaf(dS[j + 1], e1, fmaf(dp1, ai * sp1, dk1));
-          const float du0 = fmaf(ki, dp0, dS[j]), du1 = fmaf(ki, dp1, dS[j + 1]);
-          da0 = fmaf(du0, sp0, da0);
-          da1 = fmaf(du1, sp1, da1);
-          dS[j] = ai * du0;
-          dS[j + 1] = ai * du1;
+            for (int j = 0; j < F32_COLS; ++j) {
+              dS[j] = fmaf(qi, sm.dov[b][j], dS[j]);
+              kd[j] = ki * dS[j];
+            }
+            sm.part[warp][lane] = warp_reduce_scatter32(kd);
+          }
+          __syncthreads();
+          if (warp == 0) {
+            const float de = (sm.part[0][lane] + sm.part[1][lane]) + (sm.part[2][lane] + sm.part[3][lane]);
+            const float rj = sm.rv[b][lane];
+            P.dvh[off + col0 + lane] = beta * de;
+            const float db = warp_sum(de * rj);
+            const float ed = warp_sum(rj * beta * sm.dov[b][lane]);
+            if (lane == 0) {
+              P.dbt_p[((size_t)grp * P.total_tokens + t) * H + h] = db;
+              sm.ed[b] = ed;
+            }
+            sm.de[b][lane] = de;
+          }
+          __syncthreads();
+          const float* sp = sblk + (size_t)(m - mb0) * F32_COLS * D + i;
+          float dq0 = 0.f, dq1 = 0.f, dk0 = 0.f, dk1 = 0.f, da0 = 0.f, da1 = 0.f;
+#pragma unroll
+          for (int j = 0; j < F32_COLS; j += 2) {
+            const float sp0 = sp[(size_t)j * D], sp1 = sp[(size_t)(j + 1) * D];
+            const float dp0 = -beta * sm.de[b][j], dp1 = -beta * sm.de[b][j + 1];
+            const float e0 = sm.rv[b][j] * beta, e1 = sm.rv[b][j + 1] * beta;
+            dq0 = fmaf(sp0, sm.dov[b][j], dq0);
+            dq1 = fmaf(sp1, sm.dov[b][j + 1], dq1);
+            dk0 = fmaf(dS[j], e0, fmaf(dp0, ai * sp0, dk0));
+            dk1 = fmaf(dS[j + 1], e1, fmaf(dp1, ai * sp1, dk1));
+            const float du0 = fmaf(ki, dp0, dS[j]), du1 = fmaf(ki, dp1, dS[j + 1]);
+            da0 = fmaf(du0, sp0, da0);
+            da1 = fmaf(du1, sp1, da1);
+            dS[j] = ai * du0;
+            dS[j + 1] = ai * du1;
+          }
+          const size_t poff = (size_t)grp * P.total_tokens * rowH + off + i;
+          P.dqh_p[poff] = fmaf(ai, dq0 + dq1, ki * sm.ed[b]);
+          P.dkh_p[poff] = dk0 + dk1;
+          P.dal_p[poff] = da0 + da1;
         }
-        const size_t poff = (size_t)grp * P.total_tokens * rowH + off + i;
-        P.dqh_p[poff] = fmaf(ai, dq0 + dq1, ki * sm.ed[b]);
-        P.dkh_p[poff] = dk0 + dk1;
-        P.dal_p[poff] = da0 + da1;
+        __syncthreads();  // the block area is rewritten by the next block
       }
-      __syncthreads();  // the scratch is rewritten by the next chunk
     }
     if (P.dh0) {
 #pragma unroll
