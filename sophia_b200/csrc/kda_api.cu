@@ -93,6 +93,7 @@ struct Table {
   int* offsets;
   int* chunk_seq;
   int* err;
+  int* item_counter;  // the forward chunk kernel's dynamic item counter
 };
 
 Table carve_table(Carver& cv, int N, int64_t mc) {
@@ -100,6 +101,7 @@ Table carve_table(Carver& cv, int N, int64_t mc) {
   t.offsets = cv.take<int>((size_t)(N + 1) * 4);
   t.chunk_seq = cv.take<int>((size_t)mc * 4);
   t.err = cv.take<int>(4);
+  t.item_counter = cv.take<int>(4);
   return t;
 }
 
@@ -560,16 +562,20 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   ip.W = sv.W; ip.U = sv.U; ip.Qt = sv.Qt; ip.Kb = sv.Kb; ip.M = sv.M; ip.dC = sv.dC; ip.A = sv.A; ip.LP = sv.LP;
   ip.QN = sv.QN; ip.KN = sv.KN; ip.VN = sv.VN; ip.GM = sv.GM; ip.BT = sv.BT;
   ip.grid_chunks = pr.grid_chunks;
+  ip.item_counter = tab.item_counter;
   ip.wait_polls = g_input_wait_polls.load(std::memory_order_relaxed);
   if ((rc = encode_rows_map(&ip.maps[0], q, H, pr.TT, 67)) || (rc = encode_rows_map(&ip.maps[1], k, H, pr.TT, 67)) ||
       (rc = encode_rows_map(&ip.maps[2], v, H, pr.TT, 67)) || (rc = encode_rows_map(&ip.maps[3], g, H, pr.TT, 64)))
     return rc;
   if ((rc = set_smem(kda_fwd_intra_kernel, IntraSmem::END, "fwd intra"))) return rc;
   {
-    // persistent: one CTA per SM (the shared-memory plan allows one) walks the items
+    // persistent: one CTA per SM (the shared-memory plan allows one) walks the items;
+    // those past the grid come from a counter that starts at zero
     const long long items = (long long)pr.grid_chunks * H;
     if (items > INT_MAX) return fail(KDA_ERR_INVALID, "more than 2^31 (chunk, head) items");
     const int ctas = (int)std::min<long long>(items, sm_count());
+    const cudaError_t e = cudaMemsetAsync(tab.item_counter, 0, sizeof(int), st);
+    if (e != cudaSuccess) return fail(KDA_ERR_CUDA, std::string("item counter: ") + cudaGetErrorString(e));
     TimedLaunch tl(K_FWD_INTRA, st);
     kda_fwd_intra_kernel<<<ctas, INTRA_THREADS, IntraSmem::END, st>>>(ip);
   }

@@ -1,7 +1,8 @@
 // Forward kernels of the chunked KDA layer.
 //
-//   kda_fwd_intra_kernel  (persistent: one CTA per SM walks the (chunk, head)
-//                          items, prefetching the next item's inputs)
+//   kda_fwd_intra_kernel  (persistent: one CTA per SM walks the (chunk slot, head)
+//                          items, slot fastest: item b first, then items from a
+//                          shared counter; the next item's inputs are prefetched)
 //       raw q/k/v (pre- or post-conv), gate and beta logits
 //       -> W = T (k*2^Gam), U = T v, Qt = q*2^Gam, Kbar = k*2^(Gam_C-Gam),
 //          M = Aqk (lower incl. diag), dC = 2^Gam_C
@@ -26,6 +27,7 @@ struct FwdIntraParams {
   bf16 *QN, *KN, *VN;         // [slots x H] prologue products for the backward, or null
   float *GM, *BT;
   int grid_chunks;            // chunk slots per head: items are (slot, head), slot fastest
+  int* item_counter;          // zero at launch: items from gridDim.x on are handed out by it
   CUtensorMap maps[4];        // q, k, v, g as [T_total][H][128] bf16; boxes of 67 (q/k/v) and 64 (g) rows
   uint32_t wait_polls;        // poll limit of the wait for an item's prefetched inputs
 };
@@ -71,12 +73,35 @@ __device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, 
   }
 }
 
+// The CTA's next valid item from the shared counter (items below gridDim.x belong to
+// the CTA of that index), or n_items when none is left.  Dynamic: a CTA that starts
+// late (its SM busy with another kernel, e.g. a collective) simply takes fewer items.
+__device__ __forceinline__ int grab_item(const FwdIntraParams& P, int n_items, int G, ChunkPos& pos) {
+  for (;;) {
+    const int it = (int)gridDim.x + atomicAdd(P.item_counter, 1);
+    if (it >= n_items) return n_items;
+    pos = chunk_pos(P.seq, it % G);
+    if (pos.valid) return it;
+  }
+}
+
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const __grid_constant__ FwdIntraParams P) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = P.in.H, G = P.grid_chunks, n_items = G * H;
-  ChunkPos pos;
-  int item = next_valid_item(P.seq, blockIdx.x, n_items, G, pos);
-  if (item >= n_items) return;
+  int* nxt = reinterpret_cast<int*>(smem + IntraSmem::NXT);
+  ChunkPos pos = chunk_pos(P.seq, blockIdx.x % G);
+  int item = blockIdx.x;
+  if (!pos.valid) {  // block-uniform: one thread grabs, all read
+    if (threadIdx.x == 0) {
+      ChunkPos p0;
+      nxt[0] = grab_item(P, n_items, G, p0);
+    }
+    __syncthreads();
+    item = nxt[0];
+    if (item >= n_items) return;
+    pos = chunk_pos(P.seq, item % G);
+    __syncthreads();  // nxt is rewritten below
+  }
 
   PrologueSmem ps;
   ps.xq = reinterpret_cast<bf16*>(smem + IntraSmem::RAW);
@@ -89,7 +114,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
   ps.tot = reinterpret_cast<float*>(smem + IntraSmem::OPS);  // scratch, before operands
   ps.taps = reinterpret_cast<float*>(smem + IntraSmem::TAPS);
   ps.bias = reinterpret_cast<float*>(smem + IntraSmem::BIAS);
-  int* nxt = reinterpret_cast<int*>(smem + IntraSmem::NXT);
   uint64_t* raw_ready = reinterpret_cast<uint64_t*>(smem + IntraSmem::NXT + 16);
   const bool save_products = P.QN != nullptr;
   if (threadIdx.x == 0) {
@@ -107,7 +131,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     if (threadIdx.x == 0) {
       // the next item (its table lookups overlap this item's loads)
       ChunkPos np;
-      nxt[0] = next_valid_item(P.seq, item + gridDim.x, n_items, G, np);
+      nxt[0] = grab_item(P, n_items, G, np);
       nxt[1] = np.bos; nxt[2] = np.t0; nxt[3] = np.t1;
       // the previous item's A store reads the region the decay tile is rebuilt in
       if (P.A) tc::bulk_wait_read_all();

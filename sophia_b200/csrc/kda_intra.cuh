@@ -34,16 +34,6 @@ struct PrologueIn {
   float scale, lower_bound;
 };
 
-// Persistent chunk kernels walk the items (chunk slot, head), slot fastest,
-// in steps of the grid.  First valid item at or after `from` (pos filled), or
-// n_items.
-__device__ __forceinline__ int next_valid_item(const SeqInfo& seq, int from, int n_items, int G, ChunkPos& pos) {
-  for (int it = from; it < n_items; it += gridDim.x) {
-    pos = chunk_pos(seq, it % G);
-    if (pos.valid) return it;
-  }
-  return n_items;
-}
 
 // Shared-memory views used by the prologue.
 struct PrologueSmem {
