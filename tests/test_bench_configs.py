@@ -43,3 +43,27 @@ def test_mixer_flops_per_token():
     gemm = 2 * (1536 * 4 * inner + 1536 * 128 + 128 * inner + 1536 * bench.H + inner * 1536)
     layer = sum(bench.KERNEL_FLOPS_PER_TOKEN_HEAD.values()) * bench.H
     assert bench.mixer_flops_per_token() == 3 * gemm + layer
+
+
+def test_traffic_hash_covers_the_layer_kernels_headers():
+    """The bench line says whether its DRAM traffic figures were captured on the
+    kernels it times, by a hash of the headers the layer's five kernels are built
+    from: every such header must be in the list (and exist), so that an edit to
+    any of them marks the figures stale."""
+    import re
+    bench = _bench()
+    csrc = os.path.join(ROOT, "sophia_b200", "csrc")
+    listed = set(bench.LAYER_KERNEL_SOURCES)
+    assert all(os.path.isfile(os.path.join(csrc, f)) for f in listed)
+    # the include closure of the layer kernels' headers stays inside the list
+    roots = {"kda_fwd.cuh", "kda_fwd_state_tc.cuh", "kda_bwd_state_tc.cuh", "kda_bwd_intra.cuh", "kda_post.cuh"}
+    seen, todo = set(), list(roots)
+    while todo:
+        f = todo.pop()
+        if f in seen:
+            continue
+        seen.add(f)
+        with open(os.path.join(csrc, f)) as fh:
+            todo += re.findall(r'#include "([^"/]+\.cuh)"', fh.read())
+    assert seen <= listed, sorted(seen - listed)
+    assert len(bench.kernel_source_hash()) == 16
