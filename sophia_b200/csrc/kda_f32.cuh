@@ -292,6 +292,8 @@ __device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32]) {
 }
 
 struct F32BwdSmem {
+  float rs[C][F32_COLS];           // r of this group's columns for the chunk's tokens
+  float bs[C];                     // beta of the chunk's tokens
   float part[4][F32_COLS];         // per-warp partial sums of de
   float dov[2][F32_COLS];          // dO_t of this group's columns
   float rv[2][F32_COLS];           // r_t of this group's columns
@@ -327,19 +329,33 @@ __global__ void __launch_bounds__(F32_BWD_THREADS, 4) kda_f32_bwd_kernel(F32BwdP
       //      before token t0 + 8 b in slot b of the block-start area, then the ones
       //      before the tokens of one block in the block area
       float* const sblk = scr + (size_t)(C / F32_SUB) * F32_COLS * D;
-      // S <- the state after token t (the forward's update, bit for bit)
-      auto step = [&](float (&S)[F32_COLS], int t) {
-        const size_t off = (size_t)t * rowH + (size_t)h * D;
-        const float a = P.alpha[off + i], kk = P.kh[off + i], beta = P.bt[(size_t)t * H + h];
-        const float4* rr = reinterpret_cast<const float4*>(P.r + off + col0);
+      // the chunk's r (this group's columns) and beta, staged once for the recompute
+      for (int e = tid; e < L * (F32_COLS / 4); e += F32_BWD_THREADS) {
+        const int m = e / (F32_COLS / 4), j4 = e % (F32_COLS / 4);
+        reinterpret_cast<float4*>(sm.rs[m])[j4] =
+            __ldg(reinterpret_cast<const float4*>(P.r + (size_t)(t0 + m) * rowH + (size_t)h * D + col0) + j4);
+      }
+      if (tid < L) sm.bs[tid] = P.bt[(size_t)(t0 + tid) * H + h];
+      __syncthreads();
+      // S <- the state after token t0 + m (the forward's update, bit for bit), with this
+      // row's alpha and k of that token
+      auto step = [&](float (&S)[F32_COLS], int m, float a, float kk) {
+        const float beta = sm.bs[m];
+        const float4* rr = reinterpret_cast<const float4*>(sm.rs[m]);
 #pragma unroll
         for (int j = 0; j < F32_COLS; j += 4) {
-          const float4 r4 = __ldg(rr + j / 4);
+          const float4 r4 = rr[j / 4];
           S[j] = fmaf(kk, r4.x * beta, a * S[j]);
           S[j + 1] = fmaf(kk, r4.y * beta, a * S[j + 1]);
           S[j + 2] = fmaf(kk, r4.z * beta, a * S[j + 2]);
           S[j + 3] = fmaf(kk, r4.w * beta, a * S[j + 3]);
         }
+      };
+      // row i's alpha and k of token t0 + m
+      auto ak = [&](int m, float& a, float& kk) {
+        const size_t off = (size_t)(t0 + m) * rowH + (size_t)h * D + i;
+        a = P.alpha[off];
+        kk = P.kh[off];
       };
       auto put = [&](float* area, int slot, const float (&S)[F32_COLS]) {
         float* dst = area + (size_t)slot * F32_COLS * D + i;
@@ -360,9 +376,13 @@ __global__ void __launch_bounds__(F32_BWD_THREADS, 4) kda_f32_bwd_kernel(F32BwdP
           S[j] = v.x; S[j + 1] = v.y; S[j + 2] = v.z; S[j + 3] = v.w;
         }
         const int mlast = ((L - 1) / F32_SUB) * F32_SUB;  // the last block's first token
+        float na = 0.f, nk = 0.f;  // the next step's alpha and k, loaded a step ahead
+        if (mlast > 0) ak(0, na, nk);
         for (int m = 0; m < mlast; ++m) {
           if (m % F32_SUB == 0) put(scr, m / F32_SUB, S);
-          step(S, t0 + m);
+          const float a = na, kk = nk;
+          if (m + 1 < mlast) ak(m + 1, na, nk);
+          step(S, m, a, kk);
         }
         put(scr, mlast / F32_SUB, S);
       }
@@ -371,9 +391,15 @@ __global__ void __launch_bounds__(F32_BWD_THREADS, 4) kda_f32_bwd_kernel(F32BwdP
         {
           float S[F32_COLS];
           get(scr, blk, S);
+          float na = 0.f, nk = 0.f;
+          if (mb0 + 1 < mb1) ak(mb0, na, nk);
           for (int m = mb0; m < mb1; ++m) {
             put(sblk, m - mb0, S);
-            if (m + 1 < mb1) step(S, t0 + m);
+            if (m + 1 < mb1) {
+              const float a = na, kk = nk;
+              if (m + 2 < mb1) ak(m + 1, na, nk);
+              step(S, m, a, kk);
+            }
           }
         }
         __syncthreads();  // (each thread reads back only its own row; keeps the order simple)
