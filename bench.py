@@ -1,7 +1,7 @@
 """Benchmark of the B200 KDA layer (forward + backward), one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg1|cfg2|cfg3|cfg4]
+                    [--workload cfg1|cfg2|cfg3|cfg4|decode]
 
 Step = one forward + backward of the KDA layer (ShortConv+SiLU, L2 norms,
 gate, beta, chunked gated delta rule) over one batch of synthetic inputs of
@@ -21,7 +21,11 @@ decay and beta projections, the KDA layer, gated output RMSNorm, out-
 projection; 4 x 4096 tokens, hidden 1536, bf16 autocast) per GPU;
 ``--workload cfg4`` steps configuration 4's packed ragged batch per GPU: 16
 windows of 4096 tokens holding documents of log-uniform length in [32, 4096]
-(seed 42), one 65,536-token sequence with ``cu_seqlens``.
+(seed 42), one 65,536-token sequence with ``cu_seqlens`` built on the device
+from the windows' end-of-document tokens every step (``document_cu_seqlens``);
+``--workload decode`` steps ``kda_decode`` calls of one token for each of 256
+sequences (ShortConv with its history + the fp32 recurrence, state carried;
+the line's roofline is the decode kernel's state traffic against HBM).
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launch stream, max over ranks.
@@ -107,7 +111,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "decode"], default="cfg1")
     ap.add_argument("--profile", action="store_true",
                     help="run the warm-up and K layer steps only, print nothing (command for ncu captures)")
     ap.add_argument("--batch", type=int, default=None,
@@ -195,6 +199,7 @@ class ClockSampler:
 
 
 CFG4_WINDOWS = 16
+CFG4_EOS, CFG4_CAPACITY = 0, 128  # the end-of-document token; document-table capacity (95 documents)
 
 
 def cfg4_cu_seqlens(windows: int = CFG4_WINDOWS, seed: int = 42) -> list[int]:
@@ -214,6 +219,18 @@ def cfg4_cu_seqlens(windows: int = CFG4_WINDOWS, seed: int = 42) -> list[int]:
     return cu
 
 
+def cfg4_tokens(device) -> torch.Tensor:
+    """Configuration 4's token windows [windows, 4096] int32: random token ids
+    with the end-of-document token at the last token of every document that ends
+    inside a window (a window start begins a document anyway)."""
+    gen = torch.Generator().manual_seed(4242)
+    tok = torch.randint(1, 50000, (CFG4_WINDOWS * T,), generator=gen, dtype=torch.int32)
+    for b in cfg4_cu_seqlens()[1:-1]:
+        if b % T:
+            tok[b - 1] = CFG4_EOS
+    return tok.view(CFG4_WINDOWS, T).to(device)
+
+
 def make_inputs(B, device, seed, Tlen=T):
     g = torch.Generator(device=device).manual_seed(seed)
     rn = lambda *s, std=1.0: torch.randn(*s, device=device, generator=g) * std  # noqa: E731
@@ -228,7 +245,7 @@ def make_inputs(B, device, seed, Tlen=T):
 
 def bench_ours(a, rank, world, local_rank):
     import torch.distributed as dist
-    from sophia_b200 import _lib, dp, kda_layer
+    from sophia_b200 import _lib, document_cu_seqlens, dp, kda_layer
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
@@ -236,7 +253,7 @@ def bench_ours(a, rank, world, local_rank):
     packed = a.workload == "cfg4"
     if packed:  # one sequence of 16 packed windows, documents reset at cu_seqlens
         B, Tlen = 1, CFG4_WINDOWS * T
-        cu = torch.tensor(cfg4_cu_seqlens(), dtype=torch.int32, device=device)
+        cu = None  # built on the device from the windows' tokens in every step
     else:
         B = a.batch or (8 if a.workload == "cfg1" else len(range(CFG3_SEQS)[dp.shard(CFG3_SEQS, rank, world)]))
         Tlen, cu = T, None
@@ -245,6 +262,8 @@ def bench_ours(a, rank, world, local_rank):
     micro = min(B, CFG3_MICRO) if a.workload == "cfg3" else B
     n_micro = -(-B // micro)
     x, w = make_inputs(micro, device, 42 + rank, Tlen)
+    if packed:
+        x["tok"] = cfg4_tokens(device)
     acts = {k: x[k].clone().requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
     params = {k: v.clone().requires_grad_(True) for k, v in w.items()}
     bucket = torch.empty(dp.bucket_numel(H, D), device=device, dtype=torch.float32)
@@ -265,9 +284,13 @@ def bench_ours(a, rank, world, local_rank):
             for t in src.values():
                 t.grad = None
             sl = (lambda t: t) if rows == micro else (lambda t: t[:rows])  # noqa: E731
+            cu_mb = cu
+            if packed:  # the data path's document table, capture-safe (no host sync)
+                cu_mb, _ = document_cu_seqlens(x["tok"] if inputs is None else src["_tok"], CFG4_EOS,
+                                               CFG4_CAPACITY)
             o, _ = kda_layer(sl(src["q"]), sl(src["k"]), sl(src["v"]), sl(src["g"]), sl(src["beta"]),
                              params["A_log"], params["dt_bias"], params["conv_q"], params["conv_k"],
-                             params["conv_v"], cu_seqlens=cu)
+                             params["conv_v"], cu_seqlens=cu_mb)
             o.backward(sl(x["do"] if inputs is None else src["_do"]))
         drain()  # the previous step's reduction reads the bucket
         dp.grad_bucket(params, out=bucket)
@@ -323,7 +346,7 @@ def bench_ours(a, rank, world, local_rank):
     # weight gradients back.  The copies run on a second stream into two
     # alternating device buffers, so micro-batch i+1's inputs cross PCIe while
     # micro-batch i computes; all copies are inside the timed region.
-    host = {k: x[k].cpu().pin_memory() for k in ("q", "k", "v", "g", "beta", "do")}
+    host = {k: x[k].cpu().pin_memory() for k in ("q", "k", "v", "g", "beta", "do") + (("tok",) if packed else ())}
     bufs = [{k: torch.empty_like(x[k]) for k in host} for _ in range(2)]
     out_host = torch.empty(bucket.numel(), dtype=torch.float32).pin_memory()
     copy_stream = torch.cuda.Stream(device=device)
@@ -363,6 +386,8 @@ def bench_ours(a, rank, world, local_rank):
             st.wait_event(copied[b])
             inp = {k: bufs[b][k].requires_grad_(True) for k in ("q", "k", "v", "g", "beta")}
             inp["_do"] = bufs[b]["do"]
+            if packed:
+                inp["_tok"] = bufs[b]["tok"]
             state["i"] = i + 1
             return inp
 
@@ -436,6 +461,134 @@ def cpu_sample(tokens: int, threads: int | None = None):
     (out.o * do).sum().backward()
     dt = time.perf_counter() - t0
     return tokens / dt, dt
+
+
+DECODE_METRIC = ("KDA decode tokens/s at B=256 sequences,H=16,D=128, one token per sequence per call "
+                 "(fp32 state) + % roofline")
+DECODE_BATCH = 256  # the fp32 states (268 MB) exceed L2, so every call streams them from HBM
+
+
+def decode_bytes_per_step(B: int) -> int:
+    """Algorithmic HBM bytes of one decode call: the fp32 state read and written,
+    the conv history read and written, the bf16 token inputs and output, the
+    per-head weights."""
+    state = B * H * D * D * 4 * 2
+    conv = B * 3 * H * D * 3 * 4 * 2
+    io = B * H * D * 2 * 5 + B * H * 2
+    weights = H * D * 4 * (1 + 3 * 4) + H * 4
+    return state + conv + io + weights
+
+
+def cpu_decode_sample(B: int, steps: int, threads: int | None = None):
+    """The reference's CPU decode (oracle restatement of the per-token
+    recurrence, fp32, no gradients): `steps` calls of one token for B
+    sequences x 16 heads, the state carried.  Returns tokens/s."""
+    sys.path.insert(0, ROOT)
+    from oracle.kda_oracle import kda_layer as oracle_layer
+    if threads:
+        torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    mk = lambda *s, std=1.0: torch.randn(*s, generator=g) * std  # noqa: E731
+    A, dtb = torch.zeros(H), torch.zeros(H * D)
+    state = mk(B, H, D, D, std=0.1)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for _ in range(steps):
+            q, k, v, gg = (mk(B, 1, H, D) for _ in range(4))
+            out = oracle_layer(q, k, v, gg, mk(B, 1, H), A, dtb, initial_state=state, compute_dtype=torch.float32)
+            state = out.final_state
+    dt = time.perf_counter() - t0
+    return B * steps / dt, dt
+
+
+def bench_decode(a, rank, world, local_rank):
+    """Decode steps through ``sophia_b200.kda_decode`` (the cached-continuation
+    path: ShortConv with its history + the fp32 recurrence, one fused kernel),
+    one token per sequence per call, the state and the conv history carried
+    from call to call (weak scaling over ranks: each rank decodes its own B
+    sequences; inference, so no collective)."""
+    import torch.distributed as dist
+    from sophia_b200 import _lib, kda_decode
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    B = a.batch or DECODE_BATCH
+    g = torch.Generator(device=device).manual_seed(42 + rank)
+    rn = lambda *s, std=1.0: torch.randn(*s, device=device, generator=g) * std  # noqa: E731
+    x = {k: rn(B, 1, H, D).to(torch.bfloat16) for k in ("q", "k", "v", "g")}
+    x["beta"] = rn(B, 1, H).to(torch.bfloat16)
+    A_log, dt_bias = torch.zeros(H, device=device), torch.zeros(H * D, device=device)
+    taps = [rn(H * D, 4, std=0.5) for _ in range(3)]
+    conv_state = rn(B, 3, H * D, 3)
+    box = {"state": rn(B, H, D, D, std=0.1)}
+
+    def step(src=None):
+        src = x if src is None else src
+        o, ht = kda_decode(src["q"], src["k"], src["v"], src["g"], src["beta"], A_log, dt_bias, *taps,
+                           conv_state, initial_state=box["state"])
+        box["state"] = ht
+        return o
+
+    def timed(fn, steps, sampler=None):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        h0 = time.perf_counter()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        if sampler is not None:
+            sampler.mark(h0, time.perf_counter())
+        if world > 1:
+            dist.barrier()
+        from sophia_b200 import dp
+        return dp.max_over_ranks(e0.elapsed_time(e1), device)
+
+    with torch.no_grad():
+        for _ in range(max(a.warmup, 3)):
+            step()
+        sampler = ClockSampler(device)
+        sampler.start()
+        ms = timed(step, a.steps, sampler)
+        clocks = sampler.stop()
+        _lib.timing_reset()
+        _lib.timing_enable(True)
+        timed(step, a.steps)
+        _lib.timing_enable(False)
+        kern = _lib.timing_read()
+        _lib.timing_reset()
+        launches = sum(n for n, _ in kern.values())
+        # end to end: each call's inputs copied from pinned host memory, its output read back
+        host = {k: x[k].cpu().pin_memory() for k in ("q", "k", "v", "g", "beta")}
+        dev = {k: torch.empty_like(x[k]) for k in host}
+        out_host = torch.empty(B, 1, H, D, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            for k in host:
+                dev[k].copy_(host[k], non_blocking=True)
+            out_host.copy_(step(dev), non_blocking=True)
+
+        ms_e2e = timed(e2e_step, a.steps)
+    hbm, _, _, src = peaks()
+    n_k, k_ms = kern.get("recurrent", (0, 0.0))
+    per_launch = k_ms / max(1, n_k)
+    alg = decode_bytes_per_step(B)
+    achieved = alg / (per_launch / 1e3) / 1e9 if per_launch > 0 else 0.0
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    return {
+        "value": world * B * a.steps / (ms / 1e3), "ms": ms / a.steps, "clocks": clocks,
+        "e2e": {"value": world * B * a.steps / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": "recurrent", "achieved": round(achieved, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None, "peak_source": src,
+                     "bytes_per_launch": alg, "kernel_ms_per_step": {k: round(v[1] / a.steps, 4)
+                                                                     for k, v in kern.items() if v[0]}},
+    }
 
 
 MIXER_METRIC = "KDA mixer block fwd+bwd tokens/s at B=4,T=4096,hidden 1536,H=16,D=128 (cfg2) + % roofline"
@@ -624,7 +777,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     mixer = a.workload == "cfg2"
-    metric = MIXER_METRIC if mixer else METRIC
+    decode = a.workload == "decode"
+    metric = MIXER_METRIC if mixer else (DECODE_METRIC if decode else METRIC)
     config = {"workload": a.workload, "global_batch": (a.batch or 8) * world if a.workload == "cfg1" else 320,
               "seq_len": T, "heads": H, "head_dim": D, "chunk": 64,
               "parallelism": f"dp{world}", "l2": "inputs larger than L2 (128 MiB per tensor), no flush"}
@@ -632,7 +786,9 @@ def main():
         ncu4 = len(cfg4_cu_seqlens()) - 1
         config.update({"global_batch": world, "seq_len": CFG4_WINDOWS * T,
                        "packing": f"{CFG4_WINDOWS} windows x {T} tokens, {ncu4} documents (log-uniform lengths in "
-                                  "[32, 4096], seed 42), cu_seqlens int32, state and conv history reset per document"})
+                                  "[32, 4096], seed 42), cu_seqlens int32 built on the device from the windows' "
+                                  f"end-of-document tokens every step (capacity {CFG4_CAPACITY}), state and conv "
+                                  "history reset per document"})
     if a.workload == "cfg3":
         per_rank = len(range(CFG3_SEQS)[dp_shard(CFG3_SEQS, rank, world)])
         config.update({"global_batch": CFG3_SEQS, "micro_batch": min(per_rank, CFG3_MICRO),
@@ -643,9 +799,36 @@ def main():
     if mixer:
         config.update({"global_batch": (a.batch or 4) * world, "hidden": DIM, "decay_rank": DECAY_RANK,
                        "l2": "activations larger than L2 (48 MiB input, 256 MiB projections), no flush"})
+    if decode:
+        Bd = a.batch or DECODE_BATCH
+        config.update({"global_batch": Bd * world, "seq_len": 1, "chunk": None,
+                       "step": "one kda_decode call: one token for each sequence (ShortConv with its history + "
+                               "the recurrence), state and conv history carried",
+                       "l2": (f"fp32 states ({Bd * H * D * D * 4 >> 20} MiB) "
+                              + ("larger than L2, no flush" if Bd * H * D * D * 4 > 126e6 else "fit in L2"))})
+        if world > 1:
+            config["all_reduce"] = None
     sample = cpu_block_sample if mixer else cpu_sample
     what = "mixer block (torch fp32 ops around the oracle recurrence)" if mixer else \
         "16 heads (oracle restatement of the reference CPU path, torch fp32 autograd)"
+    if a.impl == "reference" and decode:
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        Bd = a.batch or DECODE_BATCH
+        cpu_decode_sample(Bd, max(a.warmup, 1), threads)
+        rate, secs = cpu_decode_sample(Bd, a.steps, threads)
+        config["cpu_sample"] = f"each step: one token for {Bd} sequences x {H} heads on the host (no conv history)"
+        line = {"metric": metric, "value": rate, "unit": "tokens/s", "n_gpus": a.gpus, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": secs / a.steps * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "impl": "reference",
+                "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                 "sample": f"{a.steps} decode steps of {Bd} sequences (oracle restatement of the "
+                                           "reference recurrence, fp32)"},
+                "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if a.impl == "reference":
         if rank != 0:
             return
@@ -677,7 +860,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    res = (bench_mixer if mixer else bench_ours)(a, rank, world, local_rank)
+    res = (bench_mixer if mixer else (bench_decode if decode else bench_ours))(a, rank, world, local_rank)
     if res is None:  # --profile
         if world > 1:
             import torch.distributed as dist
@@ -687,7 +870,20 @@ def main():
     cpu = None
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
-        if mixer:
+        if decode:
+            Bd = a.batch or DECODE_BATCH
+            cpu_decode_sample(Bd, 1, threads)  # warm-up
+            n_s, dt = 0, 0.0
+            while n_s < 3 or dt < 5.0:
+                _, d = cpu_decode_sample(Bd, 1, threads)
+                dt += d
+                n_s += 1
+                if dt > 20.0:
+                    break
+            cpu = {"value": Bd * n_s / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                   "sample": f"{n_s} decode steps of {Bd} sequences x {H} heads ({dt:.1f} s; oracle restatement "
+                             "of the reference recurrence, fp32, no conv history)"}
+        elif mixer:
             torch.set_num_threads(threads)
             rate, dt = cpu_block_sample(1024)
             n_s, tok = 1, 1024
@@ -701,12 +897,14 @@ def main():
                 if dt > 30.0:
                     break
             rate = n_s * tok / dt
-        cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{n_s} x (1 sequence x {tok} tokens fwd+bwd) ({dt:.1f} s), {what}"}
+        if not decode:
+            cpu = {"value": rate, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                   "sample": f"{n_s} x (1 sequence x {tok} tokens fwd+bwd) ({dt:.1f} s), {what}"}
     if rank == 0:
         line = {"metric": metric, "value": res["value"], "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
                 "warmup": a.warmup, "ms_per_step": res["ms"], "higher_is_better": True,
-                "scaling": "strong" if a.workload == "cfg3" else "weak", "vs_baseline": None, "dtype": "bf16",
+                "scaling": "strong" if a.workload == "cfg3" else "weak", "vs_baseline": None,
+                "dtype": "f32" if decode else "bf16",
                 "data": "synthetic", "config": config, "roofline": res["roofline"], "cpu_baseline": cpu,
                 "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"]}
         print(json.dumps(line), flush=True)

@@ -97,7 +97,7 @@ def timing_reset() -> None:
 
 def timing_read() -> dict[str, tuple[int, float]]:
     """{kernel name: (launches, total ms)} since the last reset."""
-    n = 16
+    n = 32
     names = (ctypes.c_char_p * n)()
     launches = (ctypes.c_int * n)()
     ms = (ctypes.c_float * n)()

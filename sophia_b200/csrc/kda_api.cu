@@ -183,12 +183,12 @@ int check_common(const void* q, const void* k, const void* v, const void* g, con
 // ---- optional per-launch device timing (CUDA events on the launch stream)
 enum KernelId {
   K_TABLE = 0, K_FWD_INTRA, K_FWD_STATE, K_BWD_STATE, K_BWD_INTRA, K_BWD_POST, K_REDUCE, K_RECURRENT,
-  K_GNORM_FWD, K_GNORM_BWD, K_F32_PREP, K_F32_FWD, K_F32_BWD, K_F32_DC, K_F32_CONV, K_COUNT
+  K_GNORM_FWD, K_GNORM_BWD, K_F32_PREP, K_F32_FWD, K_F32_BWD, K_F32_DC, K_F32_CONV, K_DOC_BOUNDS, K_COUNT
 };
 const char* const kKernelNames[K_COUNT] = {"chunk_table", "fwd_intra", "fwd_state",       "bwd_state",
                                            "bwd_intra",   "bwd_post",  "reduce",          "recurrent",
                                            "gated_norm_fwd", "gated_norm_bwd", "f32_prep", "f32_fwd",
-                                           "f32_bwd",     "f32_dc",    "f32_conv_bwd"};
+                                           "f32_bwd",     "f32_dc",    "f32_conv_bwd",    "doc_bounds"};
 
 struct Timing {
   std::mutex mu;
@@ -458,8 +458,11 @@ int kda_b200_doc_cu_seqlens(const int32_t* tokens, int64_t total_tokens, int win
   if (capacity < 1) return fail(KDA_ERR_INVALID, "capacity must be >= 1");
   if (!cu_seqlens || !n_docs || (total_tokens > 0 && !tokens))
     return fail(KDA_ERR_INVALID, "doc_cu_seqlens needs tokens, cu_seqlens and n_docs");
-  kda_doc_bounds_kernel<<<1, PACK_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-      tokens, (long long)total_tokens, window, eos_id, capacity, cu_seqlens, n_docs);
+  {
+    TimedLaunch tl(K_DOC_BOUNDS, static_cast<cudaStream_t>(stream));
+    kda_doc_bounds_kernel<<<1, PACK_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+        tokens, (long long)total_tokens, window, eos_id, capacity, cu_seqlens, n_docs);
+  }
   return launch_check("doc cu_seqlens");
 }
 
