@@ -519,9 +519,11 @@ int kda_b200_decode(const void* q, const void* k, const void* v, const void* g, 
   rp.conv_q = conv_q; rp.conv_k = conv_k; rp.conv_v = conv_v;
   rp.conv_state = conv_state;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  if ((rc = set_smem(kda_recurrent_kernel, REC_SMEM, "recurrent"))) return rc;
   {
     TimedLaunch tl(K_RECURRENT, st);
-    kda_recurrent_kernel<<<dim3(N, H), REC_THREADS, 0, st>>>(rp);
+    kda_recurrent_kernel<<<dim3(N, H), REC_THREADS, REC_SMEM, st>>>(rp);
   }
   return launch_check("recurrent");
 }

@@ -1,7 +1,8 @@
 // Token-by-token KDA recurrence for decode (fp32 state and arithmetic).
 //
-// One CTA (128 threads) per (sequence, head).  Thread v keeps column v of the
-// 128x128 state S[k][v] in registers for the whole sequence.  Per token, the
+// One CTA (128 threads) per (sequence, head).  The 128x128 state S[k][v] sits
+// in shared memory (64 KB, so three CTAs share an SM and their state loads
+// overlap each other's work) and thread v updates column v in place.  Per token, the
 // CTA builds the normalised q (times scale), the normalised k and the decay
 // alpha_k = exp(lb * sigmoid(exp(A_log) (g_k + dt_bias_k))) in shared memory,
 // then every thread runs the reference's update on its column:
@@ -24,6 +25,7 @@
 namespace kda {
 
 constexpr int REC_THREADS = 128;
+constexpr int REC_SMEM = D * D * 4;  // the fp32 state, dynamic shared memory
 
 struct RecurrentParams {
   SeqInfo seq;
@@ -64,6 +66,7 @@ __device__ __forceinline__ float rec_block_sum(float x, float* red) {
 }
 
 __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentParams P) {
+  extern __shared__ __align__(16) float rec_state[];  // [128][128]: row k, column v
   __shared__ float qn[D], kn[D], alpha[D];
   __shared__ float red[2][4];
   const int n = blockIdx.x, h = blockIdx.y, H = P.H, vi = threadIdx.x;
@@ -74,9 +77,20 @@ __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentPar
   }
   const size_t stateoff = ((size_t)n * H + h) * D * D;
 
-  float S[D];
-#pragma unroll
-  for (int kk = 0; kk < D; ++kk) S[kk] = P.h0 ? P.h0[stateoff + (size_t)kk * D + vi] : 0.f;
+  // the state -> shared memory (cp.async, 16-byte chunks, when aligned)
+  float* const S = rec_state;
+  if (P.h0) {
+    const float* src = P.h0 + stateoff;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      for (int i = vi; i < D * D / 4; i += REC_THREADS) cp_async16(S + 4 * i, src + 4 * i, true);
+    } else {
+      for (int i = vi; i < D * D; i += REC_THREADS) S[i] = src[i];
+    }
+  } else {
+    for (int i = vi; i < D * D / 4; i += REC_THREADS)
+      reinterpret_cast<float4*>(S)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  cp_async_commit();
 
   const float eA = expf(P.A_log[h]);
   const float bias = P.dt_bias[(size_t)h * D + vi];
@@ -92,6 +106,8 @@ __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentPar
       hv[s] = cs[2 * inner * 3 + s];
     }
   }
+  cp_async_wait<0>();
+  __syncthreads();  // (each thread then reads and writes only its own column)
   for (int t = bos; t < eos; ++t) {
     const size_t row = ((size_t)t * H + h) * D + vi;
     float qx = rec_load(P.q, row, P.fp32_inputs), kx = rec_load(P.k, row, P.fp32_inputs);
@@ -111,17 +127,19 @@ __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentPar
     const float beta = 1.f / (1.f + expf(-bx));
     __syncthreads();
     float pred = 0.f;
-#pragma unroll
+#pragma unroll 16
     for (int kk = 0; kk < D; ++kk) {
-      S[kk] *= alpha[kk];
-      pred = fmaf(kn[kk], S[kk], pred);
+      const float sv = S[kk * D + vi] * alpha[kk];
+      S[kk * D + vi] = sv;
+      pred = fmaf(kn[kk], sv, pred);
     }
     const float u = (vx - pred) * beta;
     float out = 0.f;
-#pragma unroll
+#pragma unroll 16
     for (int kk = 0; kk < D; ++kk) {
-      S[kk] = fmaf(kn[kk], u, S[kk]);
-      out = fmaf(qn[kk], S[kk], out);
+      const float sv = fmaf(kn[kk], u, S[kk * D + vi]);
+      S[kk * D + vi] = sv;
+      out = fmaf(qn[kk], sv, out);
     }
     if (P.fp32_inputs)
       static_cast<float*>(P.o)[row] = out;
@@ -130,8 +148,8 @@ __global__ void __launch_bounds__(REC_THREADS) kda_recurrent_kernel(RecurrentPar
     __syncthreads();  // qn/kn/alpha/red are rewritten by the next token
   }
   if (P.ht) {
-#pragma unroll
-    for (int kk = 0; kk < D; ++kk) P.ht[stateoff + (size_t)kk * D + vi] = S[kk];
+#pragma unroll 16
+    for (int kk = 0; kk < D; ++kk) P.ht[stateoff + (size_t)kk * D + vi] = S[kk * D + vi];
   }
   if (conv) {
     float* cs = P.conv_state + (size_t)n * 3 * inner * 3 + ch * 3;
