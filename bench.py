@@ -466,6 +466,10 @@ def cpu_sample(tokens: int, threads: int | None = None):
 DECODE_METRIC = ("KDA decode tokens/s at B=256 sequences,H=16,D=128, one token per sequence per call "
                  "(fp32 state) + % roofline")
 DECODE_BATCH = 256  # the fp32 states (268 MB) exceed L2, so every call streams them from HBM
+# DRAM bytes per decode call and sequence, from one ncu capture of `python bench.py
+# --workload decode --steps 20 --warmup 3` (dram__bytes_read.sum + dram__bytes_write.sum,
+# kda_recurrent_kernel, B = 256: 291.7 MB read + 233.8 MB written per launch)
+NCU_DECODE_DRAM_BYTES_PER_SEQ = 525.5e6 / 256
 
 
 def decode_bytes_per_step(B: int) -> int:
@@ -585,8 +589,10 @@ def bench_decode(a, rank, world, local_rank):
                 "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
         "gpu_launches": int(launches),
         "roofline": {"bound": "hbm", "kernel": "recurrent", "achieved": round(achieved, 1), "peak": hbm,
-                     "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None, "peak_source": src,
-                     "bytes_per_launch": alg, "kernel_ms_per_step": {k: round(v[1] / a.steps, 4)
+                     "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": round(NCU_DECODE_DRAM_BYTES_PER_SEQ * B),
+                     "traffic_source": "ncu dram bytes of this workload at B=256, scaled by the sequences",
+                     "peak_source": src, "bytes_per_launch": alg, "kernel_ms_per_step": {k: round(v[1] / a.steps, 4)
                                                                      for k, v in kern.items() if v[0]}},
     }
 
