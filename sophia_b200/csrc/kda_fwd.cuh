@@ -34,44 +34,48 @@ struct FwdIntraParams {
 
 // Shared-memory layout of the forward intra kernel (bytes).  The raw inputs,
 // taps and biases have regions of their own, so that the next item's loads can
-// land while the current item's blocks and inverse are computed.
+// land while the current item's products and inverse are computed.  The
+// tcgen05 operand tiles come first (1 KB aligned, 128B-swizzled).
 struct IntraSmem {
-  static constexpr int RAW = 0;                         // 3 x 67 x 128 bf16 (then the q/k/v product tiles)
+  static constexpr int KQ = 0;                          // [Ka; Qa] 128 x 128 bf16 (cumsum scratch before)
+  static constexpr int KC = KQ + 32768;                 // [Kc_0; ..; Kc_3] 160 x 128 bf16
+  static constexpr int KE = KC + KC_BYTES;              // Ke, then V: 64 x 128 bf16 each
+  static constexpr int RAW = KE + 32768;                // 3 x 67 x 128 bf16 (then the saved q/k/v tiles)
   static constexpr int GRAW = RAW + 3 * 67 * D * 2;     // 64 x 128 bf16
   static constexpr int GAM = GRAW + 64 * D * 2;         // 64 x LDG fp32
-  static constexpr int OPS = GAM + 64 * LDG * 4;        // 6 x 64 x LD128 bf16 (cumsum scratch before)
-  static constexpr int OPSZ = 64 * LD128 * 2;
-  static constexpr int CVEC = OPS + 6 * OPSZ;           // 6 x 128 fp32
-  static constexpr int BETA = CVEC + 6 * D * 4;         // 64 fp32
+  static constexpr int BETA = GAM + 64 * LDG * 4;       // 64 fp32
   static constexpr int BRAW = BETA + 64 * 4;            // 64 bf16
   static constexpr int TAPS = BRAW + 64 * 2;            // 3 x 128 x 4 fp32
   static constexpr int BIAS = TAPS + 3 * D * 16;        // dt_bias [128], A_log, padding
-  static constexpr int NXT = BIAS + (D + 4) * 4;        // next item: index, bos, t0, t1; then the
-                                                        // mbarrier of the raw rows (offset 16)
-  static constexpr int XTMP = NXT + 32;                 // 3 warps x 16 x 17 fp32
-  static constexpr int TBF = XTMP + 3 * 16 * 17 * 4;    // 64 x LD64 bf16
-  static constexpr int END = TBF + 64 * LD64 * 2;
+  static constexpr int NXT = BIAS + (D + 4) * 4;        // next item: index, bos, t0, t1; then the mbarriers
+                                                        // of the raw rows, the L'/M and the W/U products
+                                                        // (offsets 16, 24, 32) and the TMEM slot (40)
+  static constexpr int XTMP = NXT + 64;                 // 3 warps x 16 x 17 fp32
+  static constexpr int END = XTMP + 3 * 16 * 17 * 4;
   // aliases valid once the operands are built and the product stores completed
   static constexpr int LP = GAM;                        // 64 x LDF64 fp32
   static constexpr int AINV = LP + 64 * LDF64 * 4;      // 64 x LDF64 fp32
-  static constexpr int MSM = OPS + OPSZ;                // 64 x LD64 bf16 over Ka (dead once L' is formed)
-  static_assert(AINV + 64 * LDF64 * 4 <= OPS, "the inverse tiles overflow the decay tile");
+  // aliases valid once the L'/M products completed (the Kc tiles are dead)
+  static constexpr int TT = KC;                         // T = A diag(beta), 64 x 64 bf16 swizzled
+  static constexpr int ASW = KC + 8192;                 // A for the backward, 64 x 64 bf16 swizzled
+  static constexpr int LSW = KC + 16384;                // L' for the backward, 64 x 64 bf16 swizzled
+  static_assert(AINV + 64 * LDF64 * 4 <= BETA, "the inverse tiles overflow the decay tile");
+  static_assert(LSW + 8192 <= KE, "T, A and L' overflow the Kc tiles");
+  static_assert(KC % 1024 == 0 && KE % 1024 == 0 && (KC_BYTES / 2) % 1024 == 0, "swizzled operand atoms");
   static_assert(RAW % 16 == 0 && GAM % 16 == 0 && BETA % 16 == 0 && AINV % 16 == 0 && TAPS % 16 == 0 &&
-                    BIAS % 16 == 0 && 3 * 64 * D * 2 <= GRAW,
-                "bulk-copy and cp.async targets");
-  static_assert(64 * LD64 * 2 <= OPSZ && 16 * D * 4 <= OPSZ, "M staging or cumsum scratch overflows a tile");
-  static_assert((RAW + 67 * D * 2) % 128 == 0 && (RAW + 2 * 67 * D * 2) % 128 == 0 && GRAW % 128 == 0,
+                    BIAS % 16 == 0 && NXT % 8 == 0 && 3 * 64 * D * 2 <= GRAW - RAW,
+                "bulk-copy, cp.async and mbarrier targets");
+  static_assert(16 * D * 4 <= KC - KQ, "cumsum scratch overflows the operand tile");
+  static_assert((RAW + 67 * D * 2) % 128 == 0 && (RAW + 2 * 67 * D * 2) % 128 == 0 && GRAW % 128 == 0 &&
+                    RAW % 128 == 0,
                 "tiled TMA destinations");
   static_assert(END <= 232448, "shared memory");
 };
 
-__device__ __forceinline__ void store_rows64(bf16* gdst, const bf16* s, int ld, int nrows, int H, int h, int t0) {
-  for (int i = threadIdx.x; i < nrows * 8; i += blockDim.x) {
-    int r = i >> 3, cc = i & 7;
-    bf16x8 v = *reinterpret_cast<const bf16x8*>(s + r * ld + cc * 8);
-    *reinterpret_cast<bf16x8*>(gdst + ((size_t)(t0 + r) * H + h) * 64 + cc * 8) = v;
-  }
-}
+// TMEM columns of the forward chunk kernel: the L'/M accumulator (M = 128,
+// N = 160; row block I reads columns kc_row(I) .. kc_row(I) + 16 I + 15) at 0;
+// W and U (M = 64, N = 128, at lane offsets 0 and 16) at WU_COL.
+constexpr uint32_t WU_COL = 256;
 
 // The CTA's next valid item from the shared counter (items below gridDim.x belong to
 // the CTA of that index), or n_items when none is left.  Dynamic: a CTA that starts
@@ -86,13 +90,14 @@ __device__ __forceinline__ int grab_item(const FwdIntraParams& P, int n_items, i
 }
 
 __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const __grid_constant__ FwdIntraParams P) {
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem[];
   const int H = P.in.H, G = P.grid_chunks, n_items = G * H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int* nxt = reinterpret_cast<int*>(smem + IntraSmem::NXT);
   ChunkPos pos = chunk_pos(P.seq, blockIdx.x % G);
   int item = blockIdx.x;
   if (!pos.valid) {  // block-uniform: one thread grabs, all read
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       ChunkPos p0;
       nxt[0] = grab_item(P, n_items, G, p0);
     }
@@ -101,6 +106,10 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     if (item >= n_items) return;
     pos = chunk_pos(P.seq, item % G);
     __syncthreads();  // nxt is rewritten below
+  }
+  if (smem_u32(smem) & 1023) {  // swizzled operand tiles need 1 KB alignment (block-uniform)
+    if (tid == 0) atomicExch(&g_kda_device_error, 10);
+    return;
   }
 
   PrologueSmem ps;
@@ -111,43 +120,56 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
   ps.braw = reinterpret_cast<bf16*>(smem + IntraSmem::BRAW);
   ps.gam = reinterpret_cast<float*>(smem + IntraSmem::GAM);
   ps.beta = reinterpret_cast<float*>(smem + IntraSmem::BETA);
-  ps.tot = reinterpret_cast<float*>(smem + IntraSmem::OPS);  // scratch, before operands
+  ps.tot = reinterpret_cast<float*>(smem + IntraSmem::KQ);  // scratch, before the operands
   ps.taps = reinterpret_cast<float*>(smem + IntraSmem::TAPS);
   ps.bias = reinterpret_cast<float*>(smem + IntraSmem::BIAS);
   uint64_t* raw_ready = reinterpret_cast<uint64_t*>(smem + IntraSmem::NXT + 16);
+  uint64_t* mb_lm = raw_ready + 1;
+  uint64_t* mb_wu = raw_ready + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(raw_ready + 3);
   const bool save_products = P.QN != nullptr;
-  if (threadIdx.x == 0) {
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) {
     tc::mbar_init(raw_ready, 1);
+    tc::mbar_init(mb_lm, 1);
+    tc::mbar_init(mb_wu, 1);
     tc::fence_mbar_init();
   }
+  tc::fence_before_sync();
   __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t sb = smem_u32(smem);
+  // K-major and MN-major descriptors from a base: the address field (bits 0-13,
+  // address / 16) plus the operand's byte offset / 16
+  const uint64_t kbase = tc::smem_desc(sb, 16, 1024), mbase = tc::smem_desc(sb, 8192, 1024);
+  const uint32_t idLM = tc::idesc_bf16(128, KC_ROWS, false, false);  // [Ka; Qa] x Kc^T, both K-major
+  const uint32_t idWU = tc::idesc_bf16(64, 128, false, true);        // A = T K-major, B = Ke / V MN-major
 
   bf16 braw = prologue_issue_loads(P.in, ps, pos, item / G, P.conv, raw_ready, P.maps);
   cp_async_commit();
-  uint32_t raw_phase = 0;
+  uint32_t raw_phase = 0, mma_phase = 0;
   for (;;) {
     const int c = item % G, h = item / G;
     const int nvalid = pos.t1 - pos.t0;
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       // the next item (its table lookups overlap this item's loads)
       ChunkPos np;
       nxt[0] = grab_item(P, n_items, G, np);
       nxt[1] = np.bos; nxt[2] = np.t0; nxt[3] = np.t1;
-      // the previous item's A store reads the region the decay tile is rebuilt in
+      // the previous item's A / L' stores read the Kc region the operands are rebuilt in
       if (P.A) tc::bulk_wait_read_all();
     }
     const bool arrived = tc::mbar_wait(raw_ready, raw_phase, P.wait_polls);
     if (P.conv) zero_foreign_halo(ps, pos);
     cp_async_wait<0>();
-    if (threadIdx.x >= LOADER_T0) ps.braw[threadIdx.x - LOADER_T0] = braw;
+    if (tid >= LOADER_T0) ps.braw[tid - LOADER_T0] = braw;
     if (__syncthreads_or(!arrived)) {
       // this item's inputs did not arrive in time: record it, let the copies in
       // flight land (bounded wait) and leave without touching another item
-      if (threadIdx.x == 0) atomicExch(&g_kda_device_error, 8);
+      if (tid == 0) atomicExch(&g_kda_device_error, 8);
       tc::mbar_wait(raw_ready, raw_phase);
-      if (threadIdx.x == 0) tc::bulk_wait_all();
-      __syncthreads();
-      return;
+      break;
     }
     raw_phase ^= 1u;
 
@@ -158,7 +180,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     // cumsum tile and beta, already in shared memory) five bulk stores issued by
     // one thread; they complete while the operands are built
     if (save_products) {
-      const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
+      const int tg = tid >> 4, cg = tid & 15;
       bf16* tq = reinterpret_cast<bf16*>(smem + IntraSmem::RAW);
 #pragma unroll
       for (int r = 0; r < STRIP; ++r) {
@@ -170,7 +192,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       }
       tc::fence_async_smem();
       __syncthreads();
-      if (threadIdx.x == 0) {
+      if (tid == 0) {
         const size_t tix = tile_index(P.seq, c, h);
         constexpr uint32_t TB = TILE64_ELEMS * 2;
         tc::bulk_s2g(P.QN + tix * TILE64_ELEMS, tq, TB);
@@ -182,36 +204,25 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
       }
     }
 
-    Operands op;
-    op.Qa = reinterpret_cast<bf16*>(smem + IntraSmem::OPS);
-    op.Ka = op.Qa + 64 * LD128;
-    op.Kd = op.Ka + 64 * LD128;
-    op.Kb = op.Kd + 64 * LD128;
-    op.V = op.Kb + 64 * LD128;
-    op.Ke = op.V + 64 * LD128;
-    op.cvec = reinterpret_cast<float*>(smem + IntraSmem::CVEC);
-    op.er = nullptr;
-    op.ec = nullptr;
-    {
-      float qt[STRIP][8], kbar[STRIP][8];
-      build_operands<true>(s, ps.gam, op, qt, kbar);
-      const int tg = threadIdx.x >> 4, cg = threadIdx.x & 15;
-#pragma unroll
-      for (int r = 0; r < STRIP; ++r) {
-        int t = STRIP * tg + r;
-        if (t < nvalid) {
-          size_t off = ((size_t)(pos.t0 + t) * H + h) * D + 8 * cg;
-          *reinterpret_cast<bf16x8*>(P.Qt + off) = pack8(qt[r]);
-          *reinterpret_cast<bf16x8*>(P.Kb + off) = pack8(kbar[r]);
-        }
-      }
-      if (threadIdx.x < D)
-        P.dC[((size_t)c * H + h) * D + threadIdx.x] = ex2(ps.gam[63 * LDG + threadIdx.x]);
-    }
-    if (save_products && threadIdx.x == 0) tc::bulk_wait_read_all();  // the raw region is reused from here on
-    tc::fence_async_smem();  // this item's generic accesses of the raw rows precede the next item's bulk copies
+    build_tc_operands(s, ps.gam, smem + IntraSmem::KQ, smem + IntraSmem::KC, smem + IntraSmem::KE, P.Qt, P.Kb,
+                      pos.t0, nvalid, H, h);
+    if (tid < D) P.dC[((size_t)c * H + h) * D + tid] = ex2(ps.gam[63 * LDG + tid]);
+    if (save_products && tid == 0) tc::bulk_wait_read_all();  // the raw region is reused from here on
+    tc::fence_async_smem();  // operand tiles -> tensor cores; raw rows -> the next item's bulk copies
+    tc::fence_before_sync();
     __syncthreads();
-    // the next item's inputs stream in while this one's blocks are computed
+    if (tid == 32) {
+      // L' and M: [Ka; Qa] (M = 128) x [Kc_0; ..; Kc_3] (N = 160)
+      tc::fence_after_sync();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t a = kbase + (uint64_t)((IntraSmem::KQ + (ks >> 2) * 16384 + (ks & 3) * 32) >> 4);
+        const uint64_t b = kbase + (uint64_t)((IntraSmem::KC + (ks >> 2) * (KC_BYTES / 2) + (ks & 3) * 32) >> 4);
+        tc::mma_bf16(tbase, a, b, idLM, ks > 0);
+      }
+      tc::mma_commit(mb_lm);
+    }
+    // the next item's inputs stream in while this one's products are computed
     const int next = nxt[0];
     ChunkPos npos;
     npos.valid = next < n_items;
@@ -222,93 +233,141 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     float* Lp = reinterpret_cast<float*>(smem + IntraSmem::LP);
     float* Ainv = reinterpret_cast<float*>(smem + IntraSmem::AINV);
     float* xtmp = reinterpret_cast<float*>(smem + IntraSmem::XTMP);
-    bf16* Tbf = reinterpret_cast<bf16*>(smem + IntraSmem::TBF);
-    bf16* Msm = reinterpret_cast<bf16*>(smem + IntraSmem::MSM);
-    l_blocks(op, Lp);
-    __syncthreads();
-    // the diagonal inverse (warps 0-1) overlaps the M blocks (warps 4-15)
+    if (__syncthreads_or(!tc::mbar_wait(mb_lm, mma_phase))) {
+      // the products did not complete in time: record it, let them (and the
+      // next item's copies) land, bounded, and leave
+      if (tid == 0) atomicExch(&g_kda_device_error, 10);
+      tc::mbar_wait(mb_lm, mma_phase);
+      if (npos.valid) tc::mbar_wait(raw_ready, raw_phase);
+      break;
+    }
+    tc::fence_after_sync();
+    // L' and M out of TMEM (row i of [Ka; Qa] in lane i): warp quarter q holds
+    // rows 32 q .. 32 q + 31 (L' for q < 2, M for q >= 2), warp w / 4 = kb the
+    // columns 16 kb .. 16 kb + 15 of those rows (zero above the row's block)
     {
-      const int warp = threadIdx.x >> 5;
-      if (warp < 2) {
-        tri_inverse_diag(Lp, ps.beta, Ainv);
-      } else if (warp >= 4) {
-        if (warp < 14) lm_block_task(op, 1, warp - 4, Lp, Msm);
-        zero_m_upper(Msm, 128, INTRA_THREADS - 128);
+      const int q = warp & 3, kb = warp >> 2;
+      const int Ia = 2 * (q & 1), Ib = Ia + 1, I = lane < 16 ? Ia : Ib;
+      const int i = 32 * (q & 1) + lane;
+      const uint32_t trow = tbase + ((uint32_t)(32 * q) << 16);
+      const bool has = kb <= I, lower = q < 2;
+      float x[16], t16[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) x[e] = 0.f;
+      if (kb <= Ia) {  // warp-uniform: the block of lanes 0-15
+        tc::tmem_ld16(trow + kc_row(Ia) + 16 * kb, t16);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = lane < 16 ? t16[e] : x[e];
+      }
+      if (kb <= Ib) {  // the block of lanes 16-31
+        tc::tmem_ld16(trow + kc_row(Ib) + 16 * kb, t16);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x[e] = lane < 16 ? x[e] : t16[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int j = 16 * kb + e;
+        if (!(has && (lower ? j < i : j <= i))) x[e] = 0.f;
+      }
+      if (lower) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) Lp[i * LDF64 + 16 * kb + e] = x[e];
+        if (P.A) {
+          float x0[8], x1[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) { x0[e] = x[e]; x1[e] = x[8 + e]; }
+          bf16* lsw = reinterpret_cast<bf16*>(smem + IntraSmem::LSW);
+          *reinterpret_cast<bf16x8*>(lsw + sw64_chunk(i, 2 * kb)) = pack8(x0);
+          *reinterpret_cast<bf16x8*>(lsw + sw64_chunk(i, 2 * kb + 1)) = pack8(x1);
+        }
+      } else if (i < nvalid) {
+        uint4* dst = reinterpret_cast<uint4*>(P.M + ((size_t)(pos.t0 + i) * H + h) * 64 + 16 * kb);
+        dst[0] = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
+                            pack_bf16(x[6], x[7]));
+        dst[1] = make_uint4(pack_bf16(x[8], x[9]), pack_bf16(x[10], x[11]), pack_bf16(x[12], x[13]),
+                            pack_bf16(x[14], x[15]));
       }
     }
     __syncthreads();
+    if (warp < 2) tri_inverse_diag(Lp, ps.beta, Ainv);
+    __syncthreads();
     tri_inverse_offdiag(Lp, ps.beta, Ainv, xtmp);
-    // T = A diag(beta) as bf16 (A's strictly-upper part is not stored: zeros)
-    for (int i = threadIdx.x; i < 64 * 32; i += blockDim.x) {
-      int r = i >> 5, cc = 2 * (i & 31);
-      float x0 = (cc <= r) ? Ainv[r * LDF64 + cc] * ps.beta[cc] : 0.f;
-      float x1 = (cc + 1 <= r) ? Ainv[r * LDF64 + cc + 1] * ps.beta[cc + 1] : 0.f;
-      *reinterpret_cast<uint32_t*>(Tbf + r * LD64 + cc) = pack_bf16(x0, x1);
-    }
-    // A and L' for the backward, as bf16 tiles in its tcgen05 operand layout
-    // (zeros above the diagonal), over the dead Qa and Kd operand tiles
-    bf16* Asw = op.Qa;
-    bf16* Lsw = op.Kd;
-    if (P.A) {
-      for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
-        const int r = i >> 3, c8 = i & 7;
-        float av[8], lv[8];
+    // T = A diag(beta) (the W/U operand) and A for the backward, as bf16 tiles in
+    // the tcgen05 operand layout (A's strictly-upper part is not stored: zeros)
+    {
+      bf16* tsw = reinterpret_cast<bf16*>(smem + IntraSmem::TT);
+      bf16* asw = reinterpret_cast<bf16*>(smem + IntraSmem::ASW);
+      for (int i2 = tid; i2 < 64 * 8; i2 += blockDim.x) {
+        const int r = i2 >> 3, c8 = i2 & 7;
+        float av[8], tv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int cc = 8 * c8 + u;
           av[u] = cc <= r ? Ainv[r * LDF64 + cc] : 0.f;
-          lv[u] = cc < r ? Lp[r * LDF64 + cc] : 0.f;
+          tv[u] = av[u] * ps.beta[cc];
         }
-        *reinterpret_cast<bf16x8*>(Asw + sw64_chunk(r, c8)) = pack8(av);
-        *reinterpret_cast<bf16x8*>(Lsw + sw64_chunk(r, c8)) = pack8(lv);
+        *reinterpret_cast<bf16x8*>(tsw + sw64_chunk(r, c8)) = pack8(tv);
+        if (P.A) *reinterpret_cast<bf16x8*>(asw + sw64_chunk(r, c8)) = pack8(av);
       }
     }
-    store_rows64(P.M, Msm, LD64, nvalid, H, h, pos.t0);
-    tc::fence_async_smem();  // A and L' (written by every thread) are read by the bulk stores below
+    tc::fence_async_smem();  // T -> tensor cores; A and L' -> the bulk stores
+    tc::fence_before_sync();
     __syncthreads();
-    // one bulk store each, completed before the exit
-    if (P.A && threadIdx.x == 0) {
+    if (tid == 32) {
+      // W = T Ke (lanes 0-15 of each quarter), U = T V (lanes 16-31): M = 64, N = 128
+      tc::fence_after_sync();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint64_t a = kbase + (uint64_t)((IntraSmem::TT + 32 * ks) >> 4);
+        tc::mma_bf16(tbase + WU_COL, a, mbase + (uint64_t)((IntraSmem::KE + ks * 2048) >> 4), idWU, ks > 0);
+        tc::mma_bf16(tbase + (16u << 16) + WU_COL, a, mbase + (uint64_t)((IntraSmem::KE + 16384 + ks * 2048) >> 4),
+                     idWU, ks > 0);
+      }
+      tc::mma_commit(mb_wu);
+    }
+    // A and L' for the backward: one bulk store each, completed before the
+    // operand tiles are rebuilt
+    if (P.A && tid == 0) {
       const size_t tix = tile_index(P.seq, c, h);
-      tc::bulk_s2g(P.A + tix * TILE64N64_ELEMS, Asw, TILE64N64_ELEMS * 2);
-      tc::bulk_s2g(P.LP + tix * TILE64N64_ELEMS, Lsw, TILE64N64_ELEMS * 2);
+      tc::bulk_s2g(P.A + tix * TILE64N64_ELEMS, smem + IntraSmem::ASW, TILE64N64_ELEMS * 2);
+      tc::bulk_s2g(P.LP + tix * TILE64N64_ELEMS, smem + IntraSmem::LSW, TILE64N64_ELEMS * 2);
       tc::bulk_commit();
     }
-
-    // W = T Ke, U = T V ; warp w -> rows 16(w&3), cols 32(w>>2)
+    if (__syncthreads_or(!tc::mbar_wait(mb_wu, mma_phase))) {
+      if (tid == 0) atomicExch(&g_kda_device_error, 10);
+      tc::mbar_wait(mb_wu, mma_phase);
+      if (npos.valid) tc::mbar_wait(raw_ready, raw_phase);
+      break;
+    }
+    tc::fence_after_sync();
+    mma_phase ^= 1u;
+    // W and U out of TMEM: warp quarter s holds rows 16 s .. 16 s + 15 (lane & 15)
+    // of W (lanes 0-15) and U (lanes 16-31); warp w / 4 = qd the channels 32 qd ..
     {
-      const int warp = threadIdx.x >> 5;
-      const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
-      float accW[4][4], accU[4][4];
-      zero_acc<4>(accW);
-      zero_acc<4>(accU);
-      warp_mma<4, false, true>(accW, Tbf, LD64, m0, op.Ke, LD128, n0, 0, 64);
-      warp_mma<4, false, true>(accU, Tbf, LD64, m0, op.V, LD128, n0, 0, 64);
-      // straight from the fragments as 16-byte runs (quad transpose), no staging
+      const int sq = warp & 3, qd = warp >> 2;
+      const int r = 16 * sq + (lane & 15);
+      float acc[32];
+      tc::tmem_ld32(tbase + ((uint32_t)(32 * sq) << 16) + WU_COL + 32 * qd, acc);
+      if (r < nvalid) {
+        bf16* dst = (lane < 16 ? P.W : P.U) + ((size_t)(pos.t0 + r) * H + h) * D + 32 * qd;
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        uint32_t ww[4], wu[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          ww[j] = pack_bf16(accW[j][e], accW[j][e + 1]);
-          wu[j] = pack_bf16(accU[j][e], accU[j][e + 1]);
-        }
-        quad_transpose4(ww);
-        quad_transpose4(wu);
-        const int r = m0 + acc_row(e);
-        if (r < nvalid) {
-          const size_t off = ((size_t)(pos.t0 + r) * H + h) * D + n0 + 8 * (threadIdx.x & 3);
-          *reinterpret_cast<uint4*>(P.W + off) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
-          *reinterpret_cast<uint4*>(P.U + off) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
-        }
+        for (int c4 = 0; c4 < 4; ++c4)
+          *reinterpret_cast<uint4*>(dst + 8 * c4) =
+              make_uint4(pack_bf16(acc[8 * c4 + 0], acc[8 * c4 + 1]), pack_bf16(acc[8 * c4 + 2], acc[8 * c4 + 3]),
+                         pack_bf16(acc[8 * c4 + 4], acc[8 * c4 + 5]), pack_bf16(acc[8 * c4 + 6], acc[8 * c4 + 7]));
       }
     }
+    tc::fence_before_sync();
     if (next >= n_items) break;
     item = next;
     pos = npos;
   }
-  if (P.A && threadIdx.x == 0) tc::bulk_wait_all();  // the A store reads shared memory
+  cp_async_wait<0>();
+  if (tid == 0) tc::bulk_wait_all();  // the bulk stores read shared memory
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
 }
-
 
 // ---------------------------------------------------------------- state pass
 struct FwdStateParams {

@@ -272,173 +272,107 @@ __device__ __forceinline__ void prologue_compute(const PrologueIn& in, const Pro
   __syncthreads();
 }
 
-// Operand tiles (bf16, row stride LD128) built from the strip.
-struct Operands {
-  bf16* Qa;  // q * a        (row-side, reference r(I))
-  bf16* Ka;  // k * a
-  bf16* Kd;  // k / a        (column side of diagonal blocks)
-  bf16* Kb;  // k * b        (column side of off-diagonal blocks, reference e(J))
-  bf16* V;   // v
-  bf16* Ke;  // k * 2^Gam
-  float* cvec;  // [6][128] c_IJ = 2^(Gam_r(I) - Gam_e(J)), pair p = I(I-1)/2 + J
-  float* er;    // [4][128] 2^Gam_r(J)           (may be null)
-  float* ec;    // [4][128] 2^(Gam_C - Gam_e(J)) (may be null)
-};
-
+// Sub-chunk pair index p = I (I - 1) / 2 + J of an off-diagonal pair J < I
+// (pairs (1,0), (2,0), (2,1), (3,0), (3,1), (3,2)).
 __device__ __forceinline__ int pair_index(int I, int J) { return I * (I - 1) / 2 + J; }
 
-// Builds the operand tiles; optionally also returns the strip of q*2^Gam and
-// k*2^(Gam_C - Gam) (the forward's Qt and Kbar) through qt/kbar.
-//   a = 2^(Gam - Gam_r(J)) <= 1, ia = 1/a (exact exponent, second ex2),
-//   b = 2^(Gam_e(J) - Gam) = ia * 2^(Gam_e(J) - Gam_r(J)): a product of a
-//   factor in [1, 2^116] and one in [2^-116, 1], so neither overflows and the
-//   product is at least 2^-116.
-template <bool WANT_QK_DECAYED>
-__device__ __forceinline__ void build_operands(const Strip& s, const float* gam, const Operands& op,
-                                               float (*qt)[8], float (*kbar)[8]) {
+// Byte offset of the 16-byte chunk c8 (columns 8 c8 .. 8 c8 + 7) of row r in a
+// 128B-swizzled bf16 tile of `rows` rows: 64-column atoms of rows x 128 bytes
+// one after the other, chunk position c8 ^ (r & 7) inside a row (the tcgen05
+// operand layout of kda_tc.cuh; every atom starts on a 1 KB boundary).
+__device__ __forceinline__ uint32_t sw_rows_byte(int rows, int r, int c8) {
+  return (uint32_t)((c8 >> 3) * rows * 128 + r * 128 + (((c8 & 7) ^ (r & 7)) << 4));
+}
+
+// The forward's tcgen05 block products of L' and M.  With a = 2^(Gam - Gam_r(J))
+// (J the token's own sub-chunk, r(J) its first token) and, per row block I,
+//   Kc_I[j] = k_j 2^(Gam_r(I) - Gam_j)   for the tokens j < 16 (I + 1),
+// every entry of row block I is one dot product over the 128 channels:
+//   L'[i, j] = Ka_i . Kc_I[j],   M[i, j] = Qa_i . Kc_I[j]   (Ka = k a, Qa = q a),
+// so with the four Kc_I stacked as the rows of one B operand (N = 160), every
+// block is one M = 128 MMA chain ([Ka; Qa] against [Kc_0; ..; Kc_3]); row
+// block I reads the 16 (I + 1) columns of Kc_I and the epilogue masks them to
+// the strictly lower (L') or lower (M) part.  Bounds: a <= 1; for j in I the
+// factor of Kc_I is 2^(Gam_r(I) - Gam_j) <= 2^108 (15 tokens of log2 decay
+// >= -7.22 each); for j < r(I) it is at most 1 and is formed as
+// (k_j 2^(Gam_r(J) - Gam_j)) 2^(Gam_r(I) - Gam_r(J)), a factor in [1, 2^108]
+// times one in (0, 1]: the second flushes to zero only below 2^-126, where the
+// exact product is below 2^-18 -- negligible against the bf16 operands.
+//
+// Tiles of the operand region (128B-swizzled bf16, K-major over the channels
+// unless noted; every atom 1 KB aligned):
+//   KQ  [Ka; Qa]: 128 rows;
+//   KC  [Kc_0; Kc_1; Kc_2; Kc_3]: 160 rows, Kc_I from row kc_row(I) = 8 I (I + 1);
+//   KE  Ke = k 2^Gam, then V: 64 rows each (the MN-major B operands of
+//       W = T Ke and U = T V).
+__host__ __device__ constexpr int kc_row(int I) { return 8 * I * (I + 1); }
+constexpr int KC_ROWS = 160;             // kc_row(4)
+constexpr int KC_BYTES = KC_ROWS * 256;  // two 64-channel atoms
+
+// Builds KQ, KC and KE/V from the strip (shared-memory writes only; the caller
+// fences and syncs) and stores the strip of q 2^Gam and k 2^(Gam_C - Gam) (the
+// forward's Qt and Kbar, rows t0 .. t0 + nvalid - 1 of head h) to global memory.
+__device__ __forceinline__ void build_tc_operands(const Strip& s, const float* gam, unsigned char* kq,
+                                                  unsigned char* kc, unsigned char* kev, bf16* Qt, bf16* Kb,
+                                                  int t0, int nvalid, int H, int h) {
   const int tid = threadIdx.x;
   const int tg = tid >> 4, cg = tid & 15;
-  const int J = (STRIP * tg) >> 4;
-  const float* grow = gam + (16 * J) * LDG + 8 * cg;       // row r(J)
-  const float* gend = gam + (16 * J + 15) * LDG + 8 * cg;  // row e(J)
-  const float* gC = gam + 63 * LDG + 8 * cg;               // row C-1
-  float Gr[8], erv[8], ecv[8], rev[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    Gr[c] = grow[c];
-    float Ge = gend[c];
-    erv[c] = ex2(Gr[c]);
-    ecv[c] = ex2(gC[c] - Ge);
-    rev[c] = ex2(Ge - Gr[c]);
-  }
-#pragma unroll
-  for (int r = 0; r < STRIP; ++r) {
-    float qa[8], ka[8], kd[8], kb[8], ke[8];
+  const int J = (STRIP * tg) >> 4;  // warp-uniform (a warp holds tokens 4w .. 4w + 3)
+  const float* gch = gam + 8 * cg;
+  float Gr[8], kd[STRIP][8];
+  {
+    float erv[8], gC[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      float G = s.gam[r][c];
-      float a = ex2(G - Gr[c]);
-      float ia = ex2(Gr[c] - G);
-      float b = ia * rev[c];
-      qa[c] = s.q[r][c] * a;
-      ka[c] = s.k[r][c] * a;
-      kd[c] = s.k[r][c] * ia;
-      kb[c] = s.k[r][c] * b;
-      ke[c] = ka[c] * erv[c];
-      if (WANT_QK_DECAYED) {
-        qt[r][c] = qa[c] * erv[c];
-        kbar[r][c] = kb[c] * ecv[c];
+      Gr[c] = gch[(16 * J) * LDG + c];
+      erv[c] = ex2(Gr[c]);
+      gC[c] = gch[63 * LDG + c];
+    }
+#pragma unroll
+    for (int r = 0; r < STRIP; ++r) {
+      const int t = STRIP * tg + r;
+      float qa[8], ka[8], ke[8], qt[8], kbar[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float G = s.gam[r][c];
+        const float a = ex2(G - Gr[c]);
+        const float ia = ex2(Gr[c] - G);
+        qa[c] = s.q[r][c] * a;
+        ka[c] = s.k[r][c] * a;
+        kd[r][c] = s.k[r][c] * ia;
+        ke[c] = ka[c] * erv[c];
+        qt[c] = qa[c] * erv[c];
+        kbar[c] = s.k[r][c] * ex2(gC[c] - G);  // 2^(Gam_C - Gam) <= 1
+      }
+      *reinterpret_cast<bf16x8*>(kq + sw_rows_byte(128, t, cg)) = pack8(ka);
+      *reinterpret_cast<bf16x8*>(kq + sw_rows_byte(128, 64 + t, cg)) = pack8(qa);
+      *reinterpret_cast<bf16x8*>(kev + sw_rows_byte(64, t, cg)) = pack8(ke);
+      *reinterpret_cast<bf16x8*>(kev + 16384 + sw_rows_byte(64, t, cg)) = pack8(s.v[r]);
+      *reinterpret_cast<bf16x8*>(kc + sw_rows_byte(KC_ROWS, kc_row(J) + t, cg)) = pack8(kd[r]);
+      if (t < nvalid) {
+        const size_t off = ((size_t)(t0 + t) * H + h) * D + 8 * cg;
+        *reinterpret_cast<bf16x8*>(Qt + off) = pack8(qt);
+        *reinterpret_cast<bf16x8*>(Kb + off) = pack8(kbar);
       }
     }
-    int row = (STRIP * tg + r) * LD128 + 8 * cg;
-    *reinterpret_cast<bf16x8*>(op.Qa + row) = pack8(qa);
-    *reinterpret_cast<bf16x8*>(op.Ka + row) = pack8(ka);
-    *reinterpret_cast<bf16x8*>(op.Kd + row) = pack8(kd);
-    *reinterpret_cast<bf16x8*>(op.Kb + row) = pack8(kb);
-    *reinterpret_cast<bf16x8*>(op.V + row) = pack8(s.v[r]);
-    *reinterpret_cast<bf16x8*>(op.Ke + row) = pack8(ke);
   }
-  // per-pair and per-sub-chunk channel vectors
-  for (int i = tid; i < 6 * D; i += blockDim.x) {
-    int pidx = i / D, d = i - pidx * D;
-    int I = pidx >= 3 ? 3 : (pidx >= 1 ? 2 : 1);
-    int Jp = pidx - pair_index(I, 0);
-    op.cvec[i] = ex2(gam[(16 * I) * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
-  }
-  if (op.er) {
-    for (int i = tid; i < 4 * D; i += blockDim.x) {
-      int Jp = i / D, d = i - Jp * D;
-      op.er[i] = ex2(gam[(16 * Jp) * LDG + d]);
-      op.ec[i] = ex2(gam[63 * LDG + d] - gam[(16 * Jp + 15) * LDG + d]);
-    }
-  }
-}
-
-// Scales the 8 bf16 elements of an A fragment (k columns k0+2t, +1, +8, +9) by
-// per-channel factors.
-__device__ __forceinline__ void scale_A_frag(uint32_t (&a)[4], const float* sv, int k0) {
-  const int t = threadIdx.x & 3;
-  float s0 = sv[k0 + 2 * t], s1 = sv[k0 + 2 * t + 1];
-  float s2 = sv[k0 + 8 + 2 * t], s3 = sv[k0 + 9 + 2 * t];
-  float2 x;
-  x = unpack_bf16(a[0]); a[0] = pack_bf16(x.x * s0, x.y * s1);
-  x = unpack_bf16(a[1]); a[1] = pack_bf16(x.x * s0, x.y * s1);
-  x = unpack_bf16(a[2]); a[2] = pack_bf16(x.x * s2, x.y * s3);
-  x = unpack_bf16(a[3]); a[3] = pack_bf16(x.x * s2, x.y * s3);
-}
-
-// One 16x16 block (I, J) of X = [A_i . (B_j * 2^(Gam_i - Gam_j))] with A = Qa or
-// Ka rows of block I.  Result in acc[2][4] (two n8 tiles).
-__device__ __forceinline__ void block_product(float (&acc)[2][4], const bf16* Arow, const Operands& op,
-                                              int I, int J) {
-  zero_acc<2>(acc);
-  const bool diag = I == J;
-  const bf16* Bt = diag ? op.Kd : op.Kb;
-  const float* sv = diag ? nullptr : op.cvec + pair_index(I, J) * D;
+  // the later row blocks' copies: Kc_I = kd 2^(Gam_r(I) - Gam_r(J)), I > J
 #pragma unroll
-  for (int kk = 0; kk < D; kk += 16) {
-    uint32_t a[4], b[4];
-    load_A(a, Arow, LD128, 16 * I, kk);
-    if (!diag) scale_A_frag(a, sv, kk);
-    load_B_nk(b, Bt, LD128, 16 * J, kk);
-    mma16816(acc[0], a, b[0], b[1]);
-    mma16816(acc[1], a, b[2], b[3]);
-  }
-}
-
-// One 16x16 block of L' (which == 0, strictly lower on the diagonal, fp32 into
-// Lp, or bf16 into Msm when Lp is null) or of M (which == 1, lower-inclusive
-// on the diagonal, bf16 into Msm).
-// Blocks are numbered (0,0),(1,0),(1,1),(2,0),(2,1),(2,2),(3,0),...
-__device__ __forceinline__ void lm_block_task(const Operands& op, int which, int bi, float* Lp, bf16* Msm) {
-  int I = bi >= 6 ? 3 : (bi >= 3 ? 2 : (bi >= 1 ? 1 : 0));
-  int J = bi - I * (I + 1) / 2;
-  float acc[2][4];
-  block_product(acc, which ? op.Qa : op.Ka, op, I, J);
+  for (int d = 1; d < 4; ++d) {
+    const int I = J + d;
+    if (I < 4) {
+      float cp[8];
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
+      for (int c = 0; c < 8; ++c) cp[c] = ex2(gch[(16 * I) * LDG + c] - Gr[c]);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      int r = acc_row(e), c = acc_col(j, e);
-      int gi = 16 * I + r, gj = 16 * J + c;
-      float x = acc[j][e];
-      if (which) {
-        if (I == J && c > r) x = 0.f;
-        Msm[gi * LD64 + gj] = __float2bfloat16(x);
-      } else {
-        if (I == J && c >= r) x = 0.f;
-        if (Lp)
-          Lp[gi * LDF64 + gj] = x;
-        else
-          Msm[gi * LD64 + gj] = __float2bfloat16(x);
+      for (int r = 0; r < STRIP; ++r) {
+        float x[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) x[c] = kd[r][c] * cp[c];
+        *reinterpret_cast<bf16x8*>(kc + sw_rows_byte(KC_ROWS, kc_row(I) + STRIP * tg + r, cg)) = pack8(x);
       }
     }
-}
-
-// Zeroes the six strictly-upper 16x16 blocks of M, using threads [t0, t0+nt).
-__device__ __forceinline__ void zero_m_upper(bf16* Msm, int t0, int nt) {
-  for (int i = threadIdx.x - t0; i < 6 * 256; i += nt) {
-    int blk = i >> 8, e = i & 255;
-    int I = blk < 3 ? 0 : (blk < 5 ? 1 : 2);
-    int J = blk < 3 ? blk + 1 : (blk < 5 ? blk - 1 : 3);
-    Msm[(16 * I + (e >> 4)) * LD64 + 16 * J + (e & 15)] = __float2bfloat16(0.f);
   }
-}
-
-// L' blocks only (10 tasks over the 16 warps).  Only the lower blocks of Lp
-// are written: every reader masks the rest.  Caller syncs afterwards.
-__device__ __forceinline__ void l_blocks(const Operands& op, float* Lp) {
-  const int warp = threadIdx.x >> 5;
-  if (warp < 10) lm_block_task(op, 0, warp, Lp, nullptr);
-}
-// L' as a bf16 64 x LD64 tile, strictly lower, zeros above (warps 10-15 clear
-// the upper blocks while the others form the lower ones).  Caller syncs.
-__device__ __forceinline__ void l_blocks_bf16(const Operands& op, bf16* Lb) {
-  const int warp = threadIdx.x >> 5;
-  if (warp < 10)
-    lm_block_task(op, 0, warp, nullptr, Lb);
-  else
-    zero_m_upper(Lb, 320, INTRA_THREADS - 320);
 }
 
 // A = (I + diag(beta) Lp)^-1 (unit lower triangular, fp32; only the lower
