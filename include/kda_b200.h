@@ -203,7 +203,10 @@ int kda_b200_device_error(int reset);
  *   3     a cu_seqlens table was malformed (does not start at 0, decreases, or
  *         does not end at the token count): the layer call did nothing;
  *   5, 7  a bulk-copy wait of the backward chunk kernel ran out;
- *   8     the forward chunk kernel's wait for its prefetched inputs ran out.
+ *   8     the forward chunk kernel's wait for its prefetched inputs ran out;
+ *   9     a chunk kernel's dynamic shared memory was not 1 KB aligned (its
+ *         swizzled tensor-core tiles need it): the kernel did nothing;
+ *   10    a tensor-core completion wait of the forward chunk kernel ran out.
  * A kernel that records a timeout lets its copies in flight land (a second
  * bounded wait), frees what it holds and returns; later calls are unaffected.
  */

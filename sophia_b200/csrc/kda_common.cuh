@@ -2,12 +2,10 @@
 //
 // Tile conventions used by every kernel:
 //   * chunk of C = 64 tokens, head dim D = 128, sub-chunks of 16 tokens;
-//   * bf16 tiles in shared memory are row-major with a padded row stride
-//     (136 elements for 128-wide rows, 72 for 64-wide rows) so that eight
-//     ldmatrix row addresses hit eight distinct 4-bank groups;
-//   * warp-level tensor-core products use mma.sync m16n8k16 (bf16 in, fp32
-//     accumulate) with fragments loaded by ldmatrix; the four operand
-//     orientations (A or A^T, B or B^T) map to ldmatrix with or without .trans.
+//   * tensor-core operands are 128B-swizzled bf16 tiles (sw64_chunk below and
+//     kda_tc.cuh); the warp-level products are the tf32 16x16 blocks of the
+//     UT inverse (mma.sync m16n8k8);
+//   * staged output rows use a padded row stride (LD128 = 136 elements);
 //   * decays are kept in log2 units (Gam2 = Gam / ln 2) so every exponential is
 //     one ex2.approx.
 #pragma once
@@ -22,7 +20,6 @@ constexpr int C = 64;        // chunk length
 constexpr int D = 128;       // head dim (K = V = 128)
 constexpr int SUB = 16;      // sub-chunk length
 constexpr int LD128 = 136;   // padded row stride (elements) of 128-wide bf16 tiles
-constexpr int LD64 = 72;     // padded row stride (elements) of 64-wide bf16 tiles
 constexpr int LDF64 = 65;    // padded row stride (floats) of 64x64 fp32 tiles
 constexpr int LDG = 132;     // padded row stride (floats) of the 64x128 fp32 decay tile
 constexpr float LOG2E = 1.4426950408889634f;
@@ -108,23 +105,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // D = A(16x8 tf32, row) * B(8x8 tf32, col) + C, fp32 accumulate.
 __device__ __forceinline__ void mma1688_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -176,132 +156,6 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
-// ---------------------------------------------------------------- fragments
-// A fragment (16x16) from a row-major [m][k] tile.
-__device__ __forceinline__ void load_A(uint32_t (&a)[4], const bf16* base, int ld, int m0, int k0) {
-  int l = threadIdx.x & 31;
-  ldsm_x4(a, base + (m0 + (l & 15)) * ld + k0 + (l >> 4) * 8);
-}
-// A fragment of A = X^T where X is a row-major [k][m] tile.
-__device__ __forceinline__ void load_AT(uint32_t (&a)[4], const bf16* base, int ld, int m0, int k0) {
-  int l = threadIdx.x & 31;
-  int i = l >> 3, r = l & 7;
-  ldsm_x4_t(a, base + (k0 + (i >> 1) * 8 + r) * ld + m0 + (i & 1) * 8);
-}
-// B fragments for two adjacent n8 tiles (n0, n0+8) of B = Y^T where Y is a
-// row-major [n][k] tile.  b[0..1] -> tile n0, b[2..3] -> tile n0+8.
-__device__ __forceinline__ void load_B_nk(uint32_t (&b)[4], const bf16* base, int ld, int n0, int k0) {
-  int l = threadIdx.x & 31;
-  int i = l >> 3, r = l & 7;
-  ldsm_x4(b, base + (n0 + (i >> 1) * 8 + r) * ld + k0 + (i & 1) * 8);
-}
-// B fragments for two adjacent n8 tiles from a row-major [k][n] tile.
-__device__ __forceinline__ void load_B_kn(uint32_t (&b)[4], const bf16* base, int ld, int n0, int k0) {
-  int l = threadIdx.x & 31;
-  int i = l >> 3, r = l & 7;
-  ldsm_x4_t(b, base + (k0 + (i & 1) * 8 + r) * ld + n0 + (i >> 1) * 8);
-}
-
-// Warp product acc[16 x (8*NT)] += op(A)[16 x K] * op(B)[K x (8*NT)].
-//   TA = false: A is a row-major [m][k] tile; TA = true: A = X^T, X row-major [k][m].
-//   TB = false: B = Y^T, Y row-major [n][k];  TB = true: B row-major [k][n].
-template <int NT, bool TA, bool TB>
-__device__ __forceinline__ void warp_mma(float (&acc)[NT][4], const bf16* A, int lda, int m0,
-                                         const bf16* B, int ldb, int n0, int k0, int K) {
-  static_assert(NT % 2 == 0, "NT must be even");
-#pragma unroll 2
-  for (int kk = 0; kk < K; kk += 16) {
-    uint32_t a[4];
-    if (TA) load_AT(a, A, lda, m0, k0 + kk); else load_A(a, A, lda, m0, k0 + kk);
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t b[4];
-      if (TB) load_B_kn(b, B, ldb, n0 + 8 * j, k0 + kk); else load_B_nk(b, B, ldb, n0 + 8 * j, k0 + kk);
-      mma16816(acc[j], a, b[0], b[1]);
-      mma16816(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-// The same fragment loads for tiles in other layouts: a tile type provides
-// at(row, col) for col a multiple of 8 (the start of a contiguous 16-byte run).
-// As warp_mma with A negated (sign bits of the bf16 A fragments flipped).
-template <int NT, bool TA, bool TB>
-__device__ __forceinline__ void warp_mma_neg(float (&acc)[NT][4], const bf16* A, int lda, int m0,
-                                             const bf16* B, int ldb, int n0, int k0, int K) {
-#pragma unroll 2
-  for (int kk = 0; kk < K; kk += 16) {
-    uint32_t a[4];
-    if (TA) load_AT(a, A, lda, m0, k0 + kk); else load_A(a, A, lda, m0, k0 + kk);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) a[i] ^= 0x80008000u;
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t b[4];
-      if (TB) load_B_kn(b, B, ldb, n0 + 8 * j, k0 + kk); else load_B_nk(b, B, ldb, n0 + 8 * j, k0 + kk);
-      mma16816(acc[j], a, b[0], b[1]);
-      mma16816(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-struct PadTile {  // row-major with a padded row stride
-  const bf16* p;
-  int ld;
-  __device__ __forceinline__ const bf16* at(int r, int c) const { return p + r * ld + c; }
-};
-struct Acc64Tile;  // defined with the tile layouts below
-
-template <int NT, bool TA, bool TB, typename TAL, typename TBL>
-__device__ __forceinline__ void warp_mma_t(float (&acc)[NT][4], const TAL& A, int m0, const TBL& B, int n0, int k0,
-                                           int K) {
-  static_assert(NT % 2 == 0, "NT must be even");
-  const int l = threadIdx.x & 31, i = l >> 3, r = l & 7;
-#pragma unroll 2
-  for (int kk = 0; kk < K; kk += 16) {
-    const int k = k0 + kk;
-    uint32_t a[4];
-    if (TA) ldsm_x4_t(a, A.at(k + (i >> 1) * 8 + r, m0 + (i & 1) * 8));
-    else ldsm_x4(a, A.at(m0 + (l & 15), k + (l >> 4) * 8));
-#pragma unroll
-    for (int j = 0; j < NT; j += 2) {
-      uint32_t b[4];
-      const int n = n0 + 8 * j;
-      if (TB) ldsm_x4_t(b, B.at(k + (i & 1) * 8 + r, n + (i >> 1) * 8));
-      else ldsm_x4(b, B.at(n + (i >> 1) * 8 + r, k + (i & 1) * 8));
-      mma16816(acc[j], a, b[0], b[1]);
-      mma16816(acc[j + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-template <int NT>
-__device__ __forceinline__ void zero_acc(float (&acc)[NT][4]) {
-#pragma unroll
-  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-}
-
-// Row/col of accumulator element e (0..3) of n8 tile j for this lane.
-// Transposes the 4x4 matrix of 32-bit words held by a lane quad (lane t holds
-// row t) with two xor-shuffle rounds: afterwards lane t holds column t.  For
-// an accumulator row packed as w[j] = bf16 pair at columns 8j + 2t, 8j + 2t + 1
-// this leaves lane t with the eight consecutive columns 8t .. 8t + 7.
-__device__ __forceinline__ void quad_transpose4(uint32_t (&w)[4]) {
-  const int t = threadIdx.x & 3;
-  const bool hi2 = t & 2, hi1 = t & 1;
-  uint32_t a0 = hi2 ? w[0] : w[2], a1 = hi2 ? w[1] : w[3];
-  uint32_t b0 = __shfl_xor_sync(0xffffffffu, a0, 2), b1 = __shfl_xor_sync(0xffffffffu, a1, 2);
-  if (hi2) { w[0] = b0; w[1] = b1; } else { w[2] = b0; w[3] = b1; }
-  a0 = hi1 ? w[0] : w[1];
-  a1 = hi1 ? w[2] : w[3];
-  b0 = __shfl_xor_sync(0xffffffffu, a0, 1);
-  b1 = __shfl_xor_sync(0xffffffffu, a1, 1);
-  if (hi1) { w[0] = b0; w[2] = b1; } else { w[1] = b0; w[3] = b1; }
-}
-
-__device__ __forceinline__ int acc_row(int e) { return ((threadIdx.x & 31) >> 2) + ((e >> 1) << 3); }
-__device__ __forceinline__ int acc_col(int j, int e) { return 8 * j + 2 * (threadIdx.x & 3) + (e & 1); }
-
 // 16-byte vector of 8 bf16
 // ---------------------------------------------------------------- tile layouts
 // Per-(chunk, head) tiles exchanged between the state kernels and the chunk
@@ -330,13 +184,6 @@ __host__ __device__ __forceinline__ uint32_t acc64n64_off(int i, int j) {
 __host__ __device__ __forceinline__ uint32_t st128_off(int k, int v) {
   return (uint32_t)(((((k >> 5) * 2 + (v >> 6)) * 8 + ((v >> 3) & 7)) * 32 + (k & 31)) * 8 + (v & 7));
 }
-// A 64x128 acc64 tile in shared memory, as it arrives by a plain byte copy:
-// the eight rows an ldmatrix reads (one 16-row group, one 8-column chunk) are
-// one contiguous 128-byte run, so the reads are conflict-free.
-struct Acc64Tile {
-  const bf16* p;
-  __device__ __forceinline__ const bf16* at(int r, int c) const { return p + acc64_off(r, c); }
-};
 // Inverse maps of a 16-byte chunk index (element offset / 8) to (row, 8-chunk).
 __device__ __forceinline__ void acc64_chunk(int idx, int& row, int& cc) {
   const int lane = idx & 15, c = (idx >> 4) & 3, c0 = (idx >> 6) & 1, hf = (idx >> 7) & 1, q = idx >> 8;

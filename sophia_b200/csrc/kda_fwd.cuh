@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_fwd_intra_kernel(const _
     __syncthreads();  // nxt is rewritten below
   }
   if (smem_u32(smem) & 1023) {  // swizzled operand tiles need 1 KB alignment (block-uniform)
-    if (tid == 0) atomicExch(&g_kda_device_error, 10);
+    if (tid == 0) atomicExch(&g_kda_device_error, 9);
     return;
   }
 
@@ -382,22 +382,6 @@ struct FwdStateParams {
   float* ht;             // [N][H][128][128] or null
 };
 
-__device__ __forceinline__ void load_tile128(bf16* dst, const bf16* src, int t0, int nvalid, int H, int h) {
-  for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
-    int r = i >> 4, cc = i & 15;
-    bool ok = r < nvalid;
-    const bf16* gp = src + (ok ? ((size_t)(t0 + r) * H + h) * D + cc * 8 : 0);
-    cp_async16(dst + r * LD128 + cc * 8, gp, ok);
-  }
-}
-__device__ __forceinline__ void load_tile64(bf16* dst, const bf16* src, int t0, int nvalid, int H, int h) {
-  for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
-    int r = i >> 3, cc = i & 7;
-    bool ok = r < nvalid;
-    const bf16* gp = src + (ok ? ((size_t)(t0 + r) * H + h) * 64 + cc * 8 : 0);
-    cp_async16(dst + r * LD64 + cc * 8, gp, ok);
-  }
-}
 __device__ __forceinline__ void load_vec128(float* dst, const float* src) {
   for (int i = threadIdx.x; i < 32; i += blockDim.x) cp_async16(dst + 4 * i, src + 4 * i, true);
 }

@@ -1,19 +1,23 @@
-// Intra-chunk stages shared by the forward and backward chunk kernels.
+// Intra-chunk stages of the chunk kernels: the forward's prologue (conv, norms,
+// gate, cumsum), its tcgen05 operand build and the UT inverse.
 //
 // One CTA of 512 threads (16 warps) owns one (chunk, head).  Elementwise work
 // uses the "strip" mapping: thread tid owns tokens 2*tg, 2*tg+1 (tg = tid / 16)
 // and channels 8*cg .. 8*cg+7 (cg = tid % 16); the 16 threads of a half-warp
 // share a token pair, so a row reduction over 128 channels is a 16-lane shuffle.
 //
-// Overflow-safe factorisation of exp(Gam_i - Gam_j) (per channel, i >= j):
-//   diagonal 16x16 block (I == J):   a_i * ia_j,   a = 2^(Gam - Gam_r(I)) <= 1,
-//                                                  ia = 1/a >= 1 (<= 2^116),
-//   off-diagonal block (I > J):      a_i * c_IJ * b_j,  c_IJ = 2^(Gam_r(I) - Gam_e(J)),
-//                                                  b = 2^(Gam_e(J) - Gam) <= 1,
-// with r(I) the first and e(J) the last token of a sub-chunk.  Every factor is
-// bounded because the reference clamps the per-token log decay to [lb, 0) with
-// lb >= -5 (sixteen tokens span at most 80 nats), and a factor that underflows
-// only does so when the exact product underflows too.
+// Overflow-safe factorisations of exp(Gam_i - Gam_j) (per channel, i >= j), with
+// r(I) the first and e(J) the last token of a 16-token sub-chunk:
+//   * the backward chunk kernel scales its block products in the epilogues:
+//       diagonal 16x16 block (I == J):  a_i * ia_j,   a = 2^(Gam - Gam_r(I)) <= 1,
+//                                                     ia = 1/a >= 1 (<= 2^116),
+//       off-diagonal block (I > J):     a_i * c_IJ * b_j,  c_IJ = 2^(Gam_r(I) - Gam_e(J)),
+//                                                     b = 2^(Gam_e(J) - Gam) <= 1;
+//   * the forward chunk kernel folds the factors into its operands, one copy
+//     of the decayed k per row block (Kc_I, build_tc_operands below).
+// Every factor is bounded because the reference clamps the per-token log decay
+// to [lb, 0) with lb >= -5 (sixteen tokens span at most 80 nats), and a factor
+// that underflows only does so where the exact product is negligible.
 #pragma once
 
 #include "kda_common.cuh"
