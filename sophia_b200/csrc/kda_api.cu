@@ -277,6 +277,22 @@ int encode_rows_map(CUtensorMap* m, const void* base, int H, long long TT, int r
   return KDA_OK;
 }
 
+// A [TT][H][inner] bf16 tensor (inner = 64 or 128) for 128B-swizzled TMA boxes of
+// 64 channels x 64 rows: each box lands as one tcgen05 operand atom.
+int encode_sw128_map(CUtensorMap* m, const void* base, int H, long long TT, int inner) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(KDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)H, (cuuint64_t)TT};
+  const cuuint64_t strides[2] = {(cuuint64_t)inner * 2, (cuuint64_t)H * inner * 2};
+  const cuuint32_t box[3] = {64u, 1u, 64u};
+  const cuuint32_t elem[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KDA_ERR_CUDA, "tensor map encoding failed (CUresult " + std::to_string((int)r) + ")");
+  return KDA_OK;
+}
+
 template <typename K>
 int set_smem(K kernel, int bytes, const char* name) {
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -595,10 +611,14 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   sp.hs = sv.hs;
   sp.E = sv.E;
   sp.ht = ht;
+  if ((rc = encode_sw128_map(&sp.maps[0], sv.W, H, pr.TT, D)) || (rc = encode_sw128_map(&sp.maps[1], sv.Qt, H, pr.TT, D)) ||
+      (rc = encode_sw128_map(&sp.maps[2], sv.Kb, H, pr.TT, D)) || (rc = encode_sw128_map(&sp.maps[3], sv.U, H, pr.TT, D)) ||
+      (rc = encode_sw128_map(&sp.maps[4], sv.M, H, pr.TT, 64)))
+    return rc;
   if ((rc = set_smem(kda_fwd_state_tc_kernel, StateTcSmem::END, "fwd state"))) return rc;
   {
     TimedLaunch tl(K_FWD_STATE, st);
-    kda_fwd_state_tc_kernel<<<dim3(N, H), 256, StateTcSmem::END, st>>>(sp);
+    kda_fwd_state_tc_kernel<<<dim3(N, H), STATE_THREADS, StateTcSmem::END, st>>>(sp);
   }
   return launch_check("fwd state");
 }

@@ -380,6 +380,9 @@ struct FwdStateParams {
   bf16* hs;              // [chunks][H] st128 tiles: chunk-start states, or null
   bf16* E;               // [chunks][H] acc64 tiles: v_new, or null
   float* ht;             // [N][H][128][128] or null
+  // W, Qt, Kbar, U as [T_total][H][128] and M as [T_total][H][64] bf16, for
+  // 128B-swizzled TMA boxes of 64 channels x 64 rows (one operand atom each)
+  CUtensorMap maps[5];
 };
 
 __device__ __forceinline__ void load_vec128(float* dst, const float* src) {
