@@ -676,10 +676,14 @@ int kda_b200_bwd(const void* q, const void* k, const void* v, const void* g, con
   bs.dht = dht;
   bs.dE = bv.dE; bs.dQt = bv.dQt; bs.dW = bv.dW; bs.dKb = bv.dKb; bs.dM = bv.dM; bs.dGC = bv.dGC;
   bs.dh0 = dh0;
+  if ((rc = encode_sw128_map(&bs.maps[0], sv.M, H, pr.TT, 64)) || (rc = encode_sw128_map(&bs.maps[1], do_, H, pr.TT, D)) ||
+      (rc = encode_sw128_map(&bs.maps[2], sv.Kb, H, pr.TT, D)) || (rc = encode_sw128_map(&bs.maps[3], sv.Qt, H, pr.TT, D)) ||
+      (rc = encode_sw128_map(&bs.maps[4], sv.W, H, pr.TT, D)))
+    return rc;
   if ((rc = set_smem(kda_bwd_state_tc_kernel, BwdStateTcSmem::END, "bwd state"))) return rc;
   {
     TimedLaunch tl(K_BWD_STATE, st);
-    kda_bwd_state_tc_kernel<<<dim3(N, H), 256, BwdStateTcSmem::END, st>>>(bs);
+    kda_bwd_state_tc_kernel<<<dim3(N, H), STATE_THREADS, BwdStateTcSmem::END, st>>>(bs);
   }
   if ((rc = launch_check("bwd state"))) return rc;
 

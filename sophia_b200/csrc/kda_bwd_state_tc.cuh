@@ -1,7 +1,7 @@
 // Reverse state pass of the chunked KDA backward on the fifth-generation
 // tensor cores (tcgen05 + TMEM).
 //
-// One CTA (256 threads) per (sequence, head) walks the chunks last to first,
+// One CTA (288 threads) per (sequence, head) walks the chunks last to first,
 // carrying the gradient of the chunk-end state dS (128x128 fp32 in TMEM, one
 // lane per state row k).  Per chunk, with S0 the chunk-start state saved by
 // the forward (bf16):
@@ -14,15 +14,23 @@
 //   phase B (MMA): dS += Qt^T dO + W^T (-dE)   (M=128, R0)
 //                  dQt = dO S0^T, dW = (-dE) S0^T (M=64, R2, lanes +0 / +16)
 //   epilogue B:    dS -> bf16 operand tile of the next chunk (dh0 after the first chunk)
-// One thread issues the MMAs; completion is tracked with mbarriers whose waits
-// are bounded: on a timeout the CTA records an error and leaves through its
-// cleanup path (TMEM is always released).  The phase-A operands (M, dO, Kbar,
-// E, 2^Gam_C) are double-buffered and loaded one chunk ahead; Qt and W are
-// reloaded as soon as the dS update of the chunk before has read them, S0 once
-// its dQt/dW MMAs have; the dM epilogue runs while phase B computes.  All operand
-// tiles are 128B-swizzled; rows past the sequence end are zero.  v_new and the
-// chunk-start states arrive as acc64 / st128 tiles; dE, dKb, dQt, dW (acc64)
-// and dM (acc64n64) leave as whole per-(chunk, head) tiles in epilogue order.
+// Warp-specialised: warps 0-7 (the consumers) hold the state rows and issue the
+// MMAs from one thread; warp 8 is the producer, whose first lane loads by TMA
+// into three rings paced by full / empty mbarriers:
+//   * the phase-A stage (double-buffered, one chunk ahead): M, dO, Kbar as
+//     128B-swizzled boxes, v_new (E) by one bulk copy of the forward's
+//     swizzled tile, and 2^Gam_C;
+//   * Qt and W, reloaded once the dS update of the chunk before has read them;
+//   * S0 (one bulk copy of the forward's swizzled chunk-start state), reloaded
+//     once the dQt/dW MMAs of the chunk before have read it.
+// The dM epilogue runs while phase B computes.  Rows past the sequence end (the
+// last chunk only) arrive with the next sequence's data: the consumers zero
+// them in M, dO and Kbar, so dE, dM and dS see exactly the zero rows of a
+// zero-filled load.  Completion waits are bounded: on a timeout the CTA records
+// an error and leaves through its cleanup path (the producer stops issuing and
+// waits for its copies in flight; TMEM is always released).  dE, dKb, dQt, dW
+// (acc64) and dM (acc64n64) leave as whole per-(chunk, head) tiles in epilogue
+// order.
 #pragma once
 
 #include "kda_fwd.cuh"
@@ -34,12 +42,15 @@ struct BwdStateParams {
   SeqInfo seq;
   int H;
   const bf16 *W, *Qt, *Kb, *M, *dO;  // [T_total][H][128] (M: [T_total][H][64])
-  const bf16 *E, *hs;                // [chunks][H] acc64 / st128 tiles
+  const bf16 *E, *hs;                // [chunks][H] 128B-swizzled operand tiles (64 x 128, 128 x 128)
   const float* dC;
   const float* dht;  // [N][H][128][128] or null
   bf16 *dE, *dQt, *dW, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
   float* dGC;        // [chunks][H][128]
   float* dh0;        // [N][H][128][128] or null
+  // M as [T_total][H][64] and dO, Kbar, Qt, W as [T_total][H][128] bf16, for
+  // 128B-swizzled TMA boxes of 64 channels x 64 rows (one operand atom each)
+  CUtensorMap maps[5];
 };
 
 struct BwdStateTcSmem {
@@ -53,28 +64,11 @@ struct BwdStateTcSmem {
   static constexpr int NDE = DS + 32768;                // [64][128] bf16
   static constexpr int DC = NDE + TILE;                 // [2][128] fp32 (per stage)
   static constexpr int GCP = DC + 1024;                 // [2][128] fp32 dGC half-row partials
-  static constexpr int MISC = GCP + 1024;               // mbarriers, TMEM slot, abort flag
-  static constexpr int END = MISC + 64;
+  static constexpr int MISC = GCP + 1024;               // 12 mbarriers, TMEM slot, abort flag
+  static constexpr int END = MISC + 128;
 };
 static_assert(BwdStateTcSmem::END <= 232448, "bwd state (tcgen05) shared memory");
 
-// cp.async of an st128 state tile into two 128B-swizzled 16 KB atoms
-// (columns 0-63, 64-127); consecutive threads read consecutive 16-byte chunks.
-__device__ __forceinline__ void load_st128_sw128(unsigned char* dst, const bf16* tile) {
-  for (int idx = threadIdx.x; idx < 128 * 16; idx += blockDim.x) {
-    int r, cc;
-    st128_chunk(idx, r, cc);
-    cp_async16(dst + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4), tile + idx * 8, true);
-  }
-}
-// Same for an acc64 tile into two 128B-swizzled 8 KB atoms.
-__device__ __forceinline__ void load_acc64_sw128(unsigned char* dst, const bf16* tile) {
-  for (int idx = threadIdx.x; idx < 64 * 16; idx += blockDim.x) {
-    int r, cc;
-    acc64_chunk(idx, r, cc);
-    cp_async16(dst + (cc >> 3) * 8192 + r * 128 + (((cc & 7) ^ (r & 7)) << 4), tile + idx * 8, true);
-  }
-}
 // Eight fp32 values -> one bf16 16-byte chunk.
 __device__ __forceinline__ void store_chunk8(bf16* dst, const float* a) {
   uint4 pk;
@@ -85,13 +79,17 @@ __device__ __forceinline__ void store_chunk8(bf16* dst, const float* a) {
   *reinterpret_cast<uint4*>(dst) = pk;
 }
 
-__global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams P) {
+constexpr uint32_t BSTATE_STAGE_BYTES = 8192 + 3 * BwdStateTcSmem::TILE + 512;  // M, dO, Kbar, E, 2^Gam_C
+constexpr uint32_t BSTATE_QW_BYTES = 2 * BwdStateTcSmem::TILE;
+constexpr uint32_t BSTATE_S0_BYTES = STATE_ELEMS * 2;
+
+__global__ void __launch_bounds__(STATE_THREADS, 1) kda_bwd_state_tc_kernel(const __grid_constant__ BwdStateParams P) {
   extern __shared__ __align__(1024) unsigned char tc_smem[];  // 1 KB-aligned dynamic shared memory
   unsigned char* smem = tc_smem;
   using S_ = BwdStateTcSmem;
   const int n = blockIdx.x, h = blockIdx.y, H = P.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q = warp & 3, hf = warp >> 2;  // TMEM lane quarter, column half
+  const int q = warp & 3, hf = (warp >> 2) & 1;  // TMEM lane quarter, column half
   const int bos = seq_bos(P.seq, n), eos = seq_eos(P.seq, n);
   const int nchunks = seq_nchunks(P.seq, n);
   const int cbase = seq_chunk_base(P.seq, n);
@@ -112,7 +110,13 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     return;
   }
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + S_::MISC);  // A1, A2, B1, B2
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 4);
+  uint64_t* fullA = mbar + 4;    // [2] phase-A stage landed
+  uint64_t* emptyA = mbar + 6;   // [2] phase-A stage read
+  uint64_t* fullQW = mbar + 8;   // Qt, W landed
+  uint64_t* emptyQW = mbar + 9;  // Qt, W read
+  uint64_t* fullS0 = mbar + 10;  // S0 landed
+  uint64_t* emptyS0 = mbar + 11; // S0 read
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
   unsigned char* sQt = smem + S_::QT;
   unsigned char* sW = smem + S_::W;
@@ -123,30 +127,81 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
 
   if (warp == 0) tc::tmem_alloc(tslot, 512);
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) tc::mbar_init(mbar + i, 1);
+    for (int i = 0; i < 12; ++i) tc::mbar_init(mbar + i, 1);
     tc::fence_mbar_init();
     *abort_flag = 0;
   }
+  tc::fence_before_sync();
+  __syncthreads();  // the last barrier of all 288 threads
+  tc::fence_after_sync();
   auto stage = [&](int ci) { return smem + (ci & 1) * S_::STAGE; };
   auto stage_dc = [&](int ci) { return reinterpret_cast<float*>(smem + S_::DC) + (ci & 1) * D; };
-  auto issue_stage = [&](int ci) {
-    unsigned char* b = stage(ci);
-    const int t0 = bos + ci * C, nv = min(C, eos - t0);
-    tc::load_tile64_sw128(b + S_::M, P.M, t0, nv, H, h);
-    tc::load_tile_sw128(b + S_::DO, P.dO, t0, nv, H, h);
-    tc::load_tile_sw128(b + S_::KB, P.Kb, t0, nv, H, h);
-    load_acc64_sw128(b + S_::E, P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS);
-    load_vec128(stage_dc(ci), P.dC + ((size_t)(cbase + ci) * H + h) * D);
-  };
-  // Qt and W: read by the dS update (free once it completes); S0: read by dGC
-  // and the dQt/dW MMAs (free once those complete)
-  auto issue_qw = [&](int ci) {
-    const int t0 = bos + ci * C, nv = min(C, eos - t0);
-    tc::load_tile_sw128(sQt, P.Qt, t0, nv, H, h);
-    tc::load_tile_sw128(sW, P.W, t0, nv, H, h);
-  };
-  auto issue_s0 = [&](int ci) {
-    load_st128_sw128(sS0, P.hs + tile_index(P.seq, cbase + ci, h) * STATE_ELEMS);
+  const int last = nchunks - 1;
+
+  if (warp == STATE_CONSUMERS / 32) {
+    // ---- producer.  Chunk ci = last - it; its stage is ci & 1 and that
+    // stage's use (it >> 1); the Qt/W and S0 buffers are used once per chunk.
+    if (lane != 0) return;
+    auto load_stage = [&](int ci) {
+      unsigned char* b = stage(ci);
+      const int t0 = bos + ci * C;
+      uint64_t* f = fullA + (ci & 1);
+      tc::mbar_expect_tx(f, BSTATE_STAGE_BYTES);
+      tc::tma_load_3d(b + S_::M, &P.maps[0], 0, h, t0, f);
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        tc::tma_load_3d(b + S_::DO + a * 8192, &P.maps[1], 64 * a, h, t0, f);
+        tc::tma_load_3d(b + S_::KB + a * 8192, &P.maps[2], 64 * a, h, t0, f);
+      }
+      tc::bulk_g2s(b + S_::E, P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS, TILE64_ELEMS * 2, f);
+      tc::bulk_g2s(stage_dc(ci), P.dC + ((size_t)(cbase + ci) * H + h) * D, 512, f);
+    };
+    auto load_qw = [&](int ci) {
+      const int t0 = bos + ci * C;
+      tc::mbar_expect_tx(fullQW, BSTATE_QW_BYTES);
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        tc::tma_load_3d(sQt + a * 8192, &P.maps[3], 64 * a, h, t0, fullQW);
+        tc::tma_load_3d(sW + a * 8192, &P.maps[4], 64 * a, h, t0, fullQW);
+      }
+    };
+    auto load_s0 = [&](int ci) {
+      tc::mbar_expect_tx(fullS0, BSTATE_S0_BYTES);
+      tc::bulk_g2s(sS0, P.hs + tile_index(P.seq, cbase + ci, h) * STATE_ELEMS, BSTATE_S0_BYTES, fullS0);
+    };
+    // last issued use of each ring (-1: none), for the drain below
+    int lastA[2] = {-1, -1}, lastQW = -1, lastS0 = -1;
+    load_stage(last); lastA[last & 1] = 0;
+    load_qw(last); lastQW = 0;
+    load_s0(last); lastS0 = 0;
+    if (last >= 1) { load_stage(last - 1); lastA[(last - 1) & 1] = 0; }
+    for (int it = 1; it <= last; ++it) {
+      const int ci = last - it;
+      if (!tc::mbar_wait(emptyQW, (it - 1) & 1) || *abort_flag) break;
+      load_qw(ci); lastQW = it;
+      if (!tc::mbar_wait(emptyS0, (it - 1) & 1) || *abort_flag) break;
+      load_s0(ci); lastS0 = it;
+      if (ci >= 1) {
+        const int u = (it + 1) >> 1;  // use of stage (ci - 1) & 1 by chunk ci - 1
+        if (!tc::mbar_wait(emptyA + ((ci - 1) & 1), (u - 1) & 1) || *abort_flag) break;
+        load_stage(ci - 1); lastA[(ci - 1) & 1] = u;
+      }
+    }
+    // no copy may still be writing shared memory when the CTA ends
+    for (int s2 = 0; s2 < 2; ++s2)
+      if (lastA[s2] >= 0) tc::mbar_wait(fullA + s2, lastA[s2] & 1);
+    if (lastQW >= 0) tc::mbar_wait(fullQW, lastQW & 1);
+    if (lastS0 >= 0) tc::mbar_wait(fullS0, lastS0 & 1);
+    return;
+  }
+
+  // ---- consumers (256 threads)
+  // on a timeout: stop, release a producer waiting for a buffer, and leave
+  auto give_up = [&]() {
+    *abort_flag = 1;
+    if (tid == 0) {
+      mbar_arrive(emptyA); mbar_arrive(emptyA + 1); mbar_arrive(emptyQW); mbar_arrive(emptyS0);
+    }
   };
   // dS row krow, columns [64 hf, 64 hf + 64) -> bf16 operand tile
   auto store_ds = [&](const float (&v)[64]) {
@@ -162,16 +217,6 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     }
   };
 
-
-  const int last = nchunks - 1;
-  // cp.async groups, oldest first: per chunk ci (from the last) the loop
-  // commits [S0(ci)] and [stage(ci-1)] at its top and [Qt,W(ci-1)] in
-  // epilogue B; the prologue commits [stage(last)] and [Qt,W,S0(last)]
-  issue_stage(last);
-  cp_async_commit();
-  issue_qw(last);
-  issue_s0(last);
-  cp_async_commit();
   // dht -> registers and the bf16 operand tile
   float v[64];
   {
@@ -183,10 +228,9 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     }
     store_ds(v);
   }
-  cp_async_wait<1>();  // phase-A operands of the last chunk
   tc::fence_async_smem();
   tc::fence_before_sync();
-  __syncthreads();
+  consumer_sync();
   tc::fence_after_sync();
   const uint32_t tbase = *tslot;
   const uint32_t tq = (uint32_t)(32 * q) << 16;
@@ -220,6 +264,19 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     const size_t tix = tile_index(P.seq, cbase + ci, h);
     unsigned char* st = stage(ci);
     const float* dC = stage_dc(ci);
+    // this chunk's phase-A operands (loaded while the chunk before computed)
+    if (!tc::mbar_wait(fullA + (ci & 1), (it >> 1) & 1)) *abort_flag = 1;
+    if (nv < C) {
+      // a partial (last) chunk: the rows past the end belong to the next sequence
+      for (int i = tid; i < (C - nv) * 8 * 5; i += STATE_CONSUMERS) {
+        const int r = nv + i / 40, j = i % 40, t = j >> 3, c8 = j & 7;
+        unsigned char* base = st + (t == 0 ? S_::M : (t <= 2 ? S_::DO + (t - 1) * 8192 : S_::KB + (t - 3) * 8192));
+        *reinterpret_cast<uint4*>(base + r * 128 + (c8 << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      tc::fence_async_smem();
+      consumer_sync();
+    }
+    // (a timed-out wait is acted on after the next barrier, by every thread alike)
     // ---- phase A MMAs
     if (tid == 0) {
       tc::fence_after_sync();
@@ -259,16 +316,13 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
       tc::tmem_st32(tR0 + 32, b);
     }
     // dQt / dW of the chunk after this one; its MMAs were the last readers of S0
+    // and of that chunk's stage: both go back to the producer
     if (ci < last) {
       if (!tc::mbar_wait(mbar + 3, (it - 1) & 1)) *abort_flag = 1;
       tc::fence_after_sync();
+      if (tid == 0) { mbar_arrive(emptyS0); mbar_arrive(emptyA + ((ci + 1) & 1)); }
       r2_epilogue(ci + 1);
-      issue_s0(ci);
     }
-    cp_async_commit();
-    // the next chunk's phase-A operands (its stage held chunk ci+1, finished)
-    if (ci > 0) issue_stage(ci - 1);
-    cp_async_commit();
     // ---- epilogue A
     if (!tc::mbar_wait(mbar + 0, it & 1)) *abort_flag = 1;
     tc::fence_after_sync();
@@ -298,8 +352,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
       }
     }
     // dGC: half-row partials of rowsum((2^Gam_C dS) o S0)
-    cp_async_wait<1>();  // Qt, W, S0 of this chunk (other threads' copies too)
-    __syncthreads();
+    if (!tc::mbar_wait(fullS0, it & 1)) *abort_flag = 1;  // S0 of this chunk
     {
       const unsigned char* atom = sS0 + hf * 16384;
       float part = 0.f;
@@ -312,9 +365,10 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
       }
       gcp[hf * D + krow] = part;
     }
+    if (tid == 0 && !tc::mbar_wait(fullQW, it & 1)) *abort_flag = 1;  // Qt, W of this chunk (phase B)
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    consumer_sync();
     if (*abort_flag) { ok = false; break; }
     if (tid < D) P.dGC[cidx * D + tid] = gcp[tid] + gcp[D + tid];
     // ---- phase B MMAs
@@ -361,6 +415,7 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     // ---- epilogue B: dS of the chunk before -> operand tile (or dh0)
     if (!tc::mbar_wait(mbar + 2, it & 1)) *abort_flag = 1;
     tc::fence_after_sync();
+    if (tid == 0) mbar_arrive(emptyQW);  // the dS update has read Qt and W
     {
       float a[32], b[32];
       tc::tmem_ld32(tR0, a);
@@ -370,20 +425,14 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     }
     if (ci > 0) {
       store_ds(v);
-      issue_qw(ci - 1);  // the dS update that read Qt and W is complete
-      cp_async_commit();
-      cp_async_wait<1>();  // phase-A operands of the chunk before
-    } else {
-      cp_async_commit();
-      if (P.dh0) {
-        float* dst = P.dh0 + (((size_t)n * H + h) * D + krow) * D + 64 * hf;
+    } else if (P.dh0) {
+      float* dst = P.dh0 + (((size_t)n * H + h) * D + krow) * D + 64 * hf;
 #pragma unroll
-        for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-      }
+      for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+    consumer_sync();
     if (*abort_flag) { ok = false; break; }
   }
   if (ok) {  // dQt / dW of the first chunk
@@ -391,10 +440,12 @@ __global__ void __launch_bounds__(256, 1) kda_bwd_state_tc_kernel(BwdStateParams
     tc::fence_after_sync();
     if (ok) r2_epilogue(0);
   }
-  if (!ok && tid == 0) atomicExch(&g_kda_device_error, 1);
-  cp_async_wait<0>();
+  if (!ok) {
+    if (tid == 0) atomicExch(&g_kda_device_error, 1);
+    give_up();
+  }
   tc::fence_before_sync();
-  __syncthreads();
+  consumer_sync();
   if (warp == 0) tc::tmem_dealloc(tbase, 512);
 }
 

@@ -168,8 +168,6 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 //          [quarter 4][column half 2][32-block 2][8-chunk 4][row lane 16][8]
 //   acc64n64: a 64x64 tile from an N=64 M=64 accumulator (32 columns/thread):
 //          [quarter 4][column half 2][8-chunk 4][row lane 16][8]
-//   st128: a 128x128 state (row k in lane k%32 of warp quarter k/32):
-//          [quarter 4][column half 2][8-chunk 8][row lane 32][8]
 constexpr int TILE64_ELEMS = 64 * 128;
 constexpr int TILE64N64_ELEMS = 64 * 64;
 constexpr int A_TILE_ELEMS = 64 * LDF64;  // saved A: [64][LDF64] fp32, the inverse's own padded rows
@@ -181,9 +179,6 @@ __host__ __device__ __forceinline__ uint32_t acc64_off(int i, int v) {
 __host__ __device__ __forceinline__ uint32_t acc64n64_off(int i, int j) {
   return (uint32_t)(((((i >> 4) * 2 + (j >> 5)) * 4 + ((j >> 3) & 3)) * 16 + (i & 15)) * 8 + (j & 7));
 }
-__host__ __device__ __forceinline__ uint32_t st128_off(int k, int v) {
-  return (uint32_t)(((((k >> 5) * 2 + (v >> 6)) * 8 + ((v >> 3) & 7)) * 32 + (k & 31)) * 8 + (v & 7));
-}
 // Inverse maps of a 16-byte chunk index (element offset / 8) to (row, 8-chunk).
 __device__ __forceinline__ void acc64_chunk(int idx, int& row, int& cc) {
   const int lane = idx & 15, c = (idx >> 4) & 3, c0 = (idx >> 6) & 1, hf = (idx >> 7) & 1, q = idx >> 8;
@@ -194,11 +189,6 @@ __device__ __forceinline__ void acc64n64_chunk(int idx, int& row, int& cc) {
   const int lane = idx & 15, c = (idx >> 4) & 3, hf = (idx >> 6) & 1, q = idx >> 7;
   row = 16 * q + lane;
   cc = hf * 4 + c;
-}
-__device__ __forceinline__ void st128_chunk(int idx, int& row, int& cc) {
-  const int lane = idx & 31, c = (idx >> 5) & 7, hf = (idx >> 8) & 1, q = idx >> 9;
-  row = 32 * q + lane;
-  cc = hf * 8 + c;
 }
 
 // Element offset of 16-byte chunk c8 (columns 8*c8 .. 8*c8+7) of row r in a

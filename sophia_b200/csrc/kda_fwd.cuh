@@ -377,8 +377,8 @@ struct FwdStateParams {
   const float* dC;
   const float* h0;       // [N][H][128][128] or null
   bf16* o;               // [T_total][H][128]
-  bf16* hs;              // [chunks][H] st128 tiles: chunk-start states, or null
-  bf16* E;               // [chunks][H] acc64 tiles: v_new, or null
+  bf16* hs;              // [chunks][H] chunk-start states (128B-swizzled bf16 operand tiles), or null
+  bf16* E;               // [chunks][H] v_new (128B-swizzled bf16 operand tiles, rows past the end zero), or null
   float* ht;             // [N][H][128][128] or null
   // W, Qt, Kbar, U as [T_total][H][128] and M as [T_total][H][64] bf16, for
   // 128B-swizzled TMA boxes of 64 channels x 64 rows (one operand atom each)

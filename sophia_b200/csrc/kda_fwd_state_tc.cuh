@@ -25,8 +25,9 @@
 // tracked with mbarriers whose waits are bounded: on a timeout the CTA records
 // an error and leaves through its cleanup path (the producer stops issuing and
 // waits for its copies in flight; TMEM is always released).  v_new (E) and the
-// chunk-start states are written as per-(chunk, head) tiles in epilogue order
-// (acc64, st128), so each warp store is one contiguous run.
+// chunk-start states leave as per-(chunk, head) tiles by bulk stores of the
+// shared-memory operand tiles themselves (128B-swizzled), so the backward's
+// bulk loads land them directly as operands.
 #pragma once
 
 #include "kda_fwd.cuh"
@@ -153,20 +154,6 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
       *reinterpret_cast<uint4*>(atom + krow * 128 + ((c ^ (krow & 7)) << 4)) = pk;
     }
   };
-  // the same row -> chunk-start state tile of the backward (st128 order)
-  auto store_hs = [&](const float (&v)[64], int chunk) {
-    if (!P.hs) return;
-    bf16* dst = P.hs + tile_index(P.seq, chunk, h) * STATE_ELEMS;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 pk;
-      pk.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
-      pk.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
-      pk.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
-      pk.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
-      *reinterpret_cast<uint4*>(dst + st128_off(krow, 64 * half + 8 * c)) = pk;
-    }
-  };
   // O rows of buffer b (lanes 16-31) -> staging tile
   auto stage_o = [&](int b) {
 #pragma unroll
@@ -227,6 +214,7 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
     const int nv = min(C, eos - (bos + ci * C));
     // this chunk's operands (loaded while the chunk before computed)
     if (!tc::mbar_wait(full + stg, (ci >> 1) & 1)) *abort_flag = 1;
+    if (tid == 0 && P.E) tc::bulk_wait_read_all();  // v_new of the chunk before has left sE
     consumer_sync();
     if (*abort_flag) { ok = false; break; }
     // E = W S, O = Qt S into buffer eo
@@ -243,8 +231,14 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
                      ks > 0);
       }
       tc::mma_commit(mbarE);
+      // the chunk-start state for the backward: the bf16 operand tile itself
+      // (128B-swizzled, the layout the backward's operand slot takes)
+      if (P.hs) {
+        tc::bulk_s2g(P.hs + tile_index(P.seq, cbase + ci, h) * STATE_ELEMS, sS, STATE_ELEMS * 2);
+        tc::bulk_commit();
+      }
     }
-    // S <- diag(2^Gam_C) S in TMEM from the registers; chunk-start state out
+    // S <- diag(2^Gam_C) S in TMEM from the registers
     {
       const float dc = reinterpret_cast<const float*>(buf + StateTcSmem::DC)[krow];
       float a[32], b[32];
@@ -252,7 +246,6 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
       for (int i = 0; i < 32; ++i) { a[i] = v[i] * dc; b[i] = v[32 + i] * dc; }
       tc::tmem_st32(tS, a);
       tc::tmem_st32(tS + 32, b);
-      store_hs(v, cbase + ci);
     }
     if (ci > 0) stage_o(eo ^ 1);  // o of the previous chunk (its MMAs are complete)
     if (!tc::mbar_wait(mbarE, ci & 1)) *abort_flag = 1;
@@ -283,20 +276,22 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
               e.w = pack_bf16(u3.x - acc[8 * c + 6], u3.y - acc[8 * c + 7]);
             }
             *reinterpret_cast<uint4*>(eat + off) = e;
-            if (P.E)  // whole tile: rows past the end are zero
-              *reinterpret_cast<uint4*>(P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS +
-                                        acc64_off(r, 64 * half + 8 * chunk)) = e;
           }
         }
       }
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
+    if (tid == 0 && P.hs) tc::bulk_wait_read_all();  // the chunk-start state has left sS
     consumer_sync();
     if (*abort_flag) { ok = false; break; }
-    // O += M E ; S += Kbar^T E
+    // O += M E ; S += Kbar^T E; v_new (E, rows past the end zero) for the backward
     if (tid == 0) {
       tc::fence_after_sync();
+      if (P.E) {
+        tc::bulk_s2g(P.E + tile_index(P.seq, cbase + ci, h) * TILE64_ELEMS, sE, TILE64_ELEMS * 2);
+        tc::bulk_commit();
+      }
       const uint32_t m0 = smem_u32(buf + StateTcSmem::M), k0 = smem_u32(buf + StateTcSmem::KB);
       const uint32_t e0 = smem_u32(sE);
       const uint32_t dO = tbase + eo_col(eo) + (16u << 16);
@@ -344,6 +339,7 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
     if (tid == 0) atomicExch(&g_kda_device_error, 1);
     give_up();
   }
+  if (tid == 0) tc::bulk_wait_all();  // the bulk stores read sS / sE
   tc::fence_before_sync();
   consumer_sync();
   if (warp == 0) tc::tmem_dealloc(tbase, 512);
