@@ -4,8 +4,8 @@
 // One CTA of 512 threads per (chunk, head).  The forward's saved products --
 // normalised q and k, post-conv v (bf16, in the 128B-swizzled operand layout),
 // the decay cumsum, beta, and A = (I + diag(beta) L')^-1 and L' as bf16
-// operand tiles -- arrive by bulk copies; the state pass's gradient tiles dE,
-// dW and dM by cp.async straight into swizzled operand tiles.  With T =
+// operand tiles -- arrive by bulk copies, and so do the state pass's gradient
+// tiles dE, dW and dM (stored in the swizzled operand layout).  With T =
 // A diag(beta) and the decayed operands Qa = q a, Ka = k a, Kd = k / a,
 // Ke = k 2^Gam built in shared memory, every block product is a tcgen05 MMA
 // with M = 64 (a 64 x 128 result is two N = 64 halves at TMEM lane offsets
@@ -59,7 +59,8 @@ struct BwdIntraParams {
   PrologueIn in;
   SeqInfo seq;
   bool conv;
-  const bf16 *dE, *dW, *dQt, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
+  const bf16 *dE, *dW, *dM;              // [chunks][H] 128B-swizzled operand tiles (dM: 64 x 64)
+  const bf16 *dQt, *dKb;                 // [chunks][H] acc64 tiles
   const bf16 *A, *LP;                    // [chunks][H] bf16 64x64 swizzled tiles of A and L' from the forward
   const bf16 *QN, *KN, *VN;              // [chunks][H] bf16 64x128 swizzled prologue products of the forward
   const float *GM, *BT;                  // [chunks][H] [64][LDG] fp32 decay cumsum, [64] fp32 beta
@@ -83,7 +84,7 @@ struct BwdIntraSmem {
   static constexpr int EC = ER + 4 * D * 4;         // [4][128] 2^(Gam_C - Gam_e(J))
   static constexpr int REV = EC + 4 * D * 4;        // [4][128] 2^(Gam_e(J) - Gam_r(J))
   static constexpr int BETA = REV + 4 * D * 4;      // [64] fp32
-  static constexpr int MISC = BETA + 64 * 4;        // 9 mbarriers, TMEM slot, issued mask
+  static constexpr int MISC = BETA + 64 * 4;        // 11 mbarriers, TMEM slot, issued mask
   static constexpr int END = MISC + 128;
   // aliases (regions dead by then)
   static constexpr int DA = QN, XS = QN + T64;      // dA, X tiles (after the operand build)
@@ -228,7 +229,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   const size_t tix = tile_index(P.seq, c, h);
   // mbarriers: 0 decay cumsum and beta, 1 dQt/dKbar, 2..8 MMA groups G1..G7, 9 product tiles
   uint64_t* mb = reinterpret_cast<uint64_t*>(smem + S::MISC);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mb + 10);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mb + 11);
   volatile uint32_t* issued = tslot + 1;  // bit i: mbarrier i has work in flight
   float* gam = reinterpret_cast<float*>(smem + S::GAM);
   float* beta = reinterpret_cast<float*>(smem + S::BETA);
@@ -238,27 +239,9 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   }
   if (warp == 0) tc::tmem_alloc(tslot, 512);
   if (tid == 0) {
-    for (int i = 0; i < 10; ++i) tc::mbar_init(mb + i, 1);
+    for (int i = 0; i < 11; ++i) tc::mbar_init(mb + i, 1);
     tc::fence_mbar_init();
     *issued = 0u;
-  }
-  // the state pass's gradient tiles, straight into their swizzled operand slots
-  {
-    const bf16* gE = P.dE + tix * TILE64_ELEMS;
-    const bf16* gW = P.dW + tix * TILE64_ELEMS;
-    for (int idx = tid; idx < 64 * 16; idx += blockDim.x) {
-      int row, cc;
-      acc64_chunk(idx, row, cc);
-      const uint32_t so = 2 * sw64_chunk(row, cc);
-      cp_async16(smem + S::DE + so, gE + idx * 8, true);
-      cp_async16(smem + S::DW + so, gW + idx * 8, true);
-    }
-    for (int idx = tid; idx < 64 * 8; idx += blockDim.x) {
-      int row, cc;
-      acc64n64_chunk(idx, row, cc);
-      cp_async16(smem + S::DM + 2 * sw64_chunk(row, cc), P.dM + tix * TILE64N64_ELEMS + idx * 8, row < nv);
-    }
-    cp_async_commit();
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -276,7 +259,12 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
     tc::bulk_g2s(smem + S::V, P.VN + tix * TILE64_ELEMS, TB, mb + 9);
     tc::bulk_g2s(smem + S::AT, P.A + tix * TILE64N64_ELEMS, AB, mb + 9);
     tc::bulk_g2s(smem + S::LPT, P.LP + tix * TILE64N64_ELEMS, AB, mb + 9);
-    *issued = 0x201u;
+    // the state pass's gradient tiles dE, dW, dM, stored in the swizzled operand layout
+    tc::mbar_expect_tx(mb + 10, 2 * TB + AB);
+    tc::bulk_g2s(smem + S::DE, P.dE + tix * TILE64_ELEMS, TB, mb + 10);
+    tc::bulk_g2s(smem + S::DW, P.dW + tix * TILE64_ELEMS, TB, mb + 10);
+    tc::bulk_g2s(smem + S::DM, P.dM + tix * TILE64N64_ELEMS, AB, mb + 10);
+    *issued = 0x601u;
   }
 
   // epilogue mapping: rows 16 s .. 16 s + 15 (block I = s), 16 columns from c0
@@ -395,7 +383,8 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
         *reinterpret_cast<bf16x8*>(smem + S::TT + 2 * sw64_chunk(k, c8)) = pack8(tv);
       }
     }
-    cp_async_wait<0>();      // dE, dW, dM
+    ok = tc::mbar_wait(mb + 10, 0);  // dE, dW, dM
+    if (__syncthreads_or(!ok)) { ok = false; if (tid == 0) atomicExch(&g_kda_device_error, 7); break; }
     tc::fence_async_smem();  // operand tiles -> tensor cores; the decay region -> the bulk copy below
     tc::fence_before_sync();
     __syncthreads();
@@ -760,7 +749,7 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   if (!ok) {
     // let what is in flight finish (bounded), then release TMEM and leave
     const uint32_t iss = *issued;
-    for (int i = 0; i < 10; ++i)
+    for (int i = 0; i < 11; ++i)
       if (iss & (1u << i)) tc::mbar_wait(mb + i, 0, 1u << 22);
     cp_async_wait<0>();
     tc::fence_before_sync();

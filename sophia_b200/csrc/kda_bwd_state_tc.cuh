@@ -28,9 +28,10 @@
 // them in M, dO and Kbar, so dE, dM and dS see exactly the zero rows of a
 // zero-filled load.  Completion waits are bounded: on a timeout the CTA records
 // an error and leaves through its cleanup path (the producer stops issuing and
-// waits for its copies in flight; TMEM is always released).  dE, dKb, dQt, dW
-// (acc64) and dM (acc64n64) leave as whole per-(chunk, head) tiles in epilogue
-// order.
+// waits for its copies in flight; TMEM is always released).  dE, dW and dM
+// leave as whole per-(chunk, head) tiles in the 128B-swizzled operand layout
+// (the backward chunk kernel bulk-loads them as operands), dKb and dQt in
+// epilogue order (acc64).
 #pragma once
 
 #include "kda_fwd.cuh"
@@ -45,7 +46,8 @@ struct BwdStateParams {
   const bf16 *E, *hs;                // [chunks][H] 128B-swizzled operand tiles (64 x 128, 128 x 128)
   const float* dC;
   const float* dht;  // [N][H][128][128] or null
-  bf16 *dE, *dQt, *dW, *dKb, *dM;  // [chunks][H] acc64 tiles (dM: acc64n64)
+  bf16 *dE, *dW, *dM;              // [chunks][H] 128B-swizzled operand tiles (dM: 64 x 64)
+  bf16 *dQt, *dKb;                 // [chunks][H] acc64 tiles
   float* dGC;        // [chunks][H][128]
   float* dh0;        // [N][H][128][128] or null
   // M as [T_total][H][64] and dO, Kbar, Qt, W as [T_total][H][128] bf16, for
@@ -244,7 +246,8 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_bwd_state_tc_kernel(cons
   const uint32_t idM = tc::idesc_bf16(64, 64, false, false);    // dO E^T
   const uint32_t idB = tc::idesc_bf16(128, 128, true, true);    // Qt^T dO, W^T (-dE)
 
-  // dQt / dW of chunk cp (R2) -> acc64 tiles (whole tiles: rows past the end are zero)
+  // dQt (acc64 tile) / dW (128B-swizzled operand tile) of chunk cp (R2); whole
+  // tiles: rows past the end are zero
   auto r2_epilogue = [&](int cp) {
     bf16* tile = (hi ? P.dW : P.dQt) + tile_index(P.seq, cbase + cp, h) * TILE64_ELEMS;
 #pragma unroll
@@ -252,7 +255,10 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_bwd_state_tc_kernel(cons
       float a[32];
       tc::tmem_ld32(tR2 + c0, a);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64_off(arow, 64 * hf + c0 + 8 * c), a + 8 * c);
+      for (int c = 0; c < 4; ++c) {
+        const int v0 = 64 * hf + c0 + 8 * c;
+        store_chunk8(tile + (hi ? sw64_chunk(arow, v0 >> 3) : acc64_off(arow, v0)), a + 8 * c);
+      }
     }
   };
 
@@ -333,7 +339,10 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_bwd_state_tc_kernel(cons
         float a[32];
         tc::tmem_ld32(tR1 + c0, a);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64_off(arow, 64 * hf + c0 + 8 * c), a + 8 * c);
+        for (int c = 0; c < 4; ++c) {  // dKb: acc64 tile; dE: 128B-swizzled operand tile
+          const int v0 = 64 * hf + c0 + 8 * c;
+          store_chunk8(tile + (hi ? acc64_off(arow, v0) : sw64_chunk(arow, v0 >> 3)), a + 8 * c);
+        }
         if (!hi) {  // -dE -> operand tile (rows past the end stay zero)
           unsigned char* atom = sNDE + hf * 8192;
 #pragma unroll
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_bwd_state_tc_kernel(cons
         for (int i = 0; i < 32; ++i) m[i] = cb + i <= arow ? a[i] : 0.f;
         bf16* tile = P.dM + tix * TILE64N64_ELEMS;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) store_chunk8(tile + acc64n64_off(arow, cb + 8 * c), m + 8 * c);
+        for (int c = 0; c < 4; ++c) store_chunk8(tile + sw64_chunk(arow, (cb >> 3) + c), m + 8 * c);
       }
     }
     // ---- epilogue B: dS of the chunk before -> operand tile (or dh0)

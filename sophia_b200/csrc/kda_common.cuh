@@ -156,18 +156,17 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
-// 16-byte vector of 8 bf16
 // ---------------------------------------------------------------- tile layouts
-// Per-(chunk, head) tiles exchanged between the state kernels and the chunk
-// kernels are stored in the order their producing epilogue holds them, so that
-// every warp store is one contiguous run; consumers gather 16-byte chunks.
+// Per-(chunk, head) tiles that a kernel consumes as tcgen05 operands are stored
+// in the 128B-swizzled operand layout (sw64_chunk), so one bulk copy lands them.
+// The dQt and dKbar tiles, which the backward chunk kernel reads element-wise,
+// are stored in the order their producing epilogue holds them, so that every
+// warp store is one contiguous run.
 // Offsets are in elements; (i, v) is row, column and every chunk of 8
 // consecutive columns is contiguous.
 //   acc64: a 64x128 tile produced from an M=64 TMEM accumulator (row i sits in
 //          lane i%16 of warp quarter i/16; each thread holds 32-column blocks):
 //          [quarter 4][column half 2][32-block 2][8-chunk 4][row lane 16][8]
-//   acc64n64: a 64x64 tile from an N=64 M=64 accumulator (32 columns/thread):
-//          [quarter 4][column half 2][8-chunk 4][row lane 16][8]
 constexpr int TILE64_ELEMS = 64 * 128;
 constexpr int TILE64N64_ELEMS = 64 * 64;
 constexpr int A_TILE_ELEMS = 64 * LDF64;  // saved A: [64][LDF64] fp32, the inverse's own padded rows
@@ -175,20 +174,6 @@ constexpr int STATE_ELEMS = 128 * 128;
 __host__ __device__ __forceinline__ uint32_t acc64_off(int i, int v) {
   return (uint32_t)((((((i >> 4) * 2 + (v >> 6)) * 2 + ((v >> 5) & 1)) * 4 + ((v >> 3) & 3)) * 16 + (i & 15)) * 8 +
                     (v & 7));
-}
-__host__ __device__ __forceinline__ uint32_t acc64n64_off(int i, int j) {
-  return (uint32_t)(((((i >> 4) * 2 + (j >> 5)) * 4 + ((j >> 3) & 3)) * 16 + (i & 15)) * 8 + (j & 7));
-}
-// Inverse maps of a 16-byte chunk index (element offset / 8) to (row, 8-chunk).
-__device__ __forceinline__ void acc64_chunk(int idx, int& row, int& cc) {
-  const int lane = idx & 15, c = (idx >> 4) & 3, c0 = (idx >> 6) & 1, hf = (idx >> 7) & 1, q = idx >> 8;
-  row = 16 * q + lane;
-  cc = hf * 8 + c0 * 4 + c;
-}
-__device__ __forceinline__ void acc64n64_chunk(int idx, int& row, int& cc) {
-  const int lane = idx & 15, c = (idx >> 4) & 3, hf = (idx >> 6) & 1, q = idx >> 7;
-  row = 16 * q + lane;
-  cc = hf * 4 + c;
 }
 
 // Element offset of 16-byte chunk c8 (columns 8*c8 .. 8*c8+7) of row r in a
