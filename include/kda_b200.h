@@ -221,6 +221,16 @@ int kda_b200_device_error(int reset);
 int kda_b200_debug_set_input_wait_polls(unsigned int polls);
 
 /*
+ * Test hook of the forward state pass's producer/consumer protocol: `polls`
+ * bounds the consumers' wait for each chunk's operands (0 restores the default,
+ * 2^26), and a nonzero `withhold_loads` makes the producer warp issue no copy,
+ * so that wait can only run out.  The consumers then record code 1, wake the
+ * producer, release TMEM and return -- no fault and no hang.  Applies to calls
+ * made after it.  No counterpart in the reference.
+ */
+int kda_b200_debug_set_state_wait(unsigned int polls, int withhold_loads);
+
+/*
  * Per-kernel device timing, for benchmarks and profiling summaries.  While
  * enabled, every kernel launch of kda_b200_fwd / kda_b200_bwd is bracketed by
  * two cudaEventRecord calls on its stream.  kda_b200_timing_read synchronises

@@ -41,6 +41,7 @@ SIGNATURES = {
     "kda_b200_chunk_table": ([c_void_p, c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p], c_int),
     "kda_b200_device_error": ([c_int], c_int),
     "kda_b200_debug_set_input_wait_polls": ([ctypes.c_uint], c_int),
+    "kda_b200_debug_set_state_wait": ([ctypes.c_uint, c_int], c_int),
     "kda_b200_fwd_noalloc": ([c_void_p] * 12 + [c_int] * 5 + [c_float, c_float] + [c_void_p, c_void_p, c_void_p],
                              c_int),
     "kda_b200_timing_enable": ([c_int], c_int),

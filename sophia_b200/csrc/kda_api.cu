@@ -233,6 +233,9 @@ int launch_check(const char* what) {
 // (kda_b200_debug_set_input_wait_polls lowers it in tests).
 constexpr uint32_t kDefaultWaitPolls = 1u << 26;
 std::atomic<uint32_t> g_input_wait_polls{kDefaultWaitPolls};
+// The forward state pass's test hook (kda_b200_debug_set_state_wait).
+std::atomic<uint32_t> g_state_wait_polls{kDefaultWaitPolls};
+std::atomic<int> g_state_withhold_loads{0};
 
 // SMs of the current device (queried once per device).
 int sm_count() {
@@ -611,6 +614,8 @@ int kda_b200_fwd(const void* q, const void* k, const void* v, const void* g, con
   sp.hs = sv.hs;
   sp.E = sv.E;
   sp.ht = ht;
+  sp.wait_polls = g_state_wait_polls.load(std::memory_order_relaxed);
+  sp.withhold_loads = g_state_withhold_loads.load(std::memory_order_relaxed);
   if ((rc = encode_sw128_map(&sp.maps[0], sv.W, H, pr.TT, D)) || (rc = encode_sw128_map(&sp.maps[1], sv.Qt, H, pr.TT, D)) ||
       (rc = encode_sw128_map(&sp.maps[2], sv.Kb, H, pr.TT, D)) || (rc = encode_sw128_map(&sp.maps[3], sv.U, H, pr.TT, D)) ||
       (rc = encode_sw128_map(&sp.maps[4], sv.M, H, pr.TT, 64)))
@@ -945,6 +950,12 @@ int kda_b200_bwd_f32(const float* q, const float* k, const float* v, const float
 
 int kda_b200_debug_set_input_wait_polls(unsigned int polls) {
   g_input_wait_polls.store(polls ? polls : kDefaultWaitPolls, std::memory_order_relaxed);
+  return KDA_OK;
+}
+
+int kda_b200_debug_set_state_wait(unsigned int polls, int withhold_loads) {
+  g_state_wait_polls.store(polls ? polls : kDefaultWaitPolls, std::memory_order_relaxed);
+  g_state_withhold_loads.store(withhold_loads ? 1 : 0, std::memory_order_relaxed);
   return KDA_OK;
 }
 

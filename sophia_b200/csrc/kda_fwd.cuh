@@ -383,6 +383,8 @@ struct FwdStateParams {
   // W, Qt, Kbar, U as [T_total][H][128] and M as [T_total][H][64] bf16, for
   // 128B-swizzled TMA boxes of 64 channels x 64 rows (one operand atom each)
   CUtensorMap maps[5];
+  uint32_t wait_polls;   // poll limit of the consumers' wait for a chunk's operands
+  int withhold_loads;    // test hook: the producer issues nothing (that wait runs out)
 };
 
 __device__ __forceinline__ void load_vec128(float* dst, const float* src) {

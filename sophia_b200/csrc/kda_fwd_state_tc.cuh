@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
 
   if (warp == STATE_CONSUMERS / 32) {
     // ---- producer: chunk ci into stage ci % 2 once the stage's previous chunk is done
-    if (lane != 0) return;
+    if (lane != 0 || P.withhold_loads) return;
     int issued = 0;
     for (int ci = 0; ci < nchunks; ++ci) {
       const int st = ci & 1;
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(STATE_THREADS, 1) kda_fwd_state_tc_kernel(cons
     const int eo = ci & 1;
     const int nv = min(C, eos - (bos + ci * C));
     // this chunk's operands (loaded while the chunk before computed)
-    if (!tc::mbar_wait(full + stg, (ci >> 1) & 1)) *abort_flag = 1;
+    if (!tc::mbar_wait(full + stg, (ci >> 1) & 1, P.wait_polls)) *abort_flag = 1;
     if (tid == 0 && P.E) tc::bulk_wait_read_all();  // v_new of the chunk before has left sE
     consumer_sync();
     if (*abort_flag) { ok = false; break; }

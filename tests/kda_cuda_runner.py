@@ -21,8 +21,10 @@ def round_inputs_bf16(inp: dict) -> dict:
     return out
 
 
-def run_cuda(case: Case, inputs: dict | None = None, grads: bool = True, dtype: torch.dtype = torch.bfloat16) -> dict:
-    """dtype: the activations' dtype (bf16: the bf16 kernels; float32: the fp32 kernels)."""
+def run_cuda(case: Case, inputs: dict | None = None, grads: bool = True, dtype: torch.dtype = torch.bfloat16,
+             check_device_flag: bool = True) -> dict:
+    """dtype: the activations' dtype (bf16: the bf16 kernels; float32: the fp32 kernels).
+    check_device_flag=False leaves the device error flag unread, for the caller."""
     from sophia_b200 import chunk_kda, kda_layer
     inp = make_inputs(case) if inputs is None else inputs
     dev = "cuda"
@@ -52,8 +54,9 @@ def run_cuda(case: Case, inputs: dict | None = None, grads: bool = True, dtype: 
             g = t[k].grad
             res["d_" + k] = (torch.zeros_like(t[k]) if g is None else g).detach().float().cpu()
     torch.cuda.synchronize()
-    from sophia_b200 import _lib
-    assert _lib.device_error(reset=True) == 0, "a tensor-core kernel timed out"
+    if check_device_flag:
+        from sophia_b200 import _lib
+        assert _lib.device_error(reset=True) == 0, "a tensor-core kernel timed out"
     return res
 
 
