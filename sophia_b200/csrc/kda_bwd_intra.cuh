@@ -760,8 +760,6 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
 
   // ---- outputs: dk_hat (dq_hat left after the row side through M)
   if (r < nv) st_global16(P.dk_hat + ((size_t)(pos.t0 + r) * H + h) * D + c0, dk);
-  float dG[16];
-  ld_dg16(dgb, r, c0, dG);
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tbase, 512);
@@ -770,19 +768,23 @@ __global__ void __launch_bounds__(INTRA_THREADS, 1) kda_bwd_intra_kernel(BwdIntr
   // C = dGam_C + sum over the chunk of Kbar o dKbar: a suffix scan over the 16 rows of
   // this lane half, plus the totals of the later sub-chunk blocks.
   float* qtot = reinterpret_cast<float*>(smem + S::PSUM);  // [4][128] block totals, then [2][4][128] sums
+  {
+    // the scan runs down the columns of dGam in shared memory, in place: thread
+    // t takes channel t & 127 of block t >> 7 (a warp's 32 channels are one
+    // 128-byte span of a row, so the accesses are conflict-free)
+    const int cc = tid & 127, sb = tid >> 7;
+    float run = 0.f;
 #pragma unroll
-  for (int u = 0; u < 16; ++u) {
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
-      const float y = __shfl_down_sync(0xffffffffu, dG[u], o, 16);
-      if ((lane & 15) + o < 16) dG[u] += y;
+    for (int i = 15; i >= 0; --i) {
+      float* p = reinterpret_cast<float*>(dg_chunk(dgb, 16 * sb + i, cc)) + (cc & 3);
+      run += *p;
+      *p = run;
     }
+    qtot[sb * D + cc] = run;  // the block total
   }
-  if ((lane & 15) == 0) {
-#pragma unroll
-    for (int u = 0; u < 16; u += 4)
-      *reinterpret_cast<float4*>(qtot + s * D + c0 + u) = make_float4(dG[u], dG[u + 1], dG[u + 2], dG[u + 3]);
-  }
+  __syncthreads();
+  float dG[16];
+  ld_dg16(dgb, r, c0, dG);  // this thread's suffix sums
   cp_async_wait<0>();  // gate logits and vectors
   __syncthreads();
   float* coff = qtot + 4 * D;  // [4][128]: what the rows of block s add to their suffix sums
